@@ -1,0 +1,276 @@
+/*
+ * koemi_b200.h -- C ABI of libkoemi_b200.so, the sm_100a kernels behind the
+ * HERM forward hot path (affine scan, RMSNorm-SiLU, causal surprise with
+ * salient admission, MoE route / permute / grouped expert MLP / combine).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are device pointers to contiguous row-major data
+ *     on the device that is current when the call is made.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy
+ *     default stream. Every kernel is enqueued on that stream and the call
+ *     returns without synchronising.
+ *   - Inputs are borrowed, outputs and workspaces are owned by the caller.
+ *     The library never frees caller memory and allocates nothing on a
+ *     compute call (one small per-device status word is allocated on the
+ *     first call that uses a device).
+ *   - The return value is KOEMI_OK (0) or a negative KOEMI_ERR_* code; the
+ *     message for the calling thread is read with koemi_last_error().
+ *   - `dtype` arguments take a koemi_dtype value.
+ *
+ * Reference interfaces named below are paths inside the Koemi-5HOM project.
+ */
+#ifndef KOEMI_B200_H
+#define KOEMI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KOEMI_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define KOEMI_API __attribute__((visibility("default")))
+#else
+#define KOEMI_API
+#endif
+
+enum koemi_status {
+    KOEMI_OK = 0,
+    KOEMI_ERR_INVALID = -1,     /* bad shape, dtype, pointer or alignment */
+    KOEMI_ERR_CUDA = -2,        /* a CUDA runtime or driver call failed */
+    KOEMI_ERR_UNSUPPORTED = -3, /* valid request outside what the kernels cover */
+    KOEMI_ERR_TIMEOUT = -4,     /* a bounded device-side wait gave up */
+    KOEMI_ERR_WORKSPACE = -5    /* caller workspace smaller than required */
+};
+
+typedef enum koemi_dtype {
+    KOEMI_F32 = 0,
+    KOEMI_F16 = 1,
+    KOEMI_BF16 = 2,
+    KOEMI_F64 = 3,
+    KOEMI_I32 = 4,
+    KOEMI_I64 = 5,
+    KOEMI_BOOL = 6
+} koemi_dtype;
+
+/* ---------------------------------------------------------------- library */
+
+/* Mirrors CUDA_EXTENSION_ABI_VERSION / KOEMI_CUDA_ABI_VERSION
+ * (src/koemi/cuda_kernels/loader.py:32, core/rmsnorm_silu.cpp:74,
+ * moe/moe_kernels.cpp:257). Returns KOEMI_ABI_VERSION. */
+KOEMI_API int koemi_abi_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to `capacity`) and returns its full length. */
+KOEMI_API size_t koemi_last_error(char *buffer, size_t capacity);
+
+/* Reads and clears the device-side status word of `device`, written by a
+ * bounded wait that gave up (KOEMI_ERR_TIMEOUT) or 0. Synchronises `device`. */
+KOEMI_API int koemi_device_status(int device, int *status_out);
+
+/* Allocates the per-device status word and sets kernel attributes for
+ * `device` ahead of time. Call once per device before capturing any of
+ * these kernels into a CUDA graph; compute calls otherwise do it lazily. */
+KOEMI_API int koemi_device_init(int device);
+
+/* ------------------------------------------------------------ dense front */
+
+/* Affine recurrent scan h_t = a_t * h_{t-1} + b_t over [batch, length,
+ * features], carried from `initial` ([batch, features]; NULL = zeros).
+ * `retention` is [batch, length, features], or [batch, length] when
+ * `broadcast_retention` is nonzero (one coefficient per position).
+ * Accumulates in fp32 (fp64 for KOEMI_F64); `states` gets every h_t in dtype.
+ * Replaces dense/affine_scan.cu:119-167 (`forward` behind
+ * dense_affine_scan, dense/affine_scan.py:51-82). */
+KOEMI_API int koemi_dense_affine_scan_forward(const void *retention, const void *increment,
+                                    const void *initial, void *states,
+                                    int64_t batch, int64_t length, int64_t features,
+                                    int broadcast_retention, int dtype, void *stream);
+
+/* Reverse-time adjoint of the scan: grad_increment, grad_retention (full
+ * [batch, length, features] even when broadcast; the caller reduces) and
+ * grad_initial. Replaces dense/affine_scan.cu:169-226. */
+KOEMI_API int koemi_dense_affine_scan_backward(const void *retention, const void *initial,
+                                     const void *states, const void *grad_states,
+                                     void *grad_retention, void *grad_increment,
+                                     void *grad_initial, int64_t batch, int64_t length,
+                                     int64_t features, int broadcast_retention, int dtype,
+                                     void *stream);
+
+/* Gate epilogue of BoundedRecurrentState.gates (model/memory.py:22-26) with
+ * the padding masks of network.py:308-309, fused with the T==1 scan step:
+ * a = lo + (hi - lo) * sigmoid(pre_a), b = (1 - a) * tanh(pre_c);
+ * padding rows get a = 1, b = 0. `projections` is [rows, 2*features] fp32
+ * (pre_a | pre_c). Writes retention/increment (fp32, [rows, features]). */
+KOEMI_API int koemi_dense_bounded_gates(const float *projections, const uint8_t *valid,
+                              float *retention, float *increment, int64_t rows,
+                              int64_t features, float minimum_retention,
+                              float maximum_retention, void *stream);
+
+/* ------------------------------------------------------------- core front */
+
+/* y = silu(x * rsqrt(mean(x^2) + eps) * w), inv_rms[row] = rsqrt(...).
+ * x, w, y in dtype (F32/F16/BF16); inv_rms fp32 [rows].
+ * Replaces core/rmsnorm_silu.cu:63-91,148-217 (fused_rmsnorm_silu,
+ * core/rmsnorm_silu.py:37-42). */
+KOEMI_API int koemi_core_rmsnorm_silu_forward(const void *x, const void *weight, void *y,
+                                    float *inv_rms, int64_t rows, int64_t hidden, float eps,
+                                    int dtype, void *stream);
+
+/* Backward of the above: grad_x in dtype, grad_weight fp32 [hidden]
+ * (overwritten, deterministic two-stage reduction through `workspace` of
+ * koemi_core_rmsnorm_silu_backward_workspace() bytes).
+ * Replaces core/rmsnorm_silu.cu:94-132. */
+KOEMI_API size_t koemi_core_rmsnorm_silu_backward_workspace(int64_t rows, int64_t hidden);
+KOEMI_API int koemi_core_rmsnorm_silu_backward(const void *grad_y, const void *x, const void *weight,
+                                     const float *inv_rms, void *grad_x, float *grad_weight,
+                                     int64_t rows, int64_t hidden, void *workspace,
+                                     size_t workspace_bytes, int dtype, void *stream);
+
+/* Gated form y = silu(gate) * (x * rsqrt(mean(x^2) + eps) * w): the config-3
+ * variant of the fused norm (no reference kernel; restated from
+ * RootMeanSquareNorm, model/layers.py:14-16, and F.silu). */
+KOEMI_API int koemi_core_gated_rmsnorm_silu_forward(const void *x, const void *gate, const void *weight,
+                                          void *y, float *inv_rms, int64_t rows,
+                                          int64_t hidden, float eps, int dtype, void *stream);
+
+/* Plain RMSNorm with optional residual and row select, the three norms of the
+ * block (network.py:86,98; experts.py:127,204-205):
+ *   v = x + residual (residual may be NULL);
+ *   y = v * rsqrt(mean(v^2) + eps) * w        where keep[row] (or keep NULL)
+ *   y = x                                     where !keep[row].
+ * x/residual/y/w share `dtype`; `out_dtype` may differ (cast on store). */
+KOEMI_API int koemi_core_rmsnorm_forward(const void *x, const void *residual, const void *weight,
+                               const uint8_t *keep, void *y, int64_t rows, int64_t hidden,
+                               float eps, int dtype, int out_dtype, void *stream);
+
+/* ------------------------------------------------------------ think front */
+
+/* Causal surprise s = 1 - exp(-NLL / ln(C)) of target_ids under
+ * softmax(prior @ weight^T + bias) over C content ids; 0 where !valid.
+ * prior [rows, width], weight [C, width], bias [C] share `dtype`; out in
+ * `out_dtype` ([rows]). `nll_out` (fp32 [rows], may be NULL) receives the
+ * raw NLL. Needs koemi_think_surprise_workspace() bytes of workspace.
+ * Replaces think/surprise_kernel.cu:195-215 + 85-134 (causal_surprise,
+ * think/surprise.py:91-128) without materialising the [rows, C] logits. */
+KOEMI_API size_t koemi_think_surprise_workspace(int64_t rows, int64_t width, int64_t content_vocab,
+                                      int dtype);
+KOEMI_API int koemi_think_causal_surprise_forward(const void *prior, const void *weight, const void *bias,
+                                        const int64_t *target_ids, const uint8_t *valid,
+                                        void *out, float *nll_out, int64_t rows, int64_t width,
+                                        int64_t content_vocab, int dtype, int out_dtype,
+                                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* Salient admission and ring compaction (network.py:349 and
+ * LocalKeyValueMemory.salient_tail, model/memory.py:431-455): admits
+ * position t of row b when valid && surprise > threshold, then keeps the
+ * latest `capacity` admitted entries of [carried ring ; window] in temporal
+ * order, ring slots oldest first and empty slots (zero, invalid) leading.
+ * carried_* are [batch, carried, width] / [batch, carried]; keys/values are
+ * [batch, length, width]; outputs are [batch, capacity, width] /
+ * [batch, capacity] and must not alias the inputs.
+ * `admission_out` ([batch, length] bytes, may be NULL) receives the mask. */
+KOEMI_API int koemi_think_salient_admission(const float *carried_keys, const float *carried_values,
+                                  const uint8_t *carried_valid, const float *keys,
+                                  const float *values, const float *surprise,
+                                  const uint8_t *valid, float threshold,
+                                  float *out_keys, float *out_values, uint8_t *out_valid,
+                                  uint8_t *admission_out, int64_t batch, int64_t carried,
+                                  int64_t length, int64_t width, int64_t capacity,
+                                  void *stream);
+
+/* -------------------------------------------------------------- moe front */
+
+/* Content-hash top-k routing (model/experts.py:30-38,283-289): assignments
+ * [tokens, top_k] int64, -1 for invalid tokens, computed in 64-bit arithmetic
+ * exactly as the torch runner does. ids are KOEMI_I32 or KOEMI_I64.
+ * Replaces moe/moe_kernels.cu:45-66,352-388 (route_topk_valid,
+ * moe/__init__.py:128-176). */
+KOEMI_API int koemi_moe_route_topk(const void *token_ids, const void *previous_token_ids,
+                         const uint8_t *valid, int64_t *assignments, int64_t tokens,
+                         int64_t expert_count, int64_t top_k, int index_dtype, void *stream);
+
+/* Learned top-k gate (LearnedExpertMixture.forward, model/router.py:43-59):
+ * probabilities = softmax_fp32(gate_logits) per token, top-k in descending
+ * probability (selected on the logits, lowest expert id first among equal
+ * values), weights = raw probabilities (renormalize != 0 divides by their
+ * sum); invalid tokens get expert -1 / weight 0. gate_logits fp32
+ * [tokens, E]; `probabilities` (fp32 [tokens, E], may be NULL) receives the
+ * softmax, zeroed on invalid tokens, for the RouterStatistics sums. */
+KOEMI_API int koemi_moe_learned_topk(const float *gate_logits, const uint8_t *valid, int64_t *assignments,
+                           float *weights, float *probabilities, int64_t tokens,
+                           int64_t expert_count, int64_t top_k, int renormalize, void *stream);
+
+/* Stable permutation of token-expert pairs into expert segments
+ * (moe/moe_kernels.cu:68-145,390-499; experts.py:171-216,261-267): pair
+ * p = token*top_k + slot is valid when valid[token], 0 <= e < E and no earlier
+ * slot of that token names the same e; valid pairs are ordered by expert then
+ * by p, invalid pairs follow. Outputs: sorted_context [pairs, width] (rows of
+ * context, zero past the valid count), sorted_rows [pairs] (token of each
+ * sorted pair), sorted_experts [pairs] (E for invalid), segment_offsets
+ * [E + 1] (exclusive offsets, last = valid count) and, when non-NULL,
+ * pair_positions [pairs] (sorted index of pair p). sorted_context may be NULL
+ * to skip the gather. Bit-exact with a stable argsort. */
+KOEMI_API size_t koemi_moe_permute_workspace(int64_t tokens, int64_t top_k, int64_t expert_count);
+KOEMI_API int koemi_moe_permute_topk(const void *context, const void *assignments, const uint8_t *valid,
+                           void *sorted_context, int64_t *sorted_rows, int64_t *sorted_experts,
+                           int64_t *segment_offsets, int64_t *pair_positions, int64_t tokens,
+                           int64_t width, int64_t top_k, int64_t expert_count, int context_dtype,
+                           int assignment_dtype, void *workspace, size_t workspace_bytes,
+                           void *stream);
+
+/* Grouped gated expert MLP over sorted segments (GatedFeedForward,
+ * model/layers.py:19-29): for sorted pair i of expert e,
+ *   y_i = W_o[e] (silu(W_g[e] x_i + b_g[e]) * (W_v[e] x_i + b_v[e])) + b_o[e];
+ * rows at or past segment_offsets[E] are zero. Weights: gate/value
+ * [E, H, D], biases [E, H], output [E, D, H], output bias [E, D].
+ * BF16/F16 run on tcgen05 tensor cores (fp32 accumulate, the gated hidden
+ * rounded to dtype between the two contractions); F32 runs an fp32 FMA path.
+ * Workspace: koemi_moe_grouped_mlp_workspace() bytes.
+ * Replaces moe/moe_kernels.cu:147-199,276-320,501-558
+ * (grouped_expert_mlp_inference, moe/__init__.py:231-312). */
+KOEMI_API size_t koemi_moe_grouped_mlp_workspace(int64_t pairs, int64_t input_width, int64_t hidden_width,
+                                       int64_t expert_count, int dtype);
+KOEMI_API int koemi_moe_grouped_expert_mlp(const void *sorted_context, const int64_t *sorted_experts,
+                                 const int64_t *segment_offsets, const void *gate_weights,
+                                 const void *gate_biases, const void *value_weights,
+                                 const void *value_biases, const void *output_weights,
+                                 const void *output_biases, void *output, int64_t pairs,
+                                 int64_t input_width, int64_t hidden_width, int64_t expert_count,
+                                 int dtype, void *workspace, size_t workspace_bytes,
+                                 void *stream);
+
+/* Combine sorted expert outputs into token rows: out[row] = sum of the row's
+ * valid pair outputs / top_k, summed in sorted-pair order (deterministic, no
+ * float atomics). out [tokens, width] in dtype.
+ * Replaces moe/moe_kernels.cu:201-229,560-582 (combine_topk,
+ * moe/__init__.py:315-360). Workspace: koemi_moe_combine_workspace(). */
+KOEMI_API size_t koemi_moe_combine_workspace(int64_t tokens, int64_t pairs, int64_t top_k);
+KOEMI_API int koemi_moe_combine_topk(const void *expert_outputs, const int64_t *sorted_rows,
+                           const int64_t *segment_offsets, void *out, int64_t pairs,
+                           int64_t width, int64_t tokens, int64_t top_k, int64_t expert_count,
+                           int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Model-level fused combine: for each token row,
+ *   u = context[row] + sum_slot scale_slot * expert_out[pair_positions[row*k+slot]]
+ * over the row's valid pairs (pair_positions[p] < segment_offsets[E]), in
+ * slot order, where scale_slot = weights[row*k+slot] (or 1/top_k when
+ * weights is NULL); then out[row] = RMSNorm(u) * norm_weight where
+ * valid[row], else context[row] (experts.py:136-142; router.py:70-73,96-97).
+ * context/out fp32 [tokens, width]; expert_out in dtype. */
+KOEMI_API int koemi_moe_combine_residual_rmsnorm(const float *context, const void *expert_out,
+                                       const int64_t *pair_positions,
+                                       const int64_t *segment_offsets, const float *weights,
+                                       const uint8_t *valid, const float *norm_weight,
+                                       float *out, int64_t tokens, int64_t width,
+                                       int64_t top_k, int64_t expert_count, float eps,
+                                       int dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KOEMI_B200_H */

@@ -1,0 +1,590 @@
+// MoE front: routing, stable permutation into expert segments, gather and
+// deterministic combines. All index work is integer and bit-exact.
+//
+// Permutation = stable counting sort of pair keys (expert id, or E for an
+// invalid pair). Pass 1 counts keys per (block of 1024 pairs, bucket); one CTA
+// turns the counts into bucket-major exclusive offsets; pass 2 recomputes each
+// block's keys and scatters every pair to offset[bucket][block] + its rank
+// among equal keys inside the block (warp match-any ranks plus per-warp
+// prefix counts), which is exactly the order of a stable argsort. Keys with
+// more than 11 bits (E >= 2048) run the same counting sort once per 11-bit
+// digit, least significant digit first (an LSD radix sort).
+// Reference: moe/moe_kernels.cu:45-145 (route, pair keys, CUB 64-bit radix
+// sort, histogram, scan, gathers) and model/experts.py:171-216,261-289.
+#include "vec.cuh"
+
+namespace koemi {
+namespace {
+
+// ------------------------------------------------------------------ routing
+
+__device__ __forceinline__ uint64_t content_hash(uint64_t token, uint64_t previous) {
+    // Same arithmetic as content_dispatch_hash (experts.py:30-38): 64-bit
+    // products masked to 32 bits, two multiply-xorshift rounds.
+    uint64_t value = (token * 1000003ull + previous * 97409ull) & 0xFFFFFFFFull;
+    value ^= value >> 16;
+    value = (value * 0x45D9F3Bull) & 0xFFFFFFFFull;
+    value ^= value >> 16;
+    value = (value * 0x45D9F3Bull) & 0xFFFFFFFFull;
+    return value ^ (value >> 16);
+}
+
+template <typename Index>
+__global__ void route_topk_kernel(const Index *__restrict__ tokens, const Index *__restrict__ previous,
+                                  const uint8_t *__restrict__ valid, int64_t *__restrict__ out,
+                                  int64_t count, int64_t experts, int64_t top_k) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= count) return;
+    const bool ok = valid == nullptr || valid[t] != 0;
+    const uint64_t hash = content_hash(static_cast<uint64_t>(static_cast<int64_t>(tokens[t])),
+                                       static_cast<uint64_t>(static_cast<int64_t>(previous[t])));
+    for (int64_t s = 0; s < top_k; ++s) {
+        // int64 sum as in assign_top_k (experts.py:287-288): no 2^32 wrap.
+        const uint64_t slot_hash = hash + static_cast<uint64_t>(s) * 0x9E3779B9ull;
+        out[t * top_k + s] = ok ? static_cast<int64_t>(slot_hash % static_cast<uint64_t>(experts)) : -1;
+    }
+}
+
+// One warp per token: fp32 softmax over E logits, top-k chosen on the logits
+// (monotone in the probability) with the lowest expert id winning ties.
+__global__ void learned_topk_kernel(const float *__restrict__ logits, const uint8_t *__restrict__ valid,
+                                    int64_t *__restrict__ assignments, float *__restrict__ weights,
+                                    float *__restrict__ probabilities, int64_t tokens, int64_t experts,
+                                    int64_t top_k, int renormalize) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= tokens) return;
+    const bool ok = valid == nullptr || valid[t] != 0;
+    const float *row = logits + t * experts;
+    float m = -INFINITY;
+    for (int64_t e = lane; e < experts; e += 32) m = fmaxf(m, row[e]);
+    m = warp_max(m);
+    float sum = 0.0f;
+    for (int64_t e = lane; e < experts; e += 32) sum += expf(row[e] - m);
+    sum = warp_sum(sum);
+    if (probabilities != nullptr) {
+        for (int64_t e = lane; e < experts; e += 32) {
+            probabilities[t * experts + e] = ok ? expf(row[e] - m) / sum : 0.0f;
+        }
+    }
+    float chosen_sum = 0.0f;
+    float last_value = INFINITY;
+    int64_t last_index = -1;
+    for (int64_t k = 0; k < top_k; ++k) {
+        // Next candidate: largest logit strictly "after" (last_value, last_index)
+        // in the order (value desc, index asc).
+        float best = -INFINITY;
+        int64_t best_index = INT64_MAX;
+        for (int64_t e = lane; e < experts; e += 32) {
+            const float v = row[e];
+            const bool after = (v < last_value) || (v == last_value && e > last_index);
+            if (after && (v > best || (v == best && e < best_index))) {
+                best = v;
+                best_index = e;
+            }
+        }
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, offset);
+            const int64_t oi = __shfl_xor_sync(0xffffffffu, best_index, offset);
+            if (ov > best || (ov == best && oi < best_index)) {
+                best = ov;
+                best_index = oi;
+            }
+        }
+        last_value = best;
+        last_index = best_index;
+        const float p = expf(best - m) / sum;
+        chosen_sum += p;
+        if (lane == 0) {
+            assignments[t * top_k + k] = ok ? best_index : -1;
+            weights[t * top_k + k] = ok ? p : 0.0f;
+        }
+    }
+    if (renormalize && ok && lane == 0 && chosen_sum > 0.0f) {
+        for (int64_t k = 0; k < top_k; ++k) weights[t * top_k + k] /= chosen_sum;
+    }
+}
+
+// --------------------------------------------------------------- permutation
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kPairsPerThread = 4;
+constexpr int kPairsPerBlock = kSortThreads * kPairsPerThread;
+constexpr int kDigitBits = 11;
+constexpr int kMaxBuckets = 1 << kDigitBits;
+
+// Key of pair p: its expert when valid (first occurrence in the token's
+// slots, experts.py:261-267), else E.
+template <typename Index>
+__device__ __forceinline__ int32_t pair_key(const Index *assignments, const uint8_t *valid,
+                                            int64_t pair, int64_t top_k, int64_t experts) {
+    const int64_t token = pair / top_k;
+    const int64_t slot = pair - token * top_k;
+    const int64_t e = static_cast<int64_t>(assignments[pair]);
+    bool ok = (valid == nullptr || valid[token] != 0) && e >= 0 && e < experts;
+    for (int64_t s = 0; s < slot && ok; ++s) ok = static_cast<int64_t>(assignments[token * top_k + s]) != e;
+    return ok ? static_cast<int32_t>(e) : static_cast<int32_t>(experts);
+}
+
+template <typename Index>
+__global__ void build_keys_kernel(const Index *__restrict__ assignments, const uint8_t *__restrict__ valid,
+                                  int32_t *__restrict__ keys, int32_t *__restrict__ values, int64_t pairs,
+                                  int64_t top_k, int64_t experts) {
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (p >= pairs) return;
+    keys[p] = pair_key(assignments, valid, p, top_k, experts);
+    values[p] = static_cast<int32_t>(p);
+}
+
+// counts[bucket * blocks + block] = number of keys of `block` in `bucket`.
+__global__ __launch_bounds__(kSortThreads) void digit_count_kernel(const int32_t *__restrict__ keys, int64_t pairs,
+                                                                   int shift, int buckets,
+                                                                   int32_t *__restrict__ counts) {
+    extern __shared__ int32_t hist[];
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) hist[b] = 0;
+    __syncthreads();
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kPairsPerBlock;
+    for (int r = 0; r < kPairsPerThread; ++r) {
+        const int64_t p = base + r * kSortThreads + threadIdx.x;
+        if (p < pairs) atomicAdd(&hist[(keys[p] >> shift) & (buckets - 1)], 1);
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
+        counts[static_cast<int64_t>(b) * gridDim.x + blockIdx.x] = hist[b];
+    }
+}
+
+// Exclusive scan of the bucket-major counts array in place (one CTA).
+__global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restrict__ data, int64_t n) {
+    __shared__ int32_t warp_totals[32];
+    __shared__ int32_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    for (int64_t base = 0; base < n; base += 1024) {
+        const int64_t i = base + threadIdx.x;
+        const int32_t v = i < n ? data[i] : 0;
+        int32_t inclusive = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t other = __shfl_up_sync(0xffffffffu, inclusive, o);
+            if (lane >= o) inclusive += other;
+        }
+        if (lane == 31) warp_totals[warp] = inclusive;
+        __syncthreads();
+        if (warp == 0) {
+            int32_t t = warp_totals[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t other = __shfl_up_sync(0xffffffffu, t, o);
+                if (lane >= o) t += other;
+            }
+            warp_totals[lane] = t;
+        }
+        __syncthreads();
+        const int32_t warp_prefix = warp == 0 ? 0 : warp_totals[warp - 1];
+        const int32_t c = carry;
+        if (i < n) data[i] = c + warp_prefix + inclusive - v;
+        __syncthreads();
+        if (threadIdx.x == 0) carry = c + warp_totals[31];
+        __syncthreads();
+    }
+}
+
+// Scatter with the block's stable ranks. Round r handles pairs
+// base + r*256 + tid, so (round, warp, lane) order equals pair order.
+__global__ __launch_bounds__(kSortThreads) void digit_scatter_kernel(
+    const int32_t *__restrict__ keys_in, const int32_t *__restrict__ values_in, int64_t pairs, int shift,
+    int buckets, const int32_t *__restrict__ offsets, int32_t *__restrict__ keys_out,
+    int32_t *__restrict__ values_out) {
+    extern __shared__ int32_t shared[];
+    int32_t *running = shared;                   // [buckets]
+    int32_t *warp_counts = shared + buckets;     // [kSortWarps][buckets]
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
+        running[b] = offsets[static_cast<int64_t>(b) * gridDim.x + blockIdx.x];
+    }
+    for (int i = threadIdx.x; i < kSortWarps * buckets; i += kSortThreads) warp_counts[i] = 0;
+    __syncthreads();
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kPairsPerBlock;
+    const unsigned lower = (1u << lane) - 1u;
+    for (int r = 0; r < kPairsPerThread; ++r) {
+        const int64_t p = base + r * kSortThreads + threadIdx.x;
+        const bool live = p < pairs;
+        const int32_t key = live ? keys_in[p] : 0;
+        const int digit = live ? (key >> shift) & (buckets - 1) : -1 - lane;  // unique when dead
+        const unsigned same = __match_any_sync(0xffffffffu, digit);
+        const int rank = __popc(same & lower);
+        const bool leader = (same & lower) == 0;
+        if (live && leader) warp_counts[warp * buckets + digit] = __popc(same);
+        __syncthreads();
+        int32_t before = 0;
+        if (live) {
+            for (int w = 0; w < warp; ++w) before += warp_counts[w * buckets + digit];
+            const int32_t position = running[digit] + before + rank;
+            keys_out[position] = key;
+            values_out[position] = values_in[p];
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
+            int32_t total = 0;
+            for (int w = 0; w < kSortWarps; ++w) {
+                total += warp_counts[w * buckets + b];
+                warp_counts[w * buckets + b] = 0;
+            }
+            running[b] += total;
+        }
+        __syncthreads();
+    }
+}
+
+// segment_offsets[e] = first sorted index whose key >= e (keys are sorted).
+__global__ void segment_offsets_kernel(const int32_t *__restrict__ sorted_keys, int64_t pairs,
+                                       int64_t experts, int64_t *__restrict__ offsets) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e > experts) return;
+    int64_t lo = 0, hi = pairs;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (sorted_keys[mid] < e) lo = mid + 1; else hi = mid;
+    }
+    offsets[e] = lo;
+}
+
+__global__ void finish_permutation_kernel(const int32_t *__restrict__ sorted_keys,
+                                          const int32_t *__restrict__ sorted_pairs, int64_t pairs,
+                                          int64_t top_k, int64_t *__restrict__ sorted_rows,
+                                          int64_t *__restrict__ sorted_experts,
+                                          int64_t *__restrict__ pair_positions) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= pairs) return;
+    const int64_t pair = sorted_pairs[i];
+    if (sorted_rows != nullptr) sorted_rows[i] = pair / top_k;
+    if (sorted_experts != nullptr) sorted_experts[i] = sorted_keys[i];
+    if (pair_positions != nullptr) pair_positions[pair] = i;
+}
+
+// One warp per sorted row: copy the token's context row, zero past the
+// valid count (moe_kernels.cu:122-145).
+template <typename T>
+__global__ void gather_rows_kernel(const T *__restrict__ context, const int32_t *__restrict__ sorted_pairs,
+                                   const int64_t *__restrict__ valid_count, T *__restrict__ out,
+                                   int64_t pairs, int64_t width, int64_t top_k, bool vector) {
+    const int lane = threadIdx.x & 31;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (i >= pairs) return;
+    const bool live = i < *valid_count;
+    const int64_t row = sorted_pairs[i] / top_k;
+    T *dst = out + i * width;
+    const T *src = context + row * width;
+    if (vector) {
+        constexpr int W = 16 / sizeof(T);
+        const int64_t packets = width / W;
+        for (int64_t p = lane; p < packets; p += 32) {
+            const uint4 v = live ? load_stream(src + p * W) : make_uint4(0, 0, 0, 0);
+            store_stream(dst + p * W, v);
+        }
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = live ? src[c] : from_acc<T>(0.0f);
+    }
+}
+
+// --------------------------------------------------------------- combines
+
+// slot lists per token: count[row] (atomic), slots[row * cap + j].
+__global__ void collect_rows_kernel(const int64_t *__restrict__ sorted_rows,
+                                    const int64_t *__restrict__ segment_offsets, int64_t experts,
+                                    int64_t tokens, int32_t *__restrict__ counts,
+                                    int32_t *__restrict__ slots, int64_t cap) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= segment_offsets[experts]) return;
+    const int64_t row = sorted_rows[i];
+    if (row < 0 || row >= tokens) return;
+    const int32_t j = atomicAdd(&counts[row], 1);
+    if (j < cap) slots[row * cap + j] = static_cast<int32_t>(i);
+}
+
+template <typename T>
+__global__ void combine_rows_kernel(const T *__restrict__ y, const int32_t *__restrict__ counts,
+                                    int32_t *__restrict__ slots, int64_t cap, T *__restrict__ out,
+                                    int64_t tokens, int64_t width, float inv_k) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= tokens) return;
+    int n = counts[row];
+    if (n > cap) n = static_cast<int>(cap);
+    int32_t *list = slots + row * cap;
+    if (lane == 0) {  // ascending sorted-index order, independent of atomic order
+        for (int a = 1; a < n; ++a) {
+            const int32_t v = list[a];
+            int b = a - 1;
+            while (b >= 0 && list[b] > v) {
+                list[b + 1] = list[b];
+                --b;
+            }
+            list[b + 1] = v;
+        }
+    }
+    __syncwarp();
+    for (int64_t c = lane; c < width; c += 32) {
+        float acc = 0.0f;
+        for (int j = 0; j < n; ++j) acc += to_acc(y[static_cast<int64_t>(list[j]) * width + c]) * inv_k;
+        out[row * width + c] = from_acc<T>(acc);
+    }
+}
+
+// Fused expert combine + residual + RMSNorm (experts.py:136-142,
+// router.py:70-73,96-97): one warp per token row, fp32 context.
+template <typename T>
+__global__ void combine_residual_rmsnorm_kernel(const float *__restrict__ context, const T *__restrict__ y,
+                                                const int64_t *__restrict__ positions,
+                                                const int64_t *__restrict__ segment_offsets,
+                                                const float *__restrict__ weights,
+                                                const uint8_t *__restrict__ valid,
+                                                const float *__restrict__ norm_weight, float *__restrict__ out,
+                                                int64_t tokens, int64_t width, int64_t top_k,
+                                                int64_t experts, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= tokens) return;
+    const float *cr = context + row * width;
+    float *orow = out + row * width;
+    if (valid != nullptr && valid[row] == 0) {
+        for (int64_t c = lane; c < width; c += 32) orow[c] = cr[c];
+        return;
+    }
+    const int64_t valid_pairs = segment_offsets[experts];
+    const float inv_k = 1.0f / static_cast<float>(top_k);
+    float sum = 0.0f;
+    // pass 1: u = context + sum_slot scale * y, stored to out, sum of squares
+    for (int64_t c = lane; c < width; c += 32) {
+        float update = 0.0f;
+        for (int64_t s = 0; s < top_k; ++s) {
+            const int64_t pos = positions[row * top_k + s];
+            if (pos < 0 || pos >= valid_pairs) continue;
+            const float scale = weights != nullptr ? weights[row * top_k + s] : inv_k;
+            update += to_acc(y[pos * width + c]) * scale;
+        }
+        const float u = cr[c] + update;
+        orow[c] = u;
+        sum = fmaf(u, u, sum);
+    }
+    sum = warp_sum(sum);
+    const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+    for (int64_t c = lane; c < width; c += 32) orow[c] = orow[c] * inv * norm_weight[c];
+}
+
+// Workspace layout of the permutation.
+struct PermuteLayout {
+    int64_t blocks;
+    int buckets;
+    int passes;
+    size_t keys_a, values_a, keys_b, values_b, counts, total;
+};
+
+PermuteLayout permute_layout(int64_t pairs, int64_t experts) {
+    PermuteLayout l{};
+    l.blocks = pairs > 0 ? ceil_div(pairs, kPairsPerBlock) : 1;
+    int bits = 1;
+    while ((int64_t(1) << bits) < experts + 1) ++bits;
+    l.passes = (bits + kDigitBits - 1) / kDigitBits;
+    l.buckets = l.passes == 1 ? (1 << bits) : kMaxBuckets;
+    auto align = [](size_t v) { return (v + 255) & ~size_t(255); };
+    size_t offset = 0;
+    l.keys_a = offset; offset = align(offset + pairs * sizeof(int32_t));
+    l.values_a = offset; offset = align(offset + pairs * sizeof(int32_t));
+    l.keys_b = offset; offset = align(offset + pairs * sizeof(int32_t));
+    l.values_b = offset; offset = align(offset + pairs * sizeof(int32_t));
+    l.counts = offset; offset = align(offset + static_cast<size_t>(l.blocks) * l.buckets * sizeof(int32_t));
+    l.total = offset;
+    return l;
+}
+
+}  // namespace
+}  // namespace koemi
+
+using namespace koemi;
+
+extern "C" int koemi_moe_route_topk(const void *token_ids, const void *previous_token_ids,
+                                    const uint8_t *valid, int64_t *assignments, int64_t tokens,
+                                    int64_t expert_count, int64_t top_k, int index_dtype,
+                                    void *stream) {
+    clear_error();
+    if (tokens < 0) return fail(KOEMI_ERR_INVALID, "tokens must be non-negative");
+    if (expert_count < 1 || expert_count > (1 << 20)) return fail(KOEMI_ERR_INVALID, "expert_count must be in [1, 2^20]");
+    if (top_k < 1 || top_k > 256 || top_k > expert_count) return fail(KOEMI_ERR_INVALID, "top_k must be in [1, min(256, expert_count)]");
+    if (tokens == 0) return KOEMI_OK;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 256));
+    cudaStream_t s = as_stream(stream);
+    if (index_dtype == KOEMI_I64) {
+        route_topk_kernel<int64_t><<<blocks, 256, 0, s>>>(static_cast<const int64_t *>(token_ids),
+            static_cast<const int64_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k);
+    } else if (index_dtype == KOEMI_I32) {
+        route_topk_kernel<int32_t><<<blocks, 256, 0, s>>>(static_cast<const int32_t *>(token_ids),
+            static_cast<const int32_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k);
+    } else {
+        return fail(KOEMI_ERR_INVALID, "token ids must be int32 or int64");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_moe_learned_topk(const float *gate_logits, const uint8_t *valid,
+                                      int64_t *assignments, float *weights, float *probabilities,
+                                      int64_t tokens, int64_t expert_count, int64_t top_k,
+                                      int renormalize, void *stream) {
+    clear_error();
+    if (tokens < 0) return fail(KOEMI_ERR_INVALID, "tokens must be non-negative");
+    if (expert_count < 1 || top_k < 1 || top_k > expert_count) return fail(KOEMI_ERR_INVALID, "top_k must be in [1, expert_count]");
+    if (tokens == 0) return KOEMI_OK;
+    const int warps = 8;
+    learned_topk_kernel<<<static_cast<unsigned>(ceil_div(tokens, warps)), warps * 32, 0, as_stream(stream)>>>(
+        gate_logits, valid, assignments, weights, probabilities, tokens, expert_count, top_k, renormalize);
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" size_t koemi_moe_permute_workspace(int64_t tokens, int64_t top_k, int64_t expert_count) {
+    if (tokens < 0 || top_k < 1 || expert_count < 1) return 0;
+    return permute_layout(tokens * top_k, expert_count).total;
+}
+
+extern "C" int koemi_moe_permute_topk(const void *context, const void *assignments,
+                                      const uint8_t *valid, void *sorted_context,
+                                      int64_t *sorted_rows, int64_t *sorted_experts,
+                                      int64_t *segment_offsets, int64_t *pair_positions,
+                                      int64_t tokens, int64_t width, int64_t top_k,
+                                      int64_t expert_count, int context_dtype,
+                                      int assignment_dtype, void *workspace,
+                                      size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (tokens < 0 || width < 0) return fail(KOEMI_ERR_INVALID, "tokens and width must be non-negative");
+    if (expert_count < 1 || expert_count > (1 << 20)) return fail(KOEMI_ERR_INVALID, "expert_count must be in [1, 2^20]");
+    if (top_k < 1 || top_k > 256) return fail(KOEMI_ERR_INVALID, "top_k must be in [1, 256]");
+    if (tokens * top_k >= (int64_t(1) << 31)) return fail(KOEMI_ERR_UNSUPPORTED, "more than 2^31 pairs");
+    if (segment_offsets == nullptr) return fail(KOEMI_ERR_INVALID, "segment_offsets must be non-NULL");
+    const int64_t pairs = tokens * top_k;
+    const PermuteLayout l = permute_layout(pairs, expert_count);
+    if (workspace_bytes < l.total) return fail(KOEMI_ERR_WORKSPACE, "permute needs %zu workspace bytes", l.total);
+    cudaStream_t s = as_stream(stream);
+    if (pairs == 0) {
+        KOEMI_CUDA_TRY(cudaMemsetAsync(segment_offsets, 0, (expert_count + 1) * sizeof(int64_t), s));
+        return KOEMI_OK;
+    }
+    char *ws = static_cast<char *>(workspace);
+    int32_t *keys_a = reinterpret_cast<int32_t *>(ws + l.keys_a);
+    int32_t *values_a = reinterpret_cast<int32_t *>(ws + l.values_a);
+    int32_t *keys_b = reinterpret_cast<int32_t *>(ws + l.keys_b);
+    int32_t *values_b = reinterpret_cast<int32_t *>(ws + l.values_b);
+    int32_t *counts = reinterpret_cast<int32_t *>(ws + l.counts);
+    const unsigned pair_blocks = static_cast<unsigned>(ceil_div(pairs, 256));
+    if (assignment_dtype == KOEMI_I64) {
+        build_keys_kernel<int64_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int64_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
+    } else if (assignment_dtype == KOEMI_I32) {
+        build_keys_kernel<int32_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int32_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
+    } else {
+        return fail(KOEMI_ERR_INVALID, "assignments must be int32 or int64");
+    }
+    KOEMI_LAUNCH_CHECK();
+    const size_t count_smem = static_cast<size_t>(l.buckets) * sizeof(int32_t);
+    const size_t scatter_smem = static_cast<size_t>(l.buckets) * (kSortWarps + 1) * sizeof(int32_t);
+    if (scatter_smem > 48 * 1024) {
+        KOEMI_CUDA_TRY(cudaFuncSetAttribute(digit_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(scatter_smem)));
+    }
+    for (int pass = 0; pass < l.passes; ++pass) {
+        const int shift = pass * kDigitBits;
+        digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
+        KOEMI_LAUNCH_CHECK();
+        exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets);
+        KOEMI_LAUNCH_CHECK();
+        digit_scatter_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, scatter_smem, s>>>(
+            keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b);
+        KOEMI_LAUNCH_CHECK();
+        int32_t *t = keys_a; keys_a = keys_b; keys_b = t;
+        t = values_a; values_a = values_b; values_b = t;
+    }
+    segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
+    KOEMI_LAUNCH_CHECK();
+    finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
+    KOEMI_LAUNCH_CHECK();
+    if (sorted_context != nullptr && width > 0) {
+        const size_t es = dtype_size(context_dtype);
+        const bool vector = (width * es) % 16 == 0 && aligned(context, 16) && aligned(sorted_context, 16);
+        const unsigned blocks = static_cast<unsigned>(ceil_div(pairs, 8));
+        const int64_t *valid_count = segment_offsets + expert_count;
+        switch (context_dtype) {
+            case KOEMI_F32: gather_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float *>(context), values_a, valid_count, static_cast<float *>(sorted_context), pairs, width, top_k, vector); break;
+            case KOEMI_F16: gather_rows_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(context), values_a, valid_count, static_cast<__half *>(sorted_context), pairs, width, top_k, vector); break;
+            case KOEMI_BF16: gather_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(context), values_a, valid_count, static_cast<__nv_bfloat16 *>(sorted_context), pairs, width, top_k, vector); break;
+            default: return fail(KOEMI_ERR_INVALID, "context must be f32, f16 or bf16");
+        }
+        KOEMI_LAUNCH_CHECK();
+    }
+    return KOEMI_OK;
+}
+
+extern "C" size_t koemi_moe_combine_workspace(int64_t tokens, int64_t pairs, int64_t top_k) {
+    (void)pairs;
+    if (tokens <= 0 || top_k <= 0) return 256;
+    const size_t counts = ((static_cast<size_t>(tokens) * 4) + 255) & ~size_t(255);
+    return counts + static_cast<size_t>(tokens) * top_k * 4;
+}
+
+extern "C" int koemi_moe_combine_topk(const void *expert_outputs, const int64_t *sorted_rows,
+                                      const int64_t *segment_offsets, void *out, int64_t pairs,
+                                      int64_t width, int64_t tokens, int64_t top_k,
+                                      int64_t expert_count, int dtype, void *workspace,
+                                      size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (tokens < 0 || width < 0 || pairs < 0) return fail(KOEMI_ERR_INVALID, "sizes must be non-negative");
+    if (top_k < 1 || expert_count < 0) return fail(KOEMI_ERR_INVALID, "top_k must be positive");
+    if (tokens == 0 || width == 0) return KOEMI_OK;
+    if (workspace_bytes < koemi_moe_combine_workspace(tokens, pairs, top_k)) {
+        return fail(KOEMI_ERR_WORKSPACE, "combine needs %zu workspace bytes", koemi_moe_combine_workspace(tokens, pairs, top_k));
+    }
+    cudaStream_t s = as_stream(stream);
+    int32_t *counts = static_cast<int32_t *>(workspace);
+    int32_t *slots = reinterpret_cast<int32_t *>(static_cast<char *>(workspace) + (((static_cast<size_t>(tokens) * 4) + 255) & ~size_t(255)));
+    KOEMI_CUDA_TRY(cudaMemsetAsync(counts, 0, tokens * sizeof(int32_t), s));
+    if (pairs > 0) {
+        collect_rows_kernel<<<static_cast<unsigned>(ceil_div(pairs, 256)), 256, 0, s>>>(sorted_rows, segment_offsets, expert_count, tokens, counts, slots, top_k);
+        KOEMI_LAUNCH_CHECK();
+    }
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
+    const float inv_k = 1.0f / static_cast<float>(top_k);
+    switch (dtype) {
+        case KOEMI_F32: combine_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float *>(expert_outputs), counts, slots, top_k, static_cast<float *>(out), tokens, width, inv_k); break;
+        case KOEMI_F16: combine_rows_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(expert_outputs), counts, slots, top_k, static_cast<__half *>(out), tokens, width, inv_k); break;
+        case KOEMI_BF16: combine_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(expert_outputs), counts, slots, top_k, static_cast<__nv_bfloat16 *>(out), tokens, width, inv_k); break;
+        default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const void *expert_out,
+                                                  const int64_t *pair_positions,
+                                                  const int64_t *segment_offsets,
+                                                  const float *weights, const uint8_t *valid,
+                                                  const float *norm_weight, float *out,
+                                                  int64_t tokens, int64_t width, int64_t top_k,
+                                                  int64_t expert_count, float eps, int dtype,
+                                                  void *stream) {
+    clear_error();
+    if (tokens < 0 || width < 0 || top_k < 1) return fail(KOEMI_ERR_INVALID, "bad combine sizes");
+    if (tokens == 0 || width == 0) return KOEMI_OK;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: combine_residual_rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        case KOEMI_F16: combine_residual_rmsnorm_kernel<__half><<<blocks, 256, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        case KOEMI_BF16: combine_residual_rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}

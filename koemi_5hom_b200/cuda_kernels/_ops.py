@@ -1,0 +1,327 @@
+"""``torch.library`` custom ops over the C-ABI of ``libkoemi_b200.so``.
+
+Each op allocates its outputs and workspace from torch's caching allocator,
+then launches the native kernels on the current stream through ctypes. The
+ops are registered under the ``koemi_b200`` namespace with fake (meta)
+implementations, so they can be captured in CUDA graphs and traced. There is
+no CPU implementation: a CPU tensor reaching an op is a programming error,
+reported by the fronts before dispatch.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from koemi_5hom_b200 import _native
+from koemi_5hom_b200._native import call, dtype_code, ptr, stream_of
+
+BF16_OR_F16 = (torch.bfloat16, torch.float16)
+
+
+def _prepare(tensor: Tensor) -> int:
+    _native.ensure_device(tensor.device)
+    return stream_of(tensor)
+
+
+# ---------------------------------------------------------------- dense front
+
+@torch.library.custom_op("koemi_b200::affine_scan_forward", mutates_args=())
+def affine_scan_forward(retention: Tensor, increment: Tensor, initial: Tensor, broadcast: bool) -> Tensor:
+    stream = _prepare(increment)
+    batch, length = increment.shape[0], increment.shape[1]
+    features = increment.numel() // max(batch * length, 1) if batch * length else 0
+    states = torch.empty_like(increment)
+    call("koemi_dense_affine_scan_forward", ptr(retention), ptr(increment), ptr(initial), ptr(states),
+         batch, length, features, int(broadcast), dtype_code(increment.dtype), stream)
+    return states
+
+
+@affine_scan_forward.register_fake
+def _(retention, increment, initial, broadcast):
+    return torch.empty_like(increment)
+
+
+@torch.library.custom_op("koemi_b200::affine_scan_backward", mutates_args=())
+def affine_scan_backward(retention: Tensor, initial: Tensor, states: Tensor, grad_states: Tensor,
+                         broadcast: bool) -> tuple[Tensor, Tensor, Tensor]:
+    stream = _prepare(states)
+    batch, length = states.shape[0], states.shape[1]
+    features = states.numel() // max(batch * length, 1) if batch * length else 0
+    grad_retention = torch.empty_like(states)
+    grad_increment = torch.empty_like(states)
+    grad_initial = torch.empty_like(initial)
+    call("koemi_dense_affine_scan_backward", ptr(retention), ptr(initial), ptr(states), ptr(grad_states),
+         ptr(grad_retention), ptr(grad_increment), ptr(grad_initial), batch, length, features,
+         int(broadcast), dtype_code(states.dtype), stream)
+    return grad_retention, grad_increment, grad_initial
+
+
+@affine_scan_backward.register_fake
+def _(retention, initial, states, grad_states, broadcast):
+    return torch.empty_like(states), torch.empty_like(states), torch.empty_like(initial)
+
+
+@torch.library.custom_op("koemi_b200::bounded_gates", mutates_args=())
+def bounded_gates(projections: Tensor, valid: Tensor, minimum: float, maximum: float) -> tuple[Tensor, Tensor]:
+    stream = _prepare(projections)
+    rows, features = projections.shape[0], projections.shape[1] // 2
+    retention = projections.new_empty(rows, features)
+    increment = projections.new_empty(rows, features)
+    call("koemi_dense_bounded_gates", ptr(projections), ptr(valid), ptr(retention), ptr(increment), rows,
+         features, minimum, maximum, stream)
+    return retention, increment
+
+
+@bounded_gates.register_fake
+def _(projections, valid, minimum, maximum):
+    rows, features = projections.shape[0], projections.shape[1] // 2
+    return projections.new_empty(rows, features), projections.new_empty(rows, features)
+
+
+# ----------------------------------------------------------------- core front
+
+@torch.library.custom_op("koemi_b200::rmsnorm_silu_forward", mutates_args=())
+def rmsnorm_silu_forward(x: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    stream = _prepare(x)
+    rows, hidden = x.shape
+    y = torch.empty_like(x)
+    inv_rms = torch.empty(rows, dtype=torch.float32, device=x.device)
+    call("koemi_core_rmsnorm_silu_forward", ptr(x), ptr(weight), ptr(y), ptr(inv_rms), rows, hidden, eps,
+         dtype_code(x.dtype), stream)
+    return y, inv_rms
+
+
+@rmsnorm_silu_forward.register_fake
+def _(x, weight, eps):
+    return torch.empty_like(x), x.new_empty(x.shape[0], dtype=torch.float32)
+
+
+@torch.library.custom_op("koemi_b200::rmsnorm_silu_backward", mutates_args=())
+def rmsnorm_silu_backward(grad_y: Tensor, x: Tensor, weight: Tensor, inv_rms: Tensor,
+                          eps: float) -> tuple[Tensor, Tensor]:
+    stream = _prepare(x)
+    rows, hidden = x.shape
+    grad_x = torch.empty_like(x)
+    grad_weight = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    size = _native.library().koemi_core_rmsnorm_silu_backward_workspace(rows, hidden)
+    scratch = _native.workspace(size, x.device)
+    call("koemi_core_rmsnorm_silu_backward", ptr(grad_y), ptr(x), ptr(weight), ptr(inv_rms), ptr(grad_x),
+         ptr(grad_weight), rows, hidden, ptr(scratch), scratch.numel(), dtype_code(x.dtype), stream)
+    return grad_x, grad_weight
+
+
+@rmsnorm_silu_backward.register_fake
+def _(grad_y, x, weight, inv_rms, eps):
+    return torch.empty_like(x), x.new_empty(x.shape[1], dtype=torch.float32)
+
+
+@torch.library.custom_op("koemi_b200::gated_rmsnorm_silu", mutates_args=())
+def gated_rmsnorm_silu(x: Tensor, gate: Tensor, weight: Tensor, eps: float) -> Tensor:
+    stream = _prepare(x)
+    rows, hidden = x.shape
+    y = torch.empty_like(x)
+    call("koemi_core_gated_rmsnorm_silu_forward", ptr(x), ptr(gate), ptr(weight), ptr(y), None, rows, hidden,
+         eps, dtype_code(x.dtype), stream)
+    return y
+
+
+@gated_rmsnorm_silu.register_fake
+def _(x, gate, weight, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("koemi_b200::rms_norm", mutates_args=())
+def rms_norm(x: Tensor, residual: Tensor | None, weight: Tensor, keep: Tensor | None, eps: float,
+             out_dtype: torch.dtype) -> Tensor:
+    stream = _prepare(x)
+    rows, hidden = x.shape
+    y = torch.empty(rows, hidden, dtype=out_dtype, device=x.device)
+    call("koemi_core_rmsnorm_forward", ptr(x), ptr(residual), ptr(weight), ptr(keep), ptr(y), rows, hidden,
+         eps, dtype_code(x.dtype), dtype_code(out_dtype), stream)
+    return y
+
+
+@rms_norm.register_fake
+def _(x, residual, weight, keep, eps, out_dtype):
+    return x.new_empty(x.shape, dtype=out_dtype)
+
+
+# ---------------------------------------------------------------- think front
+
+@torch.library.custom_op("koemi_b200::causal_surprise_forward", mutates_args=())
+def causal_surprise_forward(prior: Tensor, weight: Tensor, bias: Tensor, targets: Tensor, valid: Tensor,
+                            out_dtype: torch.dtype) -> Tensor:
+    stream = _prepare(prior)
+    width = prior.shape[-1]
+    rows = prior.numel() // width
+    vocab = weight.shape[0]
+    out = torch.empty(prior.shape[:-1], dtype=out_dtype, device=prior.device)
+    size = _native.library().koemi_think_surprise_workspace(rows, width, vocab, dtype_code(prior.dtype))
+    scratch = _native.workspace(size, prior.device)
+    call("koemi_think_causal_surprise_forward", ptr(prior), ptr(weight), ptr(bias), ptr(targets), ptr(valid),
+         ptr(out), None, rows, width, vocab, dtype_code(prior.dtype), dtype_code(out_dtype), ptr(scratch),
+         scratch.numel(), stream)
+    return out
+
+
+@causal_surprise_forward.register_fake
+def _(prior, weight, bias, targets, valid, out_dtype):
+    return prior.new_empty(prior.shape[:-1], dtype=out_dtype)
+
+
+@torch.library.custom_op("koemi_b200::salient_admission", mutates_args=())
+def salient_admission(carried_keys: Tensor, carried_values: Tensor, carried_valid: Tensor, keys: Tensor,
+                      values: Tensor, surprise: Tensor, valid: Tensor, threshold: float,
+                      capacity: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    stream = _prepare(keys)
+    batch, length, width = keys.shape
+    carried = carried_keys.shape[1]
+    ring = min(carried + length, capacity)
+    out_keys = keys.new_empty(batch, ring, width)
+    out_values = keys.new_empty(batch, ring, width)
+    out_valid = torch.empty(batch, ring, dtype=torch.bool, device=keys.device)
+    admission = torch.empty(batch, length, dtype=torch.bool, device=keys.device)
+    call("koemi_think_salient_admission", ptr(carried_keys), ptr(carried_values), ptr(carried_valid),
+         ptr(keys), ptr(values), ptr(surprise), ptr(valid), threshold, ptr(out_keys), ptr(out_values),
+         ptr(out_valid), ptr(admission), batch, carried, length, width, capacity, stream)
+    return out_keys, out_values, out_valid, admission
+
+
+@salient_admission.register_fake
+def _(carried_keys, carried_values, carried_valid, keys, values, surprise, valid, threshold, capacity):
+    batch, length, width = keys.shape
+    ring = min(carried_keys.shape[1] + length, capacity)
+    return (keys.new_empty(batch, ring, width), keys.new_empty(batch, ring, width),
+            keys.new_empty(batch, ring, dtype=torch.bool), keys.new_empty(batch, length, dtype=torch.bool))
+
+
+# ------------------------------------------------------------------ moe front
+
+@torch.library.custom_op("koemi_b200::route_topk", mutates_args=())
+def route_topk(token_ids: Tensor, previous_token_ids: Tensor, valid: Tensor, expert_count: int,
+               top_k: int) -> Tensor:
+    stream = _prepare(token_ids)
+    count = token_ids.numel()
+    out = torch.empty(count, top_k, dtype=torch.int64, device=token_ids.device)
+    call("koemi_moe_route_topk", ptr(token_ids), ptr(previous_token_ids), ptr(valid), ptr(out), count,
+         expert_count, top_k, dtype_code(token_ids.dtype), stream)
+    return out
+
+
+@route_topk.register_fake
+def _(token_ids, previous_token_ids, valid, expert_count, top_k):
+    return token_ids.new_empty(token_ids.numel(), top_k, dtype=torch.int64)
+
+
+@torch.library.custom_op("koemi_b200::learned_topk", mutates_args=())
+def learned_topk(gate_logits: Tensor, valid: Tensor, top_k: int, renormalize: bool) -> tuple[Tensor, Tensor, Tensor]:
+    stream = _prepare(gate_logits)
+    tokens, experts = gate_logits.shape
+    assignments = torch.empty(tokens, top_k, dtype=torch.int64, device=gate_logits.device)
+    weights = torch.empty(tokens, top_k, dtype=torch.float32, device=gate_logits.device)
+    probabilities = torch.empty(tokens, experts, dtype=torch.float32, device=gate_logits.device)
+    call("koemi_moe_learned_topk", ptr(gate_logits), ptr(valid), ptr(assignments), ptr(weights),
+         ptr(probabilities), tokens, experts, top_k, int(renormalize), stream)
+    return assignments, weights, probabilities
+
+
+@learned_topk.register_fake
+def _(gate_logits, valid, top_k, renormalize):
+    tokens, experts = gate_logits.shape
+    return (gate_logits.new_empty(tokens, top_k, dtype=torch.int64), gate_logits.new_empty(tokens, top_k),
+            gate_logits.new_empty(tokens, experts))
+
+
+@torch.library.custom_op("koemi_b200::permute_topk", mutates_args=())
+def permute_topk(context: Tensor, assignments: Tensor, valid: Tensor, expert_count: int,
+                 gather: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    stream = _prepare(assignments)
+    tokens, top_k = assignments.shape
+    width = context.shape[-1]
+    pairs = tokens * top_k
+    device = assignments.device
+    sorted_context = torch.empty(pairs if gather else 0, width, dtype=context.dtype, device=device)
+    sorted_rows = torch.empty(pairs, dtype=torch.int64, device=device)
+    sorted_experts = torch.empty(pairs, dtype=torch.int64, device=device)
+    offsets = torch.empty(expert_count + 1, dtype=torch.int64, device=device)
+    positions = torch.empty(pairs, dtype=torch.int64, device=device)
+    size = _native.library().koemi_moe_permute_workspace(tokens, top_k, expert_count)
+    scratch = _native.workspace(size, device)
+    call("koemi_moe_permute_topk", ptr(context), ptr(assignments), ptr(valid),
+         ptr(sorted_context) if gather else None, ptr(sorted_rows), ptr(sorted_experts), ptr(offsets),
+         ptr(positions), tokens, width, top_k, expert_count, dtype_code(context.dtype),
+         dtype_code(assignments.dtype), ptr(scratch), scratch.numel(), stream)
+    return sorted_context, sorted_rows, sorted_experts, offsets, positions
+
+
+@permute_topk.register_fake
+def _(context, assignments, valid, expert_count, gather):
+    tokens, top_k = assignments.shape
+    pairs = tokens * top_k
+    return (context.new_empty(pairs if gather else 0, context.shape[-1]),
+            assignments.new_empty(pairs, dtype=torch.int64), assignments.new_empty(pairs, dtype=torch.int64),
+            assignments.new_empty(expert_count + 1, dtype=torch.int64),
+            assignments.new_empty(pairs, dtype=torch.int64))
+
+
+@torch.library.custom_op("koemi_b200::grouped_expert_mlp", mutates_args=())
+def grouped_expert_mlp(sorted_context: Tensor, sorted_experts: Tensor, segment_offsets: Tensor,
+                       gate_weights: Tensor, gate_biases: Tensor, value_weights: Tensor, value_biases: Tensor,
+                       output_weights: Tensor, output_biases: Tensor) -> Tensor:
+    stream = _prepare(sorted_context)
+    pairs, width = sorted_context.shape
+    experts, hidden, _ = gate_weights.shape
+    out = torch.empty_like(sorted_context)
+    code = dtype_code(sorted_context.dtype)
+    size = _native.library().koemi_moe_grouped_mlp_workspace(pairs, width, hidden, experts, code)
+    scratch = _native.workspace(size, sorted_context.device)
+    call("koemi_moe_grouped_expert_mlp", ptr(sorted_context), ptr(sorted_experts), ptr(segment_offsets),
+         ptr(gate_weights), ptr(gate_biases), ptr(value_weights), ptr(value_biases), ptr(output_weights),
+         ptr(output_biases), ptr(out), pairs, width, hidden, experts, code, ptr(scratch), scratch.numel(),
+         stream)
+    return out
+
+
+@grouped_expert_mlp.register_fake
+def _(sorted_context, sorted_experts, segment_offsets, gate_weights, gate_biases, value_weights, value_biases,
+      output_weights, output_biases):
+    return torch.empty_like(sorted_context)
+
+
+@torch.library.custom_op("koemi_b200::combine_topk", mutates_args=())
+def combine_topk(expert_outputs: Tensor, sorted_rows: Tensor, segment_offsets: Tensor, token_count: int,
+                 top_k: int) -> Tensor:
+    stream = _prepare(expert_outputs)
+    pairs, width = expert_outputs.shape
+    experts = segment_offsets.shape[0] - 1
+    out = torch.empty(token_count, width, dtype=expert_outputs.dtype, device=expert_outputs.device)
+    size = _native.library().koemi_moe_combine_workspace(token_count, pairs, top_k)
+    scratch = _native.workspace(size, expert_outputs.device)
+    call("koemi_moe_combine_topk", ptr(expert_outputs), ptr(sorted_rows), ptr(segment_offsets), ptr(out),
+         pairs, width, token_count, top_k, experts, dtype_code(expert_outputs.dtype), ptr(scratch),
+         scratch.numel(), stream)
+    return out
+
+
+@combine_topk.register_fake
+def _(expert_outputs, sorted_rows, segment_offsets, token_count, top_k):
+    return expert_outputs.new_empty(token_count, expert_outputs.shape[1])
+
+
+@torch.library.custom_op("koemi_b200::combine_residual_rmsnorm", mutates_args=())
+def combine_residual_rmsnorm(context: Tensor, expert_out: Tensor, pair_positions: Tensor,
+                             segment_offsets: Tensor, weights: Tensor | None, valid: Tensor,
+                             norm_weight: Tensor, top_k: int, eps: float) -> Tensor:
+    stream = _prepare(context)
+    tokens, width = context.shape
+    experts = segment_offsets.shape[0] - 1
+    out = torch.empty_like(context)
+    call("koemi_moe_combine_residual_rmsnorm", ptr(context), ptr(expert_out), ptr(pair_positions),
+         ptr(segment_offsets), ptr(weights), ptr(valid), ptr(norm_weight), ptr(out), tokens, width, top_k,
+         experts, eps, dtype_code(expert_out.dtype), stream)
+    return out
+
+
+@combine_residual_rmsnorm.register_fake
+def _(context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight, top_k, eps):
+    return torch.empty_like(context)
