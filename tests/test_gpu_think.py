@@ -1,0 +1,110 @@
+"""Think front on the GPU: fused surprise and salient admission vs the oracle."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from koemi_5hom_b200.cuda_kernels.think import causal_surprise, salient_admission
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(batch, length, width, vocab, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    prior = torch.randn(batch, length, width, generator=g).to(dtype)
+    weight = (torch.randn(vocab, width, generator=g) * width ** -0.5).to(dtype)
+    bias = (torch.randn(vocab, generator=g) * 0.1).to(dtype)
+    targets = torch.randint(0, vocab, (batch, length), generator=g)
+    valid = torch.rand(batch, length, generator=g) > 0.2
+    return prior, weight, bias, targets, valid
+
+
+@pytest.mark.parametrize("shape", [(4, 64, 128, 1024), (2, 256, 256, 256), (3, 10, 32, 299), (1, 7, 2048, 5000),
+                                   (2, 3, 16, 2)])
+def test_surprise_fp32_matches_oracle(shape, cuda):
+    prior, weight, bias, targets, valid = _case(*shape, torch.float32, seed=shape[3])
+    got = causal_surprise(*(t.to(cuda) for t in (prior, weight, bias, targets, valid)))
+    expected = ops.causal_surprise(prior, weight, bias, targets, valid)
+    assert got.dtype == torch.float32
+    torch.testing.assert_close(got.cpu().double(), expected, rtol=2e-5, atol=2e-6)
+    assert bool((got.cpu()[~valid] == 0).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_surprise_16bit_matches_oracle(dtype, cuda):
+    prior, weight, bias, targets, valid = _case(4, 33, 256, 3000, dtype, seed=7)
+    got = causal_surprise(*(t.to(cuda) for t in (prior, weight, bias, targets, valid)))
+    expected = ops.causal_surprise(prior, weight, bias, targets, valid)  # on the rounded inputs
+    assert got.dtype == dtype
+    torch.testing.assert_close(got.cpu().double(), expected.to(dtype).double(), rtol=1.6e-2, atol=4e-3)
+
+
+def test_surprise_golden_fixture(golden_ops, cuda):
+    g = golden_ops["surprise"]
+    keep = [i for i in range(g["head_weight"].shape[0]) if i != 256]
+    target = torch.where(g["target"] > 256, g["target"] - 1, g["target"])
+    got = causal_surprise(g["prior"].to(cuda), g["head_weight"][keep].contiguous().to(cuda),
+                          g["head_bias"][keep].contiguous().to(cuda), target.to(cuda), g["valid"].to(cuda))
+    torch.testing.assert_close(got.cpu(), g["surprise"], rtol=2e-5, atol=2e-6)
+
+
+def test_surprise_empty_sequence(cuda):
+    prior, weight, bias, targets, valid = _case(2, 0, 16, 10, torch.float32, seed=1)
+    out = causal_surprise(*(t.to(cuda) for t in (prior, weight, bias, targets, valid)))
+    assert out.shape == (2, 0)
+
+
+def test_surprise_rejects_out_of_range_targets(cuda):
+    prior, weight, bias, targets, valid = _case(1, 4, 16, 10, torch.float32, seed=1)
+    targets[0, 2] = 10
+    from koemi_5hom_b200.cuda_kernels.think import CudaThinkValidationError
+    with pytest.raises(CudaThinkValidationError, match=r"target_ids must be in \[0, 10\)"):
+        causal_surprise(*(t.to(cuda) for t in (prior, weight, bias, targets, valid)))
+
+
+def test_surprise_backward_matches_autograd_oracle(cuda):
+    prior, weight, bias, targets, valid = _case(2, 5, 16, 40, torch.float32, seed=2)
+    ins = [t.to(cuda).requires_grad_(True) for t in (prior, weight, bias)]
+    causal_surprise(*ins, targets.to(cuda), valid.to(cuda)).sum().backward()
+    ref = [t.double().requires_grad_(True) for t in (prior, weight, bias)]
+    ops.causal_surprise(*ref, targets, valid).sum().backward()
+    for mine, theirs in zip(ins, ref):
+        torch.testing.assert_close(mine.grad.cpu().double(), theirs.grad, rtol=2e-3, atol=2e-5)
+
+
+@pytest.mark.parametrize("name", ["grow", "compact", "long"])
+def test_salient_admission_golden(golden_ops, name, cuda):
+    g = golden_ops["salient_tail"][name]
+    surprise = g["admission"].float()  # admitted where surprise 1 > 0.5
+    valid = torch.ones_like(g["admission"])
+    k, v, ok, adm = salient_admission(*(t.to(cuda) for t in (g["carried_keys"], g["carried_values"],
+                                                            g["carried_valid"], g["keys"], g["values"], surprise,
+                                                            valid)), 0.5, g["capacity"])
+    assert torch.equal(adm.cpu(), g["admission"])
+    expected = ops.salient_tail(g["carried_keys"], g["carried_values"], g["carried_valid"], g["keys"], g["values"],
+                                g["admission"], g["capacity"])
+    assert torch.equal(ok.cpu(), expected[2])
+    assert torch.equal(k.cpu(), expected[0]) and torch.equal(v.cpu(), expected[1])
+    for (mk, mv), (rk, rv) in zip(ops.admitted_sequence(k.cpu(), v.cpu(), ok.cpu()),
+                                  ops.admitted_sequence(g["out_keys"], g["out_values"], g["out_valid"])):
+        assert torch.equal(mk, rk) and torch.equal(mv, rv)
+
+
+@pytest.mark.parametrize("carried,length,capacity", [(128, 1, 128), (0, 128, 128), (128, 128, 128), (32, 300, 32),
+                                                     (5, 0, 8)])
+def test_salient_admission_matches_oracle(carried, length, capacity, cuda):
+    g = torch.Generator().manual_seed(carried + length)
+    batch, width = 3, 24
+    ck, cv = torch.randn(batch, carried, width, generator=g), torch.randn(batch, carried, width, generator=g)
+    cvalid = torch.rand(batch, carried, generator=g) > 0.5
+    keys, values = torch.randn(batch, length, width, generator=g), torch.randn(batch, length, width, generator=g)
+    surprise = torch.rand(batch, length, generator=g)
+    valid = torch.rand(batch, length, generator=g) > 0.1
+    k, v, ok, adm = salient_admission(*(t.to(cuda) for t in (ck, cv, cvalid, keys, values, surprise, valid)),
+                                      0.6, capacity)
+    admission = valid & (surprise > 0.6)
+    expected = ops.salient_tail(ck, cv, cvalid, keys, values, admission, capacity)
+    assert torch.equal(adm.cpu(), admission)
+    assert torch.equal(ok.cpu(), expected[2])
+    assert torch.equal(k.cpu(), expected[0]) and torch.equal(v.cpu(), expected[1])

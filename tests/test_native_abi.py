@@ -1,0 +1,72 @@
+"""libkoemi_b200.so loads on any host and exports every symbol of include/koemi_b200.h."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from koemi_5hom_b200 import _native
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "koemi_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"KOEMI_API\s+\w+\s+(koemi_\w+)\s*\(", text)))
+
+
+def test_header_and_binding_table_agree():
+    assert declared_symbols() == sorted(_native.SIGNATURES)
+
+
+def test_library_loads_and_reports_abi():
+    lib = _native.library()
+    assert lib.koemi_abi_version() == _native.ABI_VERSION == 1
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIBRARY_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (koemi_\w+)", out))
+    missing = set(declared_symbols()) - exported
+    assert not missing, missing
+    # nothing but the C ABI leaks out of the library
+    assert all(name.startswith("koemi_") for name in exported)
+
+
+def test_invalid_arguments_fail_before_touching_the_device():
+    lib = _native.library()
+    status = lib.koemi_moe_route_topk(None, None, None, None, 4, 0, 1, _native.I64, None)
+    assert status == _native.KOEMI_ERR_INVALID
+    assert "expert_count" in _native.last_error()
+    status = lib.koemi_core_rmsnorm_silu_forward(None, None, None, None, 4, 8, -1.0, _native.F32, None)
+    assert status == _native.KOEMI_ERR_INVALID
+    assert "eps" in _native.last_error()
+    status = lib.koemi_dense_affine_scan_forward(None, None, None, None, 1, 4, 8, 0, 99, None)
+    assert status == _native.KOEMI_ERR_INVALID
+    with pytest.raises(_native.KoemiNativeError, match="status -1"):
+        _native.call("koemi_moe_learned_topk", None, None, None, None, None, 3, 4, 9, 0, None)
+
+
+def test_empty_work_is_a_no_op():
+    lib = _native.library()
+    assert lib.koemi_dense_affine_scan_forward(None, None, None, None, 0, 5, 8, 0, _native.F32, None) == 0
+    assert lib.koemi_moe_route_topk(None, None, None, None, 0, 4, 2, _native.I64, None) == 0
+
+
+def test_workspace_queries_are_host_only():
+    lib = _native.library()
+    assert lib.koemi_moe_permute_workspace(131072, 2, 64) >= 4 * 131072 * 2 * 4
+    assert lib.koemi_think_surprise_workspace(256, 2048, 32767, _native.BF16) > 0
+    assert lib.koemi_moe_grouped_mlp_workspace(512, 2048, 4096, 64, _native.BF16) > 0
+
+
+def test_last_error_is_truncated_safely():
+    lib = _native.library()
+    lib.koemi_moe_route_topk(None, None, None, None, 4, 0, 1, _native.I64, None)
+    buffer = ctypes.create_string_buffer(8)
+    full = lib.koemi_last_error(buffer, 8)
+    assert full > 7 and len(buffer.value) == 7
