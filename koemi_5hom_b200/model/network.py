@@ -1,0 +1,622 @@
+"""The HERM block on the native kernels, behind ``KoemiModel``'s interface.
+
+Drop-in for ``koemi.model.network.KoemiModel`` (src/koemi/model/network.py:80-441):
+same constructor argument (a ModelSettings, ours or the reference's), same
+``forward(input_ids, state=None, execution_mode=PARALLEL, warm_cache=None,
+mapping_cache=None, *, trusted_inputs=False) -> KoemiOutput`` contract, same
+``KoemiState`` fields, ``initial_state``, ``cache_inference_weights`` /
+``clear_inference_weights`` and ``load_state_dict`` of reference state dicts.
+
+Per window of ``scan_chunk`` positions each block runs:
+
+  rms_norm (core) -> gate GEMM -> bounded gates + masks (dense) -> affine
+  scan (dense) -> causal surprise over the content head (think, fused
+  log-sum-exp) -> local ring read -> associative memory read/write ->
+  salient admission + ring compaction (think) -> fusion GEMM + rms_norm
+  (core) -> route / learned top-k, stable permute, grouped expert MLP,
+  combine + residual RMSNorm (moe) -> head GEMM.
+
+Parameters are held in a packed layout (all projections that read the same
+input are one GEMM) in ``compute_dtype``; memories, reductions and the state
+stay fp32. Dense projections are cuBLAS GEMMs with fp32 outputs; every other
+step is a koemi_b200 kernel or a small torch elementwise/batched op on the
+current stream. Nothing reads device values on the host unless
+``trusted_inputs`` is False (token counting and id validation, as the
+reference does), so decode steps can be captured in CUDA graphs.
+
+``layer_count > 1`` stacks blocks between the shared embedding and head: block
+l reads block l-1's final context, keeps its own ``KoemiState`` and scores
+surprise against the shared head. The reference defines one block only.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from enum import Enum
+
+import torch
+from torch import Tensor, nn
+
+from koemi_5hom_b200.cuda_kernels import _ops
+from koemi_5hom_b200.model.settings import PAD_TOKEN_ID, ModelSettings
+from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
+
+MIN_RETENTION, MAX_RETENTION = 2.0 ** -8, 1.0 - 2.0 ** -8
+MIN_DECAY, MAX_DECAY = 2.0 ** -12, 1.0 - 2.0 ** -12
+MAX_REFINE_DECAY = 1.0 - 2.0 ** -16
+READ_EPSILON = 2.0 ** -8
+NORM_EPSILON = 1e-6
+
+
+class ExecutionMode(Enum):
+    """Mirror of koemi.model.execution.ExecutionMode."""
+
+    PARALLEL = "parallel"
+    SEQUENTIAL = "sequential"
+
+
+@dataclass(frozen=True)
+class RouterStatistics:
+    probability_mass: Tensor
+    assignment_counts: Tensor
+    valid_count: Tensor
+
+    @property
+    def balance_loss(self) -> Tensor:
+        importance = self.probability_mass / self.valid_count.clamp_min(1)
+        load = self.assignment_counts / self.assignment_counts.sum().clamp_min(1)
+        return self.probability_mass.numel() * (importance * load).sum()
+
+
+def merge_router_statistics(statistics: list[RouterStatistics]) -> RouterStatistics | None:
+    if not statistics:
+        return None
+    return RouterStatistics(sum(s.probability_mass for s in statistics), sum(s.assignment_counts for s in statistics),
+                            sum(s.valid_count for s in statistics))
+
+
+@dataclass(frozen=True)
+class KoemiOutput:
+    """Mirror of koemi.model.network.KoemiOutput (network.py:27-77)."""
+
+    logits: Tensor
+    state: KoemiState | LayeredKoemiState
+    surprise_values: Tensor
+    expert_indices: Tensor
+    valid_positions: Tensor
+    token_count: int
+    cache_hits: int
+    cache_misses: int
+    expert_count: int
+    active_expert_indices: Tensor | None = None
+    router_statistics: RouterStatistics | None = None
+    router_balance_weight: float = 0.0
+
+    @property
+    def router_loss(self) -> Tensor:
+        if self.router_statistics is None:
+            return self.logits.new_zeros(())
+        return self.router_statistics.balance_loss * self.router_balance_weight
+
+    @property
+    def expert_activation_totals(self) -> Tensor | None:
+        if self.expert_indices.numel() == 0 or self.expert_count == 0:
+            return None
+        chosen = self.active_expert_indices if self.active_expert_indices is not None else self.expert_indices.unsqueeze(-1)
+        counted = self.valid_positions.unsqueeze(-1) & chosen.ge(0) & chosen.lt(self.expert_count)
+        totals = torch.zeros(self.expert_count, dtype=torch.long, device=chosen.device)
+        return totals.scatter_add_(0, chosen.clamp(0, self.expert_count - 1).reshape(-1), counted.reshape(-1).long())
+
+    @property
+    def expert_activation_counts(self) -> tuple[int, ...]:
+        totals = self.expert_activation_totals
+        if totals is None:
+            return () if self.expert_indices.numel() == 0 else (0,) * self.expert_count
+        return tuple(int(c) for c in totals.tolist())
+
+
+def _dtype_of(name: str) -> torch.dtype:
+    return torch.bfloat16 if name == "bfloat16" else torch.float32
+
+
+class HermBlock(nn.Module):
+    """One block's parameters, packed so each input feeds a single GEMM."""
+
+    def __init__(self, settings: ModelSettings, dtype: torch.dtype, device: torch.device | None = None):
+        super().__init__()
+        d, m, e = settings.embedding_size, settings.memory_features, settings.expert_count
+        p = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=dtype, device=device), requires_grad=False)  # noqa: E731
+        self.input_norm = p(d)
+        self.gates_weight, self.gates_bias = p(2 * d, d), p(2 * d)            # retention | candidate
+        self.assoc_weight, self.assoc_bias = p(3 * d + 2, d), p(3 * d + 2)    # key | query | value | decay | write
+        self.feature_weight, self.feature_bias = p(m, d), p(m)
+        self.local_weight, self.local_bias = p(2 * d, d), p(2 * d)            # local key | local value
+        self.refine_weight, self.refine_bias = (p(1, 4 * d), p(1)) if settings.ablation == "herm" else (None, None)
+        self.fusion_weight, self.fusion_bias = p(d, 4 * d), p(d)
+        self.fusion_norm = p(d)
+        if e > 0:
+            self.expert_gate_weight, self.expert_gate_bias = p(e, 2 * d, d), p(e, 2 * d)
+            self.expert_value_weight, self.expert_value_bias = p(e, 2 * d, d), p(e, 2 * d)
+            self.expert_output_weight, self.expert_output_bias = p(e, d, 2 * d), p(e, d)
+            self.expert_norm = p(d)
+            self.router_weight = p(e, d) if settings.expert_routing == "learned" else None
+
+    def reference_map(self, settings: ModelSettings) -> list[tuple[str, str, int, int]]:
+        """(reference name, packed attribute, row start, row stop) per tensor."""
+        d = settings.embedding_size
+        out = [("input_normalizer.weight", "input_norm", 0, d)]
+
+        def linear(name: str, attr: str, start: int, stop: int) -> None:
+            out.append((f"{name}.weight", f"{attr}_weight", start, stop))
+            out.append((f"{name}.bias", f"{attr}_bias", start, stop))
+
+        linear("recurrent_state.retention_projection", "gates", 0, d)
+        linear("recurrent_state.candidate_projection", "gates", d, 2 * d)
+        linear("associative_memory.key_projection", "assoc", 0, d)
+        linear("associative_memory.query_projection", "assoc", d, 2 * d)
+        linear("associative_memory.value_projection", "assoc", 2 * d, 3 * d)
+        linear("associative_memory.decay_projection", "assoc", 3 * d, 3 * d + 1)
+        linear("associative_memory.write_projection", "assoc", 3 * d + 1, 3 * d + 2)
+        linear("associative_memory.feature_projection", "feature", 0, settings.memory_features)
+        linear("local_memory.local_key_projection", "local", 0, d)
+        linear("local_memory.local_value_projection", "local", d, 2 * d)
+        if settings.ablation == "herm":
+            linear("memory_refine_gate", "refine", 0, 1)
+        linear("fusion_projection", "fusion", 0, d)
+        out.append(("fusion_normalizer.weight", "fusion_norm", 0, d))
+        for e in range(settings.expert_count):
+            for ref, attr in (("gate_projection", "expert_gate"), ("value_projection", "expert_value"),
+                              ("output_projection", "expert_output")):
+                out.append((f"experts.experts.{e}.{ref}.weight", f"{attr}_weight", e, e + 1))
+                out.append((f"experts.experts.{e}.{ref}.bias", f"{attr}_bias", e, e + 1))
+        if settings.expert_count > 0:
+            out.append(("experts.output_normalizer.weight", "expert_norm", 0, d))
+            if settings.expert_routing == "learned":
+                out.append(("experts.gate.weight", "router_weight", 0, settings.expert_count))
+        return out
+
+
+class KoemiModel(nn.Module):
+    """HERM stack on libkoemi_b200 kernels with the reference model's interface."""
+
+    def __init__(self, settings, device: torch.device | str | None = None):
+        super().__init__()
+        self.settings = ModelSettings.coerce(settings)
+        s = self.settings
+        self.compute_dtype = _dtype_of(s.compute_dtype)
+        dev = torch.device(device) if device is not None else None
+        p = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=self.compute_dtype, device=dev), requires_grad=False)  # noqa: E731
+        self.embedding_weight = p(s.vocabulary_size, s.embedding_size)
+        self.blocks = nn.ModuleList(HermBlock(s, self.compute_dtype, dev) for _ in range(s.layer_count))
+        self.head_weight = p(s.vocabulary_size, s.embedding_size)
+        self.head_bias = p(s.vocabulary_size)
+        self._cache: dict | None = None
+        self.eval()
+
+    # ----------------------------------------------------------- parameters
+    def load_reference_parameters(self, params: dict[str, Tensor], layer: int | None = None) -> None:
+        """Load reference-named tensors (KoemiModel.state_dict() names) into
+        block ``layer`` (all blocks when None), plus embedding and head."""
+        with torch.no_grad():
+            self.embedding_weight.copy_(params["embedding.weight"])
+            self.head_weight.copy_(params["token_predictor.weight"])
+            self.head_bias.copy_(params["token_predictor.bias"])
+            for index, block in enumerate(self.blocks):
+                if layer is not None and index != layer:
+                    continue
+                for name, attr, start, stop in block.reference_map(self.settings):
+                    getattr(block, attr)[start:stop].copy_(params[name].reshape(getattr(block, attr)[start:stop].shape))
+        self.clear_inference_weights()
+
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        if "embedding.weight" in state_dict:  # a reference state dict
+            self.load_reference_parameters(dict(state_dict))
+            return nn.modules.module._IncompatibleKeys([], [])
+        result = super().load_state_dict(state_dict, strict=strict, assign=assign)
+        self.clear_inference_weights()
+        return result
+
+    def initialize_parameters(self, seed: int, init: str = "normal") -> None:
+        """Seeded random parameters drawn on the parameters' device: N(0, 0.02)
+        Linear weights, N(0, 0.002) biases, N(0, 1) embedding (zero PAD row),
+        norm weights 1 + 0.05 N(0, 1) (``init="normal"``, the config-5 recipe)."""
+        generator = torch.Generator(device=self.head_weight.device).manual_seed(seed)
+        with torch.no_grad():
+            for name, tensor in self.named_parameters():
+                if tensor is None:
+                    continue
+                if name.endswith("norm") or name.endswith("_norm"):
+                    tensor.copy_(1.0 + 0.05 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
+                elif name == "embedding_weight":
+                    tensor.copy_(torch.randn(tensor.shape, generator=generator, device=tensor.device))
+                    tensor[PAD_TOKEN_ID].zero_()
+                elif name.endswith("bias"):
+                    tensor.copy_(0.002 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
+                else:
+                    tensor.copy_(0.02 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
+        self.clear_inference_weights()
+
+    def cache_inference_weights(self) -> None:
+        """Precompute the content head (head rows without PAD) and fp32 copies
+        of the small vectors the kernels read. Valid until parameters change."""
+        s = self.settings
+        keep = torch.cat((torch.arange(0, PAD_TOKEN_ID), torch.arange(PAD_TOKEN_ID + 1, s.vocabulary_size)))
+        keep = keep.to(self.head_weight.device)
+        if s.vocabulary_size == PAD_TOKEN_ID + 1:
+            content_w, content_b = self.head_weight[:PAD_TOKEN_ID], self.head_bias[:PAD_TOKEN_ID]
+        else:
+            content_w, content_b = self.head_weight.index_select(0, keep), self.head_bias.index_select(0, keep)
+        f32 = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
+        blocks = []
+        for block in self.blocks:
+            entry = {name: f32(getattr(block, name, None)) for name in
+                     ("input_norm", "gates_bias", "assoc_bias", "feature_bias", "local_bias", "refine_bias",
+                      "fusion_bias", "fusion_norm", "expert_norm")}
+            blocks.append(entry)
+        self._cache = {"content_w": content_w.contiguous(), "content_b": content_b.contiguous(),
+                       "head_b": f32(self.head_bias), "blocks": blocks}
+
+    def clear_inference_weights(self) -> None:
+        self._cache = None
+
+    def train(self, mode: bool = True):
+        if mode:
+            raise RuntimeError("the B200 HERM model is inference-only")
+        return super().train(False)
+
+    @property
+    def device(self) -> torch.device:
+        return self.head_weight.device
+
+    def initial_state(self, batch_size: int, device: torch.device | None = None):
+        s = self.settings
+        device = device or self.device
+        if s.layer_count == 1:
+            return KoemiState.create(batch_size, s.embedding_size, s.memory_features, device)
+        return LayeredKoemiState(tuple(KoemiState.create(batch_size, s.embedding_size, s.memory_features, device)
+                                       for _ in range(s.layer_count)), 0)
+
+    def static_state(self, batch_size: int, device: torch.device | None = None):
+        s = self.settings
+        device = device or self.device
+        make = lambda: KoemiState.create_static(batch_size, s.embedding_size, s.memory_features,  # noqa: E731
+                                                s.local_memory_size, s.salience_memory_size, device)
+        if s.layer_count == 1:
+            return make()
+        return LayeredKoemiState(tuple(make() for _ in range(s.layer_count)), 0)
+
+    # ------------------------------------------------------------- forward
+    def forward(self, input_ids: Tensor, state=None, execution_mode: ExecutionMode = ExecutionMode.PARALLEL,
+                warm_cache=None, mapping_cache=None, *, trusted_inputs: bool = False,
+                last_logits_only: bool = False) -> KoemiOutput:
+        """``last_logits_only`` (an extension) returns logits for the final
+        position only, ``[batch, 1, vocabulary]``; prefill callers read only
+        that row (fast_decode.py:222, generation.py:220)."""
+        if warm_cache is not None or mapping_cache is not None:
+            raise NotImplementedError("warm/mapping caches are not part of the B200 hot path")
+        if not trusted_inputs:
+            self._validate_input_ids(input_ids)
+        if self._cache is None:
+            self.cache_inference_weights()
+        state = state if state is not None else self.initial_state(input_ids.shape[0], input_ids.device)
+        window = 1 if getattr(execution_mode, "value", execution_mode) == "sequential" else self.settings.scan_chunk
+        length = input_ids.shape[1]
+        outputs = []
+        with torch.no_grad():
+            for start in range(0, length, window):
+                last = start + window >= length
+                piece = self._window(input_ids[:, start:start + window], state, trusted_inputs,
+                                     logits=(not last_logits_only) or last, last_only=last_logits_only)
+                outputs.append(piece)
+                state = piece.state
+        if len(outputs) == 1:
+            return outputs[0]
+        return _concatenate(outputs, last_logits_only)
+
+    def _validate_input_ids(self, input_ids: Tensor) -> None:
+        if input_ids.ndim != 2:
+            raise ValueError("input_ids must have shape [batch, sequence]")
+        if input_ids.numel() == 0:
+            raise ValueError("input_ids must not be empty")
+        if int(input_ids.min()) < 0 or int(input_ids.max()) >= self.settings.vocabulary_size:
+            raise ValueError("input_ids contain values outside the model vocabulary")
+
+    def _window(self, ids: Tensor, state, trusted: bool, logits: bool, last_only: bool) -> KoemiOutput:
+        s = self.settings
+        valid = ids != PAD_TOKEN_ID
+        layer_states = state.layers if isinstance(state, LayeredKoemiState) else (state,)
+        x = self.embedding_weight.index_select(0, ids.reshape(-1)).float().reshape(*ids.shape, s.embedding_size)
+        new_states, statistics = [], []
+        result = None
+        for index, block in enumerate(self.blocks):
+            result = self._block_window(block, self._cache["blocks"][index], x, ids, valid, layer_states[index])
+            x = result["final"]
+            new_states.append(result["state"])
+            if result["statistics"] is not None:
+                statistics.append(result["statistics"])
+        step = layer_states[0].step_index + ids.shape[1]
+        if isinstance(state, LayeredKoemiState):
+            new_state = LayeredKoemiState(tuple(_with_step(st, step) for st in new_states), step)
+        else:
+            new_state = _with_step(new_states[0], step)
+        if logits:
+            head_in = x[:, -1:] if last_only else x
+            out_logits = self._linear(head_in, self.head_weight, self._cache["head_b"])
+        else:
+            out_logits = x.new_empty(ids.shape[0], 0, s.vocabulary_size)
+        return KoemiOutput(
+            logits=out_logits,
+            state=new_state,
+            surprise_values=result["surprise"],
+            expert_indices=result["expert_indices"],
+            valid_positions=valid,
+            token_count=ids.numel() if trusted else int(valid.sum()),
+            cache_hits=0,
+            cache_misses=0,
+            expert_count=s.expert_count if s.ablation != "affine" else 0,
+            active_expert_indices=result["active"],
+            router_statistics=merge_router_statistics(statistics),
+            router_balance_weight=s.expert_load_balance_weight,
+        )
+
+    def _linear(self, x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+        """fp32 [.., n] = x [.., k] @ weight[n, k]^T (+ bias): cuBLAS, fp32 out."""
+        flat = x.reshape(-1, x.shape[-1])
+        if self.compute_dtype == torch.float32:
+            y = flat @ weight.T if bias is None else torch.addmm(bias, flat, weight.T)
+        else:
+            y = torch.mm(flat.to(self.compute_dtype), weight.T, out_dtype=torch.float32)
+            if bias is not None:
+                y += bias
+        return y.reshape(*x.shape[:-1], weight.shape[0])
+
+    def _block_window(self, block: HermBlock, cache: dict, x: Tensor, ids: Tensor, valid: Tensor,
+                      state: KoemiState) -> dict:
+        s = self.settings
+        batch, length = ids.shape
+        d = s.embedding_size
+        rows = batch * length
+        valid_flat = valid.reshape(-1)
+
+        # input norm (core), gates (dense), scan (dense): network.py:305-310
+        u = _ops.rms_norm(x.reshape(rows, d), None, cache["input_norm"], None, NORM_EPSILON, torch.float32)
+        pre = self._linear(u, block.gates_weight, cache["gates_bias"])
+        retention, increment = _ops.bounded_gates(pre, valid_flat, MIN_RETENTION, MAX_RETENTION)
+        h = _ops.affine_scan_forward(retention.reshape(batch, length, d), increment.reshape(batch, length, d),
+                                     state.working_state.contiguous(), False)
+        last_ids = _last_valid_ids(ids, valid, state.last_token_ids)
+
+        if s.ablation == "affine":  # network.py:443-480
+            new_state = KoemiState(h[:, -1], state.memory_basis, state.memory_normalizer, state.refine_basis,
+                                   state.refine_normalizer, state.local_keys, state.local_values, state.local_valid,
+                                   state.salient_keys, state.salient_values, state.salient_valid, last_ids,
+                                   state.step_index)
+            none = torch.full_like(ids, -1)
+            return {"final": h, "state": new_state, "surprise": torch.zeros(batch, length, device=h.device),
+                    "expert_indices": none, "active": None, "statistics": None}
+
+        # causal surprise on the prior state (think): network.py:320-325,677-698
+        if s.ablation == "no_surprise":
+            surprise = torch.zeros(batch, length, device=h.device)
+        else:
+            prior = torch.cat((state.working_state.unsqueeze(1), h[:, :-1]), dim=1)
+            targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
+            surprise = _ops.causal_surprise_forward(prior.to(self.compute_dtype), self._cache["content_w"],
+                                                    self._cache["content_b"], targets, valid, torch.float32)
+
+        # local ring entries + sliding-window read: memory.py:297-361
+        local = self._linear(h, block.local_weight, cache["local_bias"])
+        keep = valid.unsqueeze(-1)
+        keys = torch.where(keep, local[..., :d], 0.0)
+        values = torch.where(keep, local[..., d:], 0.0)
+        local_value, novelty = _local_read(state.local_keys, state.local_values, state.local_valid, keys, values, valid,
+                                           h, s.local_memory_size)
+
+        # associative memory: memory.py:82-144,244-255
+        assoc = self._linear(h, block.assoc_weight, cache["assoc_bias"])
+        key, query = assoc[..., :d], assoc[..., d:2 * d]
+        mem_value = torch.tanh(assoc[..., 2 * d:3 * d])
+        decay = MIN_DECAY + (MAX_DECAY - MIN_DECAY) * torch.sigmoid(assoc[..., 3 * d])
+        write = torch.sigmoid(assoc[..., 3 * d + 1])
+        both = self._linear(torch.stack((key, query)), block.feature_weight, cache["feature_bias"]).softmax(dim=-1)
+        features, query_features = both[0], both[1]
+        fast_decay = torch.where(valid, decay, 1.0)
+        fast_write = torch.where(valid, write * (0.25 + 0.75 * surprise.clamp(0.0, 1.0)), 0.0)
+        fast_read, basis, normalizer = _associative_scan_read(state.memory_basis, state.memory_normalizer, fast_decay,
+                                                              mem_value, features, fast_write, query_features)
+
+        # salient admission + read (think): network.py:349-358; memory.py:405-455
+        salient_keys, salient_values, salient_valid, admission = _ops.salient_admission(
+            state.salient_keys.contiguous(), state.salient_values.contiguous(), state.salient_valid.contiguous(),
+            keys.contiguous(), values.contiguous(), surprise, valid, float(s.salience_threshold),
+            int(s.salience_memory_size))
+        salient_value = _salient_read(state.salient_keys, state.salient_values, state.salient_valid, keys, values,
+                                      admission, h)
+
+        if s.ablation == "herm":  # memory.py:257-268; network.py:366-386,709-721
+            refine_decay = (1.0 - (1.0 - decay) * s.refine_decay_rate).clamp(max=MAX_REFINE_DECAY)
+            refine_decay = torch.where(valid, refine_decay, 1.0)
+            refine_write = torch.where(valid, write * surprise.clamp(0.0, 1.0) * novelty.clamp(0.0, 1.0), 0.0)
+            error = (mem_value - fast_read).clamp(-2.0, 2.0)
+            refine_read, refine_basis, refine_normalizer = _associative_scan_read(
+                state.refine_basis, state.refine_normalizer, refine_decay, error, features, refine_write,
+                query_features)
+            gate = torch.sigmoid(self._linear(torch.cat((h, fast_read, refine_read, local_value), dim=-1),
+                                              block.refine_weight, cache["refine_bias"]))
+            memory_value = fast_read + gate * refine_read
+        else:
+            memory_value = fast_read
+            refine_basis, refine_normalizer = state.refine_basis, state.refine_normalizer
+
+        # fusion (cuBLAS + core rms_norm): network.py:723-732
+        fused = self._linear(torch.cat((h, memory_value, local_value, salient_value), dim=-1), block.fusion_weight,
+                             cache["fusion_bias"])
+        context = _ops.rms_norm(fused.reshape(rows, d), None, cache["fusion_norm"], None, NORM_EPSILON, torch.float32)
+
+        # experts (moe): experts.py:90-143; router.py:43-97
+        statistics = None
+        if s.expert_count == 0:
+            final = context.reshape(batch, length, d)
+            expert_indices = torch.full_like(ids, -1)
+            active = expert_indices.unsqueeze(-1)
+        else:
+            if s.expert_routing == "learned":
+                masked = torch.where(valid_flat.unsqueeze(-1), context, 0.0)
+                gate_logits = self._linear(masked, block.router_weight, None)
+                assignments, weights, probabilities = _ops.learned_topk(gate_logits, valid_flat, s.expert_top_k,
+                                                                        bool(s.router_renormalize))
+                counts = torch.zeros(s.expert_count, device=h.device)
+                counts.scatter_add_(0, assignments.clamp_min(0).reshape(-1),
+                                    valid_flat.unsqueeze(-1).expand_as(assignments).reshape(-1).float())
+                statistics = RouterStatistics(probabilities.sum(dim=0), counts, valid_flat.sum().float())
+            else:
+                previous = _previous_ids(ids, valid, state.last_token_ids)
+                assignments = _ops.route_topk(ids.reshape(-1), previous.reshape(-1), valid_flat, s.expert_count,
+                                              s.expert_top_k)
+                weights = None
+            gathered = context.to(self.compute_dtype)
+            sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
+                gathered, assignments, valid_flat, s.expert_count, True)
+            expert_out = _ops.grouped_expert_mlp(sorted_context, sorted_experts, offsets, block.expert_gate_weight,
+                                                 block.expert_gate_bias, block.expert_value_weight,
+                                                 block.expert_value_bias, block.expert_output_weight,
+                                                 block.expert_output_bias)
+            final = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid_flat,
+                                                  cache["expert_norm"], s.expert_top_k, NORM_EPSILON)
+            final = final.reshape(batch, length, d)
+            active = assignments.reshape(batch, length, s.expert_top_k)
+            expert_indices = active[..., 0]
+
+        all_keys = torch.cat((state.local_keys, keys), dim=1)
+        all_values = torch.cat((state.local_values, values), dim=1)
+        all_valid = torch.cat((state.local_valid, valid), dim=1)
+        cut = max(0, all_keys.shape[1] - s.local_memory_size)
+        new_state = KoemiState(
+            working_state=h[:, -1],
+            memory_basis=basis,
+            memory_normalizer=normalizer,
+            refine_basis=refine_basis,
+            refine_normalizer=refine_normalizer,
+            local_keys=all_keys[:, cut:],
+            local_values=all_values[:, cut:],
+            local_valid=all_valid[:, cut:],
+            salient_keys=salient_keys,
+            salient_values=salient_values,
+            salient_valid=salient_valid,
+            last_token_ids=last_ids,
+            step_index=state.step_index,
+        )
+        return {"final": final, "state": new_state, "surprise": surprise, "expert_indices": expert_indices,
+                "active": active, "statistics": statistics}
+
+
+# ------------------------------------------------------------------ memories
+
+def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid, queries, window):
+    """Softmax read over the ``window`` slots strictly before each query plus
+    novelty = 1 - max cosine (memory.py:332-383); 0 / 1 when nothing is eligible."""
+    batch, length, width = queries.shape
+    carried = carried_keys.shape[1]
+    all_keys = torch.cat((carried_keys, keys), dim=1)
+    all_values = torch.cat((carried_values, values), dim=1)
+    all_valid = torch.cat((carried_valid, valid), dim=1)
+    own = carried + torch.arange(length, device=queries.device).unsqueeze(1)
+    source = torch.arange(all_keys.shape[1], device=queries.device).unsqueeze(0)
+    eligible = ((source < own) & (source >= own - window)).unsqueeze(0) & all_valid.unsqueeze(1)
+    scores = torch.einsum("bsd,btd->bts", all_keys, queries) / math.sqrt(width)
+    scores = scores.masked_fill(~eligible, float("-inf"))
+    any_slot = eligible.any(dim=-1, keepdim=True)
+    weights = torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0)
+    value = torch.einsum("bts,bsd->btd", weights, all_values)
+    nq = queries / queries.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    nk = all_keys / all_keys.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    similarity = torch.einsum("bsd,btd->bts", nk, nq).masked_fill(~eligible, float("-inf"))
+    novelty = torch.where(any_slot.squeeze(-1), 1.0 - similarity.amax(dim=-1), 1.0)
+    return value, novelty.clamp(0.0, 1.0)
+
+
+def _salient_read(carried_keys, carried_values, carried_valid, keys, values, admission, queries):
+    """Read over every valid carried slot plus earlier admitted window entries
+    (memory.py:405-429)."""
+    batch, length, width = queries.shape
+    all_keys = torch.cat((carried_keys, keys), dim=1)
+    all_values = torch.cat((carried_values, values), dim=1)
+    position = torch.arange(length, device=queries.device)
+    earlier = position.unsqueeze(1) > position.unsqueeze(0)
+    eligible = torch.cat((carried_valid.unsqueeze(1).expand(batch, length, carried_keys.shape[1]),
+                          admission.unsqueeze(1) & earlier.unsqueeze(0)), dim=-1)
+    scores = torch.einsum("bsd,btd->bts", all_keys, queries) / math.sqrt(width)
+    scores = scores.masked_fill(~eligible, float("-inf"))
+    any_slot = eligible.any(dim=-1, keepdim=True)
+    weights = torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0)
+    return torch.einsum("bts,bsd->btd", weights, all_values)
+
+
+def _associative_scan_read(basis, normalizer, decay, value, features, write, query_features):
+    """Rank-one decayed memory over one window, in closed form.
+
+    With D_t = prod_{j<=t} decay_j, the read at t sees the carried memory scaled
+    by D_{t-1} and every earlier write s < t scaled by D_{t-1} / D_s; the
+    window's last memory carries D_{T-1} and D_{T-1} / D_s. Computed in log
+    space as cumulative sums (memory.py:97-144), fp32."""
+    log_decay = torch.log(decay)
+    cumulative = torch.cumsum(log_decay, dim=1)
+    before = cumulative - log_decay
+    length = value.shape[1]
+    position = torch.arange(length, device=value.device)
+    strictly_earlier = position.unsqueeze(1) > position.unsqueeze(0)
+    pair = torch.exp((before.unsqueeze(-1) - cumulative.unsqueeze(1)).masked_fill(~strictly_earlier, float("-inf")))
+    influence = pair * torch.einsum("bsm,btm->bts", features, query_features) * write.unsqueeze(1)
+    carried_scale = torch.exp(before)
+    numerator = carried_scale.unsqueeze(-1) * torch.einsum("bdm,btm->btd", basis, query_features)
+    numerator = numerator + torch.einsum("bts,bsd->btd", influence, value)
+    denominator = carried_scale * torch.einsum("bm,btm->bt", normalizer, query_features) + influence.sum(dim=-1)
+    regularized = denominator.unsqueeze(-1) + READ_EPSILON
+    read = (denominator.unsqueeze(-1) / regularized) * numerator / regularized
+    total = cumulative[:, -1]
+    survive = torch.exp(total.unsqueeze(1) - cumulative) * write
+    scale = torch.exp(total)
+    new_basis = scale[:, None, None] * basis + torch.einsum("bs,bsd,bsm->bdm", survive, value, features)
+    new_normalizer = scale[:, None] * normalizer + torch.einsum("bs,bsm->bm", survive, features)
+    return read, new_basis, new_normalizer
+
+
+def _previous_ids(ids: Tensor, valid: Tensor, carried: Tensor) -> Tensor:
+    """Last valid id strictly before each position, else the carried id (network.py:742-749)."""
+    length = ids.shape[1]
+    index = torch.arange(length, device=ids.device).expand_as(ids)
+    latest = torch.cummax(torch.where(valid, index, -1), dim=1).values
+    before = torch.cat((torch.full_like(latest[:, :1], -1), latest[:, :-1]), dim=1)
+    return torch.where(before >= 0, ids.gather(1, before.clamp_min(0)), carried.unsqueeze(1))
+
+
+def _last_valid_ids(ids: Tensor, valid: Tensor, carried: Tensor) -> Tensor:
+    length = ids.shape[1]
+    index = torch.arange(length, device=ids.device).expand_as(ids)
+    last = torch.where(valid, index, -1).amax(dim=1)
+    return torch.where(last >= 0, ids.gather(1, last.clamp_min(0).unsqueeze(1)).squeeze(1), carried)
+
+
+def _with_step(state: KoemiState, step: int) -> KoemiState:
+    return KoemiState(*(getattr(state, f) for f in KOEMI_STATE_FIELDS), step_index=step)
+
+
+def _concatenate(pieces: list[KoemiOutput], last_only: bool) -> KoemiOutput:
+    first = pieces[0]
+    logits = pieces[-1].logits if last_only else torch.cat([p.logits for p in pieces], dim=1)
+    active = (torch.cat([p.active_expert_indices for p in pieces], dim=1)
+              if first.active_expert_indices is not None else None)
+    return KoemiOutput(
+        logits=logits,
+        state=pieces[-1].state,
+        surprise_values=torch.cat([p.surprise_values for p in pieces], dim=1),
+        expert_indices=torch.cat([p.expert_indices for p in pieces], dim=1),
+        valid_positions=torch.cat([p.valid_positions for p in pieces], dim=1),
+        token_count=sum(p.token_count for p in pieces),
+        cache_hits=0,
+        cache_misses=0,
+        expert_count=first.expert_count,
+        active_expert_indices=active,
+        router_statistics=merge_router_statistics([p.router_statistics for p in pieces if p.router_statistics]),
+        router_balance_weight=first.router_balance_weight,
+    )

@@ -1,0 +1,136 @@
+"""The B200 HERM model against the reference goldens and the oracle.
+
+Gates (from the north star): fp32 model within 1e-4 of the reference on
+logits/surprise/state, expert ids and admitted salient sets exact, identical
+greedy decode; bf16 model within 2e-2 max-abs on logits.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import load_golden
+from herm_weights import HermShape, herm_parameters
+from koemi_5hom_b200.model import ExecutionMode, KoemiModel, ModelSettings
+from koemi_5hom_b200.runtime import BatchDecoder, SamplingPolicy, TokenSampler
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def build(name: str, compute_dtype: str = "float32", device="cuda"):
+    fx = load_golden(name)
+    case = fx["case"]
+    settings = ModelSettings(**case["settings"], compute_dtype=compute_dtype)
+    shape = HermShape(settings.vocabulary_size, settings.embedding_size, settings.memory_features,
+                      settings.expert_count, settings.expert_routing, settings.ablation)
+    params = herm_parameters(shape, case["seed"], case["init"],
+                             dtype=torch.bfloat16 if case.get("bf16") else torch.float32)
+    model = KoemiModel(settings, device=device)
+    model.load_reference_parameters({k: v.to(device) for k, v in params.items()})
+    return fx, model
+
+
+def greedy_decode(model, ids, steps, capture_graph):
+    decoder = BatchDecoder(model, capture_graph=capture_graph)
+    sampler = TokenSampler(SamplingPolicy(greedy=True), model.device)
+    logits = decoder.prefill(ids)
+    tokens, first_logits = [], []
+    for step in range(steps):
+        token = sampler(logits)
+        tokens.append(token)
+        if step < 4:
+            first_logits.append(logits.clone())
+        logits = decoder.step(token)
+    return torch.cat(tokens, dim=1), torch.stack(first_logits, dim=1), decoder.state
+
+
+@pytest.mark.parametrize("name", ["c1", "c1_t065", "herm_learned"])
+def test_fp32_model_matches_reference_forward(name):
+    fx, model = build(name)
+    out = model(fx["ids"].cuda())
+    pos = fx["logit_positions"]
+    torch.testing.assert_close(out.logits[:, pos].cpu(), fx["logits"], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(out.surprise_values.cpu(), fx["surprise"], rtol=1e-5, atol=1e-5)
+    assert torch.equal(out.expert_indices.cpu(), fx["expert_indices"])
+    assert torch.equal(out.active_expert_indices.cpu(), fx["active_expert_indices"])
+    assert torch.equal(out.valid_positions.cpu(), fx["valid_positions"])
+    for field, expected in fx["state"].items():
+        mine = getattr(out.state, field).cpu()
+        if field.startswith("salient"):
+            continue
+        assert mine.shape == expected.shape, field
+        torch.testing.assert_close(mine.to(expected.dtype), expected, rtol=1e-4, atol=1e-5)
+    mine = ops.admitted_sequence(out.state.salient_keys.cpu(), out.state.salient_values.cpu(),
+                                 out.state.salient_valid.cpu())
+    theirs = ops.admitted_sequence(fx["state"]["salient_keys"], fx["state"]["salient_values"],
+                                   fx["state"]["salient_valid"])
+    for (mk, mv), (rk, rv) in zip(mine, theirs):
+        assert mk.shape == rk.shape  # the admitted set is bit-exact in size and order
+        torch.testing.assert_close(mk, rk, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(mv, rv, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["c1", "c1_t065", "herm_learned"])
+@pytest.mark.parametrize("capture_graph", [False, True])
+def test_fp32_greedy_decode_matches_reference(name, capture_graph):
+    fx, model = build(name)
+    tokens, first_logits, state = greedy_decode(model, fx["ids"].cuda(), fx["case"]["decode"], capture_graph)
+    assert torch.equal(tokens.cpu(), fx["decode_tokens"])
+    torch.testing.assert_close(first_logits.cpu(), fx["decode_logits"], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(state.working_state.cpu(), fx["decode_state"]["working_state"], rtol=1e-4, atol=1e-4)
+    assert torch.equal(state.local_valid.cpu(), fx["decode_state"]["local_valid"])
+    assert torch.equal(state.salient_valid.sum(1).cpu(), fx["decode_state"]["salient_valid"].sum(1))
+
+
+def test_bf16_model_within_logit_gate():
+    fx, model = build("c5_small", compute_dtype="bfloat16")
+    out = model(fx["ids"].cuda())
+    pos = fx["logit_positions"]
+    error = (out.logits[:, pos].cpu() - fx["logits"]).abs().max().item()
+    assert error <= 2e-2, error
+    assert torch.equal(out.expert_indices.cpu(), fx["expert_indices"])  # hash routing on ids
+    tokens, first_logits, _ = greedy_decode(model, fx["ids"].cuda(), fx["case"]["decode"], capture_graph=True)
+    assert (first_logits.cpu() - fx["decode_logits"]).abs().max().item() <= 2e-2
+    assert torch.equal(tokens.cpu(), fx["decode_tokens"])
+
+
+def test_sequential_mode_matches_parallel():
+    fx, model = build("c1_t065")
+    ids = fx["ids"][:, :40].cuda()
+    parallel = model(ids)
+    sequential = model(ids, execution_mode=ExecutionMode.SEQUENTIAL)
+    torch.testing.assert_close(sequential.logits, parallel.logits, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(sequential.surprise_values, parallel.surprise_values, rtol=1e-4, atol=1e-4)
+    assert torch.equal(sequential.expert_indices, parallel.expert_indices)
+
+
+def test_decode_step_never_reads_device_values(monkeypatch):
+    """tests/runtime/test_fast_decode.py:21-45,162-181 of the reference: the
+    trusted decode step must not synchronise with the host."""
+    fx, model = build("c1_t065")
+    decoder = BatchDecoder(model)
+    logits = decoder.prefill(fx["ids"].cuda())
+    token = logits.argmax(dim=-1, keepdim=True)
+
+    def forbidden(*_args, **_kwargs):
+        raise AssertionError("host synchronisation inside the decode step")
+
+    for name in ("item", "tolist", "__int__", "__float__", "__bool__"):
+        monkeypatch.setattr(torch.Tensor, name, forbidden)
+    for _ in range(3):
+        logits = decoder.step(token)
+        token = logits.argmax(dim=-1, keepdim=True)
+
+
+def test_layered_stack_decodes_identically_with_and_without_graph():
+    settings = ModelSettings(vocabulary_size=2048, embedding_size=128, memory_features=16, local_memory_size=16,
+                             salience_memory_size=16, expert_count=8, expert_top_k=2, salience_threshold=0.6,
+                             layer_count=3, compute_dtype="bfloat16")
+    model = KoemiModel(settings, device="cuda")
+    model.initialize_parameters(seed=3)
+    ids = torch.randint(0, 2047, (4, 40), generator=torch.Generator().manual_seed(1)).cuda()
+    ids = torch.where(ids >= 256, ids + 1, ids)
+    eager, _, _ = greedy_decode(model, ids, 12, capture_graph=False)
+    graphed, _, _ = greedy_decode(model, ids, 12, capture_graph=True)
+    assert torch.equal(eager, graphed)
