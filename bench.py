@@ -1,0 +1,407 @@
+"""HERM batched-decode benchmark on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (config 5): HERM stack with vocabulary 32768, d_model 2048, 24
+blocks, memory features 16, 128 local + 128 salient ring slots, 64 experts
+top-2 (d_ff 4096), bf16 weights, fp32 state; 256 streams per GPU, each with a
+2048-token prompt of uniform random ids (PAD excluded), prefilled untimed,
+then greedy decode. Weights are seeded random (N(0, 0.02)), inputs synthetic.
+One step = one decode step of every stream (256 tokens per GPU). The timed
+region is K CUDA-graph replays of that step between barriers, timed with CUDA
+events on the decode stream, max over ranks; every step reads ~100 GB, far
+more than the 126 MB L2, so no flush is needed.
+
+Multi-GPU: one process per GPU (torchrun), each rank decodes its own 256
+streams with a full replica (data parallel, no collective on the step):
+``scaling`` is "weak".
+
+``--impl reference`` times the CPU oracle port of the same decode step on the
+host cores (rank 0 only; the reference is Python and does not travel to the
+GPU box) and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s at 1/2/4/8 B200; per-kernel % of HBM / tensor-core roofline"
+UNIT = "tokens/s"
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--layers", type=int, default=24)
+    p.add_argument("--streams", type=int, default=256, help="decode streams per GPU")
+    p.add_argument("--prompt-len", type=int, default=2048)
+    p.add_argument("--vocab", type=int, default=32768)
+    p.add_argument("--width", type=int, default=2048)
+    p.add_argument("--experts", type=int, default=64)
+    p.add_argument("--top-k", type=int, default=2)
+    p.add_argument("--threshold", type=float, default=0.64,
+                   help="salience threshold (fixed rule of network.py:349; ~mean+1 sigma at random init)")
+    p.add_argument("--cpu-sample-streams", type=int, default=4)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
+    return p.parse_args(argv)
+
+
+def settings_for(args):
+    from koemi_5hom_b200.model import ModelSettings
+    return ModelSettings(vocabulary_size=args.vocab, embedding_size=args.width, memory_features=16,
+                         local_memory_size=128, salience_memory_size=128, salience_threshold=args.threshold,
+                         expert_count=args.experts, expert_top_k=args.top_k, scan_chunk=128,
+                         layer_count=args.layers, compute_dtype="bfloat16")
+
+
+def workload_config(args, world):
+    return {"workload": "config5_herm_batched_decode", "model": "HERM (random init, N(0,0.02))",
+            "layers": args.layers, "vocab": args.vocab, "d_model": args.width, "d_ff": 2 * args.width,
+            "experts": args.experts, "top_k": args.top_k, "local_slots": 128, "salient_slots": 128,
+            "streams_per_gpu": args.streams, "global_batch": args.streams * world, "prompt_len": args.prompt_len,
+            "seq_len": 1, "salience_threshold": args.threshold, "parallelism": f"dp{world}",
+            "weights": "bf16", "state": "fp32", "l2": "per-step reads >> 126 MB L2 (no flush needed)"}
+
+
+def prompts_for(args, rank, device):
+    import torch
+    g = torch.Generator().manual_seed(1000 + rank)
+    ids = torch.randint(0, args.vocab - 1, (args.streams, args.prompt_len), generator=g)
+    return torch.where(ids >= 256, ids + 1, ids).to(device)
+
+
+# ------------------------------------------------------------ clock sampling
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.process = None
+
+    def __enter__(self):
+        try:
+            self.process = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                             "--format=csv,noheader,nounits", "-lms", "100"],
+                                            stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.process = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.process is not None:
+            self.process.terminate()
+            try:
+                self.process.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.process.kill()
+        self.file.flush()
+
+    def summary(self) -> dict:
+        rows = []
+        with open(self.file.name) as handle:
+            for line in handle:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# ----------------------------------------------------------------- CPU side
+class CpuBaseline:
+    """The oracle port of one decode step on the host cores: one HERM block of
+    config-5 width for ``streams`` streams with static rings full of random
+    content. Parameters are drawn lazily, so only the experts the sample
+    routes to are materialised. The per-step time of the block is scaled to
+    the configured stack depth (stated in ``sample``)."""
+
+    def __init__(self, args, streams: int):
+        import torch
+        sys.path.insert(0, str(ROOT / "tests" / "golden"))
+        from herm_weights import HermShape, parameter_shapes
+        from oracle.herm import HermConfig, HermOracle
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.args, self.streams = args, streams
+        s = settings_for(args)
+        config = HermConfig(vocabulary_size=s.vocabulary_size, embedding_size=s.embedding_size,
+                            memory_features=s.memory_features, local_memory_size=s.local_memory_size,
+                            salience_memory_size=s.salience_memory_size, salience_threshold=s.salience_threshold,
+                            expert_count=s.expert_count, expert_top_k=s.expert_top_k)
+        shapes = {name: dims for name, dims, _ in
+                  parameter_shapes(HermShape(s.vocabulary_size, s.embedding_size, s.memory_features, s.expert_count))}
+
+        class LazyParams(dict):
+            def __missing__(self, name):
+                g = torch.Generator().manual_seed(sum(map(ord, name)))
+                value = (torch.randn(shapes[name], generator=g) * 0.02).bfloat16().float()
+                self[name] = value
+                return value
+
+            def get(self, name, default=None):
+                return self[name] if name in shapes else default
+
+        params = LazyParams()
+        oracle = HermOracle.__new__(HermOracle)
+        oracle.config, oracle.dtype, oracle.p = config, torch.float32, params
+        keep = [i for i in range(s.vocabulary_size) if i != 256]
+        oracle.content_w = params["token_predictor.weight"][keep]
+        oracle.content_b = params["token_predictor.bias"][keep]
+        g = torch.Generator().manual_seed(7)
+        state = oracle.initial_state(streams)
+        d = s.embedding_size
+        for ring, size in (("local", s.local_memory_size), ("salient", s.salience_memory_size)):
+            state[f"{ring}_keys"] = torch.randn(streams, size, d, generator=g)
+            state[f"{ring}_values"] = torch.randn(streams, size, d, generator=g)
+            state[f"{ring}_valid"] = torch.ones(streams, size, dtype=torch.bool)
+        state["working_state"] = torch.randn(streams, d, generator=g) * 0.1
+        self.oracle, self.state = oracle, state
+        self.token = torch.randint(0, 255, (streams, 1), generator=g)
+        self.cores = torch.get_num_threads()
+        self.block_step()  # warm-up; materialises the routed experts
+
+    def block_step(self) -> float:
+        started = time.perf_counter()
+        out = self.oracle.window(self.token, self.state)
+        seconds = time.perf_counter() - started
+        self.state = out["state"]
+        self.token = self.oracle.greedy(out["logits"][:, -1])
+        return seconds
+
+    def measure(self, steps: int) -> dict:
+        per_block = statistics.median(self.block_step() for _ in range(steps))
+        per_step = per_block * self.args.layers
+        return {"value": self.streams / per_step, "unit": UNIT, "cores": self.cores, "kind": "port",
+                "sample": (f"oracle port (torch CPU fp32, {self.cores} threads): {self.streams} streams x 1 "
+                           f"config-5 block, median of {steps} decode steps = {per_block:.3f} s per block-step, "
+                           f"x {self.args.layers} blocks = {per_step:.2f} s per decode step")}
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    started = time.perf_counter()
+    baseline = CpuBaseline(args, args.cpu_sample_streams)
+    for _ in range(args.warmup):
+        baseline.block_step()
+    result = baseline.measure(args.steps)
+    value = result["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.cpu_sample_streams / value * 1000.0,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, 1),
+            "cpu_baseline": {"kind": "port", "cores": result["cores"], "sample": result["sample"], "value": value,
+                             "unit": UNIT},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - started}
+    emit(line, args)
+
+
+def emit(line: dict, args) -> None:
+    text = json.dumps(line)
+    print(text, flush=True)
+    if args.out:
+        Path(args.out).write_text(text + "\n")
+
+
+# ----------------------------------------------------------------- GPU side
+def count_native_kernels(model, decoder, token) -> int:
+    """Kernels of libkoemi_b200 launched by one eager decode step."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from koemi_5hom_b200.runtime.fast_decode import clone_state
+    state = clone_state(decoder._state)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        model(token, state, trusted_inputs=True)
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "koemi" in e.name)
+
+
+def measure_expert_mlp(model, decoder, token, repeats: int = 20) -> dict:
+    """Time the dominant kernel (grouped expert MLP of block 0) alone on a real
+    decode step's sorted pairs, CUDA events on its stream."""
+    import torch
+    from koemi_5hom_b200.cuda_kernels import _ops
+    s = model.settings
+    block = model.blocks[0]
+    g = torch.Generator(device="cuda").manual_seed(5)
+    context = torch.randn(token.shape[0], s.embedding_size, device="cuda", generator=g).bfloat16()
+    prev = torch.randint(0, s.vocabulary_size, token.shape, device="cuda", generator=g)
+    valid = torch.ones(token.shape[0], dtype=torch.bool, device="cuda")
+    assignments = _ops.route_topk(token.reshape(-1), prev.reshape(-1), valid, s.expert_count, s.expert_top_k)
+    sc, _, se, offsets, _ = _ops.permute_topk(context, assignments, valid, s.expert_count, True)
+    args = (sc, se, offsets, block.expert_gate_weight, block.expert_gate_bias, block.expert_value_weight,
+            block.expert_value_bias, block.expert_output_weight, block.expert_output_bias)
+    for _ in range(3):
+        _ops.grouped_expert_mlp(*args)
+    stream = torch.cuda.current_stream()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(repeats):
+        _ops.grouped_expert_mlp(*args)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    seconds = start.elapsed_time(stop) / 1000.0 / repeats
+    counts = torch.diff(offsets).cpu()
+    touched = int((counts > 0).sum())
+    d, h = s.embedding_size, 2 * s.embedding_size
+    pairs = int(offsets[-1])
+    weight_bytes = touched * 3 * d * h * 2 + touched * (2 * h + d) * 2
+    activation_bytes = pairs * d * 2 * 2 + pairs * h * 2 * 2
+    algorithmic = weight_bytes + activation_bytes
+    return {"seconds": seconds, "bytes": algorithmic, "touched_experts": touched, "pairs": pairs}
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+    from koemi_5hom_b200 import _native
+    from koemi_5hom_b200.model import KoemiModel
+    from koemi_5hom_b200.runtime import BatchDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    _native.ensure_device(device)
+    wall_start = time.perf_counter()
+
+    model = KoemiModel(settings_for(args), device=device)
+    model.initialize_parameters(seed=0)
+    prompts = prompts_for(args, rank, device)
+    decoder = BatchDecoder(model, capture_graph=True)
+    torch.cuda.synchronize()
+    prefill_start = time.perf_counter()
+    logits = decoder.prefill(prompts)
+    torch.cuda.synchronize()
+    prefill_seconds = time.perf_counter() - prefill_start
+    del prompts
+
+    token = logits.argmax(dim=-1, keepdim=True)
+    eager_kernels = count_native_kernels(model, decoder, token)
+    for _ in range(max(args.warmup, 1)):
+        logits = decoder.step(token)
+        token = logits.argmax(dim=-1, keepdim=True)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            logits = decoder.step(token)
+            token = logits.argmax(dim=-1, keepdim=True)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    seconds = start.elapsed_time(stop) / 1000.0
+    clock_summary = clocks.summary()
+    if world > 1:
+        t = torch.tensor([seconds], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        seconds = float(t.item())
+    ms_per_step = seconds / args.steps * 1000.0
+    value = args.streams * world * args.steps / seconds
+
+    # end to end: pinned host ids in, sampled ids back to the host, every step
+    host_in = torch.empty(args.streams, 1, dtype=torch.long).pin_memory()
+    host_out = torch.empty(args.streams, 1, dtype=torch.long).pin_memory()
+    host_in.copy_(token.cpu())
+    device_ids = torch.empty_like(token)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2e_start = time.perf_counter()
+    for _ in range(args.steps):
+        device_ids.copy_(host_in, non_blocking=True)
+        logits = decoder.step(device_ids)
+        host_out.copy_(logits.argmax(dim=-1, keepdim=True), non_blocking=True)
+        stream.synchronize()
+        host_in.copy_(host_out)
+    e2e_seconds = time.perf_counter() - e2e_start
+    if world > 1:
+        t = torch.tensor([e2e_seconds], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_seconds = float(t.item())
+    e2e_value = args.streams * world * args.steps / e2e_seconds
+
+    mlp = measure_expert_mlp(model, decoder, token)
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = mlp["bytes"] / mlp["seconds"] / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+        "clocks": clock_summary,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 8,
+                "d2h_bytes_per_step": host_out.numel() * 8},
+        "gpu_launches": eager_kernels * args.steps,
+        "roofline": {"kernel": "koemi_moe_grouped_expert_mlp (decode step, one block)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm_peak,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s",
+                     "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                     "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
+                     "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},
+        "prefill_s": prefill_seconds,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        del decoder
+        torch.cuda.empty_cache()
+        line["cpu_baseline"] = CpuBaseline(args, args.cpu_sample_streams).measure(3)
+    line["wall_s"] = time.perf_counter() - wall_start
+    if rank == 0:
+        emit(line, args)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main(argv=None) -> None:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -92,7 +92,7 @@ class KoemiNativeError(RuntimeError):
         self.status = status
 
 
-_LOCK = threading.Lock()
+_LOCK = threading.RLock()
 _LIBRARY: ctypes.CDLL | None = None
 _INITIALISED_DEVICES: set[int] = set()
 
@@ -154,9 +154,10 @@ def ensure_device(device: torch.device) -> None:
     index = device.index if device.index is not None else torch.cuda.current_device()
     if index in _INITIALISED_DEVICES:
         return
+    handle = library()  # takes _LOCK itself on the first load
     with _LOCK:
         if index not in _INITIALISED_DEVICES:
-            check("koemi_device_init", library().koemi_device_init(index))
+            check("koemi_device_init", handle.koemi_device_init(index))
             _INITIALISED_DEVICES.add(index)
 
 

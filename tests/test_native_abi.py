@@ -70,3 +70,30 @@ def test_last_error_is_truncated_safely():
     buffer = ctypes.create_string_buffer(8)
     full = lib.koemi_last_error(buffer, 8)
     assert full > 7 and len(buffer.value) == 7
+
+
+def test_device_init_path_loads_library_without_deadlock(monkeypatch):
+    """ensure_device() as the first call into the library (the model's path)
+    must not self-deadlock on the loader lock."""
+    import threading
+
+    monkeypatch.setattr(_native, "_LIBRARY", None)
+    monkeypatch.setattr(_native, "_INITIALISED_DEVICES", set())
+    calls = []
+
+    class FakeDevice:
+        index = 0
+
+    def run():
+        try:
+            _native.ensure_device(FakeDevice())
+        except _native.KoemiNativeError as error:  # no GPU here: init reports a CUDA error
+            calls.append(error)
+        else:
+            calls.append(None)
+
+    worker = threading.Thread(target=run, daemon=True)
+    worker.start()
+    worker.join(timeout=30)
+    assert not worker.is_alive(), "ensure_device deadlocked"
+    assert calls
