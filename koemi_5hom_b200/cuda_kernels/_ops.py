@@ -23,10 +23,17 @@ def _prepare(tensor: Tensor) -> int:
     return stream_of(tensor)
 
 
+def _dense(*tensors):
+    """Row-major views of the inputs: the kernels take raw pointers, so a
+    strided view (a window slice of the ids, a transposed weight) is copied."""
+    return tuple(t if t is None or t.is_contiguous() else t.contiguous() for t in tensors)
+
+
 # ---------------------------------------------------------------- dense front
 
 @torch.library.custom_op("koemi_b200::affine_scan_forward", mutates_args=())
 def affine_scan_forward(retention: Tensor, increment: Tensor, initial: Tensor, broadcast: bool) -> Tensor:
+    retention, increment, initial = _dense(retention, increment, initial)
     stream = _prepare(increment)
     batch, length = increment.shape[0], increment.shape[1]
     features = increment.numel() // max(batch * length, 1) if batch * length else 0
@@ -44,6 +51,7 @@ def _(retention, increment, initial, broadcast):
 @torch.library.custom_op("koemi_b200::affine_scan_backward", mutates_args=())
 def affine_scan_backward(retention: Tensor, initial: Tensor, states: Tensor, grad_states: Tensor,
                          broadcast: bool) -> tuple[Tensor, Tensor, Tensor]:
+    retention, initial, states, grad_states = _dense(retention, initial, states, grad_states)
     stream = _prepare(states)
     batch, length = states.shape[0], states.shape[1]
     features = states.numel() // max(batch * length, 1) if batch * length else 0
@@ -63,6 +71,7 @@ def _(retention, initial, states, grad_states, broadcast):
 
 @torch.library.custom_op("koemi_b200::bounded_gates", mutates_args=())
 def bounded_gates(projections: Tensor, valid: Tensor, minimum: float, maximum: float) -> tuple[Tensor, Tensor]:
+    projections, valid = _dense(projections, valid)
     stream = _prepare(projections)
     rows, features = projections.shape[0], projections.shape[1] // 2
     retention = projections.new_empty(rows, features)
@@ -82,6 +91,7 @@ def _(projections, valid, minimum, maximum):
 
 @torch.library.custom_op("koemi_b200::rmsnorm_silu_forward", mutates_args=())
 def rmsnorm_silu_forward(x: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    x, weight = _dense(x, weight)
     stream = _prepare(x)
     rows, hidden = x.shape
     y = torch.empty_like(x)
@@ -99,6 +109,7 @@ def _(x, weight, eps):
 @torch.library.custom_op("koemi_b200::rmsnorm_silu_backward", mutates_args=())
 def rmsnorm_silu_backward(grad_y: Tensor, x: Tensor, weight: Tensor, inv_rms: Tensor,
                           eps: float) -> tuple[Tensor, Tensor]:
+    grad_y, x, weight, inv_rms = _dense(grad_y, x, weight, inv_rms)
     stream = _prepare(x)
     rows, hidden = x.shape
     grad_x = torch.empty_like(x)
@@ -117,6 +128,7 @@ def _(grad_y, x, weight, inv_rms, eps):
 
 @torch.library.custom_op("koemi_b200::gated_rmsnorm_silu", mutates_args=())
 def gated_rmsnorm_silu(x: Tensor, gate: Tensor, weight: Tensor, eps: float) -> Tensor:
+    x, gate, weight = _dense(x, gate, weight)
     stream = _prepare(x)
     rows, hidden = x.shape
     y = torch.empty_like(x)
@@ -133,6 +145,7 @@ def _(x, gate, weight, eps):
 @torch.library.custom_op("koemi_b200::rms_norm", mutates_args=())
 def rms_norm(x: Tensor, residual: Tensor | None, weight: Tensor, keep: Tensor | None, eps: float,
              out_dtype: torch.dtype) -> Tensor:
+    x, residual, weight, keep = _dense(x, residual, weight, keep)
     stream = _prepare(x)
     rows, hidden = x.shape
     y = torch.empty(rows, hidden, dtype=out_dtype, device=x.device)
@@ -151,6 +164,7 @@ def _(x, residual, weight, keep, eps, out_dtype):
 @torch.library.custom_op("koemi_b200::causal_surprise_forward", mutates_args=())
 def causal_surprise_forward(prior: Tensor, weight: Tensor, bias: Tensor, targets: Tensor, valid: Tensor,
                             out_dtype: torch.dtype) -> Tensor:
+    prior, weight, bias, targets, valid = _dense(prior, weight, bias, targets, valid)
     stream = _prepare(prior)
     width = prior.shape[-1]
     rows = prior.numel() // width
@@ -173,6 +187,7 @@ def _(prior, weight, bias, targets, valid, out_dtype):
 def salient_admission(carried_keys: Tensor, carried_values: Tensor, carried_valid: Tensor, keys: Tensor,
                       values: Tensor, surprise: Tensor, valid: Tensor, threshold: float,
                       capacity: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    carried_keys, carried_values, carried_valid, keys, values, surprise, valid = _dense(carried_keys, carried_values, carried_valid, keys, values, surprise, valid)
     stream = _prepare(keys)
     batch, length, width = keys.shape
     carried = carried_keys.shape[1]
@@ -200,6 +215,7 @@ def _(carried_keys, carried_values, carried_valid, keys, values, surprise, valid
 @torch.library.custom_op("koemi_b200::route_topk", mutates_args=())
 def route_topk(token_ids: Tensor, previous_token_ids: Tensor, valid: Tensor, expert_count: int,
                top_k: int) -> Tensor:
+    token_ids, previous_token_ids, valid = _dense(token_ids, previous_token_ids, valid)
     stream = _prepare(token_ids)
     count = token_ids.numel()
     out = torch.empty(count, top_k, dtype=torch.int64, device=token_ids.device)
@@ -215,6 +231,7 @@ def _(token_ids, previous_token_ids, valid, expert_count, top_k):
 
 @torch.library.custom_op("koemi_b200::learned_topk", mutates_args=())
 def learned_topk(gate_logits: Tensor, valid: Tensor, top_k: int, renormalize: bool) -> tuple[Tensor, Tensor, Tensor]:
+    gate_logits, valid = _dense(gate_logits, valid)
     stream = _prepare(gate_logits)
     tokens, experts = gate_logits.shape
     assignments = torch.empty(tokens, top_k, dtype=torch.int64, device=gate_logits.device)
@@ -235,6 +252,7 @@ def _(gate_logits, valid, top_k, renormalize):
 @torch.library.custom_op("koemi_b200::permute_topk", mutates_args=())
 def permute_topk(context: Tensor, assignments: Tensor, valid: Tensor, expert_count: int,
                  gather: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    context, assignments, valid = _dense(context, assignments, valid)
     stream = _prepare(assignments)
     tokens, top_k = assignments.shape
     width = context.shape[-1]
@@ -268,6 +286,7 @@ def _(context, assignments, valid, expert_count, gather):
 def grouped_expert_mlp(sorted_context: Tensor, sorted_experts: Tensor, segment_offsets: Tensor,
                        gate_weights: Tensor, gate_biases: Tensor, value_weights: Tensor, value_biases: Tensor,
                        output_weights: Tensor, output_biases: Tensor) -> Tensor:
+    sorted_context, sorted_experts, segment_offsets, gate_weights, gate_biases, value_weights, value_biases, output_weights, output_biases = _dense(sorted_context, sorted_experts, segment_offsets, gate_weights, gate_biases, value_weights, value_biases, output_weights, output_biases)
     stream = _prepare(sorted_context)
     pairs, width = sorted_context.shape
     experts, hidden, _ = gate_weights.shape
@@ -291,6 +310,7 @@ def _(sorted_context, sorted_experts, segment_offsets, gate_weights, gate_biases
 @torch.library.custom_op("koemi_b200::combine_topk", mutates_args=())
 def combine_topk(expert_outputs: Tensor, sorted_rows: Tensor, segment_offsets: Tensor, token_count: int,
                  top_k: int) -> Tensor:
+    expert_outputs, sorted_rows, segment_offsets = _dense(expert_outputs, sorted_rows, segment_offsets)
     stream = _prepare(expert_outputs)
     pairs, width = expert_outputs.shape
     experts = segment_offsets.shape[0] - 1
@@ -312,6 +332,7 @@ def _(expert_outputs, sorted_rows, segment_offsets, token_count, top_k):
 def combine_residual_rmsnorm(context: Tensor, expert_out: Tensor, pair_positions: Tensor,
                              segment_offsets: Tensor, weights: Tensor | None, valid: Tensor,
                              norm_weight: Tensor, top_k: int, eps: float) -> Tensor:
+    context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight = _dense(context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight)
     stream = _prepare(context)
     tokens, width = context.shape
     experts = segment_offsets.shape[0] - 1

@@ -323,6 +323,7 @@ class KoemiModel(nn.Module):
 
     def _window(self, ids: Tensor, state, trusted: bool, logits: bool, last_only: bool) -> KoemiOutput:
         s = self.settings
+        ids = ids.contiguous()  # a window slice of the prompt is strided
         valid = ids != PAD_TOKEN_ID
         layer_states = state.layers if isinstance(state, LayeredKoemiState) else (state,)
         x = self.embedding_weight.index_select(0, ids.reshape(-1)).float().reshape(*ids.shape, s.embedding_size)

@@ -108,3 +108,18 @@ def test_salient_admission_matches_oracle(carried, length, capacity, cuda):
     assert torch.equal(adm.cpu(), admission)
     assert torch.equal(ok.cpu(), expected[2])
     assert torch.equal(k.cpu(), expected[0]) and torch.equal(v.cpu(), expected[1])
+
+
+def test_surprise_accepts_strided_targets(cuda):
+    """A window slice of the ids (ids[:, a:b]) is not contiguous; the op must
+    read it by value, not by raw pointer."""
+    prior, weight, bias, targets, valid = _case(2, 40, 32, 256, torch.float32, seed=9)
+    wide = torch.randint(0, 256, (2, 100), generator=torch.Generator().manual_seed(3))
+    wide[:, 30:70] = targets
+    strided = wide.to(cuda)[:, 30:70]
+    assert not strided.is_contiguous()
+    from koemi_5hom_b200.cuda_kernels import _ops
+    got = _ops.causal_surprise_forward(prior.to(cuda), weight.to(cuda), bias.to(cuda), strided, valid.to(cuda),
+                                       torch.float32)
+    torch.testing.assert_close(got.cpu().double(), ops.causal_surprise(prior, weight, bias, targets, valid),
+                               rtol=2e-5, atol=2e-6)
