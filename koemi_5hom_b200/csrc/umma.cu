@@ -1,25 +1,574 @@
-// tcgen05 tensor-core paths (grouped expert MLP, surprise head). Until the
-// tensor-core kernels are enabled these entry points decline the work and the
-// callers run their fp32 FMA kernels.
-#include "common.cuh"
+// tcgen05 tensor-core GEMMs with fused epilogues, for sm_100a.
+//
+// One persistent kernel per problem, one CTA per SM (192 KB of shared memory,
+// all 512 TMEM columns). Warp roles:
+//   warp 0      TMA producer: per K block of 64, loads the A tile [128 x 64]
+//               and the B tile [256 x 64] (bf16/f16, 128B-swizzled K-major)
+//               into a 4-stage shared-memory ring;
+//   warp 1      allocates TMEM; one thread issues tcgen05.mma
+//               (M=128, N=256, K=16, fp32 accumulate) into one of two
+//               256-column accumulators and commits stage/accumulator
+//               completion to mbarriers;
+//   warps 2..5  epilogue: tcgen05.ld each accumulator row (one TMEM lane per
+//               thread), apply the fused epilogue, store to global memory,
+//               release the accumulator.
+// The epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Problems:
+//   kGated   expert GEMM 1: B = [gate rows n*128.. ; value rows n*128..] of
+//            the tile's expert; hidden = silu(g + bg) * (v + bv) (dtype).
+//   kOutput  expert GEMM 2: y = hidden W_o^T + b_o (dtype).
+//   kSurprise head contraction: logits = prior W^T + b folded into per-row
+//            (max, sum exp, target logit) partials per 256-wide vocab tile.
+// Grouped problems map tiles to (expert, row tile) on the device from
+// segment_offsets; rows past a segment's end are computed but never stored.
+//
+// Every mbarrier wait is bounded; a wait that runs out raises a CTA abort
+// flag, records KOEMI_ERR_TIMEOUT in the device status word and every role
+// leaves its loop, so the CTA frees its TMEM and exits. No multicast loads.
+#include "vec.cuh"
 
 namespace koemi {
 
-int grouped_mlp_umma(const void *, const int64_t *, const void *, const void *, const void *, const void *,
-                     const void *, const void *, void *, int64_t, int64_t, int64_t, int64_t, int, void *,
-                     size_t, cudaStream_t, bool *handled) {
-    *handled = false;
+__global__ void tile_prefix_kernel(const int64_t *offsets, int64_t experts, int64_t tile_rows, int32_t *prefix);
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = kBM * kBK * 2;
+constexpr uint32_t kBBytes = kBN * kBK * 2;
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemColumns = 512;
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+
+enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2 };
+
+struct UmmaArgs {
+    CUtensorMap map_a;
+    CUtensorMap map_b0;
+    CUtensorMap map_b1;
+    int64_t k;
+    int64_t rows;             // rows of A (pairs or prior rows)
+    int64_t n_tiles;          // tiles along N
+    int64_t b_rows_per_group; // rows of B per expert (0 for surprise)
+    int64_t n_out;            // valid output columns (H, D or C)
+    int64_t out_stride;       // elements per output row
+    int64_t experts;
+    int64_t band;             // surprise: row tiles per band (tile order swizzle)
+    const int64_t *offsets;
+    const int32_t *tile_prefix;
+    const void *bias0;
+    const void *bias1;
+    void *out;
+    float *partials;
+    const int64_t *targets;
+    int *status;
+    uint32_t idesc;
+};
+
+// ------------------------------------------------------------------ PTX
+
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_address) {
+    uint64_t desc = 0;
+    desc |= static_cast<uint64_t>((smem_address & 0x3FFFF) >> 4);  // start address
+    desc |= static_cast<uint64_t>(1) << 16;                          // LBO (unused for swizzled K-major)
+    desc |= static_cast<uint64_t>(1024 >> 4) << 32;                  // SBO: 8 rows x 128 B
+    desc |= static_cast<uint64_t>(1) << 46;                          // descriptor version (sm100)
+    desc |= static_cast<uint64_t>(2) << 61;                          // 128-byte swizzle
+    return desc;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+#define KOEMI_TMEM_LD32(taddr, v)                                                                              \
+    asm volatile(                                                                                              \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, " \
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"    \
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),     \
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),             \
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),           \
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),           \
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])                                                                \
+        : "r"(taddr))
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Bounded wait that also watches the CTA abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
+    for (uint32_t spin = 0; spin < kWaitSpinLimit; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 255) == 255 && *abort) return false;
+    }
+    *abort = 1;
+    if (status != nullptr) atomicExch(status, KOEMI_ERR_TIMEOUT);
+    return false;
+}
+
+// ------------------------------------------------------------- scheduling
+
+struct Tile {
+    int64_t row0;      // first A row of the tile
+    int64_t row_end;   // rows >= row_end are not stored
+    int64_t n;         // tile index along N
+    int64_t group;     // expert (grouped) or 0
+    int64_t m_tile;    // row tile index (surprise: partial slot)
+};
+
+template <int kProblem>
+__device__ __forceinline__ int64_t total_tiles(const UmmaArgs &a) {
+    if (kProblem == kSurprise) return ((a.rows + kBM - 1) / kBM) * a.n_tiles;
+    return static_cast<int64_t>(a.tile_prefix[a.experts]) * a.n_tiles;
+}
+
+template <int kProblem>
+__device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
+    Tile tile{};
+    if (kProblem == kSurprise) {
+        // bands of `band` row tiles; inside a band walk N first so each vocab
+        // tile is reused from L2 by every row tile of the band
+        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        const int64_t per_band = a.band * a.n_tiles;
+        const int64_t band = t / per_band;
+        const int64_t in_band = t - band * per_band;
+        const int64_t band_rows = min(a.band, m_tiles - band * a.band);
+        tile.n = in_band / band_rows;
+        tile.m_tile = band * a.band + (in_band - tile.n * band_rows);
+        tile.row0 = tile.m_tile * kBM;
+        tile.row_end = a.rows;
+        return tile;
+    }
+    const int64_t mt = t / a.n_tiles;
+    tile.n = t - mt * a.n_tiles;
+    int64_t lo = 0, hi = a.experts;
+    while (lo + 1 < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (a.tile_prefix[mid] <= mt) lo = mid; else hi = mid;
+    }
+    tile.group = lo;
+    tile.row0 = a.offsets[lo] + (mt - a.tile_prefix[lo]) * kBM;
+    tile.row_end = a.offsets[lo + 1];
+    tile.m_tile = mt;
+    return tile;
+}
+
+// ---------------------------------------------------------------- kernel
+
+template <int kProblem, typename T>
+__global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    uint8_t *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+    uint8_t *stages = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *acc_full = empty + kStages;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t tiles = total_tiles<kProblem>(args);
+    const int64_t k_blocks = (args.k + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kTmemColumns));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tensor_map(&args.map_a);
+            prefetch_tensor_map(&args.map_b0);
+            if (kProblem == kGated) prefetch_tensor_map(&args.map_b1);
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+                const Tile tile = tile_at<kProblem>(args, t);
+                for (int64_t kb = 0; kb < k_blocks; ++kb) {
+                    if (!wait_or_abort(&empty[stage], phase ^ 1, abort, args.status)) break;
+                    uint8_t *a_dst = stages + stage * kStageBytes;
+                    uint8_t *b_dst = a_dst + kABytes;
+                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    const int32_t kc = static_cast<int32_t>(kb * kBK);
+                    tma_load_2d(a_dst, &args.map_a, &full[stage], kc, static_cast<int32_t>(tile.row0));
+                    if (kProblem == kGated) {
+                        const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * 128);
+                        tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
+                        tma_load_2d(b_dst + kBBytes / 2, &args.map_b1, &full[stage], kc, r);
+                    } else {
+                        const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kBN);
+                        tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
+                    }
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+                if (!wait_or_abort(&acc_empty[acc], acc_phase ^ 1, abort, args.status)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(acc * kBN);
+                bool ok = true;
+                for (int64_t kb = 0; kb < k_blocks; ++kb) {
+                    if (!wait_or_abort(&full[stage], phase, abort, args.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(stages + stage * kStageBytes);
+                    const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        umma_f16(tmem_d, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
+                                 args.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31
+        const int quarter = warp & 3;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+            const Tile tile = tile_at<kProblem>(args, t);
+            if (!wait_or_abort(&acc_full[acc], acc_phase, abort, args.status)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
+            const int64_t row = tile.row0 + quarter * 32 + lane;
+            const bool row_ok = row < tile.row_end && row < args.rows;
+            if (kProblem == kGated) {
+                const T *bg = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
+                const T *bv = static_cast<const T *>(args.bias1) + tile.group * args.b_rows_per_group;
+                T *out = static_cast<T *>(args.out);
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t g[32], v[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, g);
+                    KOEMI_TMEM_LD32(taddr + 128 + c * 32, v);
+                    tmem_wait_ld();
+                    const int64_t col0 = tile.n * 128 + c * 32;
+                    if (row_ok && col0 < args.n_out) {
+                        float h[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int64_t col = col0 + j;
+                            const float gb = col < args.n_out ? to_acc(bg[col]) : 0.0f;
+                            const float vb = col < args.n_out ? to_acc(bv[col]) : 0.0f;
+                            h[j] = siluf_(__uint_as_float(g[j]) + gb) * (__uint_as_float(v[j]) + vb);
+                        }
+                        T *dst = out + row * args.out_stride + col0;
+                        if (col0 + 32 <= args.n_out) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                float part[8];
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) part[e] = h[q * 8 + e];
+                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part, T());
+                            }
+                        } else {
+                            for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = from_acc<T>(h[j]);
+                        }
+                    }
+                }
+            } else if (kProblem == kOutput) {
+                const T *bo = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
+                T *out = static_cast<T *>(args.out);
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t y[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, y);
+                    tmem_wait_ld();
+                    const int64_t col0 = tile.n * kBN + c * 32;
+                    if (row_ok && col0 < args.n_out) {
+                        float o[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int64_t col = col0 + j;
+                            o[j] = __uint_as_float(y[j]) + (col < args.n_out ? to_acc(bo[col]) : 0.0f);
+                        }
+                        T *dst = out + row * args.out_stride + col0;
+                        if (col0 + 32 <= args.n_out) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                float part[8];
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) part[e] = o[q * 8 + e];
+                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part, T());
+                            }
+                        } else {
+                            for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = from_acc<T>(o[j]);
+                        }
+                    }
+                }
+            } else {
+                const T *bias = static_cast<const T *>(args.bias0);
+                const int64_t target = row_ok ? args.targets[row] : -1;
+                float run_max = -INFINITY, run_sum = 0.0f, target_logit = -INFINITY;
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t y[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, y);
+                    tmem_wait_ld();
+                    const int64_t col0 = tile.n * kBN + c * 32;
+                    float l[32];
+                    float chunk_max = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t col = col0 + j;
+                        l[j] = col < args.n_out ? __uint_as_float(y[j]) + to_acc(bias[col]) : -INFINITY;
+                        chunk_max = fmaxf(chunk_max, l[j]);
+                    }
+                    if (target >= col0 && target < col0 + 32) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j == target) target_logit = l[j];
+                        }
+                    }
+                    if (chunk_max != -INFINITY) {
+                        const float m = fmaxf(run_max, chunk_max);
+                        float s = run_sum * expf(run_max - m);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) s += expf(l[j] - m);
+                        run_max = m;
+                        run_sum = s;
+                    }
+                }
+                if (row_ok) {
+                    float *p = args.partials + (tile.n * args.rows + row) * 3;
+                    p[0] = run_max;
+                    p[1] = run_sum;
+                    p[2] = target_logit;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemColumns));
+    }
+}
+
+// ------------------------------------------------------------------- host
+
+uint32_t make_idesc(int dtype) {
+    const uint32_t ab = dtype == KOEMI_BF16 ? 1u : 0u;  // 0 = f16, 1 = bf16
+    uint32_t idesc = 0;
+    idesc |= 1u << 4;                       // D format: f32
+    idesc |= ab << 7;                       // A format
+    idesc |= ab << 10;                      // B format
+    idesc |= static_cast<uint32_t>(kBN >> 3) << 17;
+    idesc |= static_cast<uint32_t>(kBM >> 4) << 24;
+    return idesc;
+}
+
+int encode_kmajor(CUtensorMap *map, int dtype, const void *base, int64_t rows, int64_t k, uint32_t box_rows) {
+    const CUtensorMapDataType type = dtype == KOEMI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(k) * 2};
+    const uint32_t box[2] = {kBK, box_rows};
+    return encode_tensor_map(map, type, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int kProblem>
+int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stream) {
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16> : umma_gemm_kernel<kProblem, __half>;
+    KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
+    int64_t grid = sm_count();
+    if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
+    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(args);
+    KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
 
-size_t grouped_mlp_umma_workspace(int64_t, int64_t, int64_t, int64_t, int) { return 0; }
+bool umma_shape_ok(const void *p, int64_t k) { return k % 8 == 0 && aligned(p, 16) && k > 0; }
 
-int surprise_umma_forward(const void *, const void *, const void *, const int64_t *, int64_t, int64_t, int64_t,
-                          int, float *, int64_t, cudaStream_t, bool *handled) {
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern __global__ void zero_tail_rows_kernel(void *out, const int64_t *offsets, int64_t experts, int64_t pairs,
+                                             int64_t row_bytes);
+
+size_t grouped_mlp_umma_workspace(int64_t pairs, int64_t input_width, int64_t hidden_width, int64_t expert_count,
+                                  int dtype) {
+    (void)input_width;
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return 0;
+    return align256((expert_count + 1) * sizeof(int32_t)) + align256(static_cast<size_t>(pairs) * hidden_width * 2);
+}
+
+int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets, const void *gate_w, const void *gate_b,
+                     const void *value_w, const void *value_b, const void *out_w, const void *out_b, void *output,
+                     int64_t pairs, int64_t input_width, int64_t hidden_width, int64_t expert_count, int dtype,
+                     void *workspace, size_t workspace_bytes, cudaStream_t stream, bool *handled) {
     *handled = false;
+    const int64_t d = input_width, h = hidden_width;
+    if (!umma_shape_ok(sorted_context, d) || !umma_shape_ok(gate_w, d) || !umma_shape_ok(value_w, d) ||
+        !umma_shape_ok(out_w, h) || pairs >= (int64_t(1) << 31) || expert_count * h >= (int64_t(1) << 31) ||
+        expert_count * d >= (int64_t(1) << 31)) {
+        return KOEMI_OK;  // the fp32 FMA path takes shapes TMA cannot describe
+    }
+    if (workspace_bytes < grouped_mlp_umma_workspace(pairs, d, h, expert_count, dtype)) {
+        return fail(KOEMI_ERR_WORKSPACE, "grouped MLP tensor-core path needs more workspace");
+    }
+    char *ws = static_cast<char *>(workspace);
+    int32_t *prefix = reinterpret_cast<int32_t *>(ws);
+    void *hidden = ws + align256((expert_count + 1) * sizeof(int32_t));
+    tile_prefix_kernel<<<1, 1, 0, stream>>>(segment_offsets, expert_count, kBM, prefix);
+    KOEMI_LAUNCH_CHECK();
+    const int64_t max_m_tiles = (pairs + kBM - 1) / kBM + expert_count;
+
+    UmmaArgs g1{};
+    int rc = encode_kmajor(&g1.map_a, dtype, sorted_context, pairs, d, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g1.map_b0, dtype, gate_w, expert_count * h, d, 128);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g1.map_b1, dtype, value_w, expert_count * h, d, 128);
+    if (rc != KOEMI_OK) return rc;
+    g1.k = d;
+    g1.rows = pairs;
+    g1.n_tiles = (h + 127) / 128;
+    g1.b_rows_per_group = h;
+    g1.n_out = h;
+    g1.out_stride = h;
+    g1.experts = expert_count;
+    g1.offsets = segment_offsets;
+    g1.tile_prefix = prefix;
+    g1.bias0 = gate_b;
+    g1.bias1 = value_b;
+    g1.out = hidden;
+    g1.status = device_status_word();
+    g1.idesc = make_idesc(dtype);
+    rc = launch<kGated>(g1, dtype, max_m_tiles * g1.n_tiles, stream);
+    if (rc != KOEMI_OK) return rc;
+
+    UmmaArgs g2{};
+    rc = encode_kmajor(&g2.map_a, dtype, hidden, pairs, h, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g2.map_b0, dtype, out_w, expert_count * d, h, kBN);
+    if (rc != KOEMI_OK) return rc;
+    g2.k = h;
+    g2.rows = pairs;
+    g2.n_tiles = (d + kBN - 1) / kBN;
+    g2.b_rows_per_group = d;
+    g2.n_out = d;
+    g2.out_stride = d;
+    g2.experts = expert_count;
+    g2.offsets = segment_offsets;
+    g2.tile_prefix = prefix;
+    g2.bias0 = out_b;
+    g2.out = output;
+    g2.status = g1.status;
+    g2.idesc = g1.idesc;
+    rc = launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
+    if (rc != KOEMI_OK) return rc;
+    zero_tail_rows_kernel<<<256, 256, 0, stream>>>(output, segment_offsets, expert_count, pairs, d * 2);
+    KOEMI_LAUNCH_CHECK();
+    *handled = true;
     return KOEMI_OK;
 }
 
-int64_t surprise_umma_slices(int64_t, int64_t, int64_t, int) { return 0; }
+int64_t surprise_umma_slices(int64_t rows, int64_t width, int64_t content_vocab, int dtype) {
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return 0;
+    if (width % 8 != 0 || rows <= 0 || content_vocab >= (int64_t(1) << 31)) return 0;
+    return (content_vocab + kBN - 1) / kBN;
+}
+
+int surprise_umma_forward(const void *prior, const void *weight, const void *bias, const int64_t *targets,
+                          int64_t rows, int64_t width, int64_t content_vocab, int dtype, float *partials,
+                          int64_t slices, cudaStream_t stream, bool *handled) {
+    *handled = false;
+    if (!umma_shape_ok(prior, width) || !umma_shape_ok(weight, width) || rows >= (int64_t(1) << 31) ||
+        slices != surprise_umma_slices(rows, width, content_vocab, dtype)) {
+        return KOEMI_OK;
+    }
+    UmmaArgs a{};
+    int rc = encode_kmajor(&a.map_a, dtype, prior, rows, width, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&a.map_b0, dtype, weight, content_vocab, width, kBN);
+    if (rc != KOEMI_OK) return rc;
+    a.k = width;
+    a.rows = rows;
+    a.n_tiles = slices;
+    a.b_rows_per_group = 0;
+    a.n_out = content_vocab;
+    a.out_stride = 0;
+    a.experts = 1;
+    a.band = 16;
+    a.bias0 = bias;
+    a.partials = partials;
+    a.targets = targets;
+    a.status = device_status_word();
+    a.idesc = make_idesc(dtype);
+    const int64_t tiles = ((rows + kBM - 1) / kBM) * slices;
+    rc = launch<kSurprise>(a, dtype, tiles, stream);
+    if (rc != KOEMI_OK) return rc;
+    *handled = true;
+    return KOEMI_OK;
+}
 
 }  // namespace koemi

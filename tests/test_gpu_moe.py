@@ -185,3 +185,44 @@ def test_moe_baseline_config_routing_properties(cuda):
     assert np.array_equal(rows.cpu().numpy(), o_rows)
     assert np.array_equal(offsets.cpu().numpy(), o_offsets)
     assert torch.equal(sc[:4096], x[rows[:4096]])
+
+
+def _sampled_rows_check(sc, se, offsets, y, weights, rows, dtype, tol):
+    """Oracle (fp64, hidden rounded to dtype) on a sample of sorted rows."""
+    gw, gb, vw, vb, ow, ob = weights
+    for i in rows:
+        e = int(se[i])
+        x = sc[i:i + 1].cpu().double()
+        hidden = ops.silu(x @ gw[e].cpu().double().T + gb[e].cpu().double()) * (
+            x @ vw[e].cpu().double().T + vb[e].cpu().double())
+        hidden = hidden.to(dtype).double()
+        expected = hidden @ ow[e].cpu().double().T + ob[e].cpu().double()
+        got = y[i].cpu().double()
+        scale = expected.abs().max().item() + 1e-6
+        torch.testing.assert_close(got / scale, expected[0].to(dtype).double() / scale, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("tokens,d,h,e,k", [(131072, 1024, 2048, 64, 2), (256, 2048, 4096, 64, 2)])
+def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
+    """Config 4 (131072 tokens, d=1024, d_ff=2048, 64 experts, top-2) and the
+    config-5 decode step (256 streams, d=2048, d_ff=4096): sampled rows of
+    every segment position class against the fp64 oracle."""
+    g = torch.Generator(device=cuda).manual_seed(tokens)
+    x = torch.randn(tokens, d, generator=g, device=cuda).bfloat16()
+    scores = torch.rand(tokens, e, generator=g, device=cuda)
+    assignments = scores.topk(k, dim=-1).indices
+    valid = torch.ones(tokens, dtype=torch.bool, device=cuda)
+    weights = tuple((torch.randn(*s, generator=g, device=cuda) * 0.02).bfloat16() for s in
+                    ((e, h, d), (e, h), (e, h, d), (e, h), (e, d, h), (e, d)))
+    sc, rows, se, offsets, _ = _ops.permute_topk(x, assignments, valid, e, True)
+    y = _ops.grouped_expert_mlp(sc, se, offsets, *weights)
+    torch.cuda.synchronize()
+    off = offsets.cpu()
+    sample = set()
+    for expert in (0, 1, e // 2, e - 1):
+        begin, end = int(off[expert]), int(off[expert + 1])
+        for r in (begin, begin + 1, begin + 127, begin + 128, (begin + end) // 2, end - 1):
+            if begin <= r < end:
+                sample.add(r)
+    _sampled_rows_check(sc, se, offsets, y, weights, sorted(sample), torch.bfloat16, 3e-2)
+    assert bool(torch.isfinite(y).all())

@@ -123,3 +123,18 @@ def test_surprise_accepts_strided_targets(cuda):
                                        torch.float32)
     torch.testing.assert_close(got.cpu().double(), ops.causal_surprise(prior, weight, bias, targets, valid),
                                rtol=2e-5, atol=2e-6)
+
+
+def test_surprise_tensor_core_decode_shape(cuda):
+    """Config-5 decode: 256 rows x d=2048 against the 32767-entry content head
+    (bf16 operands, fp32 accumulate); sampled rows vs the fp64 oracle."""
+    g = torch.Generator().manual_seed(12)
+    prior = torch.randn(1, 256, 2048, generator=g).bfloat16()
+    weight = (torch.randn(32767, 2048, generator=g) * 0.02).bfloat16()
+    bias = (torch.randn(32767, generator=g) * 0.002).bfloat16()
+    targets = torch.randint(0, 32767, (1, 256), generator=g)
+    valid = torch.ones(1, 256, dtype=torch.bool)
+    got = causal_surprise(*(t.to(cuda) for t in (prior, weight, bias, targets, valid)))
+    pick = [0, 1, 127, 128, 200, 255]
+    expected = ops.causal_surprise(prior[:, pick], weight, bias, targets[:, pick], valid[:, pick])
+    torch.testing.assert_close(got[:, pick].cpu().double(), expected.bfloat16().double(), rtol=1.6e-2, atol=4e-3)
