@@ -39,3 +39,15 @@ def load_golden(name: str) -> dict:
 @pytest.fixture
 def cuda():
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(request):
+    """After every GPU test, the library's device status word must be clear:
+    a bounded device-side wait that gave up is a failure, never silent."""
+    yield
+    if "gpu" in request.keywords and torch.cuda.is_available():
+        from koemi_5hom_b200 import _native
+        if _native._LIBRARY is not None and _native._INITIALISED_DEVICES:
+            for index in list(_native._INITIALISED_DEVICES):
+                assert _native.device_status(torch.device("cuda", index)) == 0, "device-side wait timed out"
