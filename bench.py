@@ -57,6 +57,8 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
+    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "expert_decode", "surprise_decode", "surprise_prefill"),
+                   default=None, help="time one operator at its BASELINE shape instead of the decode step")
     return p.parse_args(argv)
 
 
@@ -322,11 +324,13 @@ def run_b200(args) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("decode_timed")
         start.record(stream)
         for _ in range(args.steps):
             logits = decoder.step(token)
             token = logits.argmax(dim=-1, keepdim=True)
         stop.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -395,8 +399,94 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------- operators
+def _time_op(fn, steps: int, warmup: int) -> float:
+    import torch
+    for _ in range(max(warmup, 1)):
+        fn()
+    stream = torch.cuda.current_stream()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / 1000.0 / steps
+
+
+def run_op(args) -> None:
+    """One operator at its BASELINE.json shape, CUDA-event timed; inputs are
+    larger than L2 (stated per op), so back-to-back launches read HBM."""
+    import torch
+    from koemi_5hom_b200 import _native
+    from koemi_5hom_b200.cuda_kernels import _ops
+    device = torch.device("cuda", 0)
+    _native.ensure_device(device)
+    g = torch.Generator(device=device).manual_seed(0)
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    hbm, tensor = peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0)
+    if args.op == "scan":  # config 2: B=8, T=4096, D=1024, a = sigmoid(N(0,1)), b ~ N(0,1), h0 = 0
+        a = torch.sigmoid(torch.randn(8, 4096, 1024, device=device, generator=g)).bfloat16()
+        b = torch.randn(8, 4096, 1024, device=device, generator=g).bfloat16()
+        h0 = torch.zeros(8, 1024, device=device, dtype=torch.bfloat16)
+        seconds = _time_op(lambda: _ops.affine_scan_forward(a, b, h0, False), args.steps, args.warmup)
+        work, unit, peak, bound = 3 * a.numel() * 2 / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = "B=8 T=4096 D=1024 bf16 (201 MB per launch > L2)"
+    elif args.op == "rmsnorm":  # config 3: 65536 x 2048 bf16, gated form silu(gate) * rmsnorm(x) * w
+        x = torch.randn(65536, 2048, device=device, generator=g).bfloat16()
+        gate = torch.randn(65536, 2048, device=device, generator=g).bfloat16()
+        w = (1.0 + 0.02 * torch.randn(2048, device=device, generator=g)).bfloat16()
+        seconds = _time_op(lambda: _ops.gated_rmsnorm_silu(x, gate, w, 1e-6), args.steps, args.warmup)
+        work, unit, peak, bound = 3 * x.numel() * 2 / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = "65536 x 2048 bf16, gated (805 MB per launch > L2)"
+    elif args.op in ("moe", "expert_decode"):
+        tokens, d, e = (131072, 1024, 64) if args.op == "moe" else (256, 2048, 64)
+        h = 2 * d
+        x = torch.randn(tokens, d, device=device, generator=g).bfloat16()
+        ids = torch.randint(0, 256, (tokens,), device=device, generator=g)
+        prev = torch.randint(0, 256, (tokens,), device=device, generator=g)
+        valid = torch.ones(tokens, dtype=torch.bool, device=device)
+        weights = [(torch.randn(*s, device=device, generator=g) * 0.02).bfloat16() for s in
+                   ((e, h, d), (e, h), (e, h, d), (e, h), (e, d, h), (e, d))]
+        assignments = _ops.route_topk(ids, prev, valid, e, 2)
+        sc, _, se, offsets, _ = _ops.permute_topk(x, assignments, valid, e, True)
+        seconds = _time_op(lambda: _ops.grouped_expert_mlp(sc, se, offsets, *weights), args.steps, args.warmup)
+        pairs = int(offsets[-1])
+        if args.op == "moe":
+            work, unit, peak, bound = pairs * 6 * d * h / seconds / 1e12, "TFLOP/s", tensor, "tensor"
+            shape = f"config 4: {tokens} tokens, {pairs} pairs, d={d}, d_ff={h}, E={e}, top-2 (hash route)"
+        else:
+            touched = int((torch.diff(offsets) > 0).sum())
+            moved = touched * 3 * d * h * 2 + pairs * (2 * d + 4 * h) * 2
+            work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
+            shape = f"config 5 decode step: {pairs} pairs, {touched} experts touched, d={d}, d_ff={h} (3.2 GB weights > L2)"
+    else:  # surprise head: decode (256 rows) or one prefill window (32768 rows) of config 5
+        rows = 256 if args.op == "surprise_decode" else 32768
+        prior = torch.randn(rows, 2048, device=device, generator=g).bfloat16()
+        weight = (torch.randn(32767, 2048, device=device, generator=g) * 0.02).bfloat16()
+        bias = (torch.randn(32767, device=device, generator=g) * 0.002).bfloat16()
+        targets = torch.randint(0, 32767, (rows,), device=device, generator=g)
+        valid = torch.ones(rows, dtype=torch.bool, device=device)
+        seconds = _time_op(lambda: _ops.causal_surprise_forward(prior, weight, bias, targets, valid, torch.float32),
+                           args.steps, args.warmup)
+        if args.op == "surprise_decode":
+            work, unit, peak, bound = (weight.numel() * 2 + prior.numel() * 2) / seconds / 1e9, "GB/s", hbm, "hbm"
+        else:
+            work, unit, peak, bound = 2 * rows * 32767 * 2048 / seconds / 1e12, "TFLOP/s", tensor, "tensor"
+        shape = f"{rows} rows x d=2048 against the 32767-row content head (134 MB bf16 > L2)"
+    line = {"op": args.op, "shape": shape, "us_per_launch": seconds * 1e6,
+            "roofline": {"bound": bound, "achieved": work, "peak": peak, "unit": unit, "frac": work / peak,
+                         "peak_source": "MEASURED_PEAKS.json (burst)" if peaks else "fallback"}}
+    emit(line, args)
+
+
 def main(argv=None) -> None:
     args = parse_args(argv)
+    if args.op is not None:
+        run_op(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

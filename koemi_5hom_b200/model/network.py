@@ -30,6 +30,7 @@ surprise against the shared head. The reference defines one block only.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass
 from enum import Enum
@@ -307,8 +308,9 @@ class KoemiModel(nn.Module):
                 last = start + window >= length
                 piece = self._window(input_ids[:, start:start + window], state, trusted_inputs,
                                      logits=(not last_logits_only) or last, last_only=last_logits_only)
-                outputs.append(piece)
                 state = piece.state
+                # keep only per-position outputs: a window's state is superseded by the next
+                outputs.append(piece if last else dataclasses.replace(piece, state=None))
         if len(outputs) == 1:
             return outputs[0]
         return _concatenate(outputs, last_logits_only)
