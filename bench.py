@@ -34,6 +34,8 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# ~140 GB stay live during the config-5 prefill; let the allocator grow segments
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
 
 METRIC = "decode tokens/s at 1/2/4/8 B200; per-kernel % of HBM / tensor-core roofline"
 UNIT = "tokens/s"
