@@ -222,6 +222,24 @@ KOEMI_API int koemi_moe_permute_topk(const void *context, const void *assignment
                            int assignment_dtype, void *workspace, size_t workspace_bytes,
                            void *stream);
 
+/* Allocation-free variant of koemi_moe_permute_topk, for callers that cannot
+ * allocate device memory (a host runtime that only hands over buffers it
+ * already owns, or code that must not call cudaMalloc while other work is in
+ * flight). It has no counterpart in the reference. Arguments and outputs are
+ * those of koemi_moe_permute_topk minus the workspace: the scratch is a fixed
+ * 2 MiB device array inside the library, held by every GPU that loads it
+ * until the process exits, enough for 65536 token-expert pairs; larger
+ * requests fail with KOEMI_ERR_UNSUPPORTED and a message. The first call on a
+ * device looks up that array's address with the device current, so make that
+ * first call before any stream capture. All calls share the array: calls that
+ * can overlap on the GPU (different streams, different host threads) race and
+ * must be serialised by the caller. Allocates nothing. */
+KOEMI_API int koemi_moe_permute_topk_static(const void *context, const void *assignments, const uint8_t *valid,
+                                  void *sorted_context, int64_t *sorted_rows, int64_t *sorted_experts,
+                                  int64_t *segment_offsets, int64_t *pair_positions, int64_t tokens,
+                                  int64_t width, int64_t top_k, int64_t expert_count, int context_dtype,
+                                  int assignment_dtype, void *stream);
+
 /* Grouped gated expert MLP over sorted segments (GatedFeedForward,
  * model/layers.py:19-29): for sorted pair i of expert e,
  *   y_i = W_o[e] (silu(W_g[e] x_i + b_g[e]) * (W_v[e] x_i + b_v[e])) + b_o[e];

@@ -68,6 +68,8 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_moe_permute_workspace": (_sz, (_i64, _i64, _i64)),
     "koemi_moe_permute_topk": (
         _int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _p, _sz, _p)),
+    "koemi_moe_permute_topk_static": (
+        _int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _p)),
     "koemi_moe_grouped_mlp_workspace": (_sz, (_i64, _i64, _i64, _i64, _int)),
     "koemi_moe_grouped_expert_mlp": (
         _int, (_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),

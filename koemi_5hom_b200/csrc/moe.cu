@@ -588,3 +588,64 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free permutation: the same stable permutation as
+// koemi_moe_permute_topk, with its scratch in a fixed device array instead of
+// a caller workspace, for callers that cannot allocate device memory.
+#include <mutex>
+
+namespace {
+constexpr size_t kStaticPermuteScratchBytes = size_t(2) << 20;  // 2 MiB on every device that loads the library
+constexpr int kStaticScratchDevices = 64;
+std::mutex g_static_scratch_mutex;
+void *g_static_scratch[kStaticScratchDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char koemi_permute_static_scratch[kStaticPermuteScratchBytes];
+
+namespace {
+// Device address of the scratch array for the current device, looked up once
+// per device (with that device current) and cached.
+int static_permute_scratch(void **out) {
+    int device = 0;
+    KOEMI_CUDA_TRY(cudaGetDevice(&device));
+    if (device < 0 || device >= kStaticScratchDevices) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "device %d is beyond the static-scratch device table", device);
+    }
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (g_static_scratch[device] == nullptr) {
+        void *address = nullptr;
+        KOEMI_CUDA_TRY(cudaGetSymbolAddress(&address, koemi_permute_static_scratch));
+        g_static_scratch[device] = address;
+    }
+    *out = g_static_scratch[device];
+    return KOEMI_OK;
+}
+}  // namespace
+
+extern "C" int koemi_moe_permute_topk_static(const void *context, const void *assignments, const uint8_t *valid,
+                                             void *sorted_context, int64_t *sorted_rows, int64_t *sorted_experts,
+                                             int64_t *segment_offsets, int64_t *pair_positions, int64_t tokens,
+                                             int64_t width, int64_t top_k, int64_t expert_count, int context_dtype,
+                                             int assignment_dtype, void *stream) {
+    clear_error();
+    if (tokens < 0 || top_k < 1 || top_k > 256 || expert_count < 1 || expert_count > (1 << 20)) {
+        return fail(KOEMI_ERR_INVALID, "need tokens >= 0, top_k in [1, 256] and expert_count in [1, 2^20]");
+    }
+    const size_t need = koemi_moe_permute_workspace(tokens, top_k, expert_count);
+    if (need > kStaticPermuteScratchBytes) {
+        return fail(KOEMI_ERR_UNSUPPORTED,
+                    "allocation-free permute: %lld tokens x top_k %lld over %lld experts needs %zu scratch bytes, "
+                    "more than the fixed %zu (at most 65536 pairs); use koemi_moe_permute_topk with a workspace",
+                    (long long)tokens, (long long)top_k, (long long)expert_count, need, kStaticPermuteScratchBytes);
+    }
+    void *scratch = nullptr;
+    const int rc = static_permute_scratch(&scratch);
+    if (rc != KOEMI_OK) return rc;
+    // Nothing in the scratch has to start at zero: every count, key and
+    // index the permutation reads is written earlier in the same call.
+    return koemi_moe_permute_topk(context, assignments, valid, sorted_context, sorted_rows, sorted_experts,
+                                  segment_offsets, pair_positions, tokens, width, top_k, expert_count, context_dtype,
+                                  assignment_dtype, scratch, kStaticPermuteScratchBytes, stream);
+}
