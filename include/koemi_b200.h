@@ -110,6 +110,18 @@ KOEMI_API int koemi_dense_bounded_gates(const float *projections, const uint8_t 
                               int64_t features, float minimum_retention,
                               float maximum_retention, void *stream);
 
+/* Decode step of the gates and the scan (one token per stream), in place:
+ * a = lo + (hi - lo) sigmoid(pre_a), b = (1 - a) tanh(pre_c) (a = 1, b = 0 where
+ * !valid); prior_out <- working (cast to prior_dtype, may be NULL);
+ * working <- a * working + b; h_out[row * h_stride + f] <- the new working.
+ * `projections` is [batch, 2*features] fp32 (pre_a | pre_c). Fuses
+ * BoundedRecurrentState.gates (model/memory.py:22-26), the masks of
+ * network.py:308-309 and the T == 1 affine scan (model/scan.py:17-30). */
+KOEMI_API int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
+                            void *prior_out, float *h_out, int64_t h_stride, int64_t batch,
+                            int64_t features, float minimum_retention, float maximum_retention,
+                            int prior_dtype, void *stream);
+
 /* ------------------------------------------------------------- core front */
 
 /* y = silu(x * rsqrt(mean(x^2) + eps) * w), inv_rms[row] = rsqrt(...).
@@ -181,6 +193,44 @@ KOEMI_API int koemi_think_salient_admission(const float *carried_keys, const flo
                                   uint8_t *admission_out, int64_t batch, int64_t carried,
                                   int64_t length, int64_t width, int64_t capacity,
                                   void *stream);
+
+/* One decode step of both exact-memory rings of every stream, in place
+ * (LocalKeyValueMemory.read_window / read_salient_window / tail /
+ * salient_tail, model/memory.py:332-455, and the admission of
+ * network.py:349, at sequence length 1). Rings are circular: the local ring's
+ * oldest slot is *local_head for every stream; salient ring b holds
+ * salient_count[b] admitted entries starting at salient_head[b]. Reads the
+ * query rows (queries + b*query_stride, fp32 width), computes the softmax
+ * reads of both rings (scale 1/sqrt(width)) and the local novelty, then
+ * writes the new entry (entries + b*entry_stride: key | value, zeroed when
+ * !valid) over the oldest local slot and, when valid && surprise > threshold,
+ * into the salient ring (dropping its oldest entry when full). Outputs go to
+ * local_out / salient_out rows of out_stride; novelty_out and admission_out
+ * ([batch]) may be NULL. All fp32 rows 16-byte aligned, width % 4 == 0. The
+ * caller advances *local_head once per step. */
+KOEMI_API int koemi_think_ring_decode_step(
+    const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride,
+    const uint8_t *valid, const float *surprise, float threshold, float *local_keys, float *local_values,
+    uint8_t *local_valid, const int64_t *local_head, float *salient_keys, float *salient_values,
+    uint8_t *salient_valid, int32_t *salient_head, int32_t *salient_count, float *local_out,
+    float *salient_out, int64_t out_stride, float *novelty_out, uint8_t *admission_out, int64_t batch,
+    int64_t width, int64_t local_slots, int64_t salient_slots, void *stream);
+
+/* One decode step of the rank-one associative memory, in place
+ * (HierarchicalAssociativeMemory.project / read / update with the fast write
+ * terms, model/memory.py:82-95,248-255,279-287, network.py:338-347):
+ * `projections` rows (stride proj_stride) hold key | query | value_pre |
+ * decay_pre | write_pre as produced by one GEMM; feature_logits is
+ * [2, batch, features] (key then query logits of the feature projection).
+ * Writes the confidence-weighted read to read_out rows (stride read_stride)
+ * from the memory before this step's write, then basis <- decay * basis +
+ * w * tanh(value) f^T and normalizer <- decay * normalizer + w f, with
+ * w = sigmoid(write_pre) (0.25 + 0.75 clamp(surprise)) (surprise may be NULL:
+ * 0); invalid rows keep their memory. */
+KOEMI_API int koemi_assoc_decode_step(const float *projections, int64_t proj_stride,
+                            const float *feature_logits, const float *surprise, const uint8_t *valid,
+                            float *basis, float *normalizer, float *read_out, int64_t read_stride,
+                            int64_t batch, int64_t width, int64_t features, void *stream);
 
 /* -------------------------------------------------------------- moe front */
 

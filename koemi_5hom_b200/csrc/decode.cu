@@ -1,0 +1,360 @@
+// Decode-step kernels: one token per stream, state updated in place.
+//
+// The window path (model/network.py) rebuilds every ring with cat/slice each
+// step, like the reference (memory.py:385-403,431-475). At decode the rings
+// are circular instead: the local ring's oldest slot is one device-side head
+// shared by all streams (every stream writes one entry per step), and each
+// salient ring keeps its own head and count (entries are written only when a
+// token is admitted). Reads are order-independent softmax sums, so they see
+// exactly the reference's rings; the logical (oldest-first) order is restored
+// only when the state is exported.
+//
+//  koemi_dense_decode_step      gate epilogue + padding masks + scan step
+//                               (memory.py:22-26, network.py:307-310)
+//  koemi_think_ring_decode_step local and salient reads, novelty, then the
+//                               ring writes and admission (memory.py:307-361,
+//                               405-455; network.py:327-358)
+//  koemi_assoc_decode_step      feature softmaxes, confidence-weighted read of
+//                               the rank-one memory and its decayed write
+//                               (memory.py:82-95,248-255,279-287)
+#include <cmath>
+
+#include "common.cuh"
+
+namespace koemi {
+namespace {
+
+// -------------------------------------------------------------- gates+scan
+template <typename TP>
+__global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t *__restrict__ valid,
+                                    float *__restrict__ working, TP *__restrict__ prior, float *__restrict__ h_out,
+                                    int64_t h_stride, int64_t batch, int64_t features, float lo, float hi) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= batch * features) return;
+    const int64_t row = i / features;
+    const int64_t f = i - row * features;
+    const bool ok = valid == nullptr || valid[row] != 0;
+    float a = 1.0f, b = 0.0f;
+    if (ok) {
+        a = lo + (hi - lo) * sigmoidf_(pre[row * 2 * features + f]);
+        b = (1.0f - a) * tanhf(pre[row * 2 * features + features + f]);
+    }
+    const float previous = working[i];
+    if (prior != nullptr) prior[i] = from_acc<TP>(previous);
+    const float h = a * previous + b;
+    working[i] = h;
+    if (h_out != nullptr) h_out[row * h_stride + f] = h;
+}
+
+// ---------------------------------------------------------------- rings
+constexpr int kRingThreads = 256;
+constexpr int kRingWarps = kRingThreads / 32;
+
+struct RingArgs {
+    const float *queries;
+    int64_t query_stride;
+    const float *entries;  // [B, 2d]: key | value of the new entry (unmasked)
+    int64_t entry_stride;
+    const uint8_t *valid;
+    const float *surprise;
+    float threshold;
+    float *local_keys;
+    float *local_values;
+    uint8_t *local_valid;
+    const int64_t *local_head;
+    float *salient_keys;
+    float *salient_values;
+    uint8_t *salient_valid;
+    int32_t *salient_head;
+    int32_t *salient_count;
+    float *local_out;
+    float *salient_out;
+    int64_t out_stride;
+    float *novelty_out;
+    uint8_t *admission_out;
+    int64_t batch;
+    int64_t width;
+    int64_t local_slots;
+    int64_t salient_slots;
+};
+
+__device__ __forceinline__ float block_reduce(float v, float *scratch, bool take_max) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = take_max ? warp_max(v) : warp_sum(v);
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float r = scratch[0];
+    for (int w = 1; w < kRingWarps; ++w) r = take_max ? fmaxf(r, scratch[w]) : r + scratch[w];
+    return r;
+}
+
+// blockIdx.y == 0: local ring, 1: salient ring. Shared memory: q[width],
+// scores[slots], cosines[slots], reduction scratch.
+__global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
+    extern __shared__ float shared[];
+    const bool local = blockIdx.y == 0;
+    const int64_t b = blockIdx.x;
+    const int64_t d = a.width;
+    const int64_t slots = local ? a.local_slots : a.salient_slots;
+    float *q = shared;
+    float *score = q + d;
+    float *cosine = score + slots;
+    float *scratch = cosine + slots;
+    __shared__ int32_t write_slot;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float *query = a.queries + b * a.query_stride;
+    float qq = 0.0f;
+    for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
+        const float v = query[c];
+        q[c] = v;
+        qq += v * v;
+    }
+    const float q_norm = sqrtf(block_reduce(qq, scratch, false));
+    const float *keys = (local ? a.local_keys : a.salient_keys) + b * slots * d;
+    const float *values = (local ? a.local_values : a.salient_values) + b * slots * d;
+    const uint8_t *flags = (local ? a.local_valid : a.salient_valid) + b * slots;
+    const float scale = rsqrtf(static_cast<float>(d));
+    const int64_t quads = d / 4;  // the host requires width % 4 == 0
+    const float4 *q4 = reinterpret_cast<const float4 *>(q);
+
+    // pass 1: one warp per slot, dot(q, k) and |k|^2 over float4 packets
+    for (int64_t s = warp; s < slots; s += kRingWarps) {
+        if (!flags[s]) {
+            if (lane == 0) {
+                score[s] = -INFINITY;
+                cosine[s] = -INFINITY;
+            }
+            continue;
+        }
+        const float4 *k4 = reinterpret_cast<const float4 *>(keys + s * d);
+        float dot = 0.0f, kk = 0.0f;
+#pragma unroll 4
+        for (int64_t c = lane; c < quads; c += 32) {
+            const float4 k = __ldg(k4 + c);
+            const float4 x = q4[c];
+            dot += k.x * x.x + k.y * x.y + k.z * x.z + k.w * x.w;
+            kk += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
+        }
+        dot = warp_sum(dot);
+        kk = warp_sum(kk);
+        if (lane == 0) {
+            score[s] = dot * scale;
+            cosine[s] = dot / (fmaxf(sqrtf(kk), 1e-12f) * fmaxf(q_norm, 1e-12f));
+        }
+    }
+    __syncthreads();
+    float m = -INFINITY, best_cos = -INFINITY;
+    for (int64_t s = threadIdx.x; s < slots; s += kRingThreads) {
+        m = fmaxf(m, score[s]);
+        best_cos = fmaxf(best_cos, cosine[s]);
+    }
+    m = block_reduce(m, scratch, true);
+    best_cos = block_reduce(best_cos, scratch, true);
+    const bool any = m != -INFINITY;
+    float total = 0.0f;
+    for (int64_t s = threadIdx.x; s < slots; s += kRingThreads) {
+        const float w = any && score[s] != -INFINITY ? expf(score[s] - m) : 0.0f;
+        score[s] = w;
+        total += w;
+    }
+    total = block_reduce(total, scratch, false);
+    const float inv_total = any ? 1.0f / total : 0.0f;
+
+    // pass 2: each thread owns float4 columns, sums the weighted values
+    float *out = (local ? a.local_out : a.salient_out) + b * a.out_stride;
+    for (int64_t c = threadIdx.x; c < quads; c += kRingThreads) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int64_t s = 0; s < slots; ++s) {
+            const float w = score[s];
+            if (w == 0.0f) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(values + s * d) + c);
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
+        }
+        acc.x *= inv_total;
+        acc.y *= inv_total;
+        acc.z *= inv_total;
+        acc.w *= inv_total;
+        reinterpret_cast<float4 *>(out)[c] = acc;
+    }
+    const bool token_valid = a.valid == nullptr || a.valid[b] != 0;
+    if (local && threadIdx.x == 0 && a.novelty_out != nullptr) {
+        a.novelty_out[b] = any ? fminf(fmaxf(1.0f - best_cos, 0.0f), 1.0f) : 1.0f;
+    }
+
+    // writes, after every read of the slot being replaced
+    if (threadIdx.x == 0) {
+        if (local) {
+            write_slot = static_cast<int32_t>(*a.local_head);
+        } else {
+            const bool admitted = token_valid && a.surprise[b] > a.threshold;
+            if (a.admission_out != nullptr) a.admission_out[b] = admitted;
+            write_slot = -1;
+            if (admitted) {
+                const int32_t head = a.salient_head[b];
+                const int32_t count = a.salient_count[b];
+                if (count < slots) {
+                    write_slot = static_cast<int32_t>((head + count) % slots);
+                    a.salient_count[b] = count + 1;
+                } else {
+                    write_slot = head;  // the ring is full: the oldest admitted entry leaves
+                    a.salient_head[b] = static_cast<int32_t>((head + 1) % slots);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int32_t slot = write_slot;
+    if (slot < 0) return;
+    float *key_dst = (local ? a.local_keys : a.salient_keys) + (b * slots + slot) * d;
+    float *value_dst = (local ? a.local_values : a.salient_values) + (b * slots + slot) * d;
+    const float *entry = a.entries + b * a.entry_stride;
+    for (int64_t c = threadIdx.x; c < quads; c += kRingThreads) {
+        float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f), v = k;
+        if (token_valid) {
+            k = reinterpret_cast<const float4 *>(entry)[c];
+            v = reinterpret_cast<const float4 *>(entry + d)[c];
+        }
+        reinterpret_cast<float4 *>(key_dst)[c] = k;
+        reinterpret_cast<float4 *>(value_dst)[c] = v;
+    }
+    if (threadIdx.x == 0) (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
+}
+
+// ----------------------------------------------------------- associative
+constexpr int kAssocThreads = 256;
+
+__global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
+    const float *__restrict__ projections, int64_t proj_stride, const float *__restrict__ feature_logits,
+    const float *__restrict__ surprise, const uint8_t *__restrict__ valid, float *__restrict__ basis,
+    float *__restrict__ normalizer, float *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
+    int64_t m) {
+    extern __shared__ float shared[];
+    float *f = shared;       // [m] write features
+    float *qf = shared + m;  // [m] query features
+    __shared__ float s_decay, s_write, s_den;
+    const int64_t b = blockIdx.x;
+    const float *proj = projections + b * proj_stride;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        for (int which = 0; which < 2; ++which) {
+            const float *logits = feature_logits + (which * batch + b) * m;
+            float mx = -INFINITY;
+            for (int64_t j = lane; j < m; j += 32) mx = fmaxf(mx, logits[j]);
+            mx = warp_max(mx);
+            float sum = 0.0f;
+            for (int64_t j = lane; j < m; j += 32) sum += expf(logits[j] - mx);
+            sum = warp_sum(sum);
+            float *dst = which == 0 ? f : qf;
+            for (int64_t j = lane; j < m; j += 32) dst[j] = expf(logits[j] - mx) / sum;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            const bool ok = valid == nullptr || valid[b] != 0;
+            const float lo = 1.0f / 4096.0f, hi = 1.0f - 1.0f / 4096.0f;
+            const float decay = lo + (hi - lo) * sigmoidf_(proj[3 * d]);
+            const float s = surprise != nullptr ? fminf(fmaxf(surprise[b], 0.0f), 1.0f) : 0.0f;
+            const float write = sigmoidf_(proj[3 * d + 1]) * (0.25f + 0.75f * s);
+            s_decay = ok ? decay : 1.0f;
+            s_write = ok ? write : 0.0f;
+            float den = 0.0f;
+            for (int64_t j = 0; j < m; ++j) den += normalizer[b * m + j] * qf[j];
+            s_den = den;
+        }
+    }
+    __syncthreads();
+    const float decay = s_decay, write = s_write, den = s_den;
+    const float reg = den + 1.0f / 256.0f;
+    const float confidence = den / reg;
+    float *rows = basis + b * d * m;
+    for (int64_t i = threadIdx.x; i < d; i += kAssocThreads) {
+        float *row = rows + i * m;
+        const float v = tanhf(proj[2 * d + i]);
+        float num = 0.0f;
+        for (int64_t j = 0; j < m; ++j) {
+            const float x = row[j];
+            num += x * qf[j];
+            row[j] = decay * x + write * v * f[j];
+        }
+        read_out[b * read_stride + i] = confidence * num / reg;
+    }
+    __syncthreads();
+    if (threadIdx.x < m) {
+        const int64_t j = threadIdx.x;
+        normalizer[b * m + j] = decay * normalizer[b * m + j] + write * f[j];
+    }
+}
+
+}  // namespace
+}  // namespace koemi
+
+using namespace koemi;
+
+extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
+                                       void *prior_out, float *h_out, int64_t h_stride, int64_t batch,
+                                       int64_t features, float minimum_retention, float maximum_retention,
+                                       int prior_dtype, void *stream) {
+    clear_error();
+    if (batch < 0 || features < 0) return fail(KOEMI_ERR_INVALID, "negative decode sizes");
+    if (batch == 0 || features == 0) return KOEMI_OK;
+    const int64_t total = batch * features;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(total, 256));
+    cudaStream_t s = as_stream(stream);
+    switch (prior_dtype) {
+        case KOEMI_F32: decode_gates_kernel<float><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<float *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_BF16: decode_gates_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_F16: decode_gates_kernel<__half><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__half *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
+        default: return fail(KOEMI_ERR_INVALID, "prior dtype must be f32, f16 or bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_think_ring_decode_step(
+    const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride, const uint8_t *valid,
+    const float *surprise, float threshold, float *local_keys, float *local_values, uint8_t *local_valid,
+    const int64_t *local_head, float *salient_keys, float *salient_values, uint8_t *salient_valid,
+    int32_t *salient_head, int32_t *salient_count, float *local_out, float *salient_out, int64_t out_stride,
+    float *novelty_out, uint8_t *admission_out, int64_t batch, int64_t width, int64_t local_slots,
+    int64_t salient_slots, void *stream) {
+    clear_error();
+    if (batch < 0 || width < 0 || local_slots < 1 || salient_slots < 1) return fail(KOEMI_ERR_INVALID, "bad ring sizes");
+    if (batch == 0) return KOEMI_OK;
+    if (width % 4 != 0 || query_stride % 4 != 0 || entry_stride % 4 != 0 || out_stride % 4 != 0 ||
+        !aligned(queries, 16) || !aligned(entries, 16) || !aligned(local_keys, 16) || !aligned(salient_keys, 16) ||
+        !aligned(local_values, 16) || !aligned(salient_values, 16) || !aligned(local_out, 16) || !aligned(salient_out, 16)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "ring decode needs 16-byte aligned fp32 rows (width %% 4 == 0)");
+    }
+    if (batch > 2147483647) return fail(KOEMI_ERR_INVALID, "too many streams");
+    RingArgs args{queries, query_stride, entries, entry_stride, valid, surprise, threshold, local_keys, local_values,
+                  local_valid, local_head, salient_keys, salient_values, salient_valid, salient_head, salient_count,
+                  local_out, salient_out, out_stride, novelty_out, admission_out, batch, width, local_slots,
+                  salient_slots};
+    const int64_t slots = local_slots > salient_slots ? local_slots : salient_slots;
+    const size_t smem = (static_cast<size_t>(width) + 2 * slots + kRingWarps) * sizeof(float);
+    if (smem > 200 * 1024) return fail(KOEMI_ERR_UNSUPPORTED, "ring decode shared memory too large");
+    if (smem > 48 * 1024) {
+        KOEMI_CUDA_TRY(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    }
+    ring_decode_kernel<<<dim3(static_cast<unsigned>(batch), 2), kRingThreads, smem, as_stream(stream)>>>(args);
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_stride, const float *feature_logits,
+                                       const float *surprise, const uint8_t *valid, float *basis, float *normalizer,
+                                       float *read_out, int64_t read_stride, int64_t batch, int64_t width,
+                                       int64_t features, void *stream) {
+    clear_error();
+    if (batch < 0 || width < 0 || features < 1 || features > kAssocThreads) return fail(KOEMI_ERR_INVALID, "bad associative sizes");
+    if (batch == 0) return KOEMI_OK;
+    const size_t smem = 2 * static_cast<size_t>(features) * sizeof(float);
+    assoc_decode_kernel<<<static_cast<unsigned>(batch), kAssocThreads, smem, as_stream(stream)>>>(
+        projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, read_out, read_stride, batch,
+        width, features);
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}

@@ -10,7 +10,7 @@
 //
 // Two contractions per pair: hidden = silu(x Wg^T + bg) * (x Wv^T + bv),
 // then y = hidden Wo^T + bo. BF16/F16 run on tcgen05 tensor cores
-// (grouped_mlp_umma.cu); F32 (and any shape the tensor-core path rejects) runs
+// (umma.cu); F32 (and any shape the tensor-core path rejects) runs
 // the fp32 FMA tiles below. Reference: moe/moe_kernels.cu:147-199 (one CTA
 // per pair re-reading that expert's full weights).
 #include "common.cuh"
@@ -28,14 +28,24 @@ size_t grouped_mlp_umma_workspace(int64_t pairs, int64_t input_width, int64_t hi
 // Shared by both paths: tile_prefix[e] = row tiles of experts < e (E + 1 entries).
 __global__ void tile_prefix_kernel(const int64_t *__restrict__ offsets, int64_t experts, int64_t tile_rows,
                                    int32_t *__restrict__ prefix) {
-    if (blockIdx.x != 0 || threadIdx.x != 0) return;
-    int32_t total = 0;
-    for (int64_t e = 0; e < experts; ++e) {
-        prefix[e] = total;
-        const int64_t n = offsets[e + 1] - offsets[e];
-        total += static_cast<int32_t>((n + tile_rows - 1) / tile_rows);
+    // one warp: 32 experts per round, inclusive shuffle scan plus a carry
+    const int lane = threadIdx.x & 31;
+    if (blockIdx.x != 0 || threadIdx.x >= 32) return;
+    int32_t carry = 0;
+    for (int64_t base = 0; base < experts; base += 32) {
+        const int64_t e = base + lane;
+        int32_t tiles = 0;
+        if (e < experts) tiles = static_cast<int32_t>((offsets[e + 1] - offsets[e] + tile_rows - 1) / tile_rows);
+        int32_t inclusive = tiles;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t other = __shfl_up_sync(0xffffffffu, inclusive, o);
+            if (lane >= o) inclusive += other;
+        }
+        if (e < experts) prefix[e] = carry + inclusive - tiles;
+        carry += __shfl_sync(0xffffffffu, inclusive, 31);
     }
-    prefix[experts] = total;
+    if (lane == 0) prefix[experts] = carry;
 }
 
 __device__ __forceinline__ int64_t find_expert(const int32_t *prefix, int64_t experts, int64_t tile) {
@@ -147,7 +157,7 @@ int grouped_mlp_simt(const void *x, const int64_t *offsets, const void *gw, cons
                      int64_t h, int64_t experts, char *ws, cudaStream_t stream) {
     int32_t *prefix = reinterpret_cast<int32_t *>(ws);
     float *hidden = reinterpret_cast<float *>(ws + (((experts + 1) * sizeof(int32_t) + 255) & ~size_t(255)));
-    tile_prefix_kernel<<<1, 1, 0, stream>>>(offsets, experts, kBM, prefix);
+    tile_prefix_kernel<<<1, 32, 0, stream>>>(offsets, experts, kBM, prefix);
     KOEMI_LAUNCH_CHECK();
     const unsigned max_tiles = static_cast<unsigned>(ceil_div(pairs, kBM) + experts);
     grouped_gemm_simt_kernel<T, T, float, true><<<dim3(max_tiles, static_cast<unsigned>(ceil_div(h, kBN))), kThreads, 0, stream>>>(

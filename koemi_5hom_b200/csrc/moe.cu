@@ -378,6 +378,66 @@ __global__ void combine_residual_rmsnorm_kernel(const float *__restrict__ contex
     for (int64_t c = lane; c < width; c += 32) orow[c] = orow[c] * inv * norm_weight[c];
 }
 
+// Vectorised form of the above for widths that are a multiple of 4 and
+// 16-byte aligned rows, k <= 8: one warp per row, float4 context, the row's
+// k expert rows read once, the residual sum kept in `out` between passes.
+template <typename T>
+__global__ void combine_residual_rmsnorm_vec_kernel(const float *__restrict__ context, const T *__restrict__ y,
+                                                    const int64_t *__restrict__ positions,
+                                                    const int64_t *__restrict__ segment_offsets,
+                                                    const float *__restrict__ weights,
+                                                    const uint8_t *__restrict__ valid,
+                                                    const float *__restrict__ norm_weight, float *__restrict__ out,
+                                                    int64_t tokens, int64_t width, int64_t top_k, int64_t experts,
+                                                    float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= tokens) return;
+    const float4 *cr = reinterpret_cast<const float4 *>(context + row * width);
+    float4 *orow = reinterpret_cast<float4 *>(out + row * width);
+    const int64_t quads = width / 4;
+    if (valid != nullptr && valid[row] == 0) {
+        for (int64_t c = lane; c < quads; c += 32) orow[c] = cr[c];
+        return;
+    }
+    const int64_t valid_pairs = segment_offsets[experts];
+    const T *src[8];
+    float scale[8];
+    int live = 0;
+    for (int64_t s = 0; s < top_k; ++s) {
+        const int64_t pos = positions[row * top_k + s];
+        if (pos < 0 || pos >= valid_pairs) continue;
+        src[live] = y + pos * width;
+        scale[live] = weights != nullptr ? weights[row * top_k + s] : 1.0f / static_cast<float>(top_k);
+        ++live;
+    }
+    float sum = 0.0f;
+    for (int64_t c = lane; c < quads; c += 32) {
+        float4 u = cr[c];
+        for (int s = 0; s < live; ++s) {
+            const T *p = src[s] + c * 4;
+            u.x += to_acc(p[0]) * scale[s];
+            u.y += to_acc(p[1]) * scale[s];
+            u.z += to_acc(p[2]) * scale[s];
+            u.w += to_acc(p[3]) * scale[s];
+        }
+        orow[c] = u;
+        sum += u.x * u.x + u.y * u.y + u.z * u.z + u.w * u.w;
+    }
+    sum = warp_sum(sum);
+    const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+    const float4 *wq = reinterpret_cast<const float4 *>(norm_weight);
+    for (int64_t c = lane; c < quads; c += 32) {
+        float4 u = orow[c];
+        const float4 w = wq[c];
+        u.x *= inv * w.x;
+        u.y *= inv * w.y;
+        u.z *= inv * w.z;
+        u.w *= inv * w.w;
+        orow[c] = u;
+    }
+}
+
 // Workspace layout of the permutation.
 struct PermuteLayout {
     int64_t blocks;
@@ -579,6 +639,18 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     if (tokens == 0 || width == 0) return KOEMI_OK;
     const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
     cudaStream_t s = as_stream(stream);
+    const bool vector = width % 4 == 0 && top_k <= 8 && aligned(context, 16) && aligned(out, 16) &&
+                        aligned(norm_weight, 16) && aligned(expert_out, 8);
+    if (vector) {
+        switch (dtype) {
+            case KOEMI_F32: combine_residual_rmsnorm_vec_kernel<float><<<blocks, 256, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            case KOEMI_F16: combine_residual_rmsnorm_vec_kernel<__half><<<blocks, 256, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            case KOEMI_BF16: combine_residual_rmsnorm_vec_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
+        }
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    }
     switch (dtype) {
         case KOEMI_F32: combine_residual_rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
         case KOEMI_F16: combine_residual_rmsnorm_kernel<__half><<<blocks, 256, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;

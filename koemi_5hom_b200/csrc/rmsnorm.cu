@@ -173,6 +173,8 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
                 rms_rows_cached<T, kMode, 4><<<blocks, kThreads, 0, stream>>>(args);
             } else if (per_lane <= 8) {
                 rms_rows_cached<T, kMode, 8><<<blocks, kThreads, 0, stream>>>(args);
+            } else if (per_lane <= 16 && sizeof(T) == 4 && kMode == kPlain) {
+                rms_rows_cached<T, kMode, 16><<<blocks, kThreads, 0, stream>>>(args);
             } else {
                 vector_ok = false;
             }

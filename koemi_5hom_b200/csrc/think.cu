@@ -9,7 +9,7 @@
 // fp32 with at::mm, think/surprise_kernel.cu:195-215, then reduces each row,
 // :85-134). A finishing kernel merges the per-slice partials of every row in
 // slice order and writes s = 1 - exp(-NLL / ln C), 0 on invalid rows.
-// 16-bit inputs take the tcgen05 path in surprise_umma.cu when available.
+// 16-bit inputs take the tcgen05 path of umma.cu when the shape allows it.
 #include <cmath>
 
 #include "common.cuh"
@@ -111,26 +111,44 @@ __global__ __launch_bounds__(kThreads) void surprise_partial_kernel(
     }
 }
 
+// One warp per row: lanes stride over the vocabulary-slice partials, then
+// the (max, sum) pairs and the target logit are combined across the warp.
 template <typename TO>
 __global__ void surprise_finish_kernel(const float *__restrict__ partials, int64_t slices,
                                        const int64_t *__restrict__ targets, const uint8_t *__restrict__ valid,
                                        TO *__restrict__ out, float *__restrict__ nll_out, int64_t rows,
                                        float log_vocab) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= rows) return;
-    float m = -INFINITY;
-    for (int64_t s = 0; s < slices; ++s) m = fmaxf(m, partials[(s * rows + row) * 3]);
-    float total = 0.0f, target = -INFINITY;
-    for (int64_t s = 0; s < slices; ++s) {
+    float m = -INFINITY, total = 0.0f, target = -INFINITY;
+    for (int64_t s = lane; s < slices; s += 32) {
         const float *p = partials + (s * rows + row) * 3;
-        if (p[0] != -INFINITY) total += p[1] * expf(p[0] - m);
+        const float pm = p[0];
+        if (pm != -INFINITY) {
+            const float nm = fmaxf(m, pm);
+            total = total * expf(m - nm) + p[1] * expf(pm - nm);
+            m = nm;
+        }
         target = fmaxf(target, p[2]);
     }
-    const bool ok = valid == nullptr || valid[row] != 0;
-    const float nll = logf(total) + m - target;
-    const float surprise = ok ? 1.0f - expf(-nll / log_vocab) : 0.0f;
-    out[row] = from_acc<TO>(surprise);
-    if (nll_out != nullptr) nll_out[row] = ok ? nll : 0.0f;
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, offset);
+        const float ot = __shfl_xor_sync(0xffffffffu, total, offset);
+        target = fmaxf(target, __shfl_xor_sync(0xffffffffu, target, offset));
+        const float nm = fmaxf(m, om);
+        if (nm != -INFINITY) {
+            total = (m == -INFINITY ? 0.0f : total * expf(m - nm)) + (om == -INFINITY ? 0.0f : ot * expf(om - nm));
+        }
+        m = nm;
+    }
+    if (lane == 0) {
+        const bool ok = valid == nullptr || valid[row] != 0;
+        const float nll = logf(total) + m - target;
+        out[row] = from_acc<TO>(ok ? 1.0f - expf(-nll / log_vocab) : 0.0f);
+        if (nll_out != nullptr) nll_out[row] = ok ? nll : 0.0f;
+    }
 }
 
 int64_t simt_slices(int64_t rows, int64_t vocab) {
@@ -241,7 +259,7 @@ int surprise_finish(const float *partials, int64_t slices, const int64_t *target
                     void *out, float *nll_out, int64_t rows, int64_t content_vocab, int out_dtype,
                     cudaStream_t stream) {
     const float log_vocab = std::log(static_cast<float>(content_vocab));
-    const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 256));
+    const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
     switch (out_dtype) {
         case KOEMI_F32: surprise_finish_kernel<float><<<blocks, 256, 0, stream>>>(partials, slices, targets, valid, static_cast<float *>(out), nll_out, rows, log_vocab); break;
         case KOEMI_F16: surprise_finish_kernel<__half><<<blocks, 256, 0, stream>>>(partials, slices, targets, valid, static_cast<__half *>(out), nll_out, rows, log_vocab); break;

@@ -482,7 +482,7 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     char *ws = static_cast<char *>(workspace);
     int32_t *prefix = reinterpret_cast<int32_t *>(ws);
     void *hidden = ws + align256((expert_count + 1) * sizeof(int32_t));
-    tile_prefix_kernel<<<1, 1, 0, stream>>>(segment_offsets, expert_count, kBM, prefix);
+    tile_prefix_kernel<<<1, 32, 0, stream>>>(segment_offsets, expert_count, kBM, prefix);
     KOEMI_LAUNCH_CHECK();
     const int64_t max_m_tiles = (pairs + kBM - 1) / kBM + expert_count;
 

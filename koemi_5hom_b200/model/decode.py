@@ -1,0 +1,202 @@
+"""Decode-step path of the HERM stack: one token per stream, state in place.
+
+``KoemiModel.forward`` follows the reference's window semantics and rebuilds
+the rings every call (cat + slice). For decode, ``DecodeState`` keeps every
+tensor of the state at a fixed address and updates it in place:
+
+- local rings are circular, with one device-side head (the oldest slot) shared
+  by all streams and blocks, since every stream writes one entry per step;
+- salient rings are circular per stream (head + count of admitted entries);
+- working state, associative bases and normalisers are overwritten in place.
+
+A step is then: per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
+-> surprise (tcgen05 head GEMM + online LSE) -> local/assoc/feature GEMMs ->
+``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` -> fusion GEMM
+(its input rows are written in place by the three kernels) -> rms_norm ->
+route / permute / grouped expert MLP / combine; then the head GEMM. With fixed
+addresses the whole step is one CUDA graph with no copy-back of the state.
+
+``to_koemi_state`` restores the reference layout (rings oldest first, salient
+entries packed at the end) whenever a caller asks for the state.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from koemi_5hom_b200 import _native
+from koemi_5hom_b200.cuda_kernels import _ops
+from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
+from koemi_5hom_b200.model.state import KoemiState, LayeredKoemiState
+
+MIN_RETENTION, MAX_RETENTION = 2.0 ** -8, 1.0 - 2.0 ** -8
+NORM_EPSILON = 1e-6
+
+
+@dataclass
+class DecodeBlockState:
+    working: Tensor
+    memory_basis: Tensor
+    memory_normalizer: Tensor
+    refine_basis: Tensor
+    refine_normalizer: Tensor
+    local_keys: Tensor
+    local_values: Tensor
+    local_valid: Tensor
+    salient_keys: Tensor
+    salient_values: Tensor
+    salient_valid: Tensor
+    salient_head: Tensor   # int32 [B]
+    salient_count: Tensor  # int32 [B]
+
+
+@dataclass
+class DecodeState:
+    blocks: list[DecodeBlockState]
+    local_head: Tensor      # int64 [1], slot of the oldest local entry (all streams, all blocks)
+    last_token_ids: Tensor  # int64 [B]
+    step_index: int
+    layered: bool
+
+
+def supports_decode_path(settings) -> bool:
+    """The in-place path covers the reference defaults and the config-5 stack;
+    the refine ablation ('herm') keeps the window path."""
+    return settings.ablation in ("no_refine", "no_surprise") and settings.embedding_size % 4 == 0
+
+
+def from_koemi_state(state, local_slots: int, salient_slots: int) -> DecodeState:
+    """Import a static (ring-at-capacity) state: local rings keep their
+    oldest-first order (head 0); each salient ring is packed to its admitted
+    entries, oldest first, at slots [0, count)."""
+    layers = state.layers if isinstance(state, LayeredKoemiState) else (state,)
+    blocks = []
+    for layer in layers:
+        if layer.local_keys.shape[1] != local_slots or layer.salient_keys.shape[1] != salient_slots:
+            raise ValueError("decode state needs rings at capacity; call to_static_state first")
+        order = torch.argsort((~layer.salient_valid).to(torch.int8), dim=1, stable=True)
+        gather = order.unsqueeze(-1).expand_as(layer.salient_keys)
+        count = layer.salient_valid.sum(dim=1).to(torch.int32)
+        blocks.append(DecodeBlockState(
+            working=layer.working_state.float().contiguous().clone(),
+            memory_basis=layer.memory_basis.float().contiguous().clone(),
+            memory_normalizer=layer.memory_normalizer.float().contiguous().clone(),
+            refine_basis=layer.refine_basis.float().contiguous().clone(),
+            refine_normalizer=layer.refine_normalizer.float().contiguous().clone(),
+            local_keys=layer.local_keys.float().contiguous().clone(),
+            local_values=layer.local_values.float().contiguous().clone(),
+            local_valid=layer.local_valid.contiguous().clone(),
+            salient_keys=layer.salient_keys.float().gather(1, gather).contiguous(),
+            salient_values=layer.salient_values.float().gather(1, gather).contiguous(),
+            salient_valid=layer.salient_valid.gather(1, order).contiguous(),
+            salient_head=torch.zeros_like(count),
+            salient_count=count,
+        ))
+    device = layers[0].working_state.device
+    return DecodeState(blocks=blocks, local_head=torch.zeros(1, dtype=torch.int64, device=device),
+                       last_token_ids=layers[-1].last_token_ids.clone(), step_index=state.step_index,
+                       layered=isinstance(state, LayeredKoemiState))
+
+
+def to_koemi_state(dstate: DecodeState):
+    """Export in the reference layout: local rings oldest first; salient rings
+    with admitted entries oldest first, packed at the end behind empty slots."""
+    layers = []
+    for block in dstate.blocks:
+        batch, local_slots, width = block.local_keys.shape
+        salient_slots = block.salient_keys.shape[1]
+        device = block.local_keys.device
+        local_index = (dstate.local_head + torch.arange(local_slots, device=device)) % local_slots
+        logical = torch.arange(salient_slots, device=device).unsqueeze(0)
+        lead = salient_slots - block.salient_count.long().unsqueeze(1)
+        physical = (block.salient_head.long().unsqueeze(1) + logical - lead) % salient_slots
+        present = logical >= lead
+        gather = physical.unsqueeze(-1).expand(batch, salient_slots, width)
+        keep = present.unsqueeze(-1)
+        layers.append(KoemiState(
+            working_state=block.working.clone(),
+            memory_basis=block.memory_basis.clone(),
+            memory_normalizer=block.memory_normalizer.clone(),
+            refine_basis=block.refine_basis.clone(),
+            refine_normalizer=block.refine_normalizer.clone(),
+            local_keys=block.local_keys.index_select(1, local_index),
+            local_values=block.local_values.index_select(1, local_index),
+            local_valid=block.local_valid.index_select(1, local_index),
+            salient_keys=torch.where(keep, block.salient_keys.gather(1, gather), 0.0),
+            salient_values=torch.where(keep, block.salient_values.gather(1, gather), 0.0),
+            salient_valid=present & block.salient_valid.gather(1, physical),
+            last_token_ids=dstate.last_token_ids.clone(),
+            step_index=dstate.step_index,
+        ))
+    if dstate.layered:
+        return LayeredKoemiState(tuple(layers), dstate.step_index)
+    return layers[0]
+
+
+def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
+    """Advance every stream by one token in place; return fp32 logits [B, V]."""
+    s = model.settings
+    cache = model._cache
+    batch = token_ids.shape[0]
+    d = s.embedding_size
+    device = token_ids.device
+    ids = token_ids.reshape(batch).contiguous()
+    valid = ids != PAD_TOKEN_ID
+    stream = torch.cuda.current_stream(device).cuda_stream
+    call = _native.call
+    ptr = _native.ptr
+    prior_dtype = _native.dtype_code(model.compute_dtype)
+    x = model.embedding_weight.index_select(0, ids).float()
+    for index, block in enumerate(model.blocks):
+        bc = cache["blocks"][index]
+        st = dstate.blocks[index]
+        u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, torch.float32)
+        pre = model._linear(u, block.gates_weight, bc["gates_bias"])
+        concat = torch.empty(batch, 4 * d, dtype=torch.float32, device=device)  # h | memory | local | salient
+        prior = torch.empty(batch, d, dtype=model.compute_dtype, device=device)
+        call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), ptr(prior), ptr(concat), 4 * d,
+             batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
+        h = concat[:, :d]
+        if s.ablation == "no_surprise":
+            surprise = None
+        else:
+            targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
+            surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
+                                                    torch.float32)
+        local = model._linear(h, block.local_weight, bc["local_bias"])
+        assoc = model._linear(h, block.assoc_weight, bc["assoc_bias"])
+        features = model._linear(torch.stack((assoc[:, :d], assoc[:, d:2 * d])), block.feature_weight,
+                                 bc["feature_bias"])
+        scored = surprise if surprise is not None else torch.zeros(batch, device=device)
+        call("koemi_think_ring_decode_step", ptr(concat), 4 * d, ptr(local), 2 * d, ptr(valid), ptr(scored),
+             float(s.salience_threshold), ptr(st.local_keys), ptr(st.local_values), ptr(st.local_valid),
+             ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
+             ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,
+             None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], stream)
+        call("koemi_assoc_decode_step", ptr(assoc), assoc.shape[1], ptr(features), ptr(surprise), ptr(valid),
+             ptr(st.memory_basis), ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d,
+             s.memory_features, stream)
+        fused = model._linear(concat, block.fusion_weight, bc["fusion_bias"])
+        context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
+        if s.expert_count == 0:
+            x = context
+            continue
+        if s.expert_routing == "learned":
+            gate_logits = model._linear(torch.where(valid.unsqueeze(-1), context, 0.0), block.router_weight, None)
+            assignments, weights, _ = _ops.learned_topk(gate_logits, valid, s.expert_top_k, bool(s.router_renormalize))
+        else:
+            assignments = _ops.route_topk(ids, dstate.last_token_ids, valid, s.expert_count, s.expert_top_k)
+            weights = None
+        sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
+            context.to(model.compute_dtype), assignments, valid, s.expert_count, True)
+        expert_out = _ops.grouped_expert_mlp(sorted_context, sorted_experts, offsets, block.expert_gate_weight,
+                                             block.expert_gate_bias, block.expert_value_weight, block.expert_value_bias,
+                                             block.expert_output_weight, block.expert_output_bias)
+        x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid, bc["expert_norm"],
+                                          s.expert_top_k, NORM_EPSILON)
+    logits = model._linear(x, model.head_weight, cache["head_b"])
+    dstate.last_token_ids.copy_(torch.where(valid, ids, dstate.last_token_ids))
+    dstate.local_head.add_(1).remainder_(dstate.blocks[0].local_keys.shape[1])
+    return logits

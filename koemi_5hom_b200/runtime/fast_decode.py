@@ -20,6 +20,7 @@ from dataclasses import dataclass, replace
 import torch
 from torch import Tensor
 
+from koemi_5hom_b200.model.decode import decode_step, from_koemi_state, supports_decode_path, to_koemi_state
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
 from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
 
@@ -108,17 +109,27 @@ def _rows(state) -> int:
 
 
 class BatchDecoder:
-    """Fixed-shape recurrent decoding for a batch of sequences."""
+    """Fixed-shape recurrent decoding for a batch of sequences.
 
-    def __init__(self, model, *, capture_graph: bool = False, cache_expert_weights: bool = True):
+    When the model's configuration allows it (``supports_decode_path``) the
+    state lives in a ``DecodeState`` and each step updates it in place with the
+    fused decode kernels; otherwise each step runs the window path and the new
+    state replaces the old. ``capture_graph`` records one step into a CUDA graph
+    (after warm-up on a side stream) and replays it.
+    """
+
+    def __init__(self, model, *, capture_graph: bool = False, cache_expert_weights: bool = True,
+                 in_place: bool = True):
         device = model.device
         if capture_graph and device.type != "cuda":
             raise RuntimeError("CUDA graph capture requires a model on a CUDA device")
         self.model = model
         self.device = device
         self._capture_graph = capture_graph
+        self._in_place = in_place and device.type == "cuda" and supports_decode_path(model.settings)
         self._graph: torch.cuda.CUDAGraph | None = None
-        self._state = None
+        self._state = None       # window path: KoemiState / LayeredKoemiState
+        self._dstate = None      # in-place path: DecodeState
         self._static_ids: Tensor | None = None
         self._static_logits: Tensor | None = None
         self._step_index = 0
@@ -127,16 +138,26 @@ class BatchDecoder:
 
     @property
     def state(self):
-        if self._state is None:
+        if self._state is None and self._dstate is None:
             raise RuntimeError("prefill must run before the state is available")
-        if isinstance(self._state, LayeredKoemiState):
-            return self._state.with_step(self._step_index)
-        return replace(self._state, step_index=self._step_index)
+        state = to_koemi_state(self._dstate) if self._dstate is not None else self._state
+        if isinstance(state, LayeredKoemiState):
+            return state.with_step(self._step_index)
+        return replace(state, step_index=self._step_index)
 
     def adopt(self, state, step_index: int | None = None) -> None:
-        s = self.model.settings
-        self._state = to_static_state(state, s.local_memory_size, s.salience_memory_size)
+        self._set_state(state)
         self._step_index = state.step_index if step_index is None else step_index
+
+    def _set_state(self, state) -> None:
+        s = self.model.settings
+        static = to_static_state(state, s.local_memory_size, s.salience_memory_size)
+        if self._in_place:
+            self._dstate = from_koemi_state(static, s.local_memory_size, s.salience_memory_size)
+            self._state = None
+        else:
+            self._state = static
+            self._dstate = None
         self._reset_graph()
 
     def prefill(self, input_ids: Tensor) -> Tensor:
@@ -144,59 +165,72 @@ class BatchDecoder:
         self._validate_prompt(input_ids)
         trusted = not bool((input_ids == PAD_TOKEN_ID).any().item())
         output = self.model(input_ids, trusted_inputs=trusted, last_logits_only=True)
-        s = self.model.settings
-        self._state = to_static_state(output.state, s.local_memory_size, s.salience_memory_size)
+        self._set_state(output.state)
         self._step_index = input_ids.shape[1]
-        self._reset_graph()
         return output.logits[:, -1]
 
     def step(self, token_ids: Tensor) -> Tensor:
-        if self._state is None:
+        if self._state is None and self._dstate is None:
             raise RuntimeError("prefill must run before step")
         ids = self._normalize_step_input(token_ids)
         if self._capture_graph:
             return self._graph_step(ids)
+        logits = self._eager_step(ids)
+        self._step_index += 1
+        return logits
+
+    def _eager_step(self, ids: Tensor) -> Tensor:
+        if self._dstate is not None:
+            return decode_step(self.model, ids, self._dstate)
         output = self.model(ids, self._state, trusted_inputs=True)
         self._state = output.state
-        self._step_index += 1
         return output.logits[:, -1]
 
     def extend(self, token_ids: Tensor) -> Tensor:
-        if self._state is None:
+        if self._state is None and self._dstate is None:
             raise RuntimeError("prefill must run before extend")
         if not isinstance(token_ids, Tensor) or token_ids.ndim != 2 or token_ids.shape[1] == 0:
             raise ValueError("extend requires token ids with shape [batch, length]")
-        output = self.model(token_ids, self._state, trusted_inputs=True)
-        s = self.model.settings
-        self._state = to_static_state(output.state, s.local_memory_size, s.salience_memory_size)
+        output = self.model(token_ids, self.state, trusted_inputs=True)
+        self._set_state(output.state)
         self._step_index += token_ids.shape[1]
-        self._reset_graph()
         return output.logits
 
     def _graph_step(self, ids: Tensor) -> Tensor:
         if self._graph is None:
             self._static_ids = ids.clone()
-            self._state = clone_state(self._state)
-            probe = self.model(self._static_ids, self._state, trusted_inputs=True)
-            self._static_logits = probe.logits.clone()
+            if self._dstate is None:
+                self._state = clone_state(self._state)
             self._capture()
         self._static_ids.copy_(ids)
         self._graph.replay()
         self._step_index += 1
-        return self._static_logits[:, -1]
+        return self._static_logits
 
     def _capture(self) -> None:
+        """Warm up on a side stream, then record one step. The in-place path
+        advances its state during warm-up, so it warms up on a copy."""
         stream = torch.cuda.Stream(device=self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
-            for _ in range(GRAPH_WARMUP_STEPS):
-                self.model(self._static_ids, self._state, trusted_inputs=True)
+            if self._dstate is not None:
+                scratch = from_koemi_state(to_koemi_state(self._dstate), self.model.settings.local_memory_size,
+                                           self.model.settings.salience_memory_size)
+                for _ in range(GRAPH_WARMUP_STEPS):
+                    decode_step(self.model, self._static_ids, scratch)
+                del scratch
+            else:
+                for _ in range(GRAPH_WARMUP_STEPS):
+                    self.model(self._static_ids, self._state, trusted_inputs=True)
         torch.cuda.current_stream(self.device).wait_stream(stream)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            output = self.model(self._static_ids, self._state, trusted_inputs=True)
-            self._static_logits.copy_(output.logits)
-            _copy_state(self._state, output.state)
+            if self._dstate is not None:
+                self._static_logits = decode_step(self.model, self._static_ids, self._dstate)
+            else:
+                output = self.model(self._static_ids, self._state, trusted_inputs=True)
+                self._static_logits = output.logits[:, -1]
+                _copy_state(self._state, output.state)
         self._graph = graph
 
     def _reset_graph(self) -> None:
@@ -211,7 +245,8 @@ class BatchDecoder:
             token_ids = token_ids.unsqueeze(-1)
         if token_ids.ndim != 2 or token_ids.shape[1] != 1:
             raise ValueError("step requires exactly one token id per row")
-        if token_ids.shape[0] != _rows(self._state):
+        rows = self._dstate.last_token_ids.shape[0] if self._dstate is not None else _rows(self._state)
+        if token_ids.shape[0] != rows:
             raise ValueError("step token ids must carry one row per decoded sequence")
         if token_ids.dtype != torch.long:
             raise TypeError("step token ids must use torch.long")

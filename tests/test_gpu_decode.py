@@ -1,0 +1,204 @@
+"""The in-place decode path (circular rings, fused step kernels) against the
+oracle and against the window path of the same model."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from conftest import load_golden
+from herm_weights import HermShape, herm_parameters
+from koemi_5hom_b200 import _native
+from koemi_5hom_b200.model import KoemiModel, ModelSettings
+from koemi_5hom_b200.model.decode import from_koemi_state, to_koemi_state
+from koemi_5hom_b200.runtime import BatchDecoder, SamplingPolicy, TokenSampler
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _ring_case(batch, width, local_slots, salient_slots, seed, fill=0.6):
+    g = torch.Generator().manual_seed(seed)
+    t = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    lk, lv = t(batch, local_slots, width), t(batch, local_slots, width)
+    lvalid = torch.rand(batch, local_slots, generator=g) > 0.2
+    counts = [int(c) for c in torch.randint(0, salient_slots + 1, (batch,), generator=g)]
+    counts[0] = salient_slots  # one full ring, one empty ring
+    counts[-1] = 0
+    heads = [int(h) for h in torch.randint(0, salient_slots, (batch,), generator=g)]
+    sk, sv = t(batch, salient_slots, width), t(batch, salient_slots, width)
+    svalid = torch.zeros(batch, salient_slots, dtype=torch.bool)
+    for b in range(batch):
+        for i in range(counts[b]):
+            svalid[b, (heads[b] + i) % salient_slots] = True
+    query = t(batch, width)
+    entries = t(batch, 2 * width)
+    valid = torch.rand(batch, generator=g) > 0.15
+    surprise = torch.rand(batch, generator=g)
+    return dict(lk=lk, lv=lv, lvalid=lvalid, sk=sk, sv=sv, svalid=svalid, heads=heads, counts=counts, q=query,
+                entries=entries, valid=valid, surprise=surprise)
+
+
+def _logical_salient(sk, sv, head, count, slots):
+    idx = [(head + i) % slots for i in range(count)]
+    return sk[idx], sv[idx]
+
+
+@pytest.mark.parametrize("batch,width,local_slots,salient_slots", [(7, 64, 16, 12), (256, 2048, 128, 128),
+                                                                   (3, 128, 5, 9)])
+def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slots, cuda):
+    c = _ring_case(batch, width, local_slots, salient_slots, seed=width)
+    head = 3 % local_slots
+    threshold = 0.5
+    dev = lambda x: x.to(cuda).contiguous()  # noqa: E731
+    lk, lv, lvalid = dev(c["lk"]), dev(c["lv"]), dev(c["lvalid"])
+    sk, sv, svalid = dev(c["sk"]), dev(c["sv"]), dev(c["svalid"])
+    s_head = torch.tensor(c["heads"], dtype=torch.int32, device=cuda)
+    s_count = torch.tensor(c["counts"], dtype=torch.int32, device=cuda)
+    local_head = torch.tensor([head], dtype=torch.int64, device=cuda)
+    out = torch.zeros(batch, 4 * width, device=cuda)
+    novelty = torch.empty(batch, device=cuda)
+    admission = torch.empty(batch, dtype=torch.bool, device=cuda)
+    q_rows = torch.zeros(batch, 4 * width)
+    q_rows[:, :width] = c["q"]
+    q_rows = dev(q_rows)
+    entries, valid, surprise = dev(c["entries"]), dev(c["valid"]), dev(c["surprise"])
+    p = _native.ptr
+    _native.call("koemi_think_ring_decode_step", p(q_rows), 4 * width, p(entries), 2 * width, p(valid), p(surprise),
+                 threshold, p(lk), p(lv), p(lvalid), p(local_head), p(sk), p(sv), p(svalid), p(s_head), p(s_count),
+                 p(out[:, 2 * width:]), p(out[:, 3 * width:]), 4 * width, p(novelty), p(admission), batch, width,
+                 local_slots, salient_slots, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    scale = 1.0 / math.sqrt(width)
+    for b in range(batch):
+        q = c["q"][b].double()
+        # local read over every valid slot (all slots are inside the window at T=1)
+        slots = [s for s in range(local_slots) if c["lvalid"][b, s]]
+        if slots:
+            k = c["lk"][b, slots].double()
+            w = torch.softmax(k @ q * scale, dim=0)
+            expected = w @ c["lv"][b, slots].double()
+            cos = (k / k.norm(dim=-1, keepdim=True).clamp_min(1e-12)) @ (q / q.norm().clamp_min(1e-12))
+            expected_novelty = float((1 - cos.max()).clamp(0, 1))
+        else:
+            expected, expected_novelty = torch.zeros(width, dtype=torch.float64), 1.0
+        torch.testing.assert_close(out[b, 2 * width:3 * width].cpu().double(), expected, rtol=1e-4, atol=1e-5)
+        assert abs(novelty[b].item() - expected_novelty) < 1e-4
+        # salient read over the admitted entries carried in
+        ks, vs = _logical_salient(c["sk"][b], c["sv"][b], c["heads"][b], c["counts"][b], salient_slots)
+        if ks.shape[0]:
+            w = torch.softmax(ks.double() @ q * scale, dim=0)
+            expected = w @ vs.double()
+        else:
+            expected = torch.zeros(width, dtype=torch.float64)
+        torch.testing.assert_close(out[b, 3 * width:].cpu().double(), expected, rtol=1e-4, atol=1e-5)
+        # writes: the oldest local slot takes the (masked) new entry
+        entry_k = c["entries"][b, :width] if c["valid"][b] else torch.zeros(width)
+        entry_v = c["entries"][b, width:] if c["valid"][b] else torch.zeros(width)
+        assert torch.equal(lk[b, head].cpu(), entry_k) and torch.equal(lv[b, head].cpu(), entry_v)
+        assert bool(lvalid[b, head]) == bool(c["valid"][b])
+        # salient: the admitted sequence is the latest `salient_slots` of old + new
+        admitted = bool(c["valid"][b]) and float(c["surprise"][b]) > threshold
+        assert bool(admission[b]) == admitted
+        old_k, old_v = _logical_salient(c["sk"][b], c["sv"][b], c["heads"][b], c["counts"][b], salient_slots)
+        if admitted:
+            old_k = torch.cat((old_k, entry_k.unsqueeze(0)))[-salient_slots:]
+            old_v = torch.cat((old_v, entry_v.unsqueeze(0)))[-salient_slots:]
+        new_k, new_v = _logical_salient(sk[b].cpu(), sv[b].cpu(), int(s_head[b]), int(s_count[b]), salient_slots)
+        assert torch.equal(new_k, old_k) and torch.equal(new_v, old_v)
+
+
+def test_assoc_decode_step_matches_oracle(cuda):
+    g = torch.Generator().manual_seed(3)
+    batch, d, m = 9, 256, 16
+    proj = torch.randn(batch, 3 * d + 2, generator=g)
+    feats = torch.randn(2, batch, m, generator=g)
+    surprise = torch.rand(batch, generator=g)
+    valid = torch.rand(batch, generator=g) > 0.2
+    basis = torch.randn(batch, d, m, generator=g) * 0.1
+    normalizer = torch.rand(batch, m, generator=g)
+    b_dev, n_dev = basis.to(cuda), normalizer.to(cuda)
+    out = torch.zeros(batch, 4 * d, device=cuda)
+    p = _native.ptr
+    _native.call("koemi_assoc_decode_step", p(proj.to(cuda)), 3 * d + 2, p(feats.to(cuda)), p(surprise.to(cuda)),
+                 p(valid.to(cuda)), p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m,
+                 torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    f, qf = torch.softmax(feats[0].double(), -1), torch.softmax(feats[1].double(), -1)
+    decay = 2.0 ** -12 + (1 - 2.0 ** -11) * torch.sigmoid(proj[:, 3 * d].double())
+    write = torch.sigmoid(proj[:, 3 * d + 1].double()) * (0.25 + 0.75 * surprise.double().clamp(0, 1))
+    decay = torch.where(valid, decay, 1.0)
+    write = torch.where(valid, write, 0.0)
+    value = torch.tanh(proj[:, 2 * d:3 * d].double())
+    read, new_basis, new_norm = _oracle_scan_read(basis.double(), normalizer.double(), decay, value, f, write, qf)
+    torch.testing.assert_close(out[:, d:2 * d].cpu().double(), read, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(b_dev.cpu().double(), new_basis, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(n_dev.cpu().double(), new_norm, rtol=1e-5, atol=1e-6)
+
+
+def _oracle_scan_read(basis, normalizer, decay, value, features, write, qf):
+    from oracle.herm import HermOracle
+    reads, b, n = HermOracle._scan_read(None, basis, normalizer, decay.unsqueeze(1), value.unsqueeze(1),
+                                        features.unsqueeze(1), write.unsqueeze(1), qf.unsqueeze(1))
+    return reads[:, 0], b, n
+
+
+def _build(name, compute_dtype):
+    fx = load_golden(name)
+    case = fx["case"]
+    settings = ModelSettings(**case["settings"], compute_dtype=compute_dtype)
+    params = herm_parameters(HermShape(settings.vocabulary_size, settings.embedding_size, settings.memory_features,
+                                       settings.expert_count, settings.expert_routing, settings.ablation),
+                             case["seed"], case["init"], dtype=torch.bfloat16 if case.get("bf16") else torch.float32)
+    model = KoemiModel(settings, device="cuda")
+    model.load_reference_parameters({k: v.cuda() for k, v in params.items()})
+    return fx, model
+
+
+@pytest.mark.parametrize("name,dtype,steps", [("c1_t065", "float32", 64), ("c5_small", "bfloat16", 40)])
+@pytest.mark.parametrize("capture_graph", [False, True])
+def test_in_place_decoder_matches_window_decoder(name, dtype, steps, capture_graph):
+    fx, model = _build(name, dtype)
+    ids = fx["ids"].cuda()
+    sampler = TokenSampler(SamplingPolicy(greedy=True), model.device)
+    runs = []
+    for in_place in (False, True):
+        decoder = BatchDecoder(model, capture_graph=capture_graph and in_place, in_place=in_place)
+        assert (decoder._dstate is None) or in_place
+        logits = decoder.prefill(ids)
+        tokens, all_logits = [], []
+        for _ in range(steps):
+            token = sampler(logits)
+            tokens.append(token)
+            all_logits.append(logits.clone())
+            logits = decoder.step(token)
+        runs.append((torch.cat(tokens, 1), torch.stack(all_logits, 1), decoder.state))
+    (t0, l0, s0), (t1, l1, s1) = runs
+    assert torch.equal(t0, t1)
+    tol = 1e-4 if dtype == "float32" else 2e-2
+    torch.testing.assert_close(l1, l0, rtol=tol, atol=tol)
+    assert torch.equal(t1.cpu(), fx["decode_tokens"][:, :steps])
+    for field in ("working_state", "memory_basis", "memory_normalizer", "local_keys", "local_values"):
+        torch.testing.assert_close(getattr(s1, field), getattr(s0, field), rtol=1e-3, atol=1e-4)
+    assert torch.equal(s1.local_valid, s0.local_valid)
+    assert torch.equal(s1.last_token_ids, s0.last_token_ids)
+    mine = ops.admitted_sequence(s1.salient_keys.cpu(), s1.salient_values.cpu(), s1.salient_valid.cpu())
+    theirs = ops.admitted_sequence(s0.salient_keys.cpu(), s0.salient_values.cpu(), s0.salient_valid.cpu())
+    for (mk, mv), (rk, rv) in zip(mine, theirs):
+        assert mk.shape == rk.shape
+        torch.testing.assert_close(mk, rk, rtol=1e-3, atol=1e-4)
+
+
+def test_state_round_trip_through_decode_state(cuda):
+    fx, model = _build("c1_t065", "float32")
+    out = model(fx["ids"].cuda())
+    from koemi_5hom_b200.runtime import to_static_state
+    static = to_static_state(out.state, 32, 32)
+    back = to_koemi_state(from_koemi_state(static, 32, 32))
+    for field in ("working_state", "local_keys", "local_values", "local_valid", "last_token_ids"):
+        assert torch.equal(getattr(back, field), getattr(static, field)), field
+    for (mk, mv), (rk, rv) in zip(ops.admitted_sequence(back.salient_keys, back.salient_values, back.salient_valid),
+                                  ops.admitted_sequence(static.salient_keys, static.salient_values,
+                                                        static.salient_valid)):
+        assert torch.equal(mk, rk) and torch.equal(mv, rv)
