@@ -120,10 +120,12 @@ def test_assoc_decode_step_matches_oracle(cuda):
     normalizer = torch.rand(batch, m, generator=g)
     b_dev, n_dev = basis.to(cuda), normalizer.to(cuda)
     out = torch.zeros(batch, 4 * d, device=cuda)
+    # keep every device input alive until the kernel has run: a temporary's
+    # memory can be handed to the next argument's copy as soon as it is freed
+    proj_dev, feats_dev, surprise_dev, valid_dev = proj.to(cuda), feats.to(cuda), surprise.to(cuda), valid.to(cuda)
     p = _native.ptr
-    _native.call("koemi_assoc_decode_step", p(proj.to(cuda)), 3 * d + 2, p(feats.to(cuda)), p(surprise.to(cuda)),
-                 p(valid.to(cuda)), p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m,
-                 torch.cuda.current_stream().cuda_stream)
+    _native.call("koemi_assoc_decode_step", p(proj_dev), 3 * d + 2, p(feats_dev), p(surprise_dev), p(valid_dev),
+                 p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     f, qf = torch.softmax(feats[0].double(), -1), torch.softmax(feats[1].double(), -1)
     decay = 2.0 ** -12 + (1 - 2.0 ** -11) * torch.sigmoid(proj[:, 3 * d].double())
