@@ -180,7 +180,8 @@ def test_in_place_decoder_matches_window_decoder(name, dtype, steps, capture_gra
     assert torch.equal(t0, t1)
     tol = 1e-4 if dtype == "float32" else 2e-2
     torch.testing.assert_close(l1, l0, rtol=tol, atol=tol)
-    assert torch.equal(t1.cpu(), fx["decode_tokens"][:, :steps])
+    stored = min(steps, fx["decode_tokens"].shape[1])  # the golden holds this many reference steps
+    assert torch.equal(t1[:, :stored].cpu(), fx["decode_tokens"][:, :stored])
     for field in ("working_state", "memory_basis", "memory_normalizer", "local_keys", "local_values"):
         torch.testing.assert_close(getattr(s1, field), getattr(s0, field), rtol=1e-3, atol=1e-4)
     assert torch.equal(s1.local_valid, s0.local_valid)
