@@ -237,13 +237,19 @@ def emit(line: dict, args) -> None:
 
 # ----------------------------------------------------------------- GPU side
 def count_native_kernels(model, decoder, token) -> int:
-    """Kernels of libkoemi_b200 launched by one eager decode step."""
+    """Kernels of libkoemi_b200 launched by one eager decode step (on a copy of
+    the decoder's state, so the measured run is not advanced)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
+    from koemi_5hom_b200.model.decode import decode_step, from_koemi_state, to_koemi_state
     from koemi_5hom_b200.runtime.fast_decode import clone_state
-    state = clone_state(decoder._state)
+    s = model.settings
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        model(token, state, trusted_inputs=True)
+        if decoder._dstate is not None:
+            scratch = from_koemi_state(to_koemi_state(decoder._dstate), s.local_memory_size, s.salience_memory_size)
+            decode_step(model, token, scratch)
+        else:
+            model(token, clone_state(decoder._state), trusted_inputs=True)
         torch.cuda.synchronize()
     return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "koemi" in e.name)
 
