@@ -113,14 +113,28 @@ KOEMI_API int koemi_dense_bounded_gates(const float *projections, const uint8_t 
 /* Decode step of the gates and the scan (one token per stream), in place:
  * a = lo + (hi - lo) sigmoid(pre_a), b = (1 - a) tanh(pre_c) (a = 1, b = 0 where
  * !valid); prior_out <- working (cast to prior_dtype, may be NULL);
- * working <- a * working + b; h_out[row * h_stride + f] <- the new working.
+ * working <- a * working + b; h_out[row * h_stride + f] <- the new working
+ * (in prior_dtype, may be NULL).
  * `projections` is [batch, 2*features] fp32 (pre_a | pre_c). Fuses
  * BoundedRecurrentState.gates (model/memory.py:22-26), the masks of
  * network.py:308-309 and the T == 1 affine scan (model/scan.py:17-30). */
 KOEMI_API int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
-                            void *prior_out, float *h_out, int64_t h_stride, int64_t batch,
+                            void *prior_out, void *h_out, int64_t h_stride, int64_t batch,
                             int64_t features, float minimum_retention, float maximum_retention,
                             int prior_dtype, void *stream);
+
+/* Dense projection out = a W^T + bias on tcgen05 tensor cores, fp32 output:
+ * a [rows, k] (row stride a_stride elements, bf16/f16), W [n, k] (same dtype,
+ * contiguous), bias [n] (same dtype, may be NULL), out fp32 rows of
+ * out_stride. Small row counts split K across CTAs and reduce the fp32
+ * partials in a fixed order (deterministic) through `workspace` of
+ * koemi_dense_projection_workspace() bytes. The projections of the HERM block
+ * (gates, local, associative, fusion, head; network.py:97,106, memory.py:17-18,
+ * 70-75,294-295) use it at decode. k and a_stride must be multiples of 8. */
+KOEMI_API size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64_t k, int dtype);
+KOEMI_API int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
+                           float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
+                           void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------- core front */
 
@@ -205,16 +219,16 @@ KOEMI_API int koemi_think_salient_admission(const float *carried_keys, const flo
  * writes the new entry (entries + b*entry_stride: key | value, zeroed when
  * !valid) over the oldest local slot and, when valid && surprise > threshold,
  * into the salient ring (dropping its oldest entry when full). Outputs go to
- * local_out / salient_out rows of out_stride; novelty_out and admission_out
+ * local_out / salient_out rows of out_stride (out_dtype); novelty_out and admission_out
  * ([batch]) may be NULL. All fp32 rows 16-byte aligned, width % 4 == 0. The
  * caller advances *local_head once per step. */
 KOEMI_API int koemi_think_ring_decode_step(
     const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride,
     const uint8_t *valid, const float *surprise, float threshold, float *local_keys, float *local_values,
     uint8_t *local_valid, const int64_t *local_head, float *salient_keys, float *salient_values,
-    uint8_t *salient_valid, int32_t *salient_head, int32_t *salient_count, float *local_out,
-    float *salient_out, int64_t out_stride, float *novelty_out, uint8_t *admission_out, int64_t batch,
-    int64_t width, int64_t local_slots, int64_t salient_slots, void *stream);
+    uint8_t *salient_valid, int32_t *salient_head, int32_t *salient_count, void *local_out,
+    void *salient_out, int64_t out_stride, float *novelty_out, uint8_t *admission_out, int64_t batch,
+    int64_t width, int64_t local_slots, int64_t salient_slots, int out_dtype, void *stream);
 
 /* One decode step of the rank-one associative memory, in place
  * (HierarchicalAssociativeMemory.project / read / update with the fast write
@@ -222,15 +236,15 @@ KOEMI_API int koemi_think_ring_decode_step(
  * `projections` rows (stride proj_stride) hold key | query | value_pre |
  * decay_pre | write_pre as produced by one GEMM; feature_logits is
  * [2, batch, features] (key then query logits of the feature projection).
- * Writes the confidence-weighted read to read_out rows (stride read_stride)
+ * Writes the confidence-weighted read to read_out rows (stride read_stride, out_dtype)
  * from the memory before this step's write, then basis <- decay * basis +
  * w * tanh(value) f^T and normalizer <- decay * normalizer + w f, with
  * w = sigmoid(write_pre) (0.25 + 0.75 clamp(surprise)) (surprise may be NULL:
  * 0); invalid rows keep their memory. */
 KOEMI_API int koemi_assoc_decode_step(const float *projections, int64_t proj_stride,
                             const float *feature_logits, const float *surprise, const uint8_t *valid,
-                            float *basis, float *normalizer, float *read_out, int64_t read_stride,
-                            int64_t batch, int64_t width, int64_t features, void *stream);
+                            float *basis, float *normalizer, void *read_out, int64_t read_stride,
+                            int64_t batch, int64_t width, int64_t features, int out_dtype, void *stream);
 
 /* -------------------------------------------------------------- moe front */
 

@@ -27,7 +27,7 @@ namespace {
 // -------------------------------------------------------------- gates+scan
 template <typename TP>
 __global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t *__restrict__ valid,
-                                    float *__restrict__ working, TP *__restrict__ prior, float *__restrict__ h_out,
+                                    float *__restrict__ working, TP *__restrict__ prior, TP *__restrict__ h_out,
                                     int64_t h_stride, int64_t batch, int64_t features, float lo, float hi) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= batch * features) return;
@@ -43,7 +43,7 @@ __global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t
     if (prior != nullptr) prior[i] = from_acc<TP>(previous);
     const float h = a * previous + b;
     working[i] = h;
-    if (h_out != nullptr) h_out[row * h_stride + f] = h;
+    if (h_out != nullptr) h_out[row * h_stride + f] = from_acc<TP>(h);
 }
 
 // ---------------------------------------------------------------- rings
@@ -67,8 +67,8 @@ struct RingArgs {
     uint8_t *salient_valid;
     int32_t *salient_head;
     int32_t *salient_count;
-    float *local_out;
-    float *salient_out;
+    void *local_out;
+    void *salient_out;
     int64_t out_stride;
     float *novelty_out;
     uint8_t *admission_out;
@@ -91,6 +91,7 @@ __device__ __forceinline__ float block_reduce(float v, float *scratch, bool take
 
 // blockIdx.y == 0: local ring, 1: salient ring. Shared memory: q[width],
 // scores[slots], cosines[slots], reduction scratch.
+template <typename TO>
 __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     extern __shared__ float shared[];
     const bool local = blockIdx.y == 0;
@@ -162,7 +163,7 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     const float inv_total = any ? 1.0f / total : 0.0f;
 
     // pass 2: each thread owns float4 columns, sums the weighted values
-    float *out = (local ? a.local_out : a.salient_out) + b * a.out_stride;
+    TO *out = static_cast<TO *>(local ? a.local_out : a.salient_out) + b * a.out_stride;
     for (int64_t c = threadIdx.x; c < quads; c += kRingThreads) {
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int64_t s = 0; s < slots; ++s) {
@@ -174,11 +175,11 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
             acc.z += w * v.z;
             acc.w += w * v.w;
         }
-        acc.x *= inv_total;
-        acc.y *= inv_total;
-        acc.z *= inv_total;
-        acc.w *= inv_total;
-        reinterpret_cast<float4 *>(out)[c] = acc;
+        TO *dst = out + c * 4;
+        dst[0] = from_acc<TO>(acc.x * inv_total);
+        dst[1] = from_acc<TO>(acc.y * inv_total);
+        dst[2] = from_acc<TO>(acc.z * inv_total);
+        dst[3] = from_acc<TO>(acc.w * inv_total);
     }
     const bool token_valid = a.valid == nullptr || a.valid[b] != 0;
     if (local && threadIdx.x == 0 && a.novelty_out != nullptr) {
@@ -225,12 +226,16 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
 }
 
 // ----------------------------------------------------------- associative
-constexpr int kAssocThreads = 256;
+constexpr int kAssocThreads = 512;
 
+// One CTA per stream. The memory row i (m features) is read as m/4 float4
+// packets by m/4 adjacent threads, which combine their partial dot products
+// with the query features by shuffles; the decayed write goes back in place.
+template <typename TO>
 __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float *__restrict__ projections, int64_t proj_stride, const float *__restrict__ feature_logits,
     const float *__restrict__ surprise, const uint8_t *__restrict__ valid, float *__restrict__ basis,
-    float *__restrict__ normalizer, float *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
+    float *__restrict__ normalizer, TO *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
     int64_t m) {
     extern __shared__ float shared[];
     float *f = shared;       // [m] write features
@@ -270,16 +275,42 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float reg = den + 1.0f / 256.0f;
     const float confidence = den / reg;
     float *rows = basis + b * d * m;
-    for (int64_t i = threadIdx.x; i < d; i += kAssocThreads) {
-        float *row = rows + i * m;
-        const float v = tanhf(proj[2 * d + i]);
-        float num = 0.0f;
-        for (int64_t j = 0; j < m; ++j) {
-            const float x = row[j];
-            num += x * qf[j];
-            row[j] = decay * x + write * v * f[j];
+    if (m % 4 == 0 && m <= 128 && (kAssocThreads % (m / 4)) == 0 && 32 % (m / 4) == 0) {
+        const int parts = static_cast<int>(m / 4);
+        const int part = static_cast<int>(threadIdx.x) % parts;
+        const int64_t rows_per_pass = kAssocThreads / parts;
+        const float4 qv = reinterpret_cast<const float4 *>(qf)[part];
+        const float4 fv = reinterpret_cast<const float4 *>(f)[part];
+        // uniform trip count: every lane reaches the shuffles
+        for (int64_t base = 0; base < d; base += rows_per_pass) {
+            const int64_t i = base + threadIdx.x / parts;
+            const bool live = i < d;
+            float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float4 *cell = reinterpret_cast<float4 *>(rows + (live ? i : 0) * m) + part;
+            if (live) x = *cell;
+            float num = x.x * qv.x + x.y * qv.y + x.z * qv.z + x.w * qv.w;
+            for (int o = 1; o < parts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
+            if (!live) continue;
+            const float v = write * tanhf(proj[2 * d + i]);
+            x.x = decay * x.x + v * fv.x;
+            x.y = decay * x.y + v * fv.y;
+            x.z = decay * x.z + v * fv.z;
+            x.w = decay * x.w + v * fv.w;
+            *cell = x;
+            if (part == 0) read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
         }
-        read_out[b * read_stride + i] = confidence * num / reg;
+    } else {
+        for (int64_t i = threadIdx.x; i < d; i += kAssocThreads) {
+            float *row = rows + i * m;
+            const float v = tanhf(proj[2 * d + i]);
+            float num = 0.0f;
+            for (int64_t j = 0; j < m; ++j) {
+                const float x = row[j];
+                num += x * qf[j];
+                row[j] = decay * x + write * v * f[j];
+            }
+            read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
+        }
     }
     __syncthreads();
     if (threadIdx.x < m) {
@@ -294,7 +325,7 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
 using namespace koemi;
 
 extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
-                                       void *prior_out, float *h_out, int64_t h_stride, int64_t batch,
+                                       void *prior_out, void *h_out, int64_t h_stride, int64_t batch,
                                        int64_t features, float minimum_retention, float maximum_retention,
                                        int prior_dtype, void *stream) {
     clear_error();
@@ -304,9 +335,9 @@ extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *
     const unsigned blocks = static_cast<unsigned>(ceil_div(total, 256));
     cudaStream_t s = as_stream(stream);
     switch (prior_dtype) {
-        case KOEMI_F32: decode_gates_kernel<float><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<float *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
-        case KOEMI_BF16: decode_gates_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
-        case KOEMI_F16: decode_gates_kernel<__half><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__half *>(prior_out), h_out, h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_F32: decode_gates_kernel<float><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<float *>(prior_out), static_cast<float *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_BF16: decode_gates_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), static_cast<__nv_bfloat16 *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_F16: decode_gates_kernel<__half><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__half *>(prior_out), static_cast<__half *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
         default: return fail(KOEMI_ERR_INVALID, "prior dtype must be f32, f16 or bf16");
     }
     KOEMI_LAUNCH_CHECK();
@@ -317,15 +348,15 @@ extern "C" int koemi_think_ring_decode_step(
     const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride, const uint8_t *valid,
     const float *surprise, float threshold, float *local_keys, float *local_values, uint8_t *local_valid,
     const int64_t *local_head, float *salient_keys, float *salient_values, uint8_t *salient_valid,
-    int32_t *salient_head, int32_t *salient_count, float *local_out, float *salient_out, int64_t out_stride,
+    int32_t *salient_head, int32_t *salient_count, void *local_out, void *salient_out, int64_t out_stride,
     float *novelty_out, uint8_t *admission_out, int64_t batch, int64_t width, int64_t local_slots,
-    int64_t salient_slots, void *stream) {
+    int64_t salient_slots, int out_dtype, void *stream) {
     clear_error();
     if (batch < 0 || width < 0 || local_slots < 1 || salient_slots < 1) return fail(KOEMI_ERR_INVALID, "bad ring sizes");
     if (batch == 0) return KOEMI_OK;
-    if (width % 4 != 0 || query_stride % 4 != 0 || entry_stride % 4 != 0 || out_stride % 4 != 0 ||
-        !aligned(queries, 16) || !aligned(entries, 16) || !aligned(local_keys, 16) || !aligned(salient_keys, 16) ||
-        !aligned(local_values, 16) || !aligned(salient_values, 16) || !aligned(local_out, 16) || !aligned(salient_out, 16)) {
+    if (width % 4 != 0 || query_stride % 4 != 0 || entry_stride % 4 != 0 || !aligned(queries, 16) ||
+        !aligned(entries, 16) || !aligned(local_keys, 16) || !aligned(salient_keys, 16) || !aligned(local_values, 16) ||
+        !aligned(salient_values, 16)) {
         return fail(KOEMI_ERR_UNSUPPORTED, "ring decode needs 16-byte aligned fp32 rows (width %% 4 == 0)");
     }
     if (batch > 2147483647) return fail(KOEMI_ERR_INVALID, "too many streams");
@@ -336,25 +367,41 @@ extern "C" int koemi_think_ring_decode_step(
     const int64_t slots = local_slots > salient_slots ? local_slots : salient_slots;
     const size_t smem = (static_cast<size_t>(width) + 2 * slots + kRingWarps) * sizeof(float);
     if (smem > 200 * 1024) return fail(KOEMI_ERR_UNSUPPORTED, "ring decode shared memory too large");
-    if (smem > 48 * 1024) {
-        KOEMI_CUDA_TRY(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    const dim3 grid(static_cast<unsigned>(batch), 2);
+    cudaStream_t s = as_stream(stream);
+    auto run = [&](auto kernel) -> int {
+        if (smem > 48 * 1024) {
+            KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        }
+        kernel<<<grid, kRingThreads, smem, s>>>(args);
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    };
+    switch (out_dtype) {
+        case KOEMI_F32: return run(ring_decode_kernel<float>);
+        case KOEMI_BF16: return run(ring_decode_kernel<__nv_bfloat16>);
+        case KOEMI_F16: return run(ring_decode_kernel<__half>);
+        default: return fail(KOEMI_ERR_INVALID, "ring outputs must be f32, f16 or bf16");
     }
-    ring_decode_kernel<<<dim3(static_cast<unsigned>(batch), 2), kRingThreads, smem, as_stream(stream)>>>(args);
-    KOEMI_LAUNCH_CHECK();
-    return KOEMI_OK;
 }
 
 extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_stride, const float *feature_logits,
                                        const float *surprise, const uint8_t *valid, float *basis, float *normalizer,
-                                       float *read_out, int64_t read_stride, int64_t batch, int64_t width,
-                                       int64_t features, void *stream) {
+                                       void *read_out, int64_t read_stride, int64_t batch, int64_t width,
+                                       int64_t features, int out_dtype, void *stream) {
     clear_error();
     if (batch < 0 || width < 0 || features < 1 || features > kAssocThreads) return fail(KOEMI_ERR_INVALID, "bad associative sizes");
     if (batch == 0) return KOEMI_OK;
+    if (features % 4 == 0 && !aligned(basis, 16)) return fail(KOEMI_ERR_UNSUPPORTED, "basis must be 16-byte aligned");
     const size_t smem = 2 * static_cast<size_t>(features) * sizeof(float);
-    assoc_decode_kernel<<<static_cast<unsigned>(batch), kAssocThreads, smem, as_stream(stream)>>>(
-        projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, read_out, read_stride, batch,
-        width, features);
+    const unsigned grid = static_cast<unsigned>(batch);
+    cudaStream_t s = as_stream(stream);
+    switch (out_dtype) {
+        case KOEMI_F32: assoc_decode_kernel<float><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<float *>(read_out), read_stride, batch, width, features); break;
+        case KOEMI_BF16: assoc_decode_kernel<__nv_bfloat16><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<__nv_bfloat16 *>(read_out), read_stride, batch, width, features); break;
+        case KOEMI_F16: assoc_decode_kernel<__half><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<__half *>(read_out), read_stride, batch, width, features); break;
+        default: return fail(KOEMI_ERR_INVALID, "associative read output must be f32, f16 or bf16");
+    }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }

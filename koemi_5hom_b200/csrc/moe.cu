@@ -637,24 +637,26 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     clear_error();
     if (tokens < 0 || width < 0 || top_k < 1) return fail(KOEMI_ERR_INVALID, "bad combine sizes");
     if (tokens == 0 || width == 0) return KOEMI_OK;
-    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
+    const int rows_per_block = tokens >= static_cast<int64_t>(sm_count()) * 32 ? 8 : 2;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, rows_per_block));
+    const int threads = rows_per_block * 32;
     cudaStream_t s = as_stream(stream);
     const bool vector = width % 4 == 0 && top_k <= 8 && aligned(context, 16) && aligned(out, 16) &&
                         aligned(norm_weight, 16) && aligned(expert_out, 8);
     if (vector) {
         switch (dtype) {
-            case KOEMI_F32: combine_residual_rmsnorm_vec_kernel<float><<<blocks, 256, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
-            case KOEMI_F16: combine_residual_rmsnorm_vec_kernel<__half><<<blocks, 256, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
-            case KOEMI_BF16: combine_residual_rmsnorm_vec_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            case KOEMI_F32: combine_residual_rmsnorm_vec_kernel<float><<<blocks, threads, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            case KOEMI_F16: combine_residual_rmsnorm_vec_kernel<__half><<<blocks, threads, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+            case KOEMI_BF16: combine_residual_rmsnorm_vec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
             default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
         }
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     }
     switch (dtype) {
-        case KOEMI_F32: combine_residual_rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
-        case KOEMI_F16: combine_residual_rmsnorm_kernel<__half><<<blocks, 256, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
-        case KOEMI_BF16: combine_residual_rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        case KOEMI_F32: combine_residual_rmsnorm_kernel<float><<<blocks, threads, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        case KOEMI_F16: combine_residual_rmsnorm_kernel<__half><<<blocks, threads, 0, s>>>(context, static_cast<const __half *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
+        case KOEMI_BF16: combine_residual_rmsnorm_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(context, static_cast<const __nv_bfloat16 *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;
         default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
     }
     KOEMI_LAUNCH_CHECK();

@@ -54,7 +54,7 @@ template <typename T, int kMode, int NV>
 __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
     constexpr int W = Pack<T>::kWidth;
     const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= args.rows) return;
     const int64_t packets = args.hidden / W;
     const T *xr = static_cast<const T *>(args.x) + row * args.hidden;
@@ -115,7 +115,7 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
 template <typename T, typename TO, int kMode>
 __global__ __launch_bounds__(kThreads) void rms_rows_scalar(RowArgs args) {
     const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= args.rows) return;
     const int64_t hidden = args.hidden;
     const T *xr = static_cast<const T *>(args.x) + row * hidden;
@@ -156,7 +156,10 @@ __global__ __launch_bounds__(kThreads) void rms_rows_scalar(RowArgs args) {
 
 template <typename T, typename TO, int kMode>
 int launch_rows(const RowArgs &args, cudaStream_t stream) {
-    const unsigned blocks = static_cast<unsigned>(ceil_div(args.rows, kRowsPerBlock));
+    // few rows (decode steps): 2 rows per block so the rows spread over the SMs
+    const int rows_per_block = args.rows >= static_cast<int64_t>(sm_count()) * 32 ? kRowsPerBlock : 2;
+    const int threads = rows_per_block * 32;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(args.rows, rows_per_block));
     constexpr int W = Pack<T>::kWidth;
     bool vector_ok = std::is_same<T, TO>::value && args.hidden % W == 0 && aligned(args.x, 16) &&
                      aligned(args.weight, 16) && aligned(args.y, 16) &&
@@ -166,15 +169,15 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
         if (vector_ok) {
             const int64_t per_lane = ceil_div(args.hidden / W, 32);
             if (per_lane <= 1) {
-                rms_rows_cached<T, kMode, 1><<<blocks, kThreads, 0, stream>>>(args);
+                rms_rows_cached<T, kMode, 1><<<blocks, threads, 0, stream>>>(args);
             } else if (per_lane <= 2) {
-                rms_rows_cached<T, kMode, 2><<<blocks, kThreads, 0, stream>>>(args);
+                rms_rows_cached<T, kMode, 2><<<blocks, threads, 0, stream>>>(args);
             } else if (per_lane <= 4) {
-                rms_rows_cached<T, kMode, 4><<<blocks, kThreads, 0, stream>>>(args);
+                rms_rows_cached<T, kMode, 4><<<blocks, threads, 0, stream>>>(args);
             } else if (per_lane <= 8) {
-                rms_rows_cached<T, kMode, 8><<<blocks, kThreads, 0, stream>>>(args);
+                rms_rows_cached<T, kMode, 8><<<blocks, threads, 0, stream>>>(args);
             } else if (per_lane <= 16 && sizeof(T) == 4 && kMode == kPlain) {
-                rms_rows_cached<T, kMode, 16><<<blocks, kThreads, 0, stream>>>(args);
+                rms_rows_cached<T, kMode, 16><<<blocks, threads, 0, stream>>>(args);
             } else {
                 vector_ok = false;
             }
@@ -184,7 +187,7 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
             }
         }
     }
-    rms_rows_scalar<T, TO, kMode><<<blocks, kThreads, 0, stream>>>(args);
+    rms_rows_scalar<T, TO, kMode><<<blocks, threads, 0, stream>>>(args);
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }

@@ -45,7 +45,7 @@ constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemColumns = 512;
 constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
 
-enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2 };
+enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3 };
 
 struct UmmaArgs {
     CUtensorMap map_a;
@@ -59,6 +59,8 @@ struct UmmaArgs {
     int64_t out_stride;       // elements per output row
     int64_t experts;
     int64_t band;             // surprise: row tiles per band (tile order swizzle)
+    int64_t splits;           // dense: K splits (partials reduced by a second kernel when > 1)
+    int64_t k_per_split;      // dense: K blocks per split (every split non-empty)
     const int64_t *offsets;
     const int32_t *tile_prefix;
     const void *bias0;
@@ -123,6 +125,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     return false;
 }
 
+__device__ __forceinline__ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 // ------------------------------------------------------------- scheduling
 
 struct Tile {
@@ -131,17 +135,37 @@ struct Tile {
     int64_t n;         // tile index along N
     int64_t group;     // expert (grouped) or 0
     int64_t m_tile;    // row tile index (surprise: partial slot)
+    int64_t k_begin;   // K blocks [k_begin, k_end) of this tile
+    int64_t k_end;
+    int64_t split;     // dense: K split index
 };
 
 template <int kProblem>
 __device__ __forceinline__ int64_t total_tiles(const UmmaArgs &a) {
     if (kProblem == kSurprise) return ((a.rows + kBM - 1) / kBM) * a.n_tiles;
+    if (kProblem == kDense) return ((a.rows + kBM - 1) / kBM) * a.n_tiles * a.splits;
     return static_cast<int64_t>(a.tile_prefix[a.experts]) * a.n_tiles;
 }
 
 template <int kProblem>
 __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
     Tile tile{};
+    const int64_t k_blocks = (a.k + kBK - 1) / kBK;
+    tile.k_begin = 0;
+    tile.k_end = k_blocks;
+    if (kProblem == kDense) {
+        // m fastest, so CTAs running together share one weight tile from L2
+        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        tile.m_tile = t % m_tiles;
+        const int64_t rest = t / m_tiles;
+        tile.n = rest % a.n_tiles;
+        tile.split = rest / a.n_tiles;
+        tile.k_begin = tile.split * a.k_per_split;
+        tile.k_end = min(k_blocks, tile.k_begin + a.k_per_split);
+        tile.row0 = tile.m_tile * kBM;
+        tile.row_end = a.rows;
+        return tile;
+    }
     if (kProblem == kSurprise) {
         // bands of `band` row tiles; inside a band walk N first so each vocab
         // tile is reused from L2 by every row tile of the band
@@ -221,7 +245,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
             uint32_t phase = 0;
             for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
                 const Tile tile = tile_at<kProblem>(args, t);
-                for (int64_t kb = 0; kb < k_blocks; ++kb) {
+                for (int64_t kb = tile.k_begin; kb < tile.k_end; ++kb) {
                     if (!wait_or_abort(&empty[stage], phase ^ 1, abort, args.status)) break;
                     uint8_t *a_dst = stages + stage * kStageBytes;
                     uint8_t *b_dst = a_dst + kABytes;
@@ -253,8 +277,9 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                 if (!wait_or_abort(&acc_empty[acc], acc_phase ^ 1, abort, args.status)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(acc * kBN);
+                const Tile tile = tile_at<kProblem>(args, t);
                 bool ok = true;
-                for (int64_t kb = 0; kb < k_blocks; ++kb) {
+                for (int64_t kb = tile.k_begin; kb < tile.k_end; ++kb) {
                     if (!wait_or_abort(&full[stage], phase, abort, args.status)) {
                         ok = false;
                         break;
@@ -265,7 +290,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k) {
                         umma_f16(tmem_d, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
-                                 args.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                                 args.idesc, (kb > tile.k_begin || k > 0) ? 1u : 0u);
                     }
                     umma_commit(&empty[stage]);
                     if (++stage == kStages) {
@@ -356,6 +381,37 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                             }
                         } else {
                             for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = from_acc<T>(o[j]);
+                        }
+                    }
+                }
+            } else if (kProblem == kDense) {
+                // splits == 1: out = acc + bias (fp32, row stride out_stride);
+                // splits  > 1: partials[split][row][col] = acc, reduced later
+                const T *bias = static_cast<const T *>(args.bias0);
+                const bool direct = args.splits == 1;
+                float *dst_row = direct ? static_cast<float *>(args.out) + row * args.out_stride
+                                        : args.partials + (tile.split * args.rows + row) * args.n_out;
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t y[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, y);
+                    tmem_wait_ld();
+                    const int64_t col0 = tile.n * kBN + c * 32;
+                    if (row_ok && col0 < args.n_out) {
+                        float o[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int64_t col = col0 + j;
+                            o[j] = __uint_as_float(y[j]) + (direct && bias != nullptr && col < args.n_out ? to_acc(bias[col]) : 0.0f);
+                        }
+                        float *dst = dst_row + col0;
+                        if (col0 + 32 <= args.n_out && aligned16(dst)) {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                reinterpret_cast<float4 *>(dst)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                            }
+                        } else {
+                            for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = o[j];
                         }
                     }
                 }
@@ -533,6 +589,30 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     return KOEMI_OK;
 }
 
+__global__ void split_k_reduce_kernel(const float *__restrict__ partials, int64_t splits, int64_t rows, int64_t n,
+                                      const void *__restrict__ bias, int bias_dtype, float *__restrict__ out,
+                                      int64_t out_stride) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * n) return;
+    const int64_t r = i / n, c = i - r * n;
+    float acc = 0.0f;
+    if (bias != nullptr) {
+        acc = bias_dtype == KOEMI_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(bias)[c])
+                                       : __half2float(static_cast<const __half *>(bias)[c]);
+    }
+    for (int64_t s = 0; s < splits; ++s) acc += partials[(s * rows + r) * n + c];
+    out[r * out_stride + c] = acc;
+}
+
+int64_t dense_splits(int64_t rows, int64_t n, int64_t k) {
+    const int64_t tiles = ((rows + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    const int64_t k_blocks = (k + kBK - 1) / kBK;
+    int64_t splits = (sm_count() + tiles - 1) / tiles;
+    const int64_t max_splits = k_blocks / 4 > 1 ? k_blocks / 4 : 1;  // at least 4 K blocks per split
+    if (splits > max_splits) splits = max_splits;
+    return splits < 1 ? 1 : splits;
+}
+
 int64_t surprise_umma_slices(int64_t rows, int64_t width, int64_t content_vocab, int dtype) {
     if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return 0;
     if (width % 8 != 0 || rows <= 0 || content_vocab >= (int64_t(1) << 31)) return 0;
@@ -572,3 +652,78 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
 }
 
 }  // namespace koemi
+
+using namespace koemi;
+
+namespace {
+struct DensePlan {
+    int64_t splits;
+    int64_t k_per_split;
+};
+DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
+    const int64_t k_blocks = (k + kBK - 1) / kBK;
+    const int64_t wanted = dense_splits(rows, n, k);
+    const int64_t per = (k_blocks + wanted - 1) / wanted;
+    return DensePlan{(k_blocks + per - 1) / per, per};
+}
+}  // namespace
+
+extern "C" size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64_t k, int dtype) {
+    (void)dtype;
+    if (rows <= 0 || n <= 0 || k <= 0) return 256;
+    const DensePlan plan = dense_plan(rows, n, k);
+    return plan.splits > 1 ? static_cast<size_t>(plan.splits) * rows * n * sizeof(float) : 256;
+}
+
+extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
+                                      float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
+                                      void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "dense projection takes bf16 or f16 operands");
+    if (rows < 0 || n < 1 || k < 1) return fail(KOEMI_ERR_INVALID, "need rows >= 0 and positive n, k");
+    if (rows == 0) return KOEMI_OK;
+    if (k % 8 != 0 || a_stride < k || a_stride % 8 != 0 || !aligned(a, 16) || !aligned(weight, 16) ||
+        rows >= (int64_t(1) << 31) || n >= (int64_t(1) << 31)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "dense projection needs K and the A row stride to be multiples of 8 and 16-byte aligned operands");
+    }
+    const DensePlan plan = dense_plan(rows, n, k);
+    if (plan.splits > 1 && workspace_bytes < koemi_dense_projection_workspace(rows, n, k, dtype)) {
+        return fail(KOEMI_ERR_WORKSPACE, "dense projection needs %zu workspace bytes", koemi_dense_projection_workspace(rows, n, k, dtype));
+    }
+    cudaStream_t s = as_stream(stream);
+    UmmaArgs args{};
+    const CUtensorMapDataType type = dtype == KOEMI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(rows)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(a_stride) * 2};
+        const uint32_t box[2] = {kBK, kBM};
+        int rc = encode_tensor_map(&args.map_a, type, 2, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc != KOEMI_OK) return rc;
+    }
+    int rc = encode_kmajor(&args.map_b0, dtype, weight, n, k, kBN);
+    if (rc != KOEMI_OK) return rc;
+    args.k = k;
+    args.rows = rows;
+    args.n_tiles = (n + kBN - 1) / kBN;
+    args.n_out = n;
+    args.out_stride = out_stride;
+    args.experts = 1;
+    args.splits = plan.splits;
+    args.k_per_split = plan.k_per_split;
+    args.bias0 = bias;
+    args.out = out;
+    args.partials = plan.splits > 1 ? static_cast<float *>(workspace) : nullptr;
+    args.status = device_status_word();
+    args.idesc = make_idesc(dtype);
+    const int64_t tiles = ((rows + kBM - 1) / kBM) * args.n_tiles * plan.splits;
+    rc = launch<kDense>(args, dtype, tiles, s);
+    if (rc != KOEMI_OK) return rc;
+    if (plan.splits > 1) {
+        const int64_t total = rows * n;
+        split_k_reduce_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, s>>>(
+            args.partials, plan.splits, rows, n, bias, dtype, out, out_stride);
+        KOEMI_LAUNCH_CHECK();
+    }
+    return KOEMI_OK;
+}
+

@@ -87,6 +87,30 @@ def _(projections, valid, minimum, maximum):
     return projections.new_empty(rows, features), projections.new_empty(rows, features)
 
 
+@torch.library.custom_op("koemi_b200::dense_projection", mutates_args=())
+def dense_projection(a: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+    """fp32 [rows, n] = a [rows, k] @ weight[n, k]^T + bias on tensor cores
+    (bf16/f16 operands); `a` may be a view with strided rows."""
+    weight, bias = _dense(weight, bias)
+    if a.stride(-1) != 1:
+        a = a.contiguous()
+    stream = _prepare(weight)
+    rows, k = a.shape
+    n = weight.shape[0]
+    out = torch.empty(rows, n, dtype=torch.float32, device=a.device)
+    code = dtype_code(weight.dtype)
+    size = _native.library().koemi_dense_projection_workspace(rows, n, k, code)
+    scratch = _native.workspace(size, a.device)
+    call("koemi_dense_projection", ptr(a), a.stride(0), ptr(weight), ptr(bias), ptr(out), n, rows, n, k, code,
+         ptr(scratch), scratch.numel(), stream)
+    return out
+
+
+@dense_projection.register_fake
+def _(a, weight, bias):
+    return a.new_empty(a.shape[0], weight.shape[0], dtype=torch.float32)
+
+
 # ----------------------------------------------------------------- core front
 
 @torch.library.custom_op("koemi_b200::rmsnorm_silu_forward", mutates_args=())

@@ -149,12 +149,15 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     ptr = _native.ptr
     prior_dtype = _native.dtype_code(model.compute_dtype)
     x = model.embedding_weight.index_select(0, ids).float()
+    concat_dtype = model.compute_dtype
+    out_code = _native.dtype_code(concat_dtype)
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
         st = dstate.blocks[index]
         u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, torch.float32)
-        pre = model._linear(u, block.gates_weight, bc["gates_bias"])
-        concat = torch.empty(batch, 4 * d, dtype=torch.float32, device=device)  # h | memory | local | salient
+        pre = model._linear(u, block.gates_weight, block.gates_bias)
+        # fusion input rows, written in place by the step kernels: h | memory | local | salient
+        concat = torch.empty(batch, 4 * d, dtype=concat_dtype, device=device)
         prior = torch.empty(batch, d, dtype=model.compute_dtype, device=device)
         call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), ptr(prior), ptr(concat), 4 * d,
              batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
@@ -165,20 +168,21 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
             surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
                                                     torch.float32)
-        local = model._linear(h, block.local_weight, bc["local_bias"])
-        assoc = model._linear(h, block.assoc_weight, bc["assoc_bias"])
+        local = model._linear(h, block.local_weight, block.local_bias)
+        assoc = model._linear(h, block.assoc_weight, block.assoc_bias)
         features = model._linear(torch.stack((assoc[:, :d], assoc[:, d:2 * d])), block.feature_weight,
-                                 bc["feature_bias"])
+                                 block.feature_bias)
         scored = surprise if surprise is not None else torch.zeros(batch, device=device)
-        call("koemi_think_ring_decode_step", ptr(concat), 4 * d, ptr(local), 2 * d, ptr(valid), ptr(scored),
+        # ring queries read the fp32 working state (the new h) directly
+        call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), 2 * d, ptr(valid), ptr(scored),
              float(s.salience_threshold), ptr(st.local_keys), ptr(st.local_values), ptr(st.local_valid),
              ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
              ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,
-             None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], stream)
+             None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], out_code, stream)
         call("koemi_assoc_decode_step", ptr(assoc), assoc.shape[1], ptr(features), ptr(surprise), ptr(valid),
              ptr(st.memory_basis), ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d,
-             s.memory_features, stream)
-        fused = model._linear(concat, block.fusion_weight, bc["fusion_bias"])
+             s.memory_features, out_code, stream)
+        fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
         if s.expert_count == 0:
             x = context
@@ -196,7 +200,7 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
                                              block.expert_output_weight, block.expert_output_bias)
         x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid, bc["expert_norm"],
                                           s.expert_top_k, NORM_EPSILON)
-    logits = model._linear(x, model.head_weight, cache["head_b"])
+    logits = model._linear(x, model.head_weight, model.head_bias)
     dstate.last_token_ids.copy_(torch.where(valid, ids, dstate.last_token_ids))
     dstate.local_head.add_(1).remainder_(dstate.blocks[0].local_keys.shape[1])
     return logits

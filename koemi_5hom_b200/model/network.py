@@ -344,7 +344,7 @@ class KoemiModel(nn.Module):
             new_state = _with_step(new_states[0], step)
         if logits:
             head_in = x[:, -1:] if last_only else x
-            out_logits = self._linear(head_in, self.head_weight, self._cache["head_b"])
+            out_logits = self._linear(head_in, self.head_weight, self.head_bias)
         else:
             out_logits = x.new_empty(ids.shape[0], 0, s.vocabulary_size)
         return KoemiOutput(
@@ -363,14 +363,26 @@ class KoemiModel(nn.Module):
         )
 
     def _linear(self, x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
-        """fp32 [.., n] = x [.., k] @ weight[n, k]^T (+ bias): cuBLAS, fp32 out."""
+        """fp32 [.., n] = x [.., k] @ weight[n, k]^T (+ bias). bf16 weights run
+        the tcgen05 projection (fused bias, fp32 out; x may be a bf16 view with
+        strided rows); fp32 weights and shapes TMA cannot describe use cuBLAS."""
         flat = x.reshape(-1, x.shape[-1])
         if self.compute_dtype == torch.float32:
-            y = flat @ weight.T if bias is None else torch.addmm(bias, flat, weight.T)
+            if bias is None:
+                y = flat @ weight.T
+            else:
+                y = torch.addmm(bias.float(), flat, weight.T)
+            return y.reshape(*x.shape[:-1], weight.shape[0])
+        if flat.dtype != self.compute_dtype:
+            flat = flat.to(self.compute_dtype)
+        k = flat.shape[1]
+        if (k % 8 == 0 and flat.stride(1) == 1 and flat.stride(0) % 8 == 0 and flat.data_ptr() % 16 == 0
+                and flat.shape[0] > 0):
+            y = _ops.dense_projection(flat, weight, bias)
         else:
-            y = torch.mm(flat.to(self.compute_dtype), weight.T, out_dtype=torch.float32)
+            y = torch.mm(flat, weight.T, out_dtype=torch.float32)
             if bias is not None:
-                y += bias
+                y += bias.float()
         return y.reshape(*x.shape[:-1], weight.shape[0])
 
     def _block_window(self, block: HermBlock, cache: dict, x: Tensor, ids: Tensor, valid: Tensor,
@@ -383,7 +395,7 @@ class KoemiModel(nn.Module):
 
         # input norm (core), gates (dense), scan (dense): network.py:305-310
         u = _ops.rms_norm(x.reshape(rows, d), None, cache["input_norm"], None, NORM_EPSILON, torch.float32)
-        pre = self._linear(u, block.gates_weight, cache["gates_bias"])
+        pre = self._linear(u, block.gates_weight, block.gates_bias)
         retention, increment = _ops.bounded_gates(pre, valid_flat, MIN_RETENTION, MAX_RETENTION)
         h = _ops.affine_scan_forward(retention.reshape(batch, length, d), increment.reshape(batch, length, d),
                                      state.working_state.contiguous(), False)
@@ -408,7 +420,7 @@ class KoemiModel(nn.Module):
                                                     self._cache["content_b"], targets, valid, torch.float32)
 
         # local ring entries + sliding-window read: memory.py:297-361
-        local = self._linear(h, block.local_weight, cache["local_bias"])
+        local = self._linear(h, block.local_weight, block.local_bias)
         keep = valid.unsqueeze(-1)
         keys = torch.where(keep, local[..., :d], 0.0)
         values = torch.where(keep, local[..., d:], 0.0)
@@ -416,12 +428,12 @@ class KoemiModel(nn.Module):
                                            h, s.local_memory_size)
 
         # associative memory: memory.py:82-144,244-255
-        assoc = self._linear(h, block.assoc_weight, cache["assoc_bias"])
+        assoc = self._linear(h, block.assoc_weight, block.assoc_bias)
         key, query = assoc[..., :d], assoc[..., d:2 * d]
         mem_value = torch.tanh(assoc[..., 2 * d:3 * d])
         decay = MIN_DECAY + (MAX_DECAY - MIN_DECAY) * torch.sigmoid(assoc[..., 3 * d])
         write = torch.sigmoid(assoc[..., 3 * d + 1])
-        both = self._linear(torch.stack((key, query)), block.feature_weight, cache["feature_bias"]).softmax(dim=-1)
+        both = self._linear(torch.stack((key, query)), block.feature_weight, block.feature_bias).softmax(dim=-1)
         features, query_features = both[0], both[1]
         fast_decay = torch.where(valid, decay, 1.0)
         fast_write = torch.where(valid, write * (0.25 + 0.75 * surprise.clamp(0.0, 1.0)), 0.0)
@@ -445,7 +457,7 @@ class KoemiModel(nn.Module):
                 state.refine_basis, state.refine_normalizer, refine_decay, error, features, refine_write,
                 query_features)
             gate = torch.sigmoid(self._linear(torch.cat((h, fast_read, refine_read, local_value), dim=-1),
-                                              block.refine_weight, cache["refine_bias"]))
+                                              block.refine_weight, block.refine_bias))
             memory_value = fast_read + gate * refine_read
         else:
             memory_value = fast_read
@@ -453,7 +465,7 @@ class KoemiModel(nn.Module):
 
         # fusion (cuBLAS + core rms_norm): network.py:723-732
         fused = self._linear(torch.cat((h, memory_value, local_value, salient_value), dim=-1), block.fusion_weight,
-                             cache["fusion_bias"])
+                             block.fusion_bias)
         context = _ops.rms_norm(fused.reshape(rows, d), None, cache["fusion_norm"], None, NORM_EPSILON, torch.float32)
 
         # experts (moe): experts.py:90-143; router.py:43-97

@@ -68,7 +68,7 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
     _native.call("koemi_think_ring_decode_step", p(q_rows), 4 * width, p(entries), 2 * width, p(valid), p(surprise),
                  threshold, p(lk), p(lv), p(lvalid), p(local_head), p(sk), p(sv), p(svalid), p(s_head), p(s_count),
                  p(out[:, 2 * width:]), p(out[:, 3 * width:]), 4 * width, p(novelty), p(admission), batch, width,
-                 local_slots, salient_slots, torch.cuda.current_stream().cuda_stream)
+                 local_slots, salient_slots, _native.F32, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     scale = 1.0 / math.sqrt(width)
     for b in range(batch):
@@ -125,7 +125,8 @@ def test_assoc_decode_step_matches_oracle(cuda):
     proj_dev, feats_dev, surprise_dev, valid_dev = proj.to(cuda), feats.to(cuda), surprise.to(cuda), valid.to(cuda)
     p = _native.ptr
     _native.call("koemi_assoc_decode_step", p(proj_dev), 3 * d + 2, p(feats_dev), p(surprise_dev), p(valid_dev),
-                 p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m, torch.cuda.current_stream().cuda_stream)
+                 p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m, _native.F32,
+                 torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     f, qf = torch.softmax(feats[0].double(), -1), torch.softmax(feats[1].double(), -1)
     decay = 2.0 ** -12 + (1 - 2.0 ** -11) * torch.sigmoid(proj[:, 3 * d].double())

@@ -226,3 +226,20 @@ def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
                 sample.add(r)
     _sampled_rows_check(sc, se, offsets, y, weights, sorted(sample), torch.bfloat16, 3e-2)
     assert bool(torch.isfinite(y).all())
+
+
+@pytest.mark.parametrize("rows,n,k,stride,bias", [(256, 4096, 2048, 2048, True), (256, 2048, 8192, 8192, True),
+                                                  (3000, 1000, 512, 512, False), (256, 16, 2048, 8192, True),
+                                                  (7, 300, 64, 64, True)])
+def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
+    """tcgen05 projection (split-K or direct) against fp64 on the same bf16 operands."""
+    g = torch.Generator(device=cuda).manual_seed(rows + n)
+    wide = torch.randn(rows, stride, generator=g, device=cuda).bfloat16()
+    a = wide[:, :k]
+    w = (torch.randn(n, k, generator=g, device=cuda) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, generator=g, device=cuda) * 0.1).bfloat16() if bias else None
+    out = _ops.dense_projection(a, w, b)
+    expected = a.double() @ w.double().T + (b.double() if bias else 0.0)
+    torch.testing.assert_close(out.double(), expected, rtol=1e-4, atol=1e-4)
+    again = _ops.dense_projection(a, w, b)
+    assert torch.equal(out, again)  # fixed-order split-K reduction
