@@ -56,6 +56,8 @@ def parse_args(argv=None):
     p.add_argument("--top-k", type=int, default=2)
     p.add_argument("--threshold", type=float, default=0.64,
                    help="salience threshold (fixed rule of network.py:349; ~mean+1 sigma at random init)")
+    p.add_argument("--ring-dtype", choices=("bf16", "fp32"), default="bf16",
+                   help="storage type of the exact-memory rings (arithmetic stays fp32)")
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
@@ -78,7 +80,7 @@ def workload_config(args, world):
             "experts": args.experts, "top_k": args.top_k, "local_slots": 128, "salient_slots": 128,
             "streams_per_gpu": args.streams, "global_batch": args.streams * world, "prompt_len": args.prompt_len,
             "seq_len": 1, "salience_threshold": args.threshold, "parallelism": f"dp{world}",
-            "weights": "bf16", "state": "fp32", "l2": "per-step reads >> 126 MB L2 (no flush needed)"}
+            "weights": "bf16", "state": "fp32", "rings": args.ring_dtype, "l2": "per-step reads >> 126 MB L2 (no flush needed)"}
 
 
 def prompts_for(args, rank, device):
@@ -241,13 +243,11 @@ def count_native_kernels(model, decoder, token) -> int:
     the decoder's state, so the measured run is not advanced)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
-    from koemi_5hom_b200.model.decode import decode_step, from_koemi_state, to_koemi_state
+    from koemi_5hom_b200.model.decode import decode_step
     from koemi_5hom_b200.runtime.fast_decode import clone_state
-    s = model.settings
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         if decoder._dstate is not None:
-            scratch = from_koemi_state(to_koemi_state(decoder._dstate), s.local_memory_size, s.salience_memory_size)
-            decode_step(model, token, scratch)
+            decode_step(model, token, decoder._dstate.clone())
         else:
             model(token, clone_state(decoder._state), trusted_inputs=True)
         torch.cuda.synchronize()
@@ -311,7 +311,8 @@ def run_b200(args) -> None:
     model = KoemiModel(settings_for(args), device=device)
     model.initialize_parameters(seed=0)
     prompts = prompts_for(args, rank, device)
-    decoder = BatchDecoder(model, capture_graph=True)
+    ring_dtype = torch.bfloat16 if args.ring_dtype == "bf16" else torch.float32
+    decoder = BatchDecoder(model, capture_graph=True, ring_dtype=ring_dtype)
     torch.cuda.synchronize()
     prefill_start = time.perf_counter()
     logits = decoder.prefill(prompts)

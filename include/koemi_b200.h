@@ -220,15 +220,16 @@ KOEMI_API int koemi_think_salient_admission(const float *carried_keys, const flo
  * !valid) over the oldest local slot and, when valid && surprise > threshold,
  * into the salient ring (dropping its oldest entry when full). Outputs go to
  * local_out / salient_out rows of out_stride (out_dtype); novelty_out and admission_out
- * ([batch]) may be NULL. All fp32 rows 16-byte aligned, width % 4 == 0. The
- * caller advances *local_head once per step. */
+ * ([batch]) may be NULL. Ring rows are ring_dtype (KOEMI_F32, or KOEMI_BF16 to
+ * halve the ring traffic), 16-byte aligned, width a multiple of 4 (fp32) or 8
+ * (bf16); arithmetic is fp32. The caller advances *local_head once per step. */
 KOEMI_API int koemi_think_ring_decode_step(
     const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride,
-    const uint8_t *valid, const float *surprise, float threshold, float *local_keys, float *local_values,
-    uint8_t *local_valid, const int64_t *local_head, float *salient_keys, float *salient_values,
+    const uint8_t *valid, const float *surprise, float threshold, void *local_keys, void *local_values,
+    uint8_t *local_valid, const int64_t *local_head, void *salient_keys, void *salient_values,
     uint8_t *salient_valid, int32_t *salient_head, int32_t *salient_count, void *local_out,
     void *salient_out, int64_t out_stride, float *novelty_out, uint8_t *admission_out, int64_t batch,
-    int64_t width, int64_t local_slots, int64_t salient_slots, int out_dtype, void *stream);
+    int64_t width, int64_t local_slots, int64_t salient_slots, int ring_dtype, int out_dtype, void *stream);
 
 /* One decode step of the rank-one associative memory, in place
  * (HierarchicalAssociativeMemory.project / read / update with the fast write

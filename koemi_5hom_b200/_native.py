@@ -55,7 +55,7 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_dense_decode_step": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _f, _int, _p)),
     "koemi_think_ring_decode_step": (
         _int, (_p, _i64, _p, _i64, _p, _p, _f, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _i64,
-               _i64, _i64, _i64, _int, _p)),
+               _i64, _i64, _i64, _int, _int, _p)),
     "koemi_assoc_decode_step": (_int, (_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_dense_projection_workspace": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_dense_projection": (_int, (_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),

@@ -53,17 +53,17 @@ constexpr int kRingWarps = kRingThreads / 32;
 struct RingArgs {
     const float *queries;
     int64_t query_stride;
-    const float *entries;  // [B, 2d]: key | value of the new entry (unmasked)
+    const float *entries;  // [B, 2d]: key | value of the new entry (unmasked, fp32)
     int64_t entry_stride;
     const uint8_t *valid;
     const float *surprise;
     float threshold;
-    float *local_keys;
-    float *local_values;
+    void *local_keys;      // ring element type TR
+    void *local_values;
     uint8_t *local_valid;
     const int64_t *local_head;
-    float *salient_keys;
-    float *salient_values;
+    void *salient_keys;
+    void *salient_values;
     uint8_t *salient_valid;
     int32_t *salient_head;
     int32_t *salient_count;
@@ -89,10 +89,48 @@ __device__ __forceinline__ float block_reduce(float v, float *scratch, bool take
     return r;
 }
 
+// 16-byte packets of ring rows: 4 fp32 or 8 bf16 elements.
+template <typename TR>
+struct RingPacket;
+template <>
+struct RingPacket<float> {
+    static constexpr int kWidth = 4;
+    __device__ static void load(const float *p, float (&v)[4]) {
+        const float4 x = __ldg(reinterpret_cast<const float4 *>(p));
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    }
+    __device__ static void store(float *p, const float (&v)[4]) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+};
+template <>
+struct RingPacket<__nv_bfloat16> {
+    static constexpr int kWidth = 8;
+    __device__ static void load(const __nv_bfloat16 *p, float (&v)[8]) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4 *>(p));
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+    __device__ static void store(__nv_bfloat16 *p, const float (&v)[8]) {
+        uint4 x;
+        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4 *>(p) = x;
+    }
+};
+
 // blockIdx.y == 0: local ring, 1: salient ring. Shared memory: q[width],
 // scores[slots], cosines[slots], reduction scratch.
-template <typename TO>
+template <typename TR, typename TO>
 __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
+    using P = RingPacket<TR>;
+    constexpr int W = P::kWidth;
     extern __shared__ float shared[];
     const bool local = blockIdx.y == 0;
     const int64_t b = blockIdx.x;
@@ -112,14 +150,13 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
         qq += v * v;
     }
     const float q_norm = sqrtf(block_reduce(qq, scratch, false));
-    const float *keys = (local ? a.local_keys : a.salient_keys) + b * slots * d;
-    const float *values = (local ? a.local_values : a.salient_values) + b * slots * d;
+    TR *keys = static_cast<TR *>(local ? a.local_keys : a.salient_keys) + b * slots * d;
+    TR *values = static_cast<TR *>(local ? a.local_values : a.salient_values) + b * slots * d;
     const uint8_t *flags = (local ? a.local_valid : a.salient_valid) + b * slots;
     const float scale = rsqrtf(static_cast<float>(d));
-    const int64_t quads = d / 4;  // the host requires width % 4 == 0
-    const float4 *q4 = reinterpret_cast<const float4 *>(q);
+    const int64_t packets = d / W;  // the host requires width % W == 0
 
-    // pass 1: one warp per slot, dot(q, k) and |k|^2 over float4 packets
+    // pass 1: one warp per slot, dot(q, k) and |k|^2 over 16-byte packets
     for (int64_t s = warp; s < slots; s += kRingWarps) {
         if (!flags[s]) {
             if (lane == 0) {
@@ -128,14 +165,17 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
             }
             continue;
         }
-        const float4 *k4 = reinterpret_cast<const float4 *>(keys + s * d);
+        const TR *row = keys + s * d;
         float dot = 0.0f, kk = 0.0f;
 #pragma unroll 4
-        for (int64_t c = lane; c < quads; c += 32) {
-            const float4 k = __ldg(k4 + c);
-            const float4 x = q4[c];
-            dot += k.x * x.x + k.y * x.y + k.z * x.z + k.w * x.w;
-            kk += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
+        for (int64_t c = lane; c < packets; c += 32) {
+            float k[W];
+            P::load(row + c * W, k);
+#pragma unroll
+            for (int e = 0; e < W; ++e) {
+                dot = fmaf(k[e], q[c * W + e], dot);
+                kk = fmaf(k[e], k[e], kk);
+            }
         }
         dot = warp_sum(dot);
         kk = warp_sum(kk);
@@ -162,24 +202,22 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     total = block_reduce(total, scratch, false);
     const float inv_total = any ? 1.0f / total : 0.0f;
 
-    // pass 2: each thread owns float4 columns, sums the weighted values
+    // pass 2: each thread owns packets of columns and sums the weighted values
     TO *out = static_cast<TO *>(local ? a.local_out : a.salient_out) + b * a.out_stride;
-    for (int64_t c = threadIdx.x; c < quads; c += kRingThreads) {
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int64_t c = threadIdx.x; c < packets; c += kRingThreads) {
+        float acc[W];
+#pragma unroll
+        for (int e = 0; e < W; ++e) acc[e] = 0.0f;
         for (int64_t s = 0; s < slots; ++s) {
             const float w = score[s];
             if (w == 0.0f) continue;
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(values + s * d) + c);
-            acc.x += w * v.x;
-            acc.y += w * v.y;
-            acc.z += w * v.z;
-            acc.w += w * v.w;
+            float v[W];
+            P::load(values + s * d + c * W, v);
+#pragma unroll
+            for (int e = 0; e < W; ++e) acc[e] = fmaf(w, v[e], acc[e]);
         }
-        TO *dst = out + c * 4;
-        dst[0] = from_acc<TO>(acc.x * inv_total);
-        dst[1] = from_acc<TO>(acc.y * inv_total);
-        dst[2] = from_acc<TO>(acc.z * inv_total);
-        dst[3] = from_acc<TO>(acc.w * inv_total);
+#pragma unroll
+        for (int e = 0; e < W; ++e) out[c * W + e] = from_acc<TO>(acc[e] * inv_total);
     }
     const bool token_valid = a.valid == nullptr || a.valid[b] != 0;
     if (local && threadIdx.x == 0 && a.novelty_out != nullptr) {
@@ -210,17 +248,18 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     __syncthreads();
     const int32_t slot = write_slot;
     if (slot < 0) return;
-    float *key_dst = (local ? a.local_keys : a.salient_keys) + (b * slots + slot) * d;
-    float *value_dst = (local ? a.local_values : a.salient_values) + (b * slots + slot) * d;
+    TR *key_dst = keys + slot * d;
+    TR *value_dst = values + slot * d;
     const float *entry = a.entries + b * a.entry_stride;
-    for (int64_t c = threadIdx.x; c < quads; c += kRingThreads) {
-        float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f), v = k;
-        if (token_valid) {
-            k = reinterpret_cast<const float4 *>(entry)[c];
-            v = reinterpret_cast<const float4 *>(entry + d)[c];
+    for (int64_t c = threadIdx.x; c < packets; c += kRingThreads) {
+        float k[W], v[W];
+#pragma unroll
+        for (int e = 0; e < W; ++e) {
+            k[e] = token_valid ? entry[c * W + e] : 0.0f;
+            v[e] = token_valid ? entry[d + c * W + e] : 0.0f;
         }
-        reinterpret_cast<float4 *>(key_dst)[c] = k;
-        reinterpret_cast<float4 *>(value_dst)[c] = v;
+        P::store(key_dst + c * W, k);
+        P::store(value_dst + c * W, v);
     }
     if (threadIdx.x == 0) (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
 }
@@ -346,18 +385,19 @@ extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *
 
 extern "C" int koemi_think_ring_decode_step(
     const float *queries, int64_t query_stride, const float *entries, int64_t entry_stride, const uint8_t *valid,
-    const float *surprise, float threshold, float *local_keys, float *local_values, uint8_t *local_valid,
-    const int64_t *local_head, float *salient_keys, float *salient_values, uint8_t *salient_valid,
+    const float *surprise, float threshold, void *local_keys, void *local_values, uint8_t *local_valid,
+    const int64_t *local_head, void *salient_keys, void *salient_values, uint8_t *salient_valid,
     int32_t *salient_head, int32_t *salient_count, void *local_out, void *salient_out, int64_t out_stride,
     float *novelty_out, uint8_t *admission_out, int64_t batch, int64_t width, int64_t local_slots,
-    int64_t salient_slots, int out_dtype, void *stream) {
+    int64_t salient_slots, int ring_dtype, int out_dtype, void *stream) {
     clear_error();
     if (batch < 0 || width < 0 || local_slots < 1 || salient_slots < 1) return fail(KOEMI_ERR_INVALID, "bad ring sizes");
     if (batch == 0) return KOEMI_OK;
-    if (width % 4 != 0 || query_stride % 4 != 0 || entry_stride % 4 != 0 || !aligned(queries, 16) ||
-        !aligned(entries, 16) || !aligned(local_keys, 16) || !aligned(salient_keys, 16) || !aligned(local_values, 16) ||
+    if (ring_dtype != KOEMI_F32 && ring_dtype != KOEMI_BF16) return fail(KOEMI_ERR_INVALID, "rings must be f32 or bf16");
+    const int64_t packet = ring_dtype == KOEMI_F32 ? 4 : 8;
+    if (width % packet != 0 || !aligned(local_keys, 16) || !aligned(salient_keys, 16) || !aligned(local_values, 16) ||
         !aligned(salient_values, 16)) {
-        return fail(KOEMI_ERR_UNSUPPORTED, "ring decode needs 16-byte aligned fp32 rows (width %% 4 == 0)");
+        return fail(KOEMI_ERR_UNSUPPORTED, "ring decode needs 16-byte aligned ring rows (width %% %lld == 0)", (long long)packet);
     }
     if (batch > 2147483647) return fail(KOEMI_ERR_INVALID, "too many streams");
     RingArgs args{queries, query_stride, entries, entry_stride, valid, surprise, threshold, local_keys, local_values,
@@ -377,10 +417,11 @@ extern "C" int koemi_think_ring_decode_step(
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };
+    const bool bf16_ring = ring_dtype == KOEMI_BF16;
     switch (out_dtype) {
-        case KOEMI_F32: return run(ring_decode_kernel<float>);
-        case KOEMI_BF16: return run(ring_decode_kernel<__nv_bfloat16>);
-        case KOEMI_F16: return run(ring_decode_kernel<__half>);
+        case KOEMI_F32: return bf16_ring ? run(ring_decode_kernel<__nv_bfloat16, float>) : run(ring_decode_kernel<float, float>);
+        case KOEMI_BF16: return bf16_ring ? run(ring_decode_kernel<__nv_bfloat16, __nv_bfloat16>) : run(ring_decode_kernel<float, __nv_bfloat16>);
+        case KOEMI_F16: return bf16_ring ? run(ring_decode_kernel<__nv_bfloat16, __half>) : run(ring_decode_kernel<float, __half>);
         default: return fail(KOEMI_ERR_INVALID, "ring outputs must be f32, f16 or bf16");
     }
 }

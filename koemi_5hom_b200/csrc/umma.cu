@@ -607,7 +607,7 @@ __global__ void split_k_reduce_kernel(const float *__restrict__ partials, int64_
 int64_t dense_splits(int64_t rows, int64_t n, int64_t k) {
     const int64_t tiles = ((rows + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
     const int64_t k_blocks = (k + kBK - 1) / kBK;
-    int64_t splits = (sm_count() + tiles - 1) / tiles;
+    int64_t splits = sm_count() / tiles;  // tiles x splits fits in one wave of CTAs
     const int64_t max_splits = k_blocks / 4 > 1 ? k_blocks / 4 : 1;  // at least 4 K blocks per split
     if (splits > max_splits) splits = max_splits;
     return splits < 1 ? 1 : splits;

@@ -60,17 +60,38 @@ class DecodeState:
     step_index: int
     layered: bool
 
+    @property
+    def ring_dtype(self) -> torch.dtype:
+        return self.blocks[0].local_keys.dtype
+
+    def clone(self) -> "DecodeState":
+        """A deep copy at new addresses (same ring layout and dtype)."""
+        blocks = [DecodeBlockState(**{f: getattr(b, f).clone() for f in DecodeBlockState.__dataclass_fields__})
+                  for b in self.blocks]
+        return DecodeState(blocks, self.local_head.clone(), self.last_token_ids.clone(), self.step_index, self.layered)
+
 
 def supports_decode_path(settings) -> bool:
-    """The in-place path covers the reference defaults and the config-5 stack;
-    the refine ablation ('herm') keeps the window path."""
-    return settings.ablation in ("no_refine", "no_surprise") and settings.embedding_size % 4 == 0
+    """The in-place path covers the reference defaults and the config-5 stack
+    (width a multiple of 8, so fp32 and bf16 ring rows pack in 16 bytes); the
+    refine ablation ('herm') keeps the window path."""
+    return settings.ablation in ("no_refine", "no_surprise") and settings.embedding_size % 8 == 0
 
 
-def from_koemi_state(state, local_slots: int, salient_slots: int) -> DecodeState:
+RING_DTYPES = (torch.float32, torch.bfloat16)
+
+
+def from_koemi_state(state, local_slots: int, salient_slots: int,
+                     ring_dtype: torch.dtype = torch.float32) -> DecodeState:
     """Import a static (ring-at-capacity) state: local rings keep their
     oldest-first order (head 0); each salient ring is packed to its admitted
-    entries, oldest first, at slots [0, count)."""
+    entries, oldest first, at slots [0, count).
+
+    ``ring_dtype`` is the storage type of the ring keys and values: fp32 (the
+    reference's state type) or bf16, which halves the ring traffic of a decode
+    step; the ring arithmetic is fp32 either way."""
+    if ring_dtype not in RING_DTYPES:
+        raise ValueError(f"ring_dtype must be one of {RING_DTYPES}")
     layers = state.layers if isinstance(state, LayeredKoemiState) else (state,)
     blocks = []
     for layer in layers:
@@ -85,11 +106,11 @@ def from_koemi_state(state, local_slots: int, salient_slots: int) -> DecodeState
             memory_normalizer=layer.memory_normalizer.float().contiguous().clone(),
             refine_basis=layer.refine_basis.float().contiguous().clone(),
             refine_normalizer=layer.refine_normalizer.float().contiguous().clone(),
-            local_keys=layer.local_keys.float().contiguous().clone(),
-            local_values=layer.local_values.float().contiguous().clone(),
+            local_keys=layer.local_keys.to(ring_dtype).contiguous().clone(),
+            local_values=layer.local_values.to(ring_dtype).contiguous().clone(),
             local_valid=layer.local_valid.contiguous().clone(),
-            salient_keys=layer.salient_keys.float().gather(1, gather).contiguous(),
-            salient_values=layer.salient_values.float().gather(1, gather).contiguous(),
+            salient_keys=layer.salient_keys.to(ring_dtype).gather(1, gather).contiguous(),
+            salient_values=layer.salient_values.to(ring_dtype).gather(1, gather).contiguous(),
             salient_valid=layer.salient_valid.gather(1, order).contiguous(),
             salient_head=torch.zeros_like(count),
             salient_count=count,
@@ -121,11 +142,11 @@ def to_koemi_state(dstate: DecodeState):
             memory_normalizer=block.memory_normalizer.clone(),
             refine_basis=block.refine_basis.clone(),
             refine_normalizer=block.refine_normalizer.clone(),
-            local_keys=block.local_keys.index_select(1, local_index),
-            local_values=block.local_values.index_select(1, local_index),
+            local_keys=block.local_keys.index_select(1, local_index).float(),
+            local_values=block.local_values.index_select(1, local_index).float(),
             local_valid=block.local_valid.index_select(1, local_index),
-            salient_keys=torch.where(keep, block.salient_keys.gather(1, gather), 0.0),
-            salient_values=torch.where(keep, block.salient_values.gather(1, gather), 0.0),
+            salient_keys=torch.where(keep, block.salient_keys.gather(1, gather).float(), 0.0),
+            salient_values=torch.where(keep, block.salient_values.gather(1, gather).float(), 0.0),
             salient_valid=present & block.salient_valid.gather(1, physical),
             last_token_ids=dstate.last_token_ids.clone(),
             step_index=dstate.step_index,
@@ -151,6 +172,7 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     x = model.embedding_weight.index_select(0, ids).float()
     concat_dtype = model.compute_dtype
     out_code = _native.dtype_code(concat_dtype)
+    ring_code = _native.dtype_code(dstate.ring_dtype)
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
         st = dstate.blocks[index]
@@ -178,7 +200,7 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
              float(s.salience_threshold), ptr(st.local_keys), ptr(st.local_values), ptr(st.local_valid),
              ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
              ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,
-             None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], out_code, stream)
+             None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], ring_code, out_code, stream)
         call("koemi_assoc_decode_step", ptr(assoc), assoc.shape[1], ptr(features), ptr(surprise), ptr(valid),
              ptr(st.memory_basis), ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d,
              s.memory_features, out_code, stream)

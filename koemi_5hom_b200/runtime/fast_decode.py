@@ -20,7 +20,8 @@ from dataclasses import dataclass, replace
 import torch
 from torch import Tensor
 
-from koemi_5hom_b200.model.decode import decode_step, from_koemi_state, supports_decode_path, to_koemi_state
+from koemi_5hom_b200.model.decode import (RING_DTYPES, decode_step, from_koemi_state, supports_decode_path,
+                                           to_koemi_state)
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
 from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
 
@@ -119,7 +120,7 @@ class BatchDecoder:
     """
 
     def __init__(self, model, *, capture_graph: bool = False, cache_expert_weights: bool = True,
-                 in_place: bool = True):
+                 in_place: bool = True, ring_dtype: torch.dtype = torch.float32):
         device = model.device
         if capture_graph and device.type != "cuda":
             raise RuntimeError("CUDA graph capture requires a model on a CUDA device")
@@ -127,6 +128,11 @@ class BatchDecoder:
         self.device = device
         self._capture_graph = capture_graph
         self._in_place = in_place and device.type == "cuda" and supports_decode_path(model.settings)
+        if ring_dtype not in RING_DTYPES:
+            raise ValueError(f"ring_dtype must be one of {RING_DTYPES}")
+        if ring_dtype != torch.float32 and not self._in_place:
+            raise ValueError("a bf16 ring needs the in-place decode path")
+        self._ring_dtype = ring_dtype
         self._graph: torch.cuda.CUDAGraph | None = None
         self._state = None       # window path: KoemiState / LayeredKoemiState
         self._dstate = None      # in-place path: DecodeState
@@ -153,7 +159,7 @@ class BatchDecoder:
         s = self.model.settings
         static = to_static_state(state, s.local_memory_size, s.salience_memory_size)
         if self._in_place:
-            self._dstate = from_koemi_state(static, s.local_memory_size, s.salience_memory_size)
+            self._dstate = from_koemi_state(static, s.local_memory_size, s.salience_memory_size, self._ring_dtype)
             self._state = None
         else:
             self._state = static
@@ -214,8 +220,7 @@ class BatchDecoder:
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
             if self._dstate is not None:
-                scratch = from_koemi_state(to_koemi_state(self._dstate), self.model.settings.local_memory_size,
-                                           self.model.settings.salience_memory_size)
+                scratch = self._dstate.clone()
                 for _ in range(GRAPH_WARMUP_STEPS):
                     decode_step(self.model, self._static_ids, scratch)
                 del scratch

@@ -45,15 +45,21 @@ def _logical_salient(sk, sv, head, count, slots):
     return sk[idx], sv[idx]
 
 
+@pytest.mark.parametrize("ring_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("batch,width,local_slots,salient_slots", [(7, 64, 16, 12), (256, 2048, 128, 128),
                                                                    (3, 128, 5, 9)])
-def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slots, cuda):
+def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slots, ring_dtype, cuda):
     c = _ring_case(batch, width, local_slots, salient_slots, seed=width)
+    # the kernel reads stored (possibly bf16) rows and computes in fp32, so the
+    # expectation is built from the stored values
+    for key in ("lk", "lv", "sk", "sv"):
+        c[key] = c[key].to(ring_dtype).float()
     head = 3 % local_slots
     threshold = 0.5
     dev = lambda x: x.to(cuda).contiguous()  # noqa: E731
-    lk, lv, lvalid = dev(c["lk"]), dev(c["lv"]), dev(c["lvalid"])
-    sk, sv, svalid = dev(c["sk"]), dev(c["sv"]), dev(c["svalid"])
+    ring = lambda x: x.to(device=cuda, dtype=ring_dtype).contiguous()  # noqa: E731
+    lk, lv, lvalid = ring(c["lk"]), ring(c["lv"]), dev(c["lvalid"])
+    sk, sv, svalid = ring(c["sk"]), ring(c["sv"]), dev(c["svalid"])
     s_head = torch.tensor(c["heads"], dtype=torch.int32, device=cuda)
     s_count = torch.tensor(c["counts"], dtype=torch.int32, device=cuda)
     local_head = torch.tensor([head], dtype=torch.int64, device=cuda)
@@ -68,7 +74,8 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
     _native.call("koemi_think_ring_decode_step", p(q_rows), 4 * width, p(entries), 2 * width, p(valid), p(surprise),
                  threshold, p(lk), p(lv), p(lvalid), p(local_head), p(sk), p(sv), p(svalid), p(s_head), p(s_count),
                  p(out[:, 2 * width:]), p(out[:, 3 * width:]), 4 * width, p(novelty), p(admission), batch, width,
-                 local_slots, salient_slots, _native.F32, torch.cuda.current_stream().cuda_stream)
+                 local_slots, salient_slots, _native.dtype_code(ring_dtype), _native.F32,
+                 torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     scale = 1.0 / math.sqrt(width)
     for b in range(batch):
@@ -96,7 +103,8 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
         # writes: the oldest local slot takes the (masked) new entry
         entry_k = c["entries"][b, :width] if c["valid"][b] else torch.zeros(width)
         entry_v = c["entries"][b, width:] if c["valid"][b] else torch.zeros(width)
-        assert torch.equal(lk[b, head].cpu(), entry_k) and torch.equal(lv[b, head].cpu(), entry_v)
+        entry_k, entry_v = entry_k.to(ring_dtype).float(), entry_v.to(ring_dtype).float()
+        assert torch.equal(lk[b, head].cpu().float(), entry_k) and torch.equal(lv[b, head].cpu().float(), entry_v)
         assert bool(lvalid[b, head]) == bool(c["valid"][b])
         # salient: the admitted sequence is the latest `salient_slots` of old + new
         admitted = bool(c["valid"][b]) and float(c["surprise"][b]) > threshold
@@ -105,7 +113,8 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
         if admitted:
             old_k = torch.cat((old_k, entry_k.unsqueeze(0)))[-salient_slots:]
             old_v = torch.cat((old_v, entry_v.unsqueeze(0)))[-salient_slots:]
-        new_k, new_v = _logical_salient(sk[b].cpu(), sv[b].cpu(), int(s_head[b]), int(s_count[b]), salient_slots)
+        new_k, new_v = _logical_salient(sk[b].cpu().float(), sv[b].cpu().float(), int(s_head[b]), int(s_count[b]),
+                                        salient_slots)
         assert torch.equal(new_k, old_k) and torch.equal(new_v, old_v)
 
 
@@ -192,6 +201,39 @@ def test_in_place_decoder_matches_window_decoder(name, dtype, steps, capture_gra
     for (mk, mv), (rk, rv) in zip(mine, theirs):
         assert mk.shape == rk.shape
         torch.testing.assert_close(mk, rk, rtol=1e-3, atol=1e-4)
+
+
+def test_bf16_rings_keep_greedy_tokens():
+    """bf16 ring storage (fp32 arithmetic) against the fp32 rings of the same
+    bf16 model: same greedy tokens as the reference golden, logits within 2e-2."""
+    fx, model = _build("c5_small", "bfloat16")
+    ids = fx["ids"].cuda()
+    sampler = TokenSampler(SamplingPolicy(greedy=True), model.device)
+    stored = fx["decode_tokens"].shape[1]
+    runs = []
+    for ring_dtype in (torch.float32, torch.bfloat16):
+        decoder = BatchDecoder(model, capture_graph=True, ring_dtype=ring_dtype)
+        logits = decoder.prefill(ids)
+        tokens, all_logits = [], []
+        for _ in range(stored):
+            token = sampler(logits)
+            tokens.append(token)
+            all_logits.append(logits.clone())
+            logits = decoder.step(token)
+        assert decoder._dstate.ring_dtype == ring_dtype
+        runs.append((torch.cat(tokens, 1), torch.stack(all_logits, 1)))
+    (t0, l0), (t1, l1) = runs
+    assert torch.equal(t1.cpu(), fx["decode_tokens"][:, :stored])
+    assert torch.equal(t1, t0)
+    torch.testing.assert_close(l1, l0, rtol=2e-2, atol=2e-2)
+
+
+def test_bf16_ring_needs_in_place_path():
+    fx, model = _build("c1_t065", "float32")
+    with pytest.raises(ValueError, match="in-place"):
+        BatchDecoder(model, in_place=False, ring_dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="ring_dtype"):
+        BatchDecoder(model, ring_dtype=torch.float16)
 
 
 def test_state_round_trip_through_decode_state(cuda):
