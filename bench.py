@@ -61,7 +61,8 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
-    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "expert_decode", "surprise_decode", "surprise_prefill"),
+    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "expert_decode", "surprise_decode", "surprise_prefill",
+                                    "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
     return p.parse_args(argv)
 
@@ -471,6 +472,31 @@ def run_op(args) -> None:
             moved = touched * 3 * d * h * 2 + pairs * (2 * d + 4 * h) * 2
             work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
             shape = f"config 5 decode step: {pairs} pairs, {touched} experts touched, d={d}, d_ff={h} (3.2 GB weights > L2)"
+    elif args.op == "dense_decode":  # the four dense projections of one config-5 decode block, 256 rows
+        shapes = {"gates": (4096, 2048), "local": (4096, 2048), "assoc": (6146, 2048), "fusion": (2048, 8192)}
+        sets = 4  # weight sets cycled so each launch reads its weights from HBM (4 x 75 MB > L2)
+        layers = [{name: ((torch.randn(n, k, device=device, generator=g) * 0.02).bfloat16(),
+                          torch.zeros(n, device=device, dtype=torch.bfloat16)) for name, (n, k) in shapes.items()}
+                  for _ in range(sets)]
+        inputs = {k: torch.randn(256, k, device=device, generator=g).bfloat16() for k in (2048, 8192)}
+        per = {}
+        for name, (n, k) in shapes.items():
+            counter = iter(range(1 << 30))
+            fn = lambda name=name, k=k: _ops.dense_projection(  # noqa: E731
+                inputs[k], *layers[next(counter) % sets][name])
+            t = _time_op(fn, args.steps, args.warmup)
+            counter_lib = iter(range(1 << 30))
+            library = lambda name=name, k=k: torch.mm(  # noqa: E731
+                inputs[k], layers[next(counter_lib) % sets][name][0].t(), out_dtype=torch.float32)
+            t_lib = _time_op(library, args.steps, args.warmup)
+            per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + 256 * k * 2 + 256 * n * 4) / t / 1e9,
+                         "cublas_us_no_bias": t_lib * 1e6}
+        seconds = sum(v["us"] for v in per.values()) / 1e6
+        moved = sum(n * k * 2 + 256 * k * 2 + 256 * n * 4 for n, k in shapes.values())
+        work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = "config 5 decode block: 256 rows; gates 4096x2048, local 4096x2048, assoc 6146x2048, " \
+                "fusion 2048x8192 bf16 -> fp32"
+        extra = {"per_projection": per}
     else:  # surprise head: decode (256 rows) or one prefill window (32768 rows) of config 5
         rows = 256 if args.op == "surprise_decode" else 32768
         prior = torch.randn(rows, 2048, device=device, generator=g).bfloat16()
@@ -485,7 +511,7 @@ def run_op(args) -> None:
         else:
             work, unit, peak, bound = 2 * rows * 32767 * 2048 / seconds / 1e12, "TFLOP/s", tensor, "tensor"
         shape = f"{rows} rows x d=2048 against the 32767-row content head (134 MB bf16 > L2)"
-    line = {"op": args.op, "shape": shape, "us_per_launch": seconds * 1e6,
+    line = {"op": args.op, "shape": shape, "us_per_launch": seconds * 1e6, **locals().get("extra", {}),
             "roofline": {"bound": bound, "achieved": work, "peak": peak, "unit": unit, "frac": work / peak,
                          "peak_source": "MEASURED_PEAKS.json (burst)" if peaks else "fallback"}}
     emit(line, args)

@@ -234,16 +234,21 @@ KOEMI_API int koemi_think_ring_decode_step(
 /* One decode step of the rank-one associative memory, in place
  * (HierarchicalAssociativeMemory.project / read / update with the fast write
  * terms, model/memory.py:82-95,248-255,279-287, network.py:338-347):
- * `projections` rows (stride proj_stride) hold key | query | value_pre |
- * decay_pre | write_pre as produced by one GEMM; feature_logits is
- * [2, batch, features] (key then query logits of the feature projection).
+ * `projections` rows (stride proj_stride, 8-byte aligned) hold key | query |
+ * value_pre | decay_pre | write_pre as produced by one GEMM. The feature
+ * logits are either given in feature_logits ([2, batch, features]: key then
+ * query logits) or, when it is NULL, computed in the kernel from
+ * feature_weight [features, width] and feature_bias ([features] or NULL),
+ * both weight_dtype (f32, f16 or bf16), with the key / query rounded to
+ * weight_dtype and fp32 accumulation.
  * Writes the confidence-weighted read to read_out rows (stride read_stride, out_dtype)
  * from the memory before this step's write, then basis <- decay * basis +
  * w * tanh(value) f^T and normalizer <- decay * normalizer + w f, with
  * w = sigmoid(write_pre) (0.25 + 0.75 clamp(surprise)) (surprise may be NULL:
  * 0); invalid rows keep their memory. */
 KOEMI_API int koemi_assoc_decode_step(const float *projections, int64_t proj_stride,
-                            const float *feature_logits, const float *surprise, const uint8_t *valid,
+                            const float *feature_logits, const void *feature_weight, const void *feature_bias,
+                            int weight_dtype, const float *surprise, const uint8_t *valid,
                             float *basis, float *normalizer, void *read_out, int64_t read_stride,
                             int64_t batch, int64_t width, int64_t features, int out_dtype, void *stream);
 

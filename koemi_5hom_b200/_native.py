@@ -56,7 +56,8 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_think_ring_decode_step": (
         _int, (_p, _i64, _p, _i64, _p, _p, _f, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _i64,
                _i64, _i64, _i64, _int, _int, _p)),
-    "koemi_assoc_decode_step": (_int, (_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_assoc_decode_step": (_int, (_p, _i64, _p, _p, _p, _int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int,
+                                       _p)),
     "koemi_dense_projection_workspace": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_dense_projection": (_int, (_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
     "koemi_core_rmsnorm_silu_forward": (_int, (_p, _p, _p, _p, _i64, _i64, _f, _int, _p)),

@@ -19,7 +19,10 @@
 //                               (memory.py:82-95,248-255,279-287)
 #include <cmath>
 
+#include <type_traits>
+
 #include "common.cuh"
+#include "vec.cuh"
 
 namespace koemi {
 namespace {
@@ -167,7 +170,7 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
         }
         const TR *row = keys + s * d;
         float dot = 0.0f, kk = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
         for (int64_t c = lane; c < packets; c += 32) {
             float k[W];
             P::load(row + c * W, k);
@@ -202,17 +205,52 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     total = block_reduce(total, scratch, false);
     const float inv_total = any ? 1.0f / total : 0.0f;
 
+    // the slots with a nonzero weight, ascending (warp ballots; the cosine
+    // array is free once best_cos is reduced)
+    int32_t *live = reinterpret_cast<int32_t *>(cosine);
+    __shared__ int32_t live_count;
+    if (warp == 0) {
+        int32_t base = 0;
+        for (int64_t s0 = 0; s0 < slots; s0 += 32) {
+            const int64_t s = s0 + lane;
+            const bool nonzero = s < slots && score[s] != 0.0f;
+            const unsigned mask = __ballot_sync(0xffffffffu, nonzero);
+            if (nonzero) live[base + __popc(mask & ((1u << lane) - 1u))] = static_cast<int32_t>(s);
+            base += __popc(mask);
+        }
+        if (lane == 0) live_count = base;
+    }
+    __syncthreads();
+    const int32_t n_live = live_count;
+
     // pass 2: each thread owns packets of columns and sums the weighted values
+    // of the live slots in ascending order, kValueUnroll loads in flight
+    constexpr int kValueUnroll = 8;
     TO *out = static_cast<TO *>(local ? a.local_out : a.salient_out) + b * a.out_stride;
     for (int64_t c = threadIdx.x; c < packets; c += kRingThreads) {
         float acc[W];
 #pragma unroll
         for (int e = 0; e < W; ++e) acc[e] = 0.0f;
-        for (int64_t s = 0; s < slots; ++s) {
-            const float w = score[s];
-            if (w == 0.0f) continue;
+        int32_t i = 0;
+        for (; i + kValueUnroll <= n_live; i += kValueUnroll) {
+            float v[kValueUnroll][W], w[kValueUnroll];
+#pragma unroll
+            for (int u = 0; u < kValueUnroll; ++u) {
+                const int32_t slot = live[i + u];
+                w[u] = score[slot];
+                P::load(values + static_cast<int64_t>(slot) * d + c * W, v[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < kValueUnroll; ++u) {
+#pragma unroll
+                for (int e = 0; e < W; ++e) acc[e] = fmaf(w[u], v[u][e], acc[e]);
+            }
+        }
+        for (; i < n_live; ++i) {
+            const int32_t slot = live[i];
+            const float w = score[slot];
             float v[W];
-            P::load(values + s * d + c * W, v);
+            P::load(values + static_cast<int64_t>(slot) * d + c * W, v);
 #pragma unroll
             for (int e = 0; e < W; ++e) acc[e] = fmaf(w, v[e], acc[e]);
         }
@@ -267,25 +305,75 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
 // ----------------------------------------------------------- associative
 constexpr int kAssocThreads = 512;
 
+// Feature logits of the key (which = 0) and query (which = 1) rows of one
+// stream: W [m, d] (type TW) times the row rounded to TW (the numerics of a
+// TW x TW tensor-core projection with fp32 accumulation), plus bias. One warp
+// per (which, feature) task; d % 8 == 0 and 16-byte aligned weight rows use
+// 8-wide packets, 8-byte aligned fp32 projection rows.
+template <typename TW>
+__device__ void assoc_feature_logits(const float *__restrict__ proj, const TW *__restrict__ weight,
+                                     const TW *__restrict__ bias, float *__restrict__ logits, int64_t d,
+                                     int64_t m, bool vector) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t task = warp; task < 2 * m; task += kAssocThreads / 32) {
+        const int64_t which = task / m, j = task - which * m;
+        const float *x = proj + which * d;
+        const TW *w = weight + j * d;
+        float acc = 0.0f;
+        if (vector) {
+            for (int64_t c = lane * 8; c < d; c += 256) {
+                float wv[8];
+                if constexpr (std::is_same_v<TW, float>) {
+                    const float4 lo = __ldg(reinterpret_cast<const float4 *>(w + c));
+                    const float4 hi = __ldg(reinterpret_cast<const float4 *>(w + c + 4));
+                    wv[0] = lo.x; wv[1] = lo.y; wv[2] = lo.z; wv[3] = lo.w;
+                    wv[4] = hi.x; wv[5] = hi.y; wv[6] = hi.z; wv[7] = hi.w;
+                } else {
+                    unpack(__ldg(reinterpret_cast<const uint4 *>(w + c)), wv, TW{});
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const float2 xv = *reinterpret_cast<const float2 *>(x + c + e);
+                    acc = fmaf(to_acc(from_acc<TW>(xv.x)), wv[e], acc);
+                    acc = fmaf(to_acc(from_acc<TW>(xv.y)), wv[e + 1], acc);
+                }
+            }
+        } else {
+            for (int64_t c = lane; c < d; c += 32) acc = fmaf(to_acc(from_acc<TW>(x[c])), to_acc(w[c]), acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) logits[task] = acc + (bias != nullptr ? to_acc(bias[j]) : 0.0f);
+    }
+}
+
 // One CTA per stream. The memory row i (m features) is read as m/4 float4
 // packets by m/4 adjacent threads, which combine their partial dot products
 // with the query features by shuffles; the decayed write goes back in place.
-template <typename TO>
+// feature_logits ([2, batch, m]) may be NULL, in which case the logits come
+// from feature_weight / feature_bias in the kernel.
+template <typename TO, typename TW>
 __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float *__restrict__ projections, int64_t proj_stride, const float *__restrict__ feature_logits,
+    const TW *__restrict__ feature_weight, const TW *__restrict__ feature_bias, bool vector_features,
     const float *__restrict__ surprise, const uint8_t *__restrict__ valid, float *__restrict__ basis,
     float *__restrict__ normalizer, TO *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
     int64_t m) {
     extern __shared__ float shared[];
     float *f = shared;       // [m] write features
     float *qf = shared + m;  // [m] query features
+    float *own_logits = shared + 2 * m;  // [2, m] when computed here
     __shared__ float s_decay, s_write, s_den;
     const int64_t b = blockIdx.x;
     const float *proj = projections + b * proj_stride;
+    if (feature_logits == nullptr) {
+        assoc_feature_logits(proj, feature_weight, feature_bias, own_logits, d, m, vector_features);
+        __syncthreads();
+    }
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         for (int which = 0; which < 2; ++which) {
-            const float *logits = feature_logits + (which * batch + b) * m;
+            const float *logits = feature_logits != nullptr ? feature_logits + (which * batch + b) * m
+                                                            : own_logits + which * m;
             float mx = -INFINITY;
             for (int64_t j = lane; j < m; j += 32) mx = fmaxf(mx, logits[j]);
             mx = warp_max(mx);
@@ -427,22 +515,43 @@ extern "C" int koemi_think_ring_decode_step(
 }
 
 extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_stride, const float *feature_logits,
+                                       const void *feature_weight, const void *feature_bias, int weight_dtype,
                                        const float *surprise, const uint8_t *valid, float *basis, float *normalizer,
                                        void *read_out, int64_t read_stride, int64_t batch, int64_t width,
                                        int64_t features, int out_dtype, void *stream) {
     clear_error();
     if (batch < 0 || width < 0 || features < 1 || features > kAssocThreads) return fail(KOEMI_ERR_INVALID, "bad associative sizes");
     if (batch == 0) return KOEMI_OK;
+    if (feature_logits == nullptr && feature_weight == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "either feature_logits or feature_weight must be given");
+    }
     if (features % 4 == 0 && !aligned(basis, 16)) return fail(KOEMI_ERR_UNSUPPORTED, "basis must be 16-byte aligned");
-    const size_t smem = 2 * static_cast<size_t>(features) * sizeof(float);
+    const bool vector = width % 8 == 0 && aligned(feature_weight, 16) && aligned(projections, 8) && proj_stride % 2 == 0;
+    const size_t smem = 4 * static_cast<size_t>(features) * sizeof(float);
     const unsigned grid = static_cast<unsigned>(batch);
     cudaStream_t s = as_stream(stream);
+    auto run = [&](auto *out_type, auto *weight_type) -> int {
+        using TO = std::remove_pointer_t<decltype(out_type)>;
+        using TW = std::remove_pointer_t<decltype(weight_type)>;
+        assoc_decode_kernel<TO, TW><<<grid, kAssocThreads, smem, s>>>(
+            projections, proj_stride, feature_logits, static_cast<const TW *>(feature_weight),
+            static_cast<const TW *>(feature_bias), vector, surprise, valid, basis, normalizer,
+            static_cast<TO *>(read_out), read_stride, batch, width, features);
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    };
+    auto with_weight = [&](auto *out_type) -> int {
+        switch (feature_logits != nullptr ? KOEMI_F32 : weight_dtype) {
+            case KOEMI_F32: return run(out_type, static_cast<float *>(nullptr));
+            case KOEMI_BF16: return run(out_type, static_cast<__nv_bfloat16 *>(nullptr));
+            case KOEMI_F16: return run(out_type, static_cast<__half *>(nullptr));
+            default: return fail(KOEMI_ERR_INVALID, "feature weights must be f32, f16 or bf16");
+        }
+    };
     switch (out_dtype) {
-        case KOEMI_F32: assoc_decode_kernel<float><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<float *>(read_out), read_stride, batch, width, features); break;
-        case KOEMI_BF16: assoc_decode_kernel<__nv_bfloat16><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<__nv_bfloat16 *>(read_out), read_stride, batch, width, features); break;
-        case KOEMI_F16: assoc_decode_kernel<__half><<<grid, kAssocThreads, smem, s>>>(projections, proj_stride, feature_logits, surprise, valid, basis, normalizer, static_cast<__half *>(read_out), read_stride, batch, width, features); break;
+        case KOEMI_F32: return with_weight(static_cast<float *>(nullptr));
+        case KOEMI_BF16: return with_weight(static_cast<__nv_bfloat16 *>(nullptr));
+        case KOEMI_F16: return with_weight(static_cast<__half *>(nullptr));
         default: return fail(KOEMI_ERR_INVALID, "associative read output must be f32, f16 or bf16");
     }
-    KOEMI_LAUNCH_CHECK();
-    return KOEMI_OK;
 }

@@ -242,6 +242,97 @@ __global__ __launch_bounds__(kSortThreads) void digit_scatter_kernel(
     }
 }
 
+// The whole permutation in one CTA for decode-sized inputs (pairs <=
+// kSmallPairs, experts < kSmallBuckets): keys, bucket histogram, exclusive
+// scan (= segment offsets), the same stable round-based scatter as
+// digit_scatter_kernel, and the finishing outputs. The result equals the
+// multi-kernel radix path (a stable counting sort has one answer).
+constexpr int kSmallThreads = 1024;
+constexpr int kSmallWarps = kSmallThreads / 32;
+constexpr int64_t kSmallPairs = 4096;
+constexpr int64_t kSmallBuckets = 256;
+
+template <typename Index>
+__global__ __launch_bounds__(kSmallThreads) void small_permute_kernel(
+    const Index *__restrict__ assignments, const uint8_t *__restrict__ valid, int64_t pairs, int64_t top_k,
+    int64_t experts, int64_t *__restrict__ segment_offsets, int64_t *__restrict__ sorted_rows,
+    int64_t *__restrict__ sorted_experts, int64_t *__restrict__ pair_positions,
+    int32_t *__restrict__ sorted_pairs_out) {
+    extern __shared__ int32_t shared[];
+    const int buckets = static_cast<int>(experts) + 1;  // keys in [0, experts]; experts = dropped
+    const int n = static_cast<int>(pairs);
+    int32_t *keys = shared;                          // [pairs]
+    int32_t *sorted_keys = keys + n;                 // [pairs]
+    int32_t *sorted_pairs = sorted_keys + n;         // [pairs]
+    int32_t *running = sorted_pairs + n;             // [buckets]
+    int32_t *warp_counts = running + buckets;        // [kSmallWarps][buckets]
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    for (int b = threadIdx.x; b < buckets; b += kSmallThreads) running[b] = 0;
+    for (int i = threadIdx.x; i < kSmallWarps * buckets; i += kSmallThreads) warp_counts[i] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < n; p += kSmallThreads) {
+        const int32_t key = pair_key(assignments, valid, p, top_k, experts);
+        keys[p] = key;
+        atomicAdd(&running[key], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the histogram; segment_offsets[e] = first index with key >= e
+        int32_t carry = 0;
+        for (int b0 = 0; b0 < buckets; b0 += 32) {
+            const int b = b0 + lane;
+            const int32_t v = b < buckets ? running[b] : 0;
+            int32_t inclusive = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t other = __shfl_up_sync(0xffffffffu, inclusive, o);
+                if (lane >= o) inclusive += other;
+            }
+            if (b < buckets) {
+                running[b] = carry + inclusive - v;
+                segment_offsets[b] = carry + inclusive - v;
+            }
+            carry += __shfl_sync(0xffffffffu, inclusive, 31);
+        }
+    }
+    __syncthreads();
+    const unsigned lower = (1u << lane) - 1u;
+    for (int base = 0; base < n; base += kSmallThreads) {
+        const int p = base + static_cast<int>(threadIdx.x);
+        const bool live = p < n;
+        const int32_t key = live ? keys[p] : 0;
+        const int digit = live ? key : -1 - lane;  // unique when dead
+        const unsigned same = __match_any_sync(0xffffffffu, digit);
+        const int rank = __popc(same & lower);
+        if (live && (same & lower) == 0) warp_counts[warp * buckets + digit] = __popc(same);
+        __syncthreads();
+        if (live) {
+            int32_t before = 0;
+            for (int w = 0; w < warp; ++w) before += warp_counts[w * buckets + digit];
+            const int32_t position = running[digit] + before + rank;
+            sorted_keys[position] = key;
+            sorted_pairs[position] = p;
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < buckets; b += kSmallThreads) {
+            int32_t total = 0;
+            for (int w = 0; w < kSmallWarps; ++w) {
+                total += warp_counts[w * buckets + b];
+                warp_counts[w * buckets + b] = 0;
+            }
+            running[b] += total;
+        }
+        __syncthreads();
+    }
+    for (int i = threadIdx.x; i < n; i += kSmallThreads) {
+        const int32_t pair = sorted_pairs[i];
+        sorted_pairs_out[i] = pair;
+        if (sorted_rows != nullptr) sorted_rows[i] = pair / top_k;
+        if (sorted_experts != nullptr) sorted_experts[i] = sorted_keys[i];
+        if (pair_positions != nullptr) pair_positions[pair] = i;
+    }
+}
+
 // segment_offsets[e] = first sorted index whose key >= e (keys are sorted).
 __global__ void segment_offsets_kernel(const int32_t *__restrict__ sorted_keys, int64_t pairs,
                                        int64_t experts, int64_t *__restrict__ offsets) {
@@ -541,36 +632,57 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
     int32_t *keys_b = reinterpret_cast<int32_t *>(ws + l.keys_b);
     int32_t *values_b = reinterpret_cast<int32_t *>(ws + l.values_b);
     int32_t *counts = reinterpret_cast<int32_t *>(ws + l.counts);
-    const unsigned pair_blocks = static_cast<unsigned>(ceil_div(pairs, 256));
-    if (assignment_dtype == KOEMI_I64) {
-        build_keys_kernel<int64_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int64_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
-    } else if (assignment_dtype == KOEMI_I32) {
-        build_keys_kernel<int32_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int32_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
-    } else {
+    if (assignment_dtype != KOEMI_I64 && assignment_dtype != KOEMI_I32) {
         return fail(KOEMI_ERR_INVALID, "assignments must be int32 or int64");
     }
-    KOEMI_LAUNCH_CHECK();
-    const size_t count_smem = static_cast<size_t>(l.buckets) * sizeof(int32_t);
-    const size_t scatter_smem = static_cast<size_t>(l.buckets) * (kSortWarps + 1) * sizeof(int32_t);
-    if (scatter_smem > 48 * 1024) {
-        KOEMI_CUDA_TRY(cudaFuncSetAttribute(digit_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(scatter_smem)));
+    const bool wide_index = assignment_dtype == KOEMI_I64;
+    if (pairs <= kSmallPairs && expert_count < kSmallBuckets) {
+        const int buckets = static_cast<int>(expert_count) + 1;
+        const size_t smem = (3 * static_cast<size_t>(pairs) + static_cast<size_t>(buckets) * (kSmallWarps + 1)) *
+                            sizeof(int32_t);
+        auto launch = [&](auto kernel, const auto *typed) -> int {
+            if (smem > 48 * 1024) {
+                KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    static_cast<int>(smem)));
+            }
+            kernel<<<1, kSmallThreads, smem, s>>>(typed, valid, pairs, top_k, expert_count, segment_offsets,
+                                                  sorted_rows, sorted_experts, pair_positions, values_a);
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
+        };
+        const int rc = wide_index ? launch(small_permute_kernel<int64_t>, static_cast<const int64_t *>(assignments))
+                                  : launch(small_permute_kernel<int32_t>, static_cast<const int32_t *>(assignments));
+        if (rc != KOEMI_OK) return rc;
+    } else {
+        const unsigned pair_blocks = static_cast<unsigned>(ceil_div(pairs, 256));
+        if (wide_index) {
+            build_keys_kernel<int64_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int64_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
+        } else {
+            build_keys_kernel<int32_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int32_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
+        }
+        KOEMI_LAUNCH_CHECK();
+        const size_t count_smem = static_cast<size_t>(l.buckets) * sizeof(int32_t);
+        const size_t scatter_smem = static_cast<size_t>(l.buckets) * (kSortWarps + 1) * sizeof(int32_t);
+        if (scatter_smem > 48 * 1024) {
+            KOEMI_CUDA_TRY(cudaFuncSetAttribute(digit_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(scatter_smem)));
+        }
+        for (int pass = 0; pass < l.passes; ++pass) {
+            const int shift = pass * kDigitBits;
+            digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
+            KOEMI_LAUNCH_CHECK();
+            exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets);
+            KOEMI_LAUNCH_CHECK();
+            digit_scatter_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, scatter_smem, s>>>(
+                keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b);
+            KOEMI_LAUNCH_CHECK();
+            int32_t *t = keys_a; keys_a = keys_b; keys_b = t;
+            t = values_a; values_a = values_b; values_b = t;
+        }
+        segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
+        KOEMI_LAUNCH_CHECK();
+        finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
+        KOEMI_LAUNCH_CHECK();
     }
-    for (int pass = 0; pass < l.passes; ++pass) {
-        const int shift = pass * kDigitBits;
-        digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
-        KOEMI_LAUNCH_CHECK();
-        exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets);
-        KOEMI_LAUNCH_CHECK();
-        digit_scatter_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, scatter_smem, s>>>(
-            keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b);
-        KOEMI_LAUNCH_CHECK();
-        int32_t *t = keys_a; keys_a = keys_b; keys_b = t;
-        t = values_a; values_a = values_b; values_b = t;
-    }
-    segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
-    KOEMI_LAUNCH_CHECK();
-    finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
-    KOEMI_LAUNCH_CHECK();
     if (sorted_context != nullptr && width > 0) {
         const size_t es = dtype_size(context_dtype);
         const bool vector = (width * es) % 16 == 0 && aligned(context, 16) && aligned(sorted_context, 16);

@@ -10,8 +10,9 @@ tensor of the state at a fixed address and updates it in place:
 - working state, associative bases and normalisers are overwritten in place.
 
 A step is then: per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
--> surprise (tcgen05 head GEMM + online LSE) -> local/assoc/feature GEMMs ->
-``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` -> fusion GEMM
+-> surprise (tcgen05 head GEMM + online LSE) -> local/assoc GEMMs ->
+``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` (with the
+feature projection of key and query fused in) -> fusion GEMM
 (its input rows are written in place by the three kernels) -> rms_norm ->
 route / permute / grouped expert MLP / combine; then the head GEMM. With fixed
 addresses the whole step is one CUDA graph with no copy-back of the state.
@@ -173,10 +174,14 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     concat_dtype = model.compute_dtype
     out_code = _native.dtype_code(concat_dtype)
     ring_code = _native.dtype_code(dstate.ring_dtype)
+    if s.ablation == "no_surprise":
+        targets = None
+    else:
+        targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
         st = dstate.blocks[index]
-        u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, torch.float32)
+        u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, model.compute_dtype)
         pre = model._linear(u, block.gates_weight, block.gates_bias)
         # fusion input rows, written in place by the step kernels: h | memory | local | salient
         concat = torch.empty(batch, 4 * d, dtype=concat_dtype, device=device)
@@ -184,16 +189,13 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), ptr(prior), ptr(concat), 4 * d,
              batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
         h = concat[:, :d]
-        if s.ablation == "no_surprise":
+        if targets is None:
             surprise = None
         else:
-            targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
             surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
                                                     torch.float32)
         local = model._linear(h, block.local_weight, block.local_bias)
         assoc = model._linear(h, block.assoc_weight, block.assoc_bias)
-        features = model._linear(torch.stack((assoc[:, :d], assoc[:, d:2 * d])), block.feature_weight,
-                                 block.feature_bias)
         scored = surprise if surprise is not None else torch.zeros(batch, device=device)
         # ring queries read the fp32 working state (the new h) directly
         call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), 2 * d, ptr(valid), ptr(scored),
@@ -201,9 +203,10 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
              ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
              ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,
              None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], ring_code, out_code, stream)
-        call("koemi_assoc_decode_step", ptr(assoc), assoc.shape[1], ptr(features), ptr(surprise), ptr(valid),
-             ptr(st.memory_basis), ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d,
-             s.memory_features, out_code, stream)
+        # the feature projection of key and query runs inside the kernel
+        call("koemi_assoc_decode_step", ptr(assoc), assoc.stride(0), None, ptr(block.feature_weight),
+             ptr(block.feature_bias), _native.dtype_code(block.feature_weight.dtype), ptr(surprise), ptr(valid), ptr(st.memory_basis),
+             ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d, s.memory_features, out_code, stream)
         fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
         if s.expert_count == 0:

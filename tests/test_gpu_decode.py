@@ -118,11 +118,20 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
         assert torch.equal(new_k, old_k) and torch.equal(new_v, old_v)
 
 
-def test_assoc_decode_step_matches_oracle(cuda):
+@pytest.mark.parametrize("feature_source", ["logits", "f32_weight", "bf16_weight"])
+def test_assoc_decode_step_matches_oracle(feature_source, cuda):
     g = torch.Generator().manual_seed(3)
     batch, d, m = 9, 256, 16
     proj = torch.randn(batch, 3 * d + 2, generator=g)
     feats = torch.randn(2, batch, m, generator=g)
+    feature_weight = torch.randn(m, d, generator=g) * 0.1
+    feature_bias = torch.randn(m, generator=g) * 0.1
+    if feature_source != "logits":
+        # logits of the in-kernel projection: key / query rounded to the weight type, fp32 accumulation
+        wd = torch.float32 if feature_source == "f32_weight" else torch.bfloat16
+        feature_weight, feature_bias = feature_weight.to(wd), feature_bias.to(wd)
+        rows = torch.stack((proj[:, :d], proj[:, d:2 * d])).to(wd).double()
+        feats = (rows @ feature_weight.double().T + feature_bias.double()).float()
     surprise = torch.rand(batch, generator=g)
     valid = torch.rand(batch, generator=g) > 0.2
     basis = torch.randn(batch, d, m, generator=g) * 0.1
@@ -132,10 +141,12 @@ def test_assoc_decode_step_matches_oracle(cuda):
     # keep every device input alive until the kernel has run: a temporary's
     # memory can be handed to the next argument's copy as soon as it is freed
     proj_dev, feats_dev, surprise_dev, valid_dev = proj.to(cuda), feats.to(cuda), surprise.to(cuda), valid.to(cuda)
+    w_dev, wb_dev = feature_weight.to(cuda), feature_bias.to(cuda)
     p = _native.ptr
-    _native.call("koemi_assoc_decode_step", p(proj_dev), 3 * d + 2, p(feats_dev), p(surprise_dev), p(valid_dev),
-                 p(b_dev), p(n_dev), p(out[:, d:]), 4 * d, batch, d, m, _native.F32,
-                 torch.cuda.current_stream().cuda_stream)
+    logits_ptr = p(feats_dev) if feature_source == "logits" else None
+    _native.call("koemi_assoc_decode_step", p(proj_dev), 3 * d + 2, logits_ptr, p(w_dev), p(wb_dev),
+                 _native.dtype_code(w_dev.dtype), p(surprise_dev), p(valid_dev), p(b_dev), p(n_dev), p(out[:, d:]),
+                 4 * d, batch, d, m, _native.F32, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     f, qf = torch.softmax(feats[0].double(), -1), torch.softmax(feats[1].double(), -1)
     decay = 2.0 ** -12 + (1 - 2.0 ** -11) * torch.sigmoid(proj[:, 3 * d].double())

@@ -68,6 +68,31 @@ def test_permutation_is_bit_exact_with_stable_argsort(golden_ops, key, cuda):
     assert bool((sorted_context[n_valid:] == 0).all())
 
 
+@pytest.mark.parametrize("tokens,top_k,experts", [(2048, 2, 64), (2049, 2, 64), (1365, 3, 255), (1365, 3, 256),
+                                                  (256, 2, 64), (1, 1, 1), (4096, 1, 7)])
+def test_single_cta_and_radix_permutations_agree_with_oracle(tokens, top_k, experts, cuda):
+    """Both sides of the one-CTA limit (4096 pairs, 255 experts), with dropped
+    tokens, out-of-range ids and repeated slots in the assignments."""
+    g = torch.Generator().manual_seed(tokens * 7 + experts)
+    assignments = torch.randint(-1, experts + 2, (tokens, top_k), generator=g)
+    if top_k > 1:
+        assignments[::5, 1] = assignments[::5, 0]
+    valid = torch.rand(tokens, generator=g) > 0.1
+    order, rows_ref, keys_ref, offsets_ref, positions_ref = ops.permute_topk(assignments.numpy(), valid.numpy(),
+                                                                            experts)
+    context = torch.randn(tokens, 16, generator=g)
+    for dtype in (torch.int64, torch.int32):
+        sorted_context, rows, keys, offsets, positions = _ops.permute_topk(
+            context.to(cuda), assignments.to(device=cuda, dtype=dtype), valid.to(cuda), experts, True)
+        assert np.array_equal(rows.cpu().numpy(), rows_ref)
+        assert np.array_equal(keys.cpu().numpy(), keys_ref)
+        assert np.array_equal(offsets.cpu().numpy(), offsets_ref)
+        assert np.array_equal(positions.cpu().numpy(), positions_ref)
+        n_valid = int(offsets_ref[-1])
+        assert torch.equal(sorted_context[:n_valid].cpu(), context[torch.from_numpy(rows_ref[:n_valid])])
+        assert bool((sorted_context[n_valid:] == 0).all())
+
+
 def test_permute_front_and_combine_preserve_stable_pairs(cuda):
     """tests/cuda/test_moe_cuda.py:60-82 of the reference, restated."""
     context = torch.arange(12, device=cuda, dtype=torch.float32).reshape(3, 4)
