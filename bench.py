@@ -410,16 +410,33 @@ def run_b200(args) -> None:
 
 
 # ------------------------------------------------------------- operators
-def _time_op(fn, steps: int, warmup: int) -> float:
+def _time_op(fn, steps: int, warmup: int, graph: bool = False) -> float:
+    """Seconds per call of fn, CUDA events on the current stream. With
+    graph=True the calls are captured into one CUDA graph and replayed, so
+    host dispatch cost does not hide the kernel time of short launches."""
     import torch
     for _ in range(max(warmup, 1)):
         fn()
     stream = torch.cuda.current_stream()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g):
+                for _ in range(steps):
+                    fn()
+        stream.wait_stream(side)
+        g.replay()
+        run = g.replay
+    else:
+        def run():
+            for _ in range(steps):
+                fn()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record(stream)
-    for _ in range(steps):
-        fn()
+    run()
     stop.record(stream)
     torch.cuda.synchronize()
     return start.elapsed_time(stop) / 1000.0 / steps
@@ -484,11 +501,11 @@ def run_op(args) -> None:
             counter = iter(range(1 << 30))
             fn = lambda name=name, k=k: _ops.dense_projection(  # noqa: E731
                 inputs[k], *layers[next(counter) % sets][name])
-            t = _time_op(fn, args.steps, args.warmup)
+            t = _time_op(fn, args.steps, args.warmup, graph=True)
             counter_lib = iter(range(1 << 30))
             library = lambda name=name, k=k: torch.mm(  # noqa: E731
                 inputs[k], layers[next(counter_lib) % sets][name][0].t(), out_dtype=torch.float32)
-            t_lib = _time_op(library, args.steps, args.warmup)
+            t_lib = _time_op(library, args.steps, args.warmup, graph=True)
             per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + 256 * k * 2 + 256 * n * 4) / t / 1e9,
                          "cublas_us_no_bias": t_lib * 1e6}
         seconds = sum(v["us"] for v in per.values()) / 1e6

@@ -321,6 +321,7 @@ __device__ void assoc_feature_logits(const float *__restrict__ proj, const TW *_
         const TW *w = weight + j * d;
         float acc = 0.0f;
         if (vector) {
+#pragma unroll 8
             for (int64_t c = lane * 8; c < d; c += 256) {
                 float wv[8];
                 if constexpr (std::is_same_v<TW, float>) {
@@ -408,23 +409,34 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
         const int64_t rows_per_pass = kAssocThreads / parts;
         const float4 qv = reinterpret_cast<const float4 *>(qf)[part];
         const float4 fv = reinterpret_cast<const float4 *>(f)[part];
-        // uniform trip count: every lane reaches the shuffles
-        for (int64_t base = 0; base < d; base += rows_per_pass) {
-            const int64_t i = base + threadIdx.x / parts;
-            const bool live = i < d;
-            float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            float4 *cell = reinterpret_cast<float4 *>(rows + (live ? i : 0) * m) + part;
-            if (live) x = *cell;
-            float num = x.x * qv.x + x.y * qv.y + x.z * qv.z + x.w * qv.w;
-            for (int o = 1; o < parts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
-            if (!live) continue;
-            const float v = write * tanhf(proj[2 * d + i]);
-            x.x = decay * x.x + v * fv.x;
-            x.y = decay * x.y + v * fv.y;
-            x.z = decay * x.z + v * fv.z;
-            x.w = decay * x.w + v * fv.w;
-            *cell = x;
-            if (part == 0) read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
+        // uniform trip count: every lane reaches the shuffles; kPasses rows
+        // per thread are loaded before any is used, to keep loads in flight
+        constexpr int kPasses = 4;
+        for (int64_t base = 0; base < d; base += kPasses * rows_per_pass) {
+            float4 x[kPasses];
+            float value[kPasses];
+#pragma unroll
+            for (int u = 0; u < kPasses; ++u) {
+                const int64_t i = base + u * rows_per_pass + threadIdx.x / parts;
+                const bool live = i < d;
+                x[u] = live ? *(reinterpret_cast<const float4 *>(rows + i * m) + part) : make_float4(0.f, 0.f, 0.f, 0.f);
+                value[u] = live ? proj[2 * d + i] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < kPasses; ++u) {
+                const int64_t i = base + u * rows_per_pass + threadIdx.x / parts;
+                float num = x[u].x * qv.x + x[u].y * qv.y + x[u].z * qv.z + x[u].w * qv.w;
+                for (int o = 1; o < parts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
+                if (i >= d) continue;
+                const float v = write * tanhf(value[u]);
+                float4 y;
+                y.x = decay * x[u].x + v * fv.x;
+                y.y = decay * x[u].y + v * fv.y;
+                y.z = decay * x[u].z + v * fv.z;
+                y.w = decay * x[u].w + v * fv.w;
+                *(reinterpret_cast<float4 *>(rows + i * m) + part) = y;
+                if (part == 0) read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
+            }
         }
     } else {
         for (int64_t i = threadIdx.x; i < d; i += kAssocThreads) {

@@ -11,6 +11,8 @@
 // digit, least significant digit first (an LSD radix sort).
 // Reference: moe/moe_kernels.cu:45-145 (route, pair keys, CUB 64-bit radix
 // sort, histogram, scan, gathers) and model/experts.py:171-216,261-289.
+#include <type_traits>
+
 #include "vec.cuh"
 
 namespace koemi {
@@ -529,6 +531,90 @@ __global__ void combine_residual_rmsnorm_vec_kernel(const float *__restrict__ co
     }
 }
 
+// Four consecutive expert outputs as fp32 (8-byte aligned).
+template <typename T>
+__device__ __forceinline__ float4 load_quad(const T *p) {
+    if constexpr (std::is_same<T, float>::value) {
+        const float2 lo = __ldg(reinterpret_cast<const float2 *>(p));
+        const float2 hi = __ldg(reinterpret_cast<const float2 *>(p + 2));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+        union {
+            uint2 u;
+            T h[4];
+        } in;
+        in.u = __ldg(reinterpret_cast<const uint2 *>(p));
+        return make_float4(to_acc(in.h[0]), to_acc(in.h[1]), to_acc(in.h[2]), to_acc(in.h[3]));
+    }
+}
+
+// The vector combine with the row held in registers (NQ quads per lane):
+// every load of a row is issued before its values are used, and the output
+// is written once.
+template <typename T, int NQ>
+__global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__ context, const T *__restrict__ y,
+                                                       const int64_t *__restrict__ positions,
+                                                       const int64_t *__restrict__ segment_offsets,
+                                                       const float *__restrict__ weights,
+                                                       const uint8_t *__restrict__ valid,
+                                                       const float *__restrict__ norm_weight,
+                                                       float *__restrict__ out, int64_t tokens, int64_t width,
+                                                       int64_t top_k, int64_t experts, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= tokens) return;
+    const float4 *cr = reinterpret_cast<const float4 *>(context + row * width);
+    float4 *orow = reinterpret_cast<float4 *>(out + row * width);
+    const int64_t quads = width / 4;
+    float4 u[NQ];
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) {
+        const int64_t c = lane + 32 * i;
+        u[i] = c < quads ? __ldg(cr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (valid != nullptr && valid[row] == 0) {
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+            const int64_t c = lane + 32 * i;
+            if (c < quads) orow[c] = u[i];
+        }
+        return;
+    }
+    const int64_t valid_pairs = segment_offsets[experts];
+    for (int64_t s = 0; s < top_k; ++s) {
+        const int64_t pos = positions[row * top_k + s];
+        if (pos < 0 || pos >= valid_pairs) continue;
+        const T *src = y + pos * width;
+        const float scale = weights != nullptr ? weights[row * top_k + s] : 1.0f / static_cast<float>(top_k);
+        float4 e[NQ];
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+            const int64_t c = lane + 32 * i;
+            e[i] = c < quads ? load_quad(src + c * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+            u[i].x += e[i].x * scale;
+            u[i].y += e[i].y * scale;
+            u[i].z += e[i].z * scale;
+            u[i].w += e[i].w * scale;
+        }
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) sum += u[i].x * u[i].x + u[i].y * u[i].y + u[i].z * u[i].z + u[i].w * u[i].w;
+    sum = warp_sum(sum);
+    const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+    const float4 *wq = reinterpret_cast<const float4 *>(norm_weight);
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) {
+        const int64_t c = lane + 32 * i;
+        if (c >= quads) continue;
+        const float4 w = __ldg(wq + c);
+        orow[c] = make_float4(u[i].x * (inv * w.x), u[i].y * (inv * w.y), u[i].z * (inv * w.z), u[i].w * (inv * w.w));
+    }
+}
+
 // Workspace layout of the permutation.
 struct PermuteLayout {
     int64_t blocks;
@@ -755,6 +841,27 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     cudaStream_t s = as_stream(stream);
     const bool vector = width % 4 == 0 && top_k <= 8 && aligned(context, 16) && aligned(out, 16) &&
                         aligned(norm_weight, 16) && aligned(expert_out, 8);
+    const int64_t quads_per_lane = ceil_div(width / 4, 32);
+    if (vector && quads_per_lane <= 16) {
+        auto run = [&](auto kernel, const auto *typed) -> int {
+            kernel<<<blocks, threads, 0, s>>>(context, typed, pair_positions, segment_offsets, weights, valid,
+                                              norm_weight, out, tokens, width, top_k, expert_count, eps);
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
+        };
+        auto by_width = [&](const auto *typed) -> int {
+            using T = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
+            if (quads_per_lane <= 4) return run(combine_residual_rmsnorm_cached_kernel<T, 4>, typed);
+            if (quads_per_lane <= 8) return run(combine_residual_rmsnorm_cached_kernel<T, 8>, typed);
+            return run(combine_residual_rmsnorm_cached_kernel<T, 16>, typed);
+        };
+        switch (dtype) {
+            case KOEMI_F32: return by_width(static_cast<const float *>(expert_out));
+            case KOEMI_F16: return by_width(static_cast<const __half *>(expert_out));
+            case KOEMI_BF16: return by_width(static_cast<const __nv_bfloat16 *>(expert_out));
+            default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
+        }
+    }
     if (vector) {
         switch (dtype) {
             case KOEMI_F32: combine_residual_rmsnorm_vec_kernel<float><<<blocks, threads, 0, s>>>(context, static_cast<const float *>(expert_out), pair_positions, segment_offsets, weights, valid, norm_weight, out, tokens, width, top_k, expert_count, eps); break;

@@ -49,8 +49,33 @@ __device__ __forceinline__ void finish_pack(float (&v)[Pack<T>::kWidth], const f
     }
 }
 
-// Cached vector path: NV packets per lane stay in registers.
-template <typename T, int kMode, int NV>
+// Stores W fp32 results (one input packet's worth) as TO: 16 bytes, 8 bytes
+// (four 16-bit values from an fp32 packet) or 32 bytes (eight fp32 values
+// from a 16-bit packet).
+template <typename TO, int W>
+__device__ __forceinline__ void store_converted(TO *dst, const float (&v)[W]) {
+    if constexpr (sizeof(TO) * W == 16) {
+        store_stream(dst, pack(v, TO()));
+    } else if constexpr (sizeof(TO) * W == 8) {
+        union {
+            TO h[4];
+            uint2 u;
+        } out;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) out.h[e] = from_acc<TO>(v[e]);
+        *reinterpret_cast<uint2 *>(dst) = out.u;
+    } else {
+        static_assert(sizeof(TO) * W == 32, "unsupported packet conversion");
+        const float lo[4] = {v[0], v[1], v[2], v[3]};
+        const float hi[4] = {v[4], v[5], v[6], v[7]};
+        store_stream(dst, pack(lo, float()));
+        store_stream(dst + 4, pack(hi, float()));
+    }
+}
+
+// Cached vector path: NV packets of T per lane stay in registers; the
+// output may be another floating type TO.
+template <typename T, typename TO, int kMode, int NV>
 __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
     constexpr int W = Pack<T>::kWidth;
     const int lane = threadIdx.x & 31;
@@ -61,7 +86,7 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
     const T *rr = args.residual ? static_cast<const T *>(args.residual) + row * args.hidden : nullptr;
     const T *gr = kMode == kGated ? static_cast<const T *>(args.gate) + row * args.hidden : nullptr;
     const T *wr = static_cast<const T *>(args.weight);
-    T *yr = static_cast<T *>(args.y) + row * args.hidden;
+    TO *yr = static_cast<TO *>(args.y) + row * args.hidden;
     const bool keep = kMode != kPlain || args.keep == nullptr || args.keep[row] != 0;
 
     uint4 raw[NV];
@@ -99,14 +124,20 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
         const int64_t p = lane + 32 * i;
         if (p < packets) {
             if (!keep) {
-                store_stream(yr + p * W, raw[i]);
+                if constexpr (std::is_same<T, TO>::value) {
+                    store_stream(yr + p * W, raw[i]);
+                } else {
+                    float x[W];
+                    unpack(raw[i], x, T());
+                    store_converted(yr + p * W, x);
+                }
                 continue;
             }
             float w[W], g[W];
             unpack(load_cached(wr + p * W), w, T());
             if (kMode == kGated) unpack(graw[i], g, T());
             finish_pack<T, kMode>(v[i], w, g, inv);
-            store_stream(yr + p * W, pack(v[i], T()));
+            store_converted(yr + p * W, v[i]);
         }
     }
 }
@@ -161,30 +192,28 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
     const int threads = rows_per_block * 32;
     const unsigned blocks = static_cast<unsigned>(ceil_div(args.rows, rows_per_block));
     constexpr int W = Pack<T>::kWidth;
-    bool vector_ok = std::is_same<T, TO>::value && args.hidden % W == 0 && aligned(args.x, 16) &&
+    bool vector_ok = args.hidden % W == 0 && aligned(args.x, 16) &&
                      aligned(args.weight, 16) && aligned(args.y, 16) &&
                      (args.residual == nullptr || aligned(args.residual, 16)) &&
                      (kMode != kGated || aligned(args.gate, 16));
-    if constexpr (std::is_same<T, TO>::value) {
+    if (vector_ok) {
+        const int64_t per_lane = ceil_div(args.hidden / W, 32);
+        if (per_lane <= 1) {
+            rms_rows_cached<T, TO, kMode, 1><<<blocks, threads, 0, stream>>>(args);
+        } else if (per_lane <= 2) {
+            rms_rows_cached<T, TO, kMode, 2><<<blocks, threads, 0, stream>>>(args);
+        } else if (per_lane <= 4) {
+            rms_rows_cached<T, TO, kMode, 4><<<blocks, threads, 0, stream>>>(args);
+        } else if (per_lane <= 8) {
+            rms_rows_cached<T, TO, kMode, 8><<<blocks, threads, 0, stream>>>(args);
+        } else if (per_lane <= 16 && sizeof(T) == 4 && kMode == kPlain) {
+            rms_rows_cached<T, TO, kMode, 16><<<blocks, threads, 0, stream>>>(args);
+        } else {
+            vector_ok = false;
+        }
         if (vector_ok) {
-            const int64_t per_lane = ceil_div(args.hidden / W, 32);
-            if (per_lane <= 1) {
-                rms_rows_cached<T, kMode, 1><<<blocks, threads, 0, stream>>>(args);
-            } else if (per_lane <= 2) {
-                rms_rows_cached<T, kMode, 2><<<blocks, threads, 0, stream>>>(args);
-            } else if (per_lane <= 4) {
-                rms_rows_cached<T, kMode, 4><<<blocks, threads, 0, stream>>>(args);
-            } else if (per_lane <= 8) {
-                rms_rows_cached<T, kMode, 8><<<blocks, threads, 0, stream>>>(args);
-            } else if (per_lane <= 16 && sizeof(T) == 4 && kMode == kPlain) {
-                rms_rows_cached<T, kMode, 16><<<blocks, threads, 0, stream>>>(args);
-            } else {
-                vector_ok = false;
-            }
-            if (vector_ok) {
-                KOEMI_LAUNCH_CHECK();
-                return KOEMI_OK;
-            }
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
         }
     }
     rms_rows_scalar<T, TO, kMode><<<blocks, threads, 0, stream>>>(args);
