@@ -20,12 +20,16 @@
 //   kOutput  expert GEMM 2: y = hidden W_o^T + b_o (dtype).
 //   kSurprise head contraction: logits = prior W^T + b folded into per-row
 //            (max, sum exp, target logit) partials per 256-wide vocab tile.
+//   kDense / kDenseCluster  fp32 projection out = A W^T + b, optionally split
+//            along K, the splits reduced inside a thread-block cluster.
 // Grouped problems map tiles to (expert, row tile) on the device from
 // segment_offsets; rows past a segment's end are computed but never stored.
 //
 // Every mbarrier wait is bounded; a wait that runs out raises a CTA abort
 // flag, records KOEMI_ERR_TIMEOUT in the device status word and every role
 // leaves its loop, so the CTA frees its TMEM and exits. No multicast loads.
+#include <mutex>
+
 #include "vec.cuh"
 
 namespace koemi {
@@ -45,7 +49,16 @@ constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemColumns = 512;
 constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
 
-enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3 };
+enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3, kDenseCluster = 4 };
+
+// kDenseCluster: the K splits of one output tile run as one thread-block
+// cluster (one CTA per split); each CTA parks its fp32 accumulator in its own
+// shared memory, and after a cluster barrier CTA r sums column slice r over
+// all splits in split order through distributed shared memory (deterministic),
+// adds the bias and stores. Row stride of the parked accumulator, in floats
+// (padded so the per-row float4 stores of a warp hit distinct banks):
+constexpr int kAccStride = kBN + 4;
+static_assert(kBM * kAccStride * 4 <= kStages * kStageBytes, "parked accumulator must fit in the stage ring");
 
 struct UmmaArgs {
     CUtensorMap map_a;
@@ -127,6 +140,31 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 
 __device__ __forceinline__ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Cluster barrier over every thread of every CTA of the cluster, with
+// release/acquire ordering of shared-memory writes at cluster scope.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// float4 from the shared memory of CTA `rank` of this cluster, at the offset
+// that `local_addr` has in this CTA's shared memory.
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+
 // ------------------------------------------------------------- scheduling
 
 struct Tile {
@@ -143,7 +181,7 @@ struct Tile {
 template <int kProblem>
 __device__ __forceinline__ int64_t total_tiles(const UmmaArgs &a) {
     if (kProblem == kSurprise) return ((a.rows + kBM - 1) / kBM) * a.n_tiles;
-    if (kProblem == kDense) return ((a.rows + kBM - 1) / kBM) * a.n_tiles * a.splits;
+    if (kProblem == kDense || kProblem == kDenseCluster) return ((a.rows + kBM - 1) / kBM) * a.n_tiles * a.splits;
     return static_cast<int64_t>(a.tile_prefix[a.experts]) * a.n_tiles;
 }
 
@@ -153,6 +191,19 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
     const int64_t k_blocks = (a.k + kBK - 1) / kBK;
     tile.k_begin = 0;
     tile.k_end = k_blocks;
+    if (kProblem == kDenseCluster) {
+        // split fastest: the CTAs of one cluster are the splits of one tile
+        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        tile.split = t % a.splits;
+        const int64_t rest = t / a.splits;
+        tile.m_tile = rest % m_tiles;
+        tile.n = rest / m_tiles;
+        tile.k_begin = tile.split * a.k_per_split;
+        tile.k_end = min(k_blocks, tile.k_begin + a.k_per_split);
+        tile.row0 = tile.m_tile * kBM;
+        tile.row_end = a.rows;
+        return tile;
+    }
     if (kProblem == kDense) {
         // m fastest, so CTAs running together share one weight tile from L2
         const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
@@ -384,6 +435,23 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                         }
                     }
                 }
+            } else if (kProblem == kDenseCluster) {
+                // park the accumulator row in this CTA's shared memory (the
+                // stage ring is idle: every load was consumed by the MMAs
+                // that acc_full waited for)
+                float *parked = reinterpret_cast<float *>(stages) + (quarter * 32 + lane) * kAccStride;
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t y[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, y);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        reinterpret_cast<float4 *>(parked + c * 32)[q] =
+                            make_float4(__uint_as_float(y[4 * q]), __uint_as_float(y[4 * q + 1]),
+                                        __uint_as_float(y[4 * q + 2]), __uint_as_float(y[4 * q + 3]));
+                    }
+                }
             } else if (kProblem == kDense) {
                 // splits == 1: out = acc + bias (fp32, row stride out_stride);
                 // splits  > 1: partials[split][row][col] = acc, reduced later
@@ -467,6 +535,49 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (kProblem == kDenseCluster) {
+        // every thread of every CTA reaches both cluster barriers, aborted or not
+        cluster_sync_all();
+        if (!*abort && blockIdx.x < tiles) {
+            const Tile tile = tile_at<kProblem>(args, blockIdx.x);
+            const uint32_t rank = cluster_ctarank();
+            const int64_t splits = args.splits;
+            constexpr int kQuads = kBN / 4;
+            const int q_begin = static_cast<int>(rank * kQuads / splits);
+            const int q_count = static_cast<int>((rank + 1) * kQuads / splits) - q_begin;
+            const T *bias = static_cast<const T *>(args.bias0);
+            float *out = static_cast<float *>(args.out);
+            const uint32_t parked_base = smem_addr(stages);
+            for (int idx = threadIdx.x; idx < kBM * q_count; idx += kThreads) {
+                const int r = idx / q_count;
+                const int q = q_begin + (idx - r * q_count);
+                const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
+                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                for (int64_t sp = 0; sp < splits; ++sp) {
+                    const float4 v = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
+                    acc.x += v.x;
+                    acc.y += v.y;
+                    acc.z += v.z;
+                    acc.w += v.w;
+                }
+                const int64_t row = tile.row0 + r;
+                const int64_t col = tile.n * kBN + q * 4;
+                if (row >= args.rows || col >= args.n_out) continue;
+                float o[4] = {acc.x, acc.y, acc.z, acc.w};
+                if (bias != nullptr) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[e] += col + e < args.n_out ? to_acc(bias[col + e]) : 0.0f;
+                }
+                float *dst = out + row * args.out_stride + col;
+                if (col + 4 <= args.n_out && aligned16(dst)) {
+                    *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
+                }
+            }
+        }
+        cluster_sync_all();
+    }
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemColumns));
@@ -503,6 +614,62 @@ int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stre
     kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(args);
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
+}
+
+// Exactly `ctas` CTAs in clusters of `cluster` (one tile per CTA).
+template <int kProblem>
+int launch_clustered(const UmmaArgs &args, int dtype, int64_t ctas, int cluster, cudaStream_t stream) {
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16> : umma_gemm_kernel<kProblem, __half>;
+    KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
+    config.blockDim = dim3(kThreads, 1, 1);
+    config.dynamicSmemBytes = kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, kernel, args));
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+// CTAs of the dense cluster kernel that can be resident at once in clusters
+// of `cluster` (GPC boundaries leave some SMs out), cached per device.
+int64_t resident_cluster_ctas(int cluster) {
+    static std::mutex mutex;
+    static int64_t cache[64][9] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64 || cluster < 1 || cluster > 8) return 0;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (cache[device][cluster] != 0) return cache[device][cluster];
+    auto kernel = umma_gemm_kernel<kDenseCluster, __nv_bfloat16>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(cluster), 1, 1);
+    config.blockDim = dim3(kThreads, 1, 1);
+    config.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &config) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = 0;
+    }
+    cache[device][cluster] = static_cast<int64_t>(clusters) * cluster;
+    return cache[device][cluster];
 }
 
 bool umma_shape_ok(const void *p, int64_t k) { return k % 8 == 0 && aligned(p, 16) && k > 0; }
@@ -589,28 +756,16 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     return KOEMI_OK;
 }
 
-__global__ void split_k_reduce_kernel(const float *__restrict__ partials, int64_t splits, int64_t rows, int64_t n,
-                                      const void *__restrict__ bias, int bias_dtype, float *__restrict__ out,
-                                      int64_t out_stride) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= rows * n) return;
-    const int64_t r = i / n, c = i - r * n;
-    float acc = 0.0f;
-    if (bias != nullptr) {
-        acc = bias_dtype == KOEMI_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(bias)[c])
-                                       : __half2float(static_cast<const __half *>(bias)[c]);
-    }
-    for (int64_t s = 0; s < splits; ++s) acc += partials[(s * rows + r) * n + c];
-    out[r * out_stride + c] = acc;
-}
-
+// K splits of a dense projection: the largest S <= 8 whose tiles x S CTAs
+// are resident at once in clusters of S, with at least 4 K blocks per split.
 int64_t dense_splits(int64_t rows, int64_t n, int64_t k) {
     const int64_t tiles = ((rows + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
     const int64_t k_blocks = (k + kBK - 1) / kBK;
-    int64_t splits = sm_count() / tiles;  // tiles x splits fits in one wave of CTAs
-    const int64_t max_splits = k_blocks / 4 > 1 ? k_blocks / 4 : 1;  // at least 4 K blocks per split
-    if (splits > max_splits) splits = max_splits;
-    return splits < 1 ? 1 : splits;
+    for (int64_t splits = 8; splits > 1; --splits) {
+        if (k_blocks < 4 * splits) continue;
+        if (tiles * splits <= resident_cluster_ctas(static_cast<int>(splits))) return splits;
+    }
+    return 1;
 }
 
 int64_t surprise_umma_slices(int64_t rows, int64_t width, int64_t content_vocab, int dtype) {
@@ -669,10 +824,12 @@ DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
 }  // namespace
 
 extern "C" size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64_t k, int dtype) {
+    // the K splits are reduced in distributed shared memory: no scratch
+    (void)rows;
+    (void)n;
+    (void)k;
     (void)dtype;
-    if (rows <= 0 || n <= 0 || k <= 0) return 256;
-    const DensePlan plan = dense_plan(rows, n, k);
-    return plan.splits > 1 ? static_cast<size_t>(plan.splits) * rows * n * sizeof(float) : 256;
+    return 256;
 }
 
 extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
@@ -686,10 +843,9 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
         rows >= (int64_t(1) << 31) || n >= (int64_t(1) << 31)) {
         return fail(KOEMI_ERR_UNSUPPORTED, "dense projection needs K and the A row stride to be multiples of 8 and 16-byte aligned operands");
     }
+    (void)workspace;
+    (void)workspace_bytes;
     const DensePlan plan = dense_plan(rows, n, k);
-    if (plan.splits > 1 && workspace_bytes < koemi_dense_projection_workspace(rows, n, k, dtype)) {
-        return fail(KOEMI_ERR_WORKSPACE, "dense projection needs %zu workspace bytes", koemi_dense_projection_workspace(rows, n, k, dtype));
-    }
     cudaStream_t s = as_stream(stream);
     UmmaArgs args{};
     const CUtensorMapDataType type = dtype == KOEMI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -712,18 +868,11 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     args.k_per_split = plan.k_per_split;
     args.bias0 = bias;
     args.out = out;
-    args.partials = plan.splits > 1 ? static_cast<float *>(workspace) : nullptr;
+    args.partials = nullptr;
     args.status = device_status_word();
     args.idesc = make_idesc(dtype);
     const int64_t tiles = ((rows + kBM - 1) / kBM) * args.n_tiles * plan.splits;
-    rc = launch<kDense>(args, dtype, tiles, s);
-    if (rc != KOEMI_OK) return rc;
-    if (plan.splits > 1) {
-        const int64_t total = rows * n;
-        split_k_reduce_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, s>>>(
-            args.partials, plan.splits, rows, n, bias, dtype, out, out_stride);
-        KOEMI_LAUNCH_CHECK();
-    }
-    return KOEMI_OK;
+    if (plan.splits > 1) return launch_clustered<kDenseCluster>(args, dtype, tiles, static_cast<int>(plan.splits), s);
+    return launch<kDense>(args, dtype, tiles, s);
 }
 
