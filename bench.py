@@ -4,17 +4,20 @@
 
 Workload (config 5): HERM stack with vocabulary 32768, d_model 2048, 24
 blocks, memory features 16, 128 local + 128 salient ring slots, 64 experts
-top-2 (d_ff 4096), bf16 weights, fp32 state; 256 streams per GPU, each with a
-2048-token prompt of uniform random ids (PAD excluded), prefilled untimed,
-then greedy decode. Weights are seeded random (N(0, 0.02)), inputs synthetic.
-One step = one decode step of every stream (256 tokens per GPU). The timed
-region is K CUDA-graph replays of that step between barriers, timed with CUDA
-events on the decode stream, max over ranks; every step reads ~100 GB, far
-more than the 126 MB L2, so no flush is needed.
+top-2 (d_ff 4096), bf16 weights, fp32 state, bf16 ring storage; 256 streams
+in total, each with a 2048-token prompt of uniform random ids (PAD excluded),
+prefilled untimed, then greedy decode. Weights are seeded random
+(N(0, 0.02)), inputs synthetic. One step = one decode step of every stream
+(256 tokens). The timed region is K CUDA-graph replays of that step between
+barriers, timed with CUDA events on the decode stream, max over ranks; every
+step reads far more than the 126 MB L2, so no flush is needed.
 
-Multi-GPU: one process per GPU (torchrun), each rank decodes its own 256
-streams with a full replica (data parallel, no collective on the step):
-``scaling`` is "weak".
+Multi-GPU (config 5): one process per GPU (torchrun); the 256 streams are
+split data-parallel (256/N per rank) and the 64 experts expert-parallel
+(64/N per rank, two NCCL all-to-alls of the token rows per MoE block and
+step, captured in the step's CUDA graph): the total work is fixed, so
+``scaling`` is "strong". ``--weak`` keeps 256 streams per GPU with a full
+replica per rank instead (no collective on the step).
 
 ``--impl reference`` times the CPU oracle port of the same decode step on the
 host cores (rank 0 only; the reference is Python and does not travel to the
@@ -48,7 +51,10 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--layers", type=int, default=24)
-    p.add_argument("--streams", type=int, default=256, help="decode streams per GPU")
+    p.add_argument("--streams", type=int, default=256,
+                   help="decode streams in total (split over the ranks); per GPU with --weak")
+    p.add_argument("--weak", action="store_true",
+                   help="weak scaling: --streams per GPU, full model replica per rank, no expert parallelism")
     p.add_argument("--prompt-len", type=int, default=2048)
     p.add_argument("--vocab", type=int, default=32768)
     p.add_argument("--width", type=int, default=2048)
@@ -75,19 +81,42 @@ def settings_for(args):
                          layer_count=args.layers, compute_dtype="bfloat16")
 
 
+def streams_per_rank(args, world: int) -> int:
+    if args.weak:
+        return args.streams
+    if args.streams % world != 0:
+        raise SystemExit(f"--streams {args.streams} does not split over {world} ranks")
+    return args.streams // world
+
+
+def expert_parallel(args, world: int) -> bool:
+    return world > 1 and not args.weak
+
+
 def workload_config(args, world):
+    per_rank = streams_per_rank(args, world)
+    parallelism = f"dp{world}+ep{world}" if expert_parallel(args, world) else f"dp{world}"
     return {"workload": "config5_herm_batched_decode", "model": "HERM (random init, N(0,0.02))",
             "layers": args.layers, "vocab": args.vocab, "d_model": args.width, "d_ff": 2 * args.width,
             "experts": args.experts, "top_k": args.top_k, "local_slots": 128, "salient_slots": 128,
-            "streams_per_gpu": args.streams, "global_batch": args.streams * world, "prompt_len": args.prompt_len,
-            "seq_len": 1, "salience_threshold": args.threshold, "parallelism": f"dp{world}",
+            "streams_per_gpu": per_rank, "global_batch": per_rank * world, "prompt_len": args.prompt_len,
+            "seq_len": 1, "salience_threshold": args.threshold, "parallelism": parallelism,
+            "experts_per_gpu": args.experts // world if expert_parallel(args, world) else args.experts,
             "weights": "bf16", "state": "fp32", "rings": args.ring_dtype, "l2": "per-step reads >> 126 MB L2 (no flush needed)"}
 
 
-def prompts_for(args, rank, device):
+def prompts_for(args, rank, world, device):
+    """This rank's streams: rows [rank * n, (rank + 1) * n) of one seeded set
+    of prompts for all streams (weak scaling: a seeded set per rank)."""
     import torch
-    g = torch.Generator().manual_seed(1000 + rank)
-    ids = torch.randint(0, args.vocab - 1, (args.streams, args.prompt_len), generator=g)
+    per_rank = streams_per_rank(args, world)
+    if args.weak:
+        g = torch.Generator().manual_seed(1000 + rank)
+        ids = torch.randint(0, args.vocab - 1, (per_rank, args.prompt_len), generator=g)
+    else:
+        g = torch.Generator().manual_seed(1000)
+        ids = torch.randint(0, args.vocab - 1, (per_rank * world, args.prompt_len), generator=g)
+        ids = ids[rank * per_rank:(rank + 1) * per_rank]
     return torch.where(ids >= 256, ids + 1, ids).to(device)
 
 
@@ -222,8 +251,8 @@ def run_reference(args) -> None:
     value = result["value"]
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.cpu_sample_streams / value * 1000.0,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args, 1),
+            "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": workload_config(args, world),
             "cpu_baseline": {"kind": "port", "cores": result["cores"], "sample": result["sample"], "value": value,
                              "unit": UNIT},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -255,29 +284,36 @@ def count_native_kernels(model, decoder, token) -> int:
     return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "koemi" in e.name)
 
 
-def measure_expert_mlp(model, decoder, token, repeats: int = 20) -> dict:
-    """Time the dominant kernel (grouped expert MLP of block 0) alone on a real
-    decode step's sorted pairs, CUDA events on its stream."""
+def measure_expert_mlp(model, args, world: int, repeats: int = 20) -> dict:
+    """Time the dominant kernel (grouped expert MLP of block 0, this rank's
+    experts) alone, CUDA events on its stream, on the pairs a decode step of
+    all streams routes to those experts (a seeded draw of ids: the owner's
+    rows under expert parallelism, all pairs on one GPU)."""
     import torch
     from koemi_5hom_b200.cuda_kernels import _ops
     s = model.settings
     block = model.blocks[0]
+    local = block.expert_gate_weight.shape[0]
+    first = block.expert_first
+    tokens = streams_per_rank(args, world) * world if expert_parallel(args, world) else streams_per_rank(args, world)
     g = torch.Generator(device="cuda").manual_seed(5)
-    context = torch.randn(token.shape[0], s.embedding_size, device="cuda", generator=g).bfloat16()
-    prev = torch.randint(0, s.vocabulary_size, token.shape, device="cuda", generator=g)
-    valid = torch.ones(token.shape[0], dtype=torch.bool, device="cuda")
-    assignments = _ops.route_topk(token.reshape(-1), prev.reshape(-1), valid, s.expert_count, s.expert_top_k)
-    sc, _, se, offsets, _ = _ops.permute_topk(context, assignments, valid, s.expert_count, True)
-    args = (sc, se, offsets, block.expert_gate_weight, block.expert_gate_bias, block.expert_value_weight,
-            block.expert_value_bias, block.expert_output_weight, block.expert_output_bias)
+    context = torch.randn(tokens, s.embedding_size, device="cuda", generator=g).bfloat16()
+    ids = torch.randint(0, s.vocabulary_size, (tokens,), device="cuda", generator=g)
+    prev = torch.randint(0, s.vocabulary_size, (tokens,), device="cuda", generator=g)
+    valid = torch.ones(tokens, dtype=torch.bool, device="cuda")
+    assignments = _ops.route_topk(ids, prev, valid, s.expert_count, s.expert_top_k)
+    owned = (assignments >= first) & (assignments < first + local)
+    local_ids = torch.where(owned, assignments - first, -1)
+    sc, _, se, offsets, _ = _ops.permute_topk(context, local_ids, valid, local, True)
+    args_mlp = (sc, se, offsets) + block.expert_weights()
     for _ in range(3):
-        _ops.grouped_expert_mlp(*args)
+        _ops.grouped_expert_mlp(*args_mlp)
     stream = torch.cuda.current_stream()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record(stream)
     for _ in range(repeats):
-        _ops.grouped_expert_mlp(*args)
+        _ops.grouped_expert_mlp(*args_mlp)
     stop.record(stream)
     torch.cuda.synchronize()
     seconds = start.elapsed_time(stop) / 1000.0 / repeats
@@ -309,9 +345,14 @@ def run_b200(args) -> None:
     _native.ensure_device(device)
     wall_start = time.perf_counter()
 
-    model = KoemiModel(settings_for(args), device=device)
+    shard = None
+    if expert_parallel(args, world):
+        from koemi_5hom_b200.model.expert_parallel import ExpertShard
+        shard = ExpertShard.from_group(args.experts)
+    per_rank = streams_per_rank(args, world)
+    model = KoemiModel(settings_for(args), device=device, expert_shard=shard)
     model.initialize_parameters(seed=0)
-    prompts = prompts_for(args, rank, device)
+    prompts = prompts_for(args, rank, world, device)
     ring_dtype = torch.bfloat16 if args.ring_dtype == "bf16" else torch.float32
     decoder = BatchDecoder(model, capture_graph=True, ring_dtype=ring_dtype)
     torch.cuda.synchronize()
@@ -351,11 +392,11 @@ def run_b200(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         seconds = float(t.item())
     ms_per_step = seconds / args.steps * 1000.0
-    value = args.streams * world * args.steps / seconds
+    value = per_rank * world * args.steps / seconds
 
     # end to end: pinned host ids in, sampled ids back to the host, every step
-    host_in = torch.empty(args.streams, 1, dtype=torch.long).pin_memory()
-    host_out = torch.empty(args.streams, 1, dtype=torch.long).pin_memory()
+    host_in = torch.empty(per_rank, 1, dtype=torch.long).pin_memory()
+    host_out = torch.empty(per_rank, 1, dtype=torch.long).pin_memory()
     host_in.copy_(token.cpu())
     device_ids = torch.empty_like(token)
     if world > 1:
@@ -373,9 +414,9 @@ def run_b200(args) -> None:
         t = torch.tensor([e2e_seconds], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_seconds = float(t.item())
-    e2e_value = args.streams * world * args.steps / e2e_seconds
+    e2e_value = per_rank * world * args.steps / e2e_seconds
 
-    mlp = measure_expert_mlp(model, decoder, token)
+    mlp = measure_expert_mlp(model, args, world)
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
@@ -383,7 +424,8 @@ def run_b200(args) -> None:
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
         "clocks": clock_summary,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 8,

@@ -357,6 +357,34 @@ KOEMI_API int koemi_moe_combine_residual_rmsnorm(const float *context, const voi
                                        int64_t top_k, int64_t expert_count, float eps,
                                        int dtype, void *stream);
 
+/* ---------------------------------------------------- expert parallelism */
+
+/* Expert-parallel dispatch slab (no counterpart in the reference, which has
+ * no expert parallelism). Rank g of `ranks` owns experts [g * local_experts,
+ * (g + 1) * local_experts); the expert-major sorted pairs of
+ * koemi_moe_permute_topk (sorted_rows [pairs, width], sorted_experts,
+ * segment_offsets [ranks * local_experts + 1]) are therefore grouped by owner.
+ * slab [ranks * capacity, width]: row g * capacity + j = sorted row
+ * segment_offsets[g * local_experts] + j for j below owner g's count, with
+ * slab_experts[g * capacity + j] = the owner-local expert id; padding rows get
+ * slab_experts = -1 and are not written. capacity >= pairs (every pair may go
+ * to one owner), so nothing is ever dropped. The slab is what an equal-split
+ * all-to-all sends: block g to rank g. */
+KOEMI_API int koemi_moe_ep_pack(const void *sorted_rows, const int64_t *sorted_experts,
+                      const int64_t *segment_offsets, void *slab, int32_t *slab_experts,
+                      int64_t pairs, int64_t width, int64_t ranks, int64_t local_experts,
+                      int64_t capacity, int dtype, void *stream);
+
+/* Inverse of koemi_moe_ep_pack for the returned expert outputs: sorted_out
+ * [pairs, width] row i (i below segment_offsets[ranks * local_experts]) =
+ * slab row g * capacity + (i - segment_offsets[g * local_experts]) with
+ * g = sorted_experts[i] / local_experts; rows past the valid pairs are zero,
+ * as koemi_moe_grouped_expert_mlp leaves them. */
+KOEMI_API int koemi_moe_ep_unpack(const void *slab, const int64_t *sorted_experts,
+                        const int64_t *segment_offsets, void *sorted_out, int64_t pairs,
+                        int64_t width, int64_t ranks, int64_t local_experts, int64_t capacity,
+                        int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,8 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_moe_combine_workspace": (_sz, (_i64, _i64, _i64)),
     "koemi_moe_combine_topk": (
         _int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
+    "koemi_moe_ep_pack": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_moe_ep_unpack": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_moe_combine_residual_rmsnorm": (
         _int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _int, _p)),
 }

@@ -531,6 +531,64 @@ __global__ void combine_residual_rmsnorm_vec_kernel(const float *__restrict__ co
     }
 }
 
+// ------------------------------------------------------ expert parallelism
+// Rank g owns experts [g * local_experts, (g + 1) * local_experts), so the
+// expert-major sorted pairs are already grouped by owner. The dispatch slab
+// holds `capacity` rows per owner: slab row g * capacity + j is sorted row
+// segment_offsets[g * local_experts] + j while j is below that owner's count.
+
+// One warp per slab row: copy the sorted row (16-byte packets when `vector`)
+// and record its owner-local expert, -1 for padding rows.
+template <typename T>
+__global__ void ep_pack_kernel(const T *__restrict__ sorted_rows, const int64_t *__restrict__ sorted_experts,
+                               const int64_t *__restrict__ offsets, T *__restrict__ slab,
+                               int32_t *__restrict__ slab_experts, int64_t ranks, int64_t local_experts,
+                               int64_t capacity, int64_t width, bool vector) {
+    const int lane = threadIdx.x & 31;
+    const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (q >= ranks * capacity) return;
+    const int64_t g = q / capacity;
+    const int64_t i = offsets[g * local_experts] + (q - g * capacity);
+    const bool live = i < offsets[(g + 1) * local_experts];
+    if (lane == 0) slab_experts[q] = live ? static_cast<int32_t>(sorted_experts[i] - g * local_experts) : -1;
+    if (!live) return;
+    const T *src = sorted_rows + i * width;
+    T *dst = slab + q * width;
+    if (vector) {
+        constexpr int W = 16 / sizeof(T);
+        for (int64_t p = lane; p < width / W; p += 32) store_stream(dst + p * W, load_stream(src + p * W));
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = src[c];
+    }
+}
+
+// One warp per sorted row: take the row's result back from its owner's
+// returned slab rows; rows past the valid pairs are zero.
+template <typename T>
+__global__ void ep_unpack_kernel(const T *__restrict__ slab, const int64_t *__restrict__ sorted_experts,
+                                 const int64_t *__restrict__ offsets, T *__restrict__ sorted_out, int64_t pairs,
+                                 int64_t ranks, int64_t local_experts, int64_t capacity, int64_t width,
+                                 bool vector) {
+    const int lane = threadIdx.x & 31;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (i >= pairs) return;
+    T *dst = sorted_out + i * width;
+    const bool live = i < offsets[ranks * local_experts];
+    const T *src = nullptr;
+    if (live) {
+        const int64_t g = sorted_experts[i] / local_experts;
+        src = slab + (g * capacity + i - offsets[g * local_experts]) * width;
+    }
+    if (vector) {
+        constexpr int W = 16 / sizeof(T);
+        for (int64_t p = lane; p < width / W; p += 32) {
+            store_stream(dst + p * W, live ? load_stream(src + p * W) : make_uint4(0, 0, 0, 0));
+        }
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = live ? src[c] : from_acc<T>(0.0f);
+    }
+}
+
 // Four consecutive expert outputs as fp32 (8-byte aligned).
 template <typename T>
 __device__ __forceinline__ float4 load_quad(const T *p) {
@@ -941,4 +999,51 @@ extern "C" int koemi_moe_permute_topk_static(const void *context, const void *as
     return koemi_moe_permute_topk(context, assignments, valid, sorted_context, sorted_rows, sorted_experts,
                                   segment_offsets, pair_positions, tokens, width, top_k, expert_count, context_dtype,
                                   assignment_dtype, scratch, kStaticPermuteScratchBytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel dispatch and return slabs.
+
+extern "C" int koemi_moe_ep_pack(const void *sorted_rows, const int64_t *sorted_experts,
+                                 const int64_t *segment_offsets, void *slab, int32_t *slab_experts,
+                                 int64_t pairs, int64_t width, int64_t ranks, int64_t local_experts,
+                                 int64_t capacity, int dtype, void *stream) {
+    clear_error();
+    if (pairs < 0 || width < 1 || ranks < 1 || local_experts < 1) return fail(KOEMI_ERR_INVALID, "bad expert-parallel sizes");
+    if (capacity < pairs) return fail(KOEMI_ERR_INVALID, "capacity %lld is below the %lld pairs one owner may receive", (long long)capacity, (long long)pairs);
+    const int64_t rows = ranks * capacity;
+    if (rows == 0) return KOEMI_OK;
+    const size_t es = dtype_size(dtype);
+    const bool vector = (width * es) % 16 == 0 && aligned(sorted_rows, 16) && aligned(slab, 16);
+    const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: ep_pack_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float *>(sorted_rows), sorted_experts, segment_offsets, static_cast<float *>(slab), slab_experts, ranks, local_experts, capacity, width, vector); break;
+        case KOEMI_F16: ep_pack_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(sorted_rows), sorted_experts, segment_offsets, static_cast<__half *>(slab), slab_experts, ranks, local_experts, capacity, width, vector); break;
+        case KOEMI_BF16: ep_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(sorted_rows), sorted_experts, segment_offsets, static_cast<__nv_bfloat16 *>(slab), slab_experts, ranks, local_experts, capacity, width, vector); break;
+        default: return fail(KOEMI_ERR_INVALID, "rows must be f32, f16 or bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_moe_ep_unpack(const void *slab, const int64_t *sorted_experts, const int64_t *segment_offsets,
+                                   void *sorted_out, int64_t pairs, int64_t width, int64_t ranks,
+                                   int64_t local_experts, int64_t capacity, int dtype, void *stream) {
+    clear_error();
+    if (pairs < 0 || width < 1 || ranks < 1 || local_experts < 1) return fail(KOEMI_ERR_INVALID, "bad expert-parallel sizes");
+    if (capacity < pairs) return fail(KOEMI_ERR_INVALID, "capacity %lld is below the %lld pairs one owner may receive", (long long)capacity, (long long)pairs);
+    if (pairs == 0) return KOEMI_OK;
+    const size_t es = dtype_size(dtype);
+    const bool vector = (width * es) % 16 == 0 && aligned(slab, 16) && aligned(sorted_out, 16);
+    const unsigned blocks = static_cast<unsigned>(ceil_div(pairs, 8));
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: ep_unpack_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float *>(slab), sorted_experts, segment_offsets, static_cast<float *>(sorted_out), pairs, ranks, local_experts, capacity, width, vector); break;
+        case KOEMI_F16: ep_unpack_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(slab), sorted_experts, segment_offsets, static_cast<__half *>(sorted_out), pairs, ranks, local_experts, capacity, width, vector); break;
+        case KOEMI_BF16: ep_unpack_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(slab), sorted_experts, segment_offsets, static_cast<__nv_bfloat16 *>(sorted_out), pairs, ranks, local_experts, capacity, width, vector); break;
+        default: return fail(KOEMI_ERR_INVALID, "rows must be f32, f16 or bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
 }

@@ -370,3 +370,46 @@ def combine_residual_rmsnorm(context: Tensor, expert_out: Tensor, pair_positions
 @combine_residual_rmsnorm.register_fake
 def _(context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight, top_k, eps):
     return torch.empty_like(context)
+
+
+# ------------------------------------------------------- expert parallelism
+
+@torch.library.custom_op("koemi_b200::ep_pack", mutates_args=())
+def ep_pack(sorted_rows: Tensor, sorted_experts: Tensor, segment_offsets: Tensor, ranks: int, local_experts: int,
+            capacity: int) -> tuple[Tensor, Tensor]:
+    """Dispatch slab [ranks * capacity, width] and owner-local expert ids
+    (-1 = padding) of expert-major sorted rows; block g goes to rank g."""
+    sorted_rows, sorted_experts, segment_offsets = _dense(sorted_rows, sorted_experts, segment_offsets)
+    stream = _prepare(sorted_rows)
+    pairs, width = sorted_rows.shape
+    slab = torch.empty(ranks * capacity, width, dtype=sorted_rows.dtype, device=sorted_rows.device)
+    slab_experts = torch.empty(ranks * capacity, dtype=torch.int32, device=sorted_rows.device)
+    call("koemi_moe_ep_pack", ptr(sorted_rows), ptr(sorted_experts), ptr(segment_offsets), ptr(slab),
+         ptr(slab_experts), pairs, width, ranks, local_experts, capacity, dtype_code(sorted_rows.dtype), stream)
+    return slab, slab_experts
+
+
+@ep_pack.register_fake
+def _(sorted_rows, sorted_experts, segment_offsets, ranks, local_experts, capacity):
+    return (sorted_rows.new_empty(ranks * capacity, sorted_rows.shape[1]),
+            sorted_rows.new_empty(ranks * capacity, dtype=torch.int32))
+
+
+@torch.library.custom_op("koemi_b200::ep_unpack", mutates_args=())
+def ep_unpack(slab: Tensor, sorted_experts: Tensor, segment_offsets: Tensor, ranks: int, local_experts: int,
+              capacity: int) -> Tensor:
+    """Expert outputs back in the caller's sorted pair order (zero past the
+    valid pairs) from the returned slab."""
+    slab, sorted_experts, segment_offsets = _dense(slab, sorted_experts, segment_offsets)
+    stream = _prepare(slab)
+    pairs = sorted_experts.shape[0]
+    width = slab.shape[1]
+    out = torch.empty(pairs, width, dtype=slab.dtype, device=slab.device)
+    call("koemi_moe_ep_unpack", ptr(slab), ptr(sorted_experts), ptr(segment_offsets), ptr(out), pairs, width,
+         ranks, local_experts, capacity, dtype_code(slab.dtype), stream)
+    return out
+
+
+@ep_unpack.register_fake
+def _(slab, sorted_experts, segment_offsets, ranks, local_experts, capacity):
+    return slab.new_empty(sorted_experts.shape[0], slab.shape[1])

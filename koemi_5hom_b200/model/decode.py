@@ -220,9 +220,7 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             weights = None
         sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
             context.to(model.compute_dtype), assignments, valid, s.expert_count, True)
-        expert_out = _ops.grouped_expert_mlp(sorted_context, sorted_experts, offsets, block.expert_gate_weight,
-                                             block.expert_gate_bias, block.expert_value_weight, block.expert_value_bias,
-                                             block.expert_output_weight, block.expert_output_bias)
+        expert_out = model.expert_mlp(block, sorted_context, sorted_experts, offsets, mode="padded")
         x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid, bc["expert_norm"],
                                           s.expert_top_k, NORM_EPSILON)
     logits = model._linear(x, model.head_weight, model.head_bias)

@@ -39,6 +39,7 @@ import torch
 from torch import Tensor, nn
 
 from koemi_5hom_b200.cuda_kernels import _ops
+from koemi_5hom_b200.model.expert_parallel import ExpertShard, expert_parallel_mlp
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID, ModelSettings
 from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
 
@@ -123,9 +124,12 @@ def _dtype_of(name: str) -> torch.dtype:
 class HermBlock(nn.Module):
     """One block's parameters, packed so each input feeds a single GEMM."""
 
-    def __init__(self, settings: ModelSettings, dtype: torch.dtype, device: torch.device | None = None):
+    def __init__(self, settings: ModelSettings, dtype: torch.dtype, device: torch.device | None = None,
+                 expert_shard: ExpertShard | None = None):
         super().__init__()
-        d, m, e = settings.embedding_size, settings.memory_features, settings.expert_count
+        d, m = settings.embedding_size, settings.memory_features
+        self.expert_first = expert_shard.first if expert_shard is not None else 0
+        e = expert_shard.local_count if expert_shard is not None else settings.expert_count
         p = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=dtype, device=device), requires_grad=False)  # noqa: E731
         self.input_norm = p(d)
         self.gates_weight, self.gates_bias = p(2 * d, d), p(2 * d)            # retention | candidate
@@ -140,10 +144,17 @@ class HermBlock(nn.Module):
             self.expert_value_weight, self.expert_value_bias = p(e, 2 * d, d), p(e, 2 * d)
             self.expert_output_weight, self.expert_output_bias = p(e, d, 2 * d), p(e, d)
             self.expert_norm = p(d)
-            self.router_weight = p(e, d) if settings.expert_routing == "learned" else None
+            self.router_weight = p(settings.expert_count, d) if settings.expert_routing == "learned" else None
+
+    def expert_weights(self) -> tuple[Tensor, ...]:
+        """The six stacked expert tensors held by this block (this rank's
+        experts under expert parallelism), in grouped-MLP argument order."""
+        return (self.expert_gate_weight, self.expert_gate_bias, self.expert_value_weight, self.expert_value_bias,
+                self.expert_output_weight, self.expert_output_bias)
 
     def reference_map(self, settings: ModelSettings) -> list[tuple[str, str, int, int]]:
-        """(reference name, packed attribute, row start, row stop) per tensor."""
+        """(reference name, packed attribute, row start, row stop) per tensor;
+        expert tensors only for the experts this block holds."""
         d = settings.embedding_size
         out = [("input_normalizer.weight", "input_norm", 0, d)]
 
@@ -165,11 +176,13 @@ class HermBlock(nn.Module):
             linear("memory_refine_gate", "refine", 0, 1)
         linear("fusion_projection", "fusion", 0, d)
         out.append(("fusion_normalizer.weight", "fusion_norm", 0, d))
-        for e in range(settings.expert_count):
+        held = self.expert_gate_weight.shape[0] if settings.expert_count > 0 else 0
+        for local in range(held):
+            e = self.expert_first + local
             for ref, attr in (("gate_projection", "expert_gate"), ("value_projection", "expert_value"),
                               ("output_projection", "expert_output")):
-                out.append((f"experts.experts.{e}.{ref}.weight", f"{attr}_weight", e, e + 1))
-                out.append((f"experts.experts.{e}.{ref}.bias", f"{attr}_bias", e, e + 1))
+                out.append((f"experts.experts.{e}.{ref}.weight", f"{attr}_weight", local, local + 1))
+                out.append((f"experts.experts.{e}.{ref}.bias", f"{attr}_bias", local, local + 1))
         if settings.expert_count > 0:
             out.append(("experts.output_normalizer.weight", "expert_norm", 0, d))
             if settings.expert_routing == "learned":
@@ -180,15 +193,21 @@ class HermBlock(nn.Module):
 class KoemiModel(nn.Module):
     """HERM stack on libkoemi_b200 kernels with the reference model's interface."""
 
-    def __init__(self, settings, device: torch.device | str | None = None):
+    def __init__(self, settings, device: torch.device | str | None = None, expert_shard: ExpertShard | None = None):
+        """``expert_shard``: hold only this rank's experts and exchange token
+        rows with the other ranks at every MoE block (expert parallelism)."""
         super().__init__()
         self.settings = ModelSettings.coerce(settings)
         s = self.settings
+        if expert_shard is not None and (s.expert_count == 0 or expert_shard.expert_count != s.expert_count):
+            raise ValueError("the expert shard must split the model's experts")
+        self.expert_shard = expert_shard if expert_shard is not None and expert_shard.world > 1 else None
         self.compute_dtype = _dtype_of(s.compute_dtype)
         dev = torch.device(device) if device is not None else None
         p = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=self.compute_dtype, device=dev), requires_grad=False)  # noqa: E731
         self.embedding_weight = p(s.vocabulary_size, s.embedding_size)
-        self.blocks = nn.ModuleList(HermBlock(s, self.compute_dtype, dev) for _ in range(s.layer_count))
+        self.blocks = nn.ModuleList(HermBlock(s, self.compute_dtype, dev, self.expert_shard)
+                                    for _ in range(s.layer_count))
         self.head_weight = p(s.vocabulary_size, s.embedding_size)
         self.head_bias = p(s.vocabulary_size)
         self._cache: dict | None = None
@@ -220,22 +239,46 @@ class KoemiModel(nn.Module):
     def initialize_parameters(self, seed: int, init: str = "normal") -> None:
         """Seeded random parameters drawn on the parameters' device: N(0, 0.02)
         Linear weights, N(0, 0.002) biases, N(0, 1) embedding (zero PAD row),
-        norm weights 1 + 0.05 N(0, 1) (``init="normal"``, the config-5 recipe)."""
-        generator = torch.Generator(device=self.head_weight.device).manual_seed(seed)
+        norm weights 1 + 0.05 N(0, 1) (``init="normal"``, the config-5 recipe).
+        Every expert is drawn from its own seed, so a rank holding a slice of
+        the experts gets exactly the rows of the unsharded model."""
+        device = self.head_weight.device
+        generator = torch.Generator(device=device).manual_seed(seed)
+
+        def draw(tensor: Tensor, name: str, gen: torch.Generator) -> None:
+            if name.endswith("norm") or name.endswith("_norm"):
+                tensor.copy_(1.0 + 0.05 * torch.randn(tensor.shape, generator=gen, device=device))
+            elif name == "embedding_weight":
+                tensor.copy_(torch.randn(tensor.shape, generator=gen, device=device))
+                tensor[PAD_TOKEN_ID].zero_()
+            elif name.endswith("bias"):
+                tensor.copy_(0.002 * torch.randn(tensor.shape, generator=gen, device=device))
+            else:
+                tensor.copy_(0.02 * torch.randn(tensor.shape, generator=gen, device=device))
+
         with torch.no_grad():
-            for name, tensor in self.named_parameters():
+            for index, (name, tensor) in enumerate(self.named_parameters()):
                 if tensor is None:
                     continue
-                if name.endswith("norm") or name.endswith("_norm"):
-                    tensor.copy_(1.0 + 0.05 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
-                elif name == "embedding_weight":
-                    tensor.copy_(torch.randn(tensor.shape, generator=generator, device=tensor.device))
-                    tensor[PAD_TOKEN_ID].zero_()
-                elif name.endswith("bias"):
-                    tensor.copy_(0.002 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
+                leaf = name.rsplit(".", 1)[-1]
+                if leaf.startswith("expert_") and leaf != "expert_norm":
+                    block = self.blocks[int(name.split(".")[1])]
+                    for local in range(tensor.shape[0]):
+                        expert = block.expert_first + local
+                        expert_seed = (seed * 1_000_003 + index * 10_007 + expert) % (1 << 63)
+                        draw(tensor[local], leaf, torch.Generator(device=device).manual_seed(expert_seed))
                 else:
-                    tensor.copy_(0.02 * torch.randn(tensor.shape, generator=generator, device=tensor.device))
+                    draw(tensor, leaf, generator)
         self.clear_inference_weights()
+
+    def expert_mlp(self, block: HermBlock, sorted_rows: Tensor, sorted_experts: Tensor, offsets: Tensor,
+                   mode: str = "padded") -> Tensor:
+        """Grouped expert MLP over expert-major sorted rows: local on one GPU,
+        the all-to-all exchange of ``expert_parallel_mlp`` under a shard."""
+        if self.expert_shard is None:
+            return _ops.grouped_expert_mlp(sorted_rows, sorted_experts, offsets, *block.expert_weights())
+        return expert_parallel_mlp(self.expert_shard, sorted_rows, sorted_experts, offsets, block.expert_weights(),
+                                   mode)
 
     def cache_inference_weights(self) -> None:
         """Precompute the content head (head rows without PAD) and fp32 copies
@@ -492,10 +535,7 @@ class KoemiModel(nn.Module):
             gathered = context.to(self.compute_dtype)
             sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
                 gathered, assignments, valid_flat, s.expert_count, True)
-            expert_out = _ops.grouped_expert_mlp(sorted_context, sorted_experts, offsets, block.expert_gate_weight,
-                                                 block.expert_gate_bias, block.expert_value_weight,
-                                                 block.expert_value_bias, block.expert_output_weight,
-                                                 block.expert_output_bias)
+            expert_out = self.expert_mlp(block, sorted_context, sorted_experts, offsets, mode="exact")
             final = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid_flat,
                                                   cache["expert_norm"], s.expert_top_k, NORM_EPSILON)
             final = final.reshape(batch, length, d)

@@ -223,3 +223,42 @@ def combine_topk(expert_outputs, sorted_rows, offsets, token_count, top_k, dtype
     for i in range(int(offsets[-1])):
         out[int(sorted_rows[i])] += expert_outputs[i].to(dtype) / top_k
     return out
+
+
+# ---------------------------------------------------------------- expert parallelism
+# The reference has no expert parallelism; these restate the slab layout of the
+# dispatch (koemi_moe_ep_pack / koemi_moe_ep_unpack) so the exchange can be
+# checked against the single-rank grouped MLP above.
+
+def ep_pack(sorted_rows, sorted_experts, offsets, ranks: int, local_experts: int, capacity: int):
+    """Slab [ranks * capacity, width]: owner g's sorted rows at g * capacity,
+    owner-local expert ids beside them, -1 (and zero rows) for padding."""
+    width = sorted_rows.shape[1]
+    slab = torch.zeros(ranks * capacity, width, dtype=sorted_rows.dtype)
+    ids = torch.full((ranks * capacity,), -1, dtype=torch.int32)
+    for g in range(ranks):
+        begin, end = int(offsets[g * local_experts]), int(offsets[(g + 1) * local_experts])
+        slab[g * capacity:g * capacity + end - begin] = sorted_rows[begin:end]
+        ids[g * capacity:g * capacity + end - begin] = (sorted_experts[begin:end] - g * local_experts).to(torch.int32)
+    return slab, ids
+
+
+def ep_unpack(slab, sorted_experts, offsets, ranks: int, local_experts: int, capacity: int):
+    """Rows back in sorted order from the returned slab; zero past the valid pairs."""
+    out = torch.zeros(sorted_experts.shape[0], slab.shape[1], dtype=slab.dtype)
+    for g in range(ranks):
+        begin, end = int(offsets[g * local_experts]), int(offsets[(g + 1) * local_experts])
+        out[begin:end] = slab[g * capacity:g * capacity + end - begin]
+    return out
+
+
+def permute_rows(rows, assignments, valid, expert_count: int, gather: bool = True):
+    """The 5-tuple of the permute front (sorted rows, sorted token rows, sorted
+    experts, segment offsets, pair positions) from `permute_topk` above."""
+    a = assignments.cpu().numpy()
+    order, sorted_tokens, keys, offsets, positions = permute_topk(a, valid.cpu().numpy(), expert_count)
+    n_valid = int(offsets[-1])
+    sorted_rows = torch.zeros(order.size, rows.shape[1], dtype=rows.dtype)
+    sorted_rows[:n_valid] = rows[torch.from_numpy(sorted_tokens[:n_valid])]
+    return (sorted_rows, torch.from_numpy(sorted_tokens), torch.from_numpy(keys), torch.from_numpy(offsets),
+            torch.from_numpy(positions))
