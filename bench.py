@@ -327,6 +327,11 @@ def measure_expert_mlp(model, args, world: int, repeats: int = 20) -> dict:
     return {"seconds": seconds, "bytes": algorithmic, "touched_experts": touched, "pairs": pairs}
 
 
+def progress(rank: int, message: str) -> None:
+    """Timestamped, rank-tagged progress on stderr (the JSON line stays alone on stdout)."""
+    print(f"[bench rank {rank} {time.strftime('%H:%M:%S')}] {message}", file=sys.stderr, flush=True)
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -360,10 +365,12 @@ def run_b200(args) -> None:
     logits = decoder.prefill(prompts)
     torch.cuda.synchronize()
     prefill_seconds = time.perf_counter() - prefill_start
+    progress(rank, f"prefill done in {prefill_seconds:.1f} s")
     del prompts
 
     token = logits.argmax(dim=-1, keepdim=True)
     eager_kernels = count_native_kernels(model, decoder, token)
+    progress(rank, f"eager step counted {eager_kernels} native launches")
     for _ in range(max(args.warmup, 1)):
         logits = decoder.step(token)
         token = logits.argmax(dim=-1, keepdim=True)
@@ -374,6 +381,7 @@ def run_b200(args) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    progress(rank, "graph captured and warmed up; timing")
     with ClockSampler(local) as clocks:
         torch.cuda.nvtx.range_push("decode_timed")
         start.record(stream)
@@ -402,6 +410,7 @@ def run_b200(args) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    progress(rank, "timed steps done; end-to-end steps")
     e2e_start = time.perf_counter()
     for _ in range(args.steps):
         device_ids.copy_(host_in, non_blocking=True)
@@ -416,6 +425,7 @@ def run_b200(args) -> None:
         e2e_seconds = float(t.item())
     e2e_value = per_rank * world * args.steps / e2e_seconds
 
+    progress(rank, "end-to-end done; expert kernel roofline")
     mlp = measure_expert_mlp(model, args, world)
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
@@ -439,13 +449,18 @@ def run_b200(args) -> None:
                      "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},
         "prefill_s": prefill_seconds,
     }
+    # the step graph (which may hold collectives) and the peer buffers go
+    # before the process group
+    del decoder, logits
+    torch.cuda.synchronize()
+    model.close_exchanges()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        del decoder
         torch.cuda.empty_cache()
         line["cpu_baseline"] = CpuBaseline(args, args.cpu_sample_streams).measure(3)
     line["wall_s"] = time.perf_counter() - wall_start
     if rank == 0:
         emit(line, args)
+    progress(rank, "done")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

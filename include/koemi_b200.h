@@ -385,6 +385,50 @@ KOEMI_API int koemi_moe_ep_unpack(const void *slab, const int64_t *sorted_expert
                         int64_t width, int64_t ranks, int64_t local_experts, int64_t capacity,
                         int dtype, void *stream);
 
+/* Fused expert-parallel exchange over peer memory (NVLink / NVSwitch), one
+ * process per GPU, at most 8 ranks. Each rank allocates one exchange buffer of
+ * koemi_peer_exchange_bytes() with koemi_peer_buffer_alloc, shares the
+ * KOEMI_PEER_HANDLE_BYTES handle with the other ranks (any host channel) and
+ * opens theirs with koemi_peer_buffer_open (CUDA IPC; no NVLink multicast
+ * objects). `peers` is a device array [ranks] of every rank's buffer address
+ * in this process (own buffer at [rank]); `own` is this rank's buffer.
+ * One exchange, all ranks in the same order:
+ *   koemi_ep_dispatch       sender: slab rows (the koemi_moe_ep_pack layout)
+ *                           stored straight into the owners' buffers, then an
+ *                           epoch flag per owner (release, system scope);
+ *   koemi_ep_wait_dispatch  owner: waits for every sender's flag; the received
+ *                           rows are then recv_rows [ranks * capacity, width]
+ *                           with owner-local ids recv_ids (-1 padding) at the
+ *                           buffer offsets of koemi_peer_exchange_offsets;
+ *   koemi_ep_return         owner: the expert output of received row q
+ *                           (local_out[local_positions[q]]) stored back into
+ *                           its sender's buffer, then a flag per sender;
+ *   koemi_ep_collect        sender: waits for every owner's flag and writes the
+ *                           outputs in sorted pair order (zero past the valid
+ *                           pairs), as koemi_moe_ep_unpack.
+ * Every wait is bounded: a wait that runs out records KOEMI_ERR_TIMEOUT in the
+ * device status word (koemi_device_status) and the kernel returns. No
+ * counterpart in the reference, which has no expert parallelism. */
+#define KOEMI_PEER_HANDLE_BYTES 64
+KOEMI_API size_t koemi_peer_exchange_bytes(int64_t ranks, int64_t capacity, int64_t width, int dtype);
+KOEMI_API int koemi_peer_exchange_offsets(int64_t ranks, int64_t capacity, int64_t width, int dtype,
+                                size_t *ids_offset, size_t *rows_offset);
+KOEMI_API int koemi_peer_buffer_alloc(size_t bytes, void **ptr, void *handle_out);
+KOEMI_API int koemi_peer_buffer_open(const void *handle, void **ptr);
+KOEMI_API int koemi_peer_buffer_close(void *ptr);
+KOEMI_API int koemi_peer_buffer_free(void *ptr);
+KOEMI_API int koemi_ep_dispatch(const void *sorted_rows, const int64_t *sorted_experts,
+                      const int64_t *segment_offsets, const uint64_t *peers, void *own, int64_t pairs,
+                      int64_t width, int64_t rank, int64_t ranks, int64_t local_experts,
+                      int64_t capacity, int dtype, void *stream);
+KOEMI_API int koemi_ep_wait_dispatch(const void *own, int64_t ranks, void *stream);
+KOEMI_API int koemi_ep_return(const void *local_out, const int64_t *local_positions, const uint64_t *peers,
+                    void *own, int64_t width, int64_t rank, int64_t ranks, int64_t local_experts,
+                    int64_t capacity, int dtype, void *stream);
+KOEMI_API int koemi_ep_collect(const int64_t *sorted_experts, const int64_t *segment_offsets, void *sorted_out,
+                     const uint64_t *peers, void *own, int64_t pairs, int64_t width, int64_t rank,
+                     int64_t ranks, int64_t local_experts, int64_t capacity, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,16 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
     "koemi_moe_ep_pack": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_moe_ep_unpack": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_peer_exchange_bytes": (_sz, (_i64, _i64, _i64, _int)),
+    "koemi_peer_exchange_offsets": (_int, (_i64, _i64, _i64, _int, _p, _p)),
+    "koemi_peer_buffer_alloc": (_int, (_sz, _p, _p)),
+    "koemi_peer_buffer_open": (_int, (_p, _p)),
+    "koemi_peer_buffer_close": (_int, (_p,)),
+    "koemi_peer_buffer_free": (_int, (_p,)),
+    "koemi_ep_dispatch": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_ep_wait_dispatch": (_int, (_p, _i64, _p)),
+    "koemi_ep_return": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_ep_collect": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_moe_combine_residual_rmsnorm": (
         _int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _int, _p)),
 }

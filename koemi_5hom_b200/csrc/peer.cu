@@ -1,0 +1,340 @@
+// Expert-parallel exchange over peer memory (NVLink / NVSwitch).
+//
+// Every rank allocates one exchange buffer with cudaMalloc and shares it with
+// the other ranks through CUDA IPC handles (no NVLink multicast objects). The
+// dispatch and return of token rows are then plain stores into the owner's or
+// the sender's buffer, fused with the pack / unpack of the slabs, and a
+// per-exchange epoch flag written with release semantics after the last row.
+// Waiting kernels spin on the peers' flags with an iteration limit: when the
+// limit runs out they record KOEMI_ERR_TIMEOUT in the device status word and
+// return, so a missing peer never hangs the GPU.
+//
+// Buffer layout (every rank the same):
+//   [0, 256)                     header: flags[2][ranks] (uint64, written by peers),
+//                                epoch (uint64), ticket (uint32) at the end
+//   recv_ids   [ranks][capacity] int32    rows' owner-local expert ids (-1 padding)
+//   recv_rows  [ranks][capacity][width]   rows dispatched to this rank, block = sender
+//   ret_rows   [ranks][capacity][width]   outputs returned to this rank, block = owner
+#include <cstring>
+
+#include "vec.cuh"
+
+namespace koemi {
+namespace {
+
+constexpr int64_t kMaxPeerRanks = 8;
+constexpr size_t kHeaderBytes = 256;
+constexpr int64_t kEpochSlot = 2 * kMaxPeerRanks;      // uint64 index of the local epoch
+constexpr int64_t kTicketSlot = 2 * kMaxPeerRanks + 1;  // uint64 index of the CTA ticket
+constexpr uint64_t kPeerSpinLimit = uint64_t(1) << 22;  // about a second of polling
+
+struct Layout {
+    size_t ids, rows, ret, total;
+};
+
+Layout layout(int64_t ranks, int64_t capacity, int64_t width, size_t es) {
+    auto align = [](size_t v) { return (v + 255) & ~size_t(255); };
+    Layout l{};
+    l.ids = kHeaderBytes;
+    l.rows = align(l.ids + static_cast<size_t>(ranks * capacity) * 4);
+    l.ret = align(l.rows + static_cast<size_t>(ranks * capacity * width) * es);
+    l.total = align(l.ret + static_cast<size_t>(ranks * capacity * width) * es);
+    return l;
+}
+
+__device__ __forceinline__ void store_release_sys(uint64_t *p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t load_acquire_sys(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Thread 0 of every CTA waits until flags[which][r] >= epoch for every rank r
+// (bounded); the CTA then proceeds. Returns false after a timeout.
+__device__ bool wait_flags(const uint8_t *own, int which, int64_t ranks, int *status) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        const uint64_t *flags = reinterpret_cast<const uint64_t *>(own);
+        const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(own)[kEpochSlot];
+        ok = 1;
+        for (int64_t r = 0; r < ranks && ok; ++r) {
+            uint64_t spin = 0;
+            while (load_acquire_sys(flags + which * kMaxPeerRanks + r) < epoch) {
+                if (++spin == kPeerSpinLimit) {
+                    ok = 0;
+                    if (status != nullptr) atomicExch(status, KOEMI_ERR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// After every CTA's stores: the last CTA to arrive publishes `epoch` in
+// flags[which][rank] of every peer (release, system scope).
+__device__ void signal_peers(uint8_t *own, const uint64_t *peers, int which, int64_t rank, int64_t ranks,
+                             uint64_t epoch, bool advance_epoch) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    unsigned int *ticket = reinterpret_cast<unsigned int *>(reinterpret_cast<uint64_t *>(own) + kTicketSlot);
+    if (atomicAdd(ticket, 1u) != gridDim.x - 1) return;
+    __threadfence_system();
+    *ticket = 0;
+    if (advance_epoch) reinterpret_cast<volatile uint64_t *>(own)[kEpochSlot] = epoch;
+    for (int64_t g = 0; g < ranks; ++g) {
+        uint64_t *flags = reinterpret_cast<uint64_t *>(peers[g]);
+        store_release_sys(flags + which * kMaxPeerRanks + rank, epoch);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void copy_row(T *dst, const T *src, int64_t width, bool vector, int lane) {
+    if (vector) {
+        constexpr int W = 16 / sizeof(T);
+        for (int64_t p = lane; p < width / W; p += 32) {
+            *reinterpret_cast<uint4 *>(dst + p * W) = load_stream(src + p * W);
+        }
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = src[c];
+    }
+}
+
+struct ExchangeArgs {
+    const uint64_t *peers;  // [ranks] base address of every rank's buffer (own included)
+    uint8_t *own;
+    int64_t rank, ranks, local_experts, capacity, width;
+    size_t ids, rows, ret;
+    int *status;
+};
+
+// Sender: slab row (g, j) goes straight to owner g's recv block `rank`.
+template <typename T>
+__global__ void ep_dispatch_kernel(ExchangeArgs a, const T *__restrict__ sorted_rows,
+                                   const int64_t *__restrict__ sorted_experts, const int64_t *__restrict__ offsets,
+                                   bool vector) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(a.own)[kEpochSlot] + 1;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    for (int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+         q < a.ranks * a.capacity; q += warps) {
+        const int64_t g = q / a.capacity;
+        const int64_t j = q - g * a.capacity;
+        const int64_t i = offsets[g * a.local_experts] + j;
+        const bool live = i < offsets[(g + 1) * a.local_experts];
+        uint8_t *peer = reinterpret_cast<uint8_t *>(a.peers[g]);
+        const int64_t slot = a.rank * a.capacity + j;
+        if (lane == 0) {
+            reinterpret_cast<int32_t *>(peer + a.ids)[slot] =
+                live ? static_cast<int32_t>(sorted_experts[i] - g * a.local_experts) : -1;
+        }
+        if (live) copy_row(reinterpret_cast<T *>(peer + a.rows) + slot * a.width, sorted_rows + i * a.width, a.width,
+                           vector, lane);
+    }
+    signal_peers(a.own, a.peers, 0, a.rank, a.ranks, epoch, true);
+}
+
+// Owner: wait until every sender's rows of this exchange have landed.
+__global__ void ep_wait_dispatch_kernel(const uint8_t *own, int64_t ranks, int *status) {
+    wait_flags(own, 0, ranks, status);
+}
+
+// Owner: received row (s, j) with a live id goes back to sender s's ret
+// block `rank`, from the local expert outputs at local_positions[(s, j)].
+template <typename T>
+__global__ void ep_return_kernel(ExchangeArgs a, const T *__restrict__ local_out,
+                                 const int64_t *__restrict__ local_positions, bool vector) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(a.own)[kEpochSlot];
+    const int32_t *ids = reinterpret_cast<const int32_t *>(a.own + a.ids);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    for (int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+         q < a.ranks * a.capacity; q += warps) {
+        if (ids[q] < 0) continue;
+        const int64_t s = q / a.capacity;
+        const int64_t j = q - s * a.capacity;
+        uint8_t *peer = reinterpret_cast<uint8_t *>(a.peers[s]);
+        copy_row(reinterpret_cast<T *>(peer + a.ret) + (a.rank * a.capacity + j) * a.width,
+                 local_out + local_positions[q] * a.width, a.width, vector, lane);
+    }
+    signal_peers(a.own, a.peers, 1, a.rank, a.ranks, epoch, false);
+}
+
+// Sender: wait for every owner's returns, then unpack into sorted order.
+template <typename T>
+__global__ void ep_collect_kernel(ExchangeArgs a, const int64_t *__restrict__ sorted_experts,
+                                  const int64_t *__restrict__ offsets, T *__restrict__ sorted_out, int64_t pairs,
+                                  bool vector) {
+    if (!wait_flags(a.own, 1, a.ranks, a.status)) return;
+    const int lane = threadIdx.x & 31;
+    const T *ret = reinterpret_cast<const T *>(a.own + a.ret);
+    const int64_t valid = offsets[a.ranks * a.local_experts];
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); i < pairs;
+         i += warps) {
+        T *dst = sorted_out + i * a.width;
+        if (i < valid) {
+            const int64_t g = sorted_experts[i] / a.local_experts;
+            copy_row(dst, ret + (g * a.capacity + i - offsets[g * a.local_experts]) * a.width, a.width, vector, lane);
+        } else if (vector) {
+            constexpr int W = 16 / sizeof(T);
+            for (int64_t p = lane; p < a.width / W; p += 32) *reinterpret_cast<uint4 *>(dst + p * W) = make_uint4(0, 0, 0, 0);
+        } else {
+            for (int64_t c = lane; c < a.width; c += 32) dst[c] = from_acc<T>(0.0f);
+        }
+    }
+}
+
+int exchange_args(ExchangeArgs *a, const uint64_t *peers, void *own, int64_t rank, int64_t ranks,
+                  int64_t local_experts, int64_t capacity, int64_t width, int dtype) {
+    if (ranks < 1 || ranks > kMaxPeerRanks || rank < 0 || rank >= ranks) {
+        return fail(KOEMI_ERR_INVALID, "peer exchange needs 1 <= ranks <= %lld and 0 <= rank < ranks", (long long)kMaxPeerRanks);
+    }
+    if (local_experts < 1 || capacity < 1 || width < 1) return fail(KOEMI_ERR_INVALID, "bad exchange sizes");
+    const size_t es = dtype_size(dtype);
+    if (dtype != KOEMI_F32 && dtype != KOEMI_F16 && dtype != KOEMI_BF16) return fail(KOEMI_ERR_INVALID, "rows must be f32, f16 or bf16");
+    if (peers == nullptr || own == nullptr || !aligned(own, 256)) return fail(KOEMI_ERR_INVALID, "exchange buffers must be 256-byte aligned");
+    const Layout l = layout(ranks, capacity, width, es);
+    *a = ExchangeArgs{peers, static_cast<uint8_t *>(own), rank, ranks, local_experts, capacity, width, l.ids, l.rows, l.ret,
+                      device_status_word()};
+    return KOEMI_OK;
+}
+
+unsigned exchange_blocks(int64_t rows) {
+    const int64_t wanted = ceil_div(rows, 8);
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 4;
+    return static_cast<unsigned>(wanted < 1 ? 1 : (wanted > cap ? cap : wanted));
+}
+
+}  // namespace
+}  // namespace koemi
+
+using namespace koemi;
+
+extern "C" size_t koemi_peer_exchange_bytes(int64_t ranks, int64_t capacity, int64_t width, int dtype) {
+    if (ranks < 1 || capacity < 1 || width < 1 || dtype_size(dtype) == 0) return 0;
+    return layout(ranks, capacity, width, dtype_size(dtype)).total;
+}
+
+extern "C" int koemi_peer_exchange_offsets(int64_t ranks, int64_t capacity, int64_t width, int dtype,
+                                           size_t *ids_offset, size_t *rows_offset) {
+    clear_error();
+    if (ranks < 1 || capacity < 1 || width < 1 || dtype_size(dtype) == 0 || ids_offset == nullptr || rows_offset == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "bad exchange layout arguments");
+    }
+    const Layout l = layout(ranks, capacity, width, dtype_size(dtype));
+    *ids_offset = l.ids;
+    *rows_offset = l.rows;
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_peer_buffer_alloc(size_t bytes, void **ptr, void *handle_out) {
+    clear_error();
+    if (ptr == nullptr || handle_out == nullptr || bytes == 0) return fail(KOEMI_ERR_INVALID, "bad peer buffer arguments");
+    void *p = nullptr;
+    KOEMI_CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t handle;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&handle, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(KOEMI_ERR_CUDA, "peer buffer: %s", cudaGetErrorString(e));
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) <= KOEMI_PEER_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &handle, sizeof(handle));
+    *ptr = p;
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_peer_buffer_open(const void *handle, void **ptr) {
+    clear_error();
+    if (handle == nullptr || ptr == nullptr) return fail(KOEMI_ERR_INVALID, "bad peer handle arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    KOEMI_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_peer_buffer_close(void *ptr) {
+    clear_error();
+    KOEMI_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_peer_buffer_free(void *ptr) {
+    clear_error();
+    KOEMI_CUDA_TRY(cudaFree(ptr));
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_dispatch(const void *sorted_rows, const int64_t *sorted_experts, const int64_t *segment_offsets,
+                                 const uint64_t *peers, void *own, int64_t pairs, int64_t width, int64_t rank,
+                                 int64_t ranks, int64_t local_experts, int64_t capacity, int dtype, void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    if (capacity < pairs) return fail(KOEMI_ERR_INVALID, "capacity %lld is below the %lld pairs one owner may receive", (long long)capacity, (long long)pairs);
+    const bool vector = (width * static_cast<int64_t>(dtype_size(dtype))) % 16 == 0 && aligned(sorted_rows, 16);
+    const unsigned blocks = exchange_blocks(ranks * capacity);
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: ep_dispatch_kernel<float><<<blocks, 256, 0, s>>>(a, static_cast<const float *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
+        case KOEMI_F16: ep_dispatch_kernel<__half><<<blocks, 256, 0, s>>>(a, static_cast<const __half *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
+        default: ep_dispatch_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, static_cast<const __nv_bfloat16 *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_wait_dispatch(const void *own, int64_t ranks, void *stream) {
+    clear_error();
+    if (own == nullptr || ranks < 1 || ranks > kMaxPeerRanks) return fail(KOEMI_ERR_INVALID, "bad exchange wait arguments");
+    ep_wait_dispatch_kernel<<<1, 32, 0, as_stream(stream)>>>(static_cast<const uint8_t *>(own), ranks, device_status_word());
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_return(const void *local_out, const int64_t *local_positions, const uint64_t *peers, void *own,
+                               int64_t width, int64_t rank, int64_t ranks, int64_t local_experts, int64_t capacity,
+                               int dtype, void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    const bool vector = (width * static_cast<int64_t>(dtype_size(dtype))) % 16 == 0 && aligned(local_out, 16);
+    const unsigned blocks = exchange_blocks(ranks * capacity);
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: ep_return_kernel<float><<<blocks, 256, 0, s>>>(a, static_cast<const float *>(local_out), local_positions, vector); break;
+        case KOEMI_F16: ep_return_kernel<__half><<<blocks, 256, 0, s>>>(a, static_cast<const __half *>(local_out), local_positions, vector); break;
+        default: ep_return_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, static_cast<const __nv_bfloat16 *>(local_out), local_positions, vector); break;
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_collect(const int64_t *sorted_experts, const int64_t *segment_offsets, void *sorted_out,
+                                const uint64_t *peers, void *own, int64_t pairs, int64_t width, int64_t rank,
+                                int64_t ranks, int64_t local_experts, int64_t capacity, int dtype, void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    if (pairs == 0) return KOEMI_OK;
+    const bool vector = (width * static_cast<int64_t>(dtype_size(dtype))) % 16 == 0 && aligned(sorted_out, 16);
+    const unsigned blocks = exchange_blocks(pairs);
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_F32: ep_collect_kernel<float><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<float *>(sorted_out), pairs, vector); break;
+        case KOEMI_F16: ep_collect_kernel<__half><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<__half *>(sorted_out), pairs, vector); break;
+        default: ep_collect_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<__nv_bfloat16 *>(sorted_out), pairs, vector); break;
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}

@@ -139,3 +139,108 @@ def expert_parallel_mlp(shard: ExpertShard, sorted_rows: Tensor, sorted_experts:
     out = sorted_rows.new_zeros(pairs, width)
     dist.all_to_all_single(out[:valid], back, send_sizes, recv_sizes, group=group)
     return out
+
+
+class _DeviceArray:
+    """A raw device allocation seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, address: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (address, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Buffers of the fused peer-memory exchange (``koemi_ep_*``) for one
+    shard, capacity and row shape; created by all ranks together.
+
+    Every rank allocates one buffer with cudaMalloc in the native library and
+    shares its CUDA IPC handle through one all-gather on the shard's group;
+    after that the exchange needs no collective library call: dispatch and
+    return are stores into peer memory followed by epoch flags."""
+
+    def __init__(self, shard: ExpertShard, capacity: int, width: int, dtype: torch.dtype, device: torch.device):
+        import ctypes
+        import torch.distributed as dist
+        from koemi_5hom_b200 import _native
+        lib = _native.library()
+        self.shard, self.capacity, self.width, self.dtype, self.device = shard, capacity, width, dtype, device
+        code = _native.dtype_code(dtype)
+        ranks = shard.world
+        size = lib.koemi_peer_exchange_bytes(ranks, capacity, width, code)
+        if size == 0:
+            raise ValueError("bad exchange shape")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _native.check("koemi_peer_buffer_alloc", lib.koemi_peer_buffer_alloc(size, ctypes.byref(own), handle))
+        self.own = int(own.value)
+        self._opened: list[int] = []
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        handles = [torch.empty_like(mine) for _ in range(ranks)]
+        if ranks > 1:
+            dist.all_gather(handles, mine, group=shard.group)
+        addresses = []
+        for r, h in enumerate(handles):
+            if r == shard.rank:
+                addresses.append(self.own)
+                continue
+            raw = (ctypes.c_uint8 * 64)(*h.cpu().tolist())
+            peer = ctypes.c_void_p()
+            _native.check("koemi_peer_buffer_open", lib.koemi_peer_buffer_open(raw, ctypes.byref(peer)))
+            self._opened.append(int(peer.value))
+            addresses.append(int(peer.value))
+        # uint64 addresses as int64 bits
+        self.peers = torch.tensor([a - (1 << 64) if a >= (1 << 63) else a for a in addresses], dtype=torch.int64,
+                                  device=device)
+        ids_offset, rows_offset = ctypes.c_size_t(), ctypes.c_size_t()
+        _native.check("koemi_peer_exchange_offsets",
+                      lib.koemi_peer_exchange_offsets(ranks, capacity, width, code, ctypes.byref(ids_offset),
+                                                      ctypes.byref(rows_offset)))
+        rows = ranks * capacity
+        self.recv_ids = torch.as_tensor(_DeviceArray(self.own + ids_offset.value, (rows,), "<i4"), device=device)
+        element = {torch.float32: "<f4", torch.bfloat16: "<i2", torch.float16: "<f2"}[dtype]
+        recv = torch.as_tensor(_DeviceArray(self.own + rows_offset.value, (rows, width), element), device=device)
+        self.recv_rows = recv.view(dtype) if dtype == torch.bfloat16 else recv
+        if ranks > 1:
+            dist.barrier(group=shard.group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (all ranks together,
+        after the last exchange has finished on every rank)."""
+        import torch.distributed as dist
+        from koemi_5hom_b200 import _native
+        lib = _native.library()
+        torch.cuda.synchronize(self.device)
+        for address in self._opened:
+            _native.check("koemi_peer_buffer_close", lib.koemi_peer_buffer_close(address))
+        self._opened = []
+        if self.shard.world > 1:
+            dist.barrier(group=self.shard.group)  # nobody maps this rank's buffer any more
+        if self.own:
+            _native.check("koemi_peer_buffer_free", lib.koemi_peer_buffer_free(self.own))
+            self.own = 0
+
+    def run(self, sorted_rows: Tensor, sorted_experts: Tensor, offsets: Tensor, weights: tuple[Tensor, ...]) -> Tensor:
+        """The expert MLP of the global experts over this rank's sorted pairs,
+        through the owners (same contract as ``expert_parallel_mlp``)."""
+        from koemi_5hom_b200 import _native
+        from koemi_5hom_b200.cuda_kernels import _ops
+        shard = self.shard
+        pairs, width = sorted_rows.shape
+        if pairs > self.capacity or width != self.width or sorted_rows.dtype != self.dtype:
+            raise ValueError("rows do not fit this exchange")
+        sorted_rows, sorted_experts, offsets = (t.contiguous() for t in (sorted_rows, sorted_experts, offsets))
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        code = _native.dtype_code(self.dtype)
+        ptr, call = _native.ptr, _native.call
+        call("koemi_ep_dispatch", ptr(sorted_rows), ptr(sorted_experts), ptr(offsets), ptr(self.peers), self.own, pairs,
+             width, shard.rank, shard.world, shard.local_count, self.capacity, code, stream)
+        call("koemi_ep_wait_dispatch", self.own, shard.world, stream)
+        local_sorted, _, local_experts, local_offsets, local_positions = _ops.permute_topk(
+            self.recv_rows, self.recv_ids.view(-1, 1), self.recv_ids >= 0, shard.local_count, True)
+        local_out = _ops.grouped_expert_mlp(local_sorted, local_experts, local_offsets, *weights)
+        call("koemi_ep_return", ptr(local_out), ptr(local_positions), ptr(self.peers), self.own, width, shard.rank,
+             shard.world, shard.local_count, self.capacity, code, stream)
+        out = torch.empty(pairs, width, dtype=self.dtype, device=self.device)
+        call("koemi_ep_collect", ptr(sorted_experts), ptr(offsets), ptr(out), ptr(self.peers), self.own, pairs, width,
+             shard.rank, shard.world, shard.local_count, self.capacity, code, stream)
+        return out

@@ -39,7 +39,7 @@ import torch
 from torch import Tensor, nn
 
 from koemi_5hom_b200.cuda_kernels import _ops
-from koemi_5hom_b200.model.expert_parallel import ExpertShard, expert_parallel_mlp
+from koemi_5hom_b200.model.expert_parallel import ExpertShard, PeerExchange, expert_parallel_mlp
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID, ModelSettings
 from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
 
@@ -202,6 +202,10 @@ class KoemiModel(nn.Module):
         if expert_shard is not None and (s.expert_count == 0 or expert_shard.expert_count != s.expert_count):
             raise ValueError("the expert shard must split the model's experts")
         self.expert_shard = expert_shard if expert_shard is not None and expert_shard.world > 1 else None
+        # decode-step exchange of the expert rows: "peer" (fused stores into the
+        # other ranks' memory) or "nccl" (all-to-all collectives)
+        self.exchange = "peer"
+        self._exchanges: dict = {}
         self.compute_dtype = _dtype_of(s.compute_dtype)
         dev = torch.device(device) if device is not None else None
         p = lambda *shape: nn.Parameter(torch.empty(*shape, dtype=self.compute_dtype, device=dev), requires_grad=False)  # noqa: E731
@@ -277,8 +281,24 @@ class KoemiModel(nn.Module):
         the all-to-all exchange of ``expert_parallel_mlp`` under a shard."""
         if self.expert_shard is None:
             return _ops.grouped_expert_mlp(sorted_rows, sorted_experts, offsets, *block.expert_weights())
+        if mode == "padded" and self.exchange == "peer":
+            return self.peer_exchange(sorted_rows.shape[0], sorted_rows.shape[1], sorted_rows.dtype).run(
+                sorted_rows, sorted_experts, offsets, block.expert_weights())
         return expert_parallel_mlp(self.expert_shard, sorted_rows, sorted_experts, offsets, block.expert_weights(),
                                    mode)
+
+    def peer_exchange(self, capacity: int, width: int, dtype: torch.dtype) -> PeerExchange:
+        """The peer-memory exchange for decode-sized pair counts (created by
+        all ranks together on first use, then reused by every block)."""
+        key = (capacity, width, dtype)
+        if key not in self._exchanges:
+            self._exchanges[key] = PeerExchange(self.expert_shard, capacity, width, dtype, self.head_weight.device)
+        return self._exchanges[key]
+
+    def close_exchanges(self) -> None:
+        for exchange in self._exchanges.values():
+            exchange.close()
+        self._exchanges = {}
 
     def cache_inference_weights(self) -> None:
         """Precompute the content head (head rows without PAD) and fp32 copies

@@ -38,13 +38,40 @@ def test_slab_pack_and_unpack_match_oracle(ranks, local, tokens, top_k, dtype, c
     assert torch.equal(back.cpu(), ops.ep_unpack(returned, sorted_experts, offsets, ranks, local, capacity))
 
 
+@pytest.mark.parametrize("tokens,experts,steps", [(64, 8, 3), (256, 64, 2), (5, 4, 1)])
+def test_peer_exchange_with_itself_equals_grouped_mlp(tokens, experts, steps, cuda):
+    """One rank exchanging with its own buffer runs every peer kernel
+    (dispatch, flag wait, return, collect) on one GPU, repeatedly (epochs)."""
+    from koemi_5hom_b200 import _native
+    from koemi_5hom_b200.model.expert_parallel import ExpertShard, PeerExchange
+    g = torch.Generator().manual_seed(tokens)
+    width, hidden = 128, 256
+    weights = tuple((torch.randn(*shape, generator=g) * 0.05).bfloat16().to(cuda) for shape in
+                    ((experts, hidden, width), (experts, hidden), (experts, hidden, width), (experts, hidden),
+                     (experts, width, hidden), (experts, width)))
+    exchange = PeerExchange(ExpertShard(1, 0, experts), tokens * 2, width, torch.bfloat16, cuda)
+    try:
+        for step in range(steps):
+            rows = torch.randn(tokens, width, generator=g).bfloat16().to(cuda)
+            assignments = torch.randint(-1, experts, (tokens, 2), generator=g).to(cuda)
+            valid = torch.ones(tokens, dtype=torch.bool, device=cuda)
+            sorted_rows, _, sorted_experts, offsets, _ = _ops.permute_topk(rows, assignments, valid, experts, True)
+            expected = _ops.grouped_expert_mlp(sorted_rows, sorted_experts, offsets, *weights)
+            got = exchange.run(sorted_rows, sorted_experts, offsets, weights)
+            torch.cuda.synchronize()
+            assert _native.device_status(cuda) == 0
+            assert torch.equal(got, expected), step
+    finally:
+        exchange.close()
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _ep_rank(rank: int, world: int, port: int, capture_graph: bool) -> None:
+def _ep_rank(rank: int, world: int, port: int, capture_graph: bool, exchange: str) -> None:
     import torch.distributed as dist
     from koemi_5hom_b200.model import KoemiModel, ModelSettings
     from koemi_5hom_b200.model.expert_parallel import ExpertShard
@@ -62,6 +89,7 @@ def _ep_rank(rank: int, world: int, port: int, capture_graph: bool) -> None:
         full.initialize_parameters(seed=5)
         sharded = KoemiModel(settings, device=device, expert_shard=ExpertShard.from_group(8))
         sharded.initialize_parameters(seed=5)
+        sharded.exchange = exchange
         g = torch.Generator().manual_seed(40 + rank)  # each rank decodes its own streams
         prompts = torch.randint(0, 1023, (4, 24), generator=g).to(device)
         sampler = TokenSampler(SamplingPolicy(greedy=True), device)
@@ -78,15 +106,27 @@ def _ep_rank(rank: int, world: int, port: int, capture_graph: bool) -> None:
         torch.cuda.synchronize()
         import gc
         gc.collect()
+        sharded.close_exchanges()
+        from koemi_5hom_b200 import _native
+        assert _native.device_status(device) == 0
         assert torch.equal(runs[0], runs[1]), float((runs[0] - runs[1]).abs().max())
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("capture_graph", [False, True])
-def test_expert_parallel_decode_equals_unsharded_model(capture_graph):
+def test_expert_parallel_decode_equals_unsharded_model(capture_graph, exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_ep_rank, args=(2, _free_port(), capture_graph), nprocs=2, join=True)
+    context = mp.spawn(_ep_rank, args=(2, _free_port(), capture_graph, exchange), nprocs=2, join=False)
+    deadline = 300.0
+    import time
+    start = time.monotonic()
+    while not context.join(timeout=5.0):
+        if time.monotonic() - start > deadline:  # a rank that never finishes: end both, fail
+            for process in context.processes:
+                process.kill()
+            pytest.fail("expert-parallel ranks did not finish in time")
