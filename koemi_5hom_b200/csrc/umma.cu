@@ -58,6 +58,7 @@ enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3, kDenseC
 // adds the bias and stores. Row stride of the parked accumulator, in floats
 // (padded so the per-row float4 stores of a warp hit distinct banks):
 constexpr int kAccStride = kBN + 4;
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 static_assert(kBM * kAccStride * 4 <= kStages * kStageBytes, "parked accumulator must fit in the stage ring");
 
 struct UmmaArgs {
@@ -548,17 +549,27 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
             const T *bias = static_cast<const T *>(args.bias0);
             float *out = static_cast<float *>(args.out);
             const uint32_t parked_base = smem_addr(stages);
-            for (int idx = threadIdx.x; idx < kBM * q_count; idx += kThreads) {
+            const int valid_rows = static_cast<int>(min(static_cast<int64_t>(kBM), args.rows - tile.row0));
+            for (int idx = threadIdx.x; idx < valid_rows * q_count; idx += kThreads) {
                 const int r = idx / q_count;
                 const int q = q_begin + (idx - r * q_count);
                 const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
+                // every split's value is requested before any is added (the
+                // remote loads overlap), then summed in split order
+                float4 v[kMaxClusterSplits];
+#pragma unroll
+                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+                    if (sp < splits) v[sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
+                }
                 float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                for (int64_t sp = 0; sp < splits; ++sp) {
-                    const float4 v = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
-                    acc.x += v.x;
-                    acc.y += v.y;
-                    acc.z += v.z;
-                    acc.w += v.w;
+#pragma unroll
+                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+                    if (sp < splits) {
+                        acc.x += v[sp].x;
+                        acc.y += v[sp].y;
+                        acc.z += v[sp].z;
+                        acc.w += v[sp].w;
+                    }
                 }
                 const int64_t row = tile.row0 + r;
                 const int64_t col = tile.n * kBN + q * 4;
