@@ -10,7 +10,7 @@ tensor of the state at a fixed address and updates it in place:
 - working state, associative bases and normalisers are overwritten in place.
 
 A step is then: per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
--> surprise (tcgen05 head GEMM + online LSE) -> local/assoc GEMMs ->
+-> surprise (tcgen05 head GEMM + online LSE) -> one local|assoc GEMM ->
 ``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` (with the
 feature projection of key and query fused in) -> fusion GEMM
 (its input rows are written in place by the three kernels) -> rms_norm ->
@@ -194,11 +194,11 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         else:
             surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
                                                     torch.float32)
-        local = model._linear(h, block.local_weight, block.local_bias)
-        assoc = model._linear(h, block.assoc_weight, block.assoc_bias)
+        local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
+        local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
         scored = surprise if surprise is not None else torch.zeros(batch, device=device)
         # ring queries read the fp32 working state (the new h) directly
-        call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), 2 * d, ptr(valid), ptr(scored),
+        call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), local.stride(0), ptr(valid), ptr(scored),
              float(s.salience_threshold), ptr(st.local_keys), ptr(st.local_values), ptr(st.local_valid),
              ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
              ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,

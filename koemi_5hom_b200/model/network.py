@@ -316,6 +316,10 @@ class KoemiModel(nn.Module):
             entry = {name: f32(getattr(block, name, None)) for name in
                      ("input_norm", "gates_bias", "assoc_bias", "feature_bias", "local_bias", "refine_bias",
                       "fusion_bias", "fusion_norm", "expert_norm")}
+            # decode reads h once for both ring entries and associative
+            # projections: local | assoc stacked into one [5d + 2, d] GEMM
+            entry["local_assoc_weight"] = torch.cat((block.local_weight, block.assoc_weight)).contiguous()
+            entry["local_assoc_bias"] = torch.cat((block.local_bias, block.assoc_bias)).contiguous()
             blocks.append(entry)
         self._cache = {"content_w": content_w.contiguous(), "content_b": content_b.contiguous(),
                        "head_b": f32(self.head_bias), "blocks": blocks}
