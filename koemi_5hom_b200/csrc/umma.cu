@@ -179,14 +179,18 @@ struct Tile {
     int64_t split;     // dense: K split index
 };
 
-template <int kProblem>
+// kTileRows: A rows per tile, kBM, or 2 * kBM for the paired tiles of the
+// dense and surprise problems (two M=128 MMAs share every B stage).
+template <int kProblem, int kTileRows>
 __device__ __forceinline__ int64_t total_tiles(const UmmaArgs &a) {
-    if (kProblem == kSurprise) return ((a.rows + kBM - 1) / kBM) * a.n_tiles;
-    if (kProblem == kDense || kProblem == kDenseCluster) return ((a.rows + kBM - 1) / kBM) * a.n_tiles * a.splits;
+    if (kProblem == kSurprise) return ((a.rows + kTileRows - 1) / kTileRows) * a.n_tiles;
+    if (kProblem == kDense || kProblem == kDenseCluster) {
+        return ((a.rows + kTileRows - 1) / kTileRows) * a.n_tiles * a.splits;
+    }
     return static_cast<int64_t>(a.tile_prefix[a.experts]) * a.n_tiles;
 }
 
-template <int kProblem>
+template <int kProblem, int kTileRows>
 __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
     Tile tile{};
     const int64_t k_blocks = (a.k + kBK - 1) / kBK;
@@ -194,41 +198,41 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
     tile.k_end = k_blocks;
     if (kProblem == kDenseCluster) {
         // split fastest: the CTAs of one cluster are the splits of one tile
-        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        const int64_t m_tiles = (a.rows + kTileRows - 1) / kTileRows;
         tile.split = t % a.splits;
         const int64_t rest = t / a.splits;
         tile.m_tile = rest % m_tiles;
         tile.n = rest / m_tiles;
         tile.k_begin = tile.split * a.k_per_split;
         tile.k_end = min(k_blocks, tile.k_begin + a.k_per_split);
-        tile.row0 = tile.m_tile * kBM;
+        tile.row0 = tile.m_tile * kTileRows;
         tile.row_end = a.rows;
         return tile;
     }
     if (kProblem == kDense) {
         // m fastest, so CTAs running together share one weight tile from L2
-        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        const int64_t m_tiles = (a.rows + kTileRows - 1) / kTileRows;
         tile.m_tile = t % m_tiles;
         const int64_t rest = t / m_tiles;
         tile.n = rest % a.n_tiles;
         tile.split = rest / a.n_tiles;
         tile.k_begin = tile.split * a.k_per_split;
         tile.k_end = min(k_blocks, tile.k_begin + a.k_per_split);
-        tile.row0 = tile.m_tile * kBM;
+        tile.row0 = tile.m_tile * kTileRows;
         tile.row_end = a.rows;
         return tile;
     }
     if (kProblem == kSurprise) {
         // bands of `band` row tiles; inside a band walk N first so each vocab
         // tile is reused from L2 by every row tile of the band
-        const int64_t m_tiles = (a.rows + kBM - 1) / kBM;
+        const int64_t m_tiles = (a.rows + kTileRows - 1) / kTileRows;
         const int64_t per_band = a.band * a.n_tiles;
         const int64_t band = t / per_band;
         const int64_t in_band = t - band * per_band;
         const int64_t band_rows = min(a.band, m_tiles - band * a.band);
         tile.n = in_band / band_rows;
         tile.m_tile = band * a.band + (in_band - tile.n * band_rows);
-        tile.row0 = tile.m_tile * kBM;
+        tile.row0 = tile.m_tile * kTileRows;
         tile.row_end = a.rows;
         return tile;
     }
@@ -248,8 +252,19 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
 
 // ---------------------------------------------------------------- kernel
 
-template <int kProblem, typename T>
+template <int kProblem, typename T, bool kPair>
 __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
+    // paired tiles: 256 A rows (two 128-row halves) per tile, stages of
+    // A0 | A1 | B (64 KB, 3 of them), both 256-column accumulators in use
+    constexpr int kPipe = kPair ? 3 : kStages;
+    constexpr uint32_t kAStage = kPair ? 2 * kABytes : kABytes;
+    constexpr uint32_t kStage = kAStage + kBBytes;
+    constexpr int kTileRows = kPair ? 2 * kBM : kBM;
+    constexpr int kHalves = kPair ? 2 : 1;
+    constexpr int kAccBufs = kPair ? 1 : 2;
+    static_assert(kPipe * kStage <= kStages * kStageBytes, "stage ring exceeds the shared-memory budget");
+    static_assert(!kPair || kProblem == kSurprise || kProblem == kDense || kProblem == kDenseCluster,
+                  "paired tiles are for the dense and surprise problems");
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_addr(smem_raw);
     uint8_t *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -263,15 +278,15 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t tiles = total_tiles<kProblem>(args);
+    const int64_t tiles = total_tiles<kProblem, kTileRows>(args);
     const int64_t k_blocks = (args.k + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kPipe; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);
         }
@@ -296,14 +311,18 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-                const Tile tile = tile_at<kProblem>(args, t);
+                const Tile tile = tile_at<kProblem, kTileRows>(args, t);
                 for (int64_t kb = tile.k_begin; kb < tile.k_end; ++kb) {
                     if (!wait_or_abort(&empty[stage], phase ^ 1, abort, args.status)) break;
-                    uint8_t *a_dst = stages + stage * kStageBytes;
-                    uint8_t *b_dst = a_dst + kABytes;
-                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    uint8_t *a_dst = stages + stage * kStage;
+                    uint8_t *b_dst = a_dst + kAStage;
+                    mbar_arrive_expect_tx(&full[stage], kStage);
                     const int32_t kc = static_cast<int32_t>(kb * kBK);
                     tma_load_2d(a_dst, &args.map_a, &full[stage], kc, static_cast<int32_t>(tile.row0));
+                    if (kPair) {  // rows past the end read as zeros (full box bytes still arrive)
+                        tma_load_2d(a_dst + kABytes, &args.map_a, &full[stage], kc,
+                                    static_cast<int32_t>(tile.row0 + kBM));
+                    }
                     if (kProblem == kGated) {
                         const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * 128);
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
@@ -312,7 +331,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                         const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kBN);
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
                     }
-                    if (++stage == kStages) {
+                    if (++stage == kPipe) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -329,7 +348,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                 if (!wait_or_abort(&acc_empty[acc], acc_phase ^ 1, abort, args.status)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(acc * kBN);
-                const Tile tile = tile_at<kProblem>(args, t);
+                const Tile tile = tile_at<kProblem, kTileRows>(args, t);
                 bool ok = true;
                 for (int64_t kb = tile.k_begin; kb < tile.k_end; ++kb) {
                     if (!wait_or_abort(&full[stage], phase, abort, args.status)) {
@@ -337,22 +356,27 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_addr(stages + stage * kStageBytes);
-                    const uint32_t b_addr = a_addr + kABytes;
+                    const uint32_t a_addr = smem_addr(stages + stage * kStage);
+                    const uint32_t b_addr = a_addr + kAStage;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k) {
+                        const uint32_t accumulate = (kb > tile.k_begin || k > 0) ? 1u : 0u;
                         umma_f16(tmem_d, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
-                                 args.idesc, (kb > tile.k_begin || k > 0) ? 1u : 0u);
+                                 args.idesc, accumulate);
+                        if (kPair) {
+                            umma_f16(tmem_d + kBN, sw128_kmajor_desc(a_addr + kABytes + k * 32),
+                                     sw128_kmajor_desc(b_addr + k * 32), args.idesc, accumulate);
+                        }
                     }
                     umma_commit(&empty[stage]);
-                    if (++stage == kStages) {
+                    if (++stage == kPipe) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[acc]);
-                if (++acc == 2) {
+                if (++acc == kAccBufs) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
@@ -366,11 +390,13 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-            const Tile tile = tile_at<kProblem>(args, t);
+            const Tile tile = tile_at<kProblem, kTileRows>(args, t);
             if (!wait_or_abort(&acc_full[acc], acc_phase, abort, args.status)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
-            const int64_t row = tile.row0 + quarter * 32 + lane;
+#pragma unroll 1
+            for (int h = 0; h < kHalves; ++h) {
+            const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>((acc + h) * kBN);
+            const int64_t row = tile.row0 + h * kBM + quarter * 32 + lane;
             const bool row_ok = row < tile.row_end && row < args.rows;
             if (kProblem == kGated) {
                 const T *bg = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
@@ -437,22 +463,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                     }
                 }
             } else if (kProblem == kDenseCluster) {
-                // park the accumulator row in this CTA's shared memory (the
-                // stage ring is idle: every load was consumed by the MMAs
-                // that acc_full waited for)
-                float *parked = reinterpret_cast<float *>(stages) + (quarter * 32 + lane) * kAccStride;
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t y[32];
-                    KOEMI_TMEM_LD32(taddr + c * 32, y);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        reinterpret_cast<float4 *>(parked + c * 32)[q] =
-                            make_float4(__uint_as_float(y[4 * q]), __uint_as_float(y[4 * q + 1]),
-                                        __uint_as_float(y[4 * q + 2]), __uint_as_float(y[4 * q + 3]));
-                    }
-                }
+                // parked and reduced after the role loops, one half at a time
             } else if (kProblem == kDense) {
                 // splits == 1: out = acc + bias (fp32, row stride out_stride);
                 // splits  > 1: partials[split][row][col] = acc, reduced later
@@ -524,10 +535,11 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                     p[2] = target_logit;
                 }
             }
+            }  // halves
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            if (++acc == 2) {
+            if (++acc == kAccBufs) {
                 acc = 0;
                 acc_phase ^= 1;
             }
@@ -537,19 +549,47 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
     tc_fence_before();
     __syncthreads();
     if constexpr (kProblem == kDenseCluster) {
-        // every thread of every CTA reaches both cluster barriers, aborted or not
-        cluster_sync_all();
-        if (!*abort && blockIdx.x < tiles) {
-            const Tile tile = tile_at<kProblem>(args, blockIdx.x);
-            const uint32_t rank = cluster_ctarank();
-            const int64_t splits = args.splits;
-            constexpr int kQuads = kBN / 4;
-            const int q_begin = static_cast<int>(rank * kQuads / splits);
-            const int q_count = static_cast<int>((rank + 1) * kQuads / splits) - q_begin;
-            const T *bias = static_cast<const T *>(args.bias0);
-            float *out = static_cast<float *>(args.out);
-            const uint32_t parked_base = smem_addr(stages);
-            const int valid_rows = static_cast<int>(min(static_cast<int64_t>(kBM), args.rows - tile.row0));
+        // Per 128-row half: the epilogue warps park the accumulator rows in
+        // this CTA's shared memory (the stage ring is idle: every load was
+        // consumed by the MMAs that acc_full covered), a cluster barrier, CTA r
+        // sums column slice r over the splits through distributed shared
+        // memory, a second barrier. Every thread of every CTA reaches every
+        // cluster barrier, aborted or not.
+        const bool have_tile = !*abort && blockIdx.x < tiles;
+        const Tile tile = tile_at<kProblem, kTileRows>(args, blockIdx.x < tiles ? blockIdx.x : 0);
+        const uint32_t rank = cluster_ctarank();
+        const int64_t splits = args.splits;
+        constexpr int kQuads = kBN / 4;
+        const int q_begin = static_cast<int>(rank * kQuads / splits);
+        const int q_count = static_cast<int>((rank + 1) * kQuads / splits) - q_begin;
+        const T *bias = static_cast<const T *>(args.bias0);
+        float *out = static_cast<float *>(args.out);
+        const uint32_t parked_base = smem_addr(stages);
+        for (int h = 0; h < kHalves; ++h) {
+            const int64_t half_row0 = tile.row0 + h * kBM;
+            if (have_tile && warp >= 2) {
+                tc_fence_after();
+                const int quarter = warp & 3;
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                       static_cast<uint32_t>(h * kBN);
+                float *parked = reinterpret_cast<float *>(stages) + (quarter * 32 + lane) * kAccStride;
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t y[32];
+                    KOEMI_TMEM_LD32(taddr + c * 32, y);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        reinterpret_cast<float4 *>(parked + c * 32)[q] =
+                            make_float4(__uint_as_float(y[4 * q]), __uint_as_float(y[4 * q + 1]),
+                                        __uint_as_float(y[4 * q + 2]), __uint_as_float(y[4 * q + 3]));
+                    }
+                }
+            }
+            cluster_sync_all();
+            const int valid_rows = have_tile ? static_cast<int>(max(static_cast<int64_t>(0),
+                                                                    min(static_cast<int64_t>(kBM), args.rows - half_row0)))
+                                             : 0;
             for (int idx = threadIdx.x; idx < valid_rows * q_count; idx += kThreads) {
                 const int r = idx / q_count;
                 const int q = q_begin + (idx - r * q_count);
@@ -571,9 +611,9 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                         acc.w += v[sp].w;
                     }
                 }
-                const int64_t row = tile.row0 + r;
+                const int64_t row = half_row0 + r;
                 const int64_t col = tile.n * kBN + q * 4;
-                if (row >= args.rows || col >= args.n_out) continue;
+                if (col >= args.n_out) continue;
                 float o[4] = {acc.x, acc.y, acc.z, acc.w};
                 if (bias != nullptr) {
 #pragma unroll
@@ -586,8 +626,9 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                     for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
                 }
             }
+            cluster_sync_all();
         }
-        cluster_sync_all();
+        tc_fence_before();
     }
     if (warp == 1) {
         tc_fence_after();
@@ -616,9 +657,10 @@ int encode_kmajor(CUtensorMap *map, int dtype, const void *base, int64_t rows, i
     return encode_tensor_map(map, type, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int kProblem>
+template <int kProblem, bool kPair = false>
 int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stream) {
-    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16> : umma_gemm_kernel<kProblem, __half>;
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
+                                      : umma_gemm_kernel<kProblem, __half, kPair>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
@@ -628,9 +670,10 @@ int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stre
 }
 
 // Exactly `ctas` CTAs in clusters of `cluster` (one tile per CTA).
-template <int kProblem>
+template <int kProblem, bool kPair = false>
 int launch_clustered(const UmmaArgs &args, int dtype, int64_t ctas, int cluster, cudaStream_t stream) {
-    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16> : umma_gemm_kernel<kProblem, __half>;
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
+                                      : umma_gemm_kernel<kProblem, __half, kPair>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     cudaLaunchConfig_t config{};
     config.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
@@ -658,7 +701,7 @@ int64_t resident_cluster_ctas(int cluster) {
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64 || cluster < 1 || cluster > 8) return 0;
     std::lock_guard<std::mutex> lock(mutex);
     if (cache[device][cluster] != 0) return cache[device][cluster];
-    auto kernel = umma_gemm_kernel<kDenseCluster, __nv_bfloat16>;
+    auto kernel = umma_gemm_kernel<kDenseCluster, __nv_bfloat16, false>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) != cudaSuccess) {
         cudaGetLastError();
         return 0;
@@ -769,8 +812,12 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
 
 // K splits of a dense projection: the largest S <= 8 whose tiles x S CTAs
 // are resident at once in clusters of S, with at least 4 K blocks per split.
+// A rows per tile: two 128-row halves share each B stage once there are
+// more than 128 rows (half the weight traffic per A row of a single tile).
+int64_t tile_rows(int64_t rows) { return rows > kBM ? 2 * kBM : kBM; }
+
 int64_t dense_splits(int64_t rows, int64_t n, int64_t k) {
-    const int64_t tiles = ((rows + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * ((n + kBN - 1) / kBN);
     const int64_t k_blocks = (k + kBK - 1) / kBK;
     for (int64_t splits = 8; splits > 1; --splits) {
         if (k_blocks < 4 * splits) continue;
@@ -804,14 +851,15 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
     a.n_out = content_vocab;
     a.out_stride = 0;
     a.experts = 1;
-    a.band = 16;
     a.bias0 = bias;
     a.partials = partials;
     a.targets = targets;
     a.status = device_status_word();
     a.idesc = make_idesc(dtype);
-    const int64_t tiles = ((rows + kBM - 1) / kBM) * slices;
-    rc = launch<kSurprise>(a, dtype, tiles, stream);
+    const bool pair = tile_rows(rows) > kBM;
+    a.band = pair ? 8 : 16;  // 2048 rows per band either way
+    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * slices;
+    rc = pair ? launch<kSurprise, true>(a, dtype, tiles, stream) : launch<kSurprise, false>(a, dtype, tiles, stream);
     if (rc != KOEMI_OK) return rc;
     *handled = true;
     return KOEMI_OK;
@@ -882,8 +930,13 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     args.partials = nullptr;
     args.status = device_status_word();
     args.idesc = make_idesc(dtype);
-    const int64_t tiles = ((rows + kBM - 1) / kBM) * args.n_tiles * plan.splits;
-    if (plan.splits > 1) return launch_clustered<kDenseCluster>(args, dtype, tiles, static_cast<int>(plan.splits), s);
-    return launch<kDense>(args, dtype, tiles, s);
+    const bool pair = tile_rows(rows) > kBM;
+    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * args.n_tiles * plan.splits;
+    if (plan.splits > 1) {
+        const int cluster = static_cast<int>(plan.splits);
+        return pair ? launch_clustered<kDenseCluster, true>(args, dtype, tiles, cluster, s)
+                    : launch_clustered<kDenseCluster, false>(args, dtype, tiles, cluster, s);
+    }
+    return pair ? launch<kDense, true>(args, dtype, tiles, s) : launch<kDense, false>(args, dtype, tiles, s);
 }
 
