@@ -357,6 +357,29 @@ KOEMI_API int koemi_moe_combine_residual_rmsnorm(const float *context, const voi
                                        int64_t top_k, int64_t expert_count, float eps,
                                        int dtype, void *stream);
 
+/* koemi_moe_combine_residual_rmsnorm for a chain of blocks: the combined,
+ * normalised row x is stored as out_dtype, or, when next_norm_weight (fp32
+ * [width]) is given, the next block's input RMSNorm(x) * next_norm_weight
+ * (same eps) is stored instead, so x never goes to memory. Needs width % 4
+ * == 0, width <= 2048, top_k <= 8, 16-byte aligned rows. No counterpart in
+ * the reference (a fusion of two of its steps). */
+KOEMI_API int koemi_moe_combine_residual_rmsnorm_next(const float *context, const void *expert_out,
+                                            const int64_t *pair_positions,
+                                            const int64_t *segment_offsets, const float *weights,
+                                            const uint8_t *valid, const float *norm_weight,
+                                            const float *next_norm_weight, void *out, int out_dtype,
+                                            int64_t tokens, int64_t width, int64_t top_k,
+                                            int64_t expert_count, float eps, int dtype, void *stream);
+
+/* Sorted pair rows of a permutation already computed by koemi_moe_permute_topk:
+ * out[i] = rows[sorted_rows[i]] converted from rows_dtype to out_dtype for
+ * i < segment_offsets[expert_count], zero past it. Lets one permutation serve
+ * several row sets (the hash route of a decode step is the same in every
+ * block). Needs width % 4 == 0 and 16-byte aligned rows. */
+KOEMI_API int koemi_moe_gather_rows(const void *rows, int rows_dtype, const int64_t *sorted_rows,
+                          const int64_t *segment_offsets, int64_t expert_count, void *out, int out_dtype,
+                          int64_t pairs, int64_t width, void *stream);
+
 /* ---------------------------------------------------- expert parallelism */
 
 /* Expert-parallel dispatch slab (no counterpart in the reference, which has

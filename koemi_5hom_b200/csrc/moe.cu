@@ -606,23 +606,43 @@ __device__ __forceinline__ float4 load_quad(const T *p) {
     }
 }
 
+// Four fp32 values stored as TO (16 bytes of fp32 or 8 bytes of a 16-bit type).
+template <typename TO>
+__device__ __forceinline__ void store_quad(TO *dst, float4 v) {
+    if constexpr (std::is_same<TO, float>::value) {
+        *reinterpret_cast<float4 *>(dst) = v;
+    } else {
+        union {
+            TO h[4];
+            uint2 u;
+        } out;
+        out.h[0] = from_acc<TO>(v.x);
+        out.h[1] = from_acc<TO>(v.y);
+        out.h[2] = from_acc<TO>(v.z);
+        out.h[3] = from_acc<TO>(v.w);
+        *reinterpret_cast<uint2 *>(dst) = out.u;
+    }
+}
+
 // The vector combine with the row held in registers (NQ quads per lane):
 // every load of a row is issued before its values are used, and the output
-// is written once.
-template <typename T, int NQ>
+// is written once. With `next_norm`, the stored row is instead the next
+// block's normalised input RMSNorm(x) * next_norm of the combined row x.
+template <typename T, int NQ, typename TO>
 __global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__ context, const T *__restrict__ y,
                                                        const int64_t *__restrict__ positions,
                                                        const int64_t *__restrict__ segment_offsets,
                                                        const float *__restrict__ weights,
                                                        const uint8_t *__restrict__ valid,
                                                        const float *__restrict__ norm_weight,
-                                                       float *__restrict__ out, int64_t tokens, int64_t width,
-                                                       int64_t top_k, int64_t experts, float eps) {
+                                                       const float *__restrict__ next_norm, TO *__restrict__ out,
+                                                       int64_t tokens, int64_t width, int64_t top_k, int64_t experts,
+                                                       float eps) {
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= tokens) return;
     const float4 *cr = reinterpret_cast<const float4 *>(context + row * width);
-    float4 *orow = reinterpret_cast<float4 *>(out + row * width);
+    TO *orow = out + row * width;
     const int64_t quads = width / 4;
     float4 u[NQ];
 #pragma unroll
@@ -630,46 +650,64 @@ __global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__
         const int64_t c = lane + 32 * i;
         u[i] = c < quads ? __ldg(cr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (valid != nullptr && valid[row] == 0) {
+    const bool combine = valid == nullptr || valid[row] != 0;
+    if (combine) {
+        const int64_t valid_pairs = segment_offsets[experts];
+        for (int64_t s = 0; s < top_k; ++s) {
+            const int64_t pos = positions[row * top_k + s];
+            if (pos < 0 || pos >= valid_pairs) continue;
+            const T *src = y + pos * width;
+            const float scale = weights != nullptr ? weights[row * top_k + s] : 1.0f / static_cast<float>(top_k);
+            float4 e[NQ];
+#pragma unroll
+            for (int i = 0; i < NQ; ++i) {
+                const int64_t c = lane + 32 * i;
+                e[i] = c < quads ? load_quad(src + c * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < NQ; ++i) {
+                u[i].x += e[i].x * scale;
+                u[i].y += e[i].y * scale;
+                u[i].z += e[i].z * scale;
+                u[i].w += e[i].w * scale;
+            }
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) sum += u[i].x * u[i].x + u[i].y * u[i].y + u[i].z * u[i].z + u[i].w * u[i].w;
+        sum = warp_sum(sum);
+        const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+        const float4 *wq = reinterpret_cast<const float4 *>(norm_weight);
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
             const int64_t c = lane + 32 * i;
-            if (c < quads) orow[c] = u[i];
+            const float4 w = c < quads ? __ldg(wq + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            u[i] = make_float4(u[i].x * (inv * w.x), u[i].y * (inv * w.y), u[i].z * (inv * w.z), u[i].w * (inv * w.w));
         }
-        return;
     }
-    const int64_t valid_pairs = segment_offsets[experts];
-    for (int64_t s = 0; s < top_k; ++s) {
-        const int64_t pos = positions[row * top_k + s];
-        if (pos < 0 || pos >= valid_pairs) continue;
-        const T *src = y + pos * width;
-        const float scale = weights != nullptr ? weights[row * top_k + s] : 1.0f / static_cast<float>(top_k);
-        float4 e[NQ];
+    if (next_norm != nullptr) {  // the input norm of the next block, as rms_rows_cached computes it
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+            sum = fmaf(u[i].x, u[i].x, sum);
+            sum = fmaf(u[i].y, u[i].y, sum);
+            sum = fmaf(u[i].z, u[i].z, sum);
+            sum = fmaf(u[i].w, u[i].w, sum);
+        }
+        sum = warp_sum(sum);
+        const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+        const float4 *nq = reinterpret_cast<const float4 *>(next_norm);
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
             const int64_t c = lane + 32 * i;
-            e[i] = c < quads ? load_quad(src + c * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int i = 0; i < NQ; ++i) {
-            u[i].x += e[i].x * scale;
-            u[i].y += e[i].y * scale;
-            u[i].z += e[i].z * scale;
-            u[i].w += e[i].w * scale;
+            const float4 w = c < quads ? __ldg(nq + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            u[i] = make_float4(u[i].x * inv * w.x, u[i].y * inv * w.y, u[i].z * inv * w.z, u[i].w * inv * w.w);
         }
     }
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NQ; ++i) sum += u[i].x * u[i].x + u[i].y * u[i].y + u[i].z * u[i].z + u[i].w * u[i].w;
-    sum = warp_sum(sum);
-    const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
-    const float4 *wq = reinterpret_cast<const float4 *>(norm_weight);
 #pragma unroll
     for (int i = 0; i < NQ; ++i) {
         const int64_t c = lane + 32 * i;
-        if (c >= quads) continue;
-        const float4 w = __ldg(wq + c);
-        orow[c] = make_float4(u[i].x * (inv * w.x), u[i].y * (inv * w.y), u[i].z * (inv * w.z), u[i].w * (inv * w.w));
+        if (c < quads) store_quad(orow + c * 4, u[i]);
     }
 }
 
@@ -903,15 +941,15 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     if (vector && quads_per_lane <= 16) {
         auto run = [&](auto kernel, const auto *typed) -> int {
             kernel<<<blocks, threads, 0, s>>>(context, typed, pair_positions, segment_offsets, weights, valid,
-                                              norm_weight, out, tokens, width, top_k, expert_count, eps);
+                                              norm_weight, nullptr, out, tokens, width, top_k, expert_count, eps);
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
         };
         auto by_width = [&](const auto *typed) -> int {
             using T = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
-            if (quads_per_lane <= 4) return run(combine_residual_rmsnorm_cached_kernel<T, 4>, typed);
-            if (quads_per_lane <= 8) return run(combine_residual_rmsnorm_cached_kernel<T, 8>, typed);
-            return run(combine_residual_rmsnorm_cached_kernel<T, 16>, typed);
+            if (quads_per_lane <= 4) return run(combine_residual_rmsnorm_cached_kernel<T, 4, float>, typed);
+            if (quads_per_lane <= 8) return run(combine_residual_rmsnorm_cached_kernel<T, 8, float>, typed);
+            return run(combine_residual_rmsnorm_cached_kernel<T, 16, float>, typed);
         };
         switch (dtype) {
             case KOEMI_F32: return by_width(static_cast<const float *>(expert_out));
@@ -1046,4 +1084,119 @@ extern "C" int koemi_moe_ep_unpack(const void *slab, const int64_t *sorted_exper
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Combine fused with the next block's input norm (decode chains of blocks).
+
+extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, const void *expert_out,
+                                                       const int64_t *pair_positions,
+                                                       const int64_t *segment_offsets, const float *weights,
+                                                       const uint8_t *valid, const float *norm_weight,
+                                                       const float *next_norm_weight, void *out, int out_dtype,
+                                                       int64_t tokens, int64_t width, int64_t top_k,
+                                                       int64_t expert_count, float eps, int dtype, void *stream) {
+    clear_error();
+    if (tokens < 0 || width < 0 || top_k < 1) return fail(KOEMI_ERR_INVALID, "bad combine sizes");
+    if (tokens == 0 || width == 0) return KOEMI_OK;
+    const int64_t quads_per_lane = ceil_div(width / 4, 32);
+    if (width % 4 != 0 || quads_per_lane > 16 || top_k > 8 || !aligned(context, 16) || !aligned(norm_weight, 16) ||
+        !aligned(expert_out, 8) || !aligned(out, 16) || (next_norm_weight != nullptr && !aligned(next_norm_weight, 16))) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "fused combine needs width %% 4 == 0, width <= 2048, top_k <= 8 and aligned rows");
+    }
+    const int rows_per_block = tokens >= static_cast<int64_t>(sm_count()) * 32 ? 8 : 2;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, rows_per_block));
+    const int threads = rows_per_block * 32;
+    cudaStream_t s = as_stream(stream);
+    auto run = [&](auto *typed, auto *out_typed) -> int {
+        using T = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
+        using TO = std::remove_pointer_t<decltype(out_typed)>;
+        auto launch = [&](auto kernel) -> int {
+            kernel<<<blocks, threads, 0, s>>>(context, typed, pair_positions, segment_offsets, weights, valid,
+                                              norm_weight, next_norm_weight, out_typed, tokens, width, top_k,
+                                              expert_count, eps);
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
+        };
+        if (quads_per_lane <= 4) return launch(combine_residual_rmsnorm_cached_kernel<T, 4, TO>);
+        if (quads_per_lane <= 8) return launch(combine_residual_rmsnorm_cached_kernel<T, 8, TO>);
+        return launch(combine_residual_rmsnorm_cached_kernel<T, 16, TO>);
+    };
+    auto by_out = [&](auto *typed) -> int {
+        switch (out_dtype) {
+            case KOEMI_F32: return run(typed, static_cast<float *>(out));
+            case KOEMI_BF16: return run(typed, static_cast<__nv_bfloat16 *>(out));
+            case KOEMI_F16: return run(typed, static_cast<__half *>(out));
+            default: return fail(KOEMI_ERR_INVALID, "output must be f32, f16 or bf16");
+        }
+    };
+    switch (dtype) {
+        case KOEMI_F32: return by_out(static_cast<const float *>(expert_out));
+        case KOEMI_F16: return by_out(static_cast<const __half *>(expert_out));
+        case KOEMI_BF16: return by_out(static_cast<const __nv_bfloat16 *>(expert_out));
+        default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Gather of sorted pair rows with a type conversion, for callers that reuse
+// one permutation for several row sets (the hash route of a decode step is
+// the same for every block; only the rows differ).
+
+template <typename TI, typename TO>
+__global__ void gather_convert_kernel(const TI *__restrict__ rows, const int64_t *__restrict__ sorted_rows,
+                                      const int64_t *__restrict__ valid_count, TO *__restrict__ out, int64_t pairs,
+                                      int64_t width) {
+    const int lane = threadIdx.x & 31;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (i >= pairs) return;
+    const bool live = i < *valid_count;
+    const TI *src = rows + (live ? sorted_rows[i] : 0) * width;
+    TO *dst = out + i * width;
+    for (int64_t c = lane * 4; c < width; c += 128) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) {
+            if constexpr (std::is_same<TI, float>::value) {
+                v = __ldg(reinterpret_cast<const float4 *>(src + c));
+            } else {
+                v = load_quad(src + c);
+            }
+        }
+        store_quad(dst + c, v);
+    }
+}
+
+extern "C" int koemi_moe_gather_rows(const void *rows, int rows_dtype, const int64_t *sorted_rows,
+                                     const int64_t *segment_offsets, int64_t expert_count, void *out, int out_dtype,
+                                     int64_t pairs, int64_t width, void *stream) {
+    clear_error();
+    if (pairs < 0 || width < 1 || expert_count < 0) return fail(KOEMI_ERR_INVALID, "bad gather sizes");
+    if (pairs == 0) return KOEMI_OK;
+    if (width % 4 != 0 || !aligned(rows, 16) || !aligned(out, 16)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "row gather needs width %% 4 == 0 and 16-byte aligned rows");
+    }
+    const unsigned blocks = static_cast<unsigned>(ceil_div(pairs, 8));
+    const int64_t *valid_count = segment_offsets + expert_count;
+    cudaStream_t s = as_stream(stream);
+    auto run = [&](const auto *in, auto *typed_out) -> int {
+        using TI = std::remove_cv_t<std::remove_pointer_t<decltype(in)>>;
+        using TO = std::remove_pointer_t<decltype(typed_out)>;
+        gather_convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(in, sorted_rows, valid_count, typed_out, pairs, width);
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    };
+    auto by_out = [&](const auto *in) -> int {
+        switch (out_dtype) {
+            case KOEMI_F32: return run(in, static_cast<float *>(out));
+            case KOEMI_BF16: return run(in, static_cast<__nv_bfloat16 *>(out));
+            case KOEMI_F16: return run(in, static_cast<__half *>(out));
+            default: return fail(KOEMI_ERR_INVALID, "output must be f32, f16 or bf16");
+        }
+    };
+    switch (rows_dtype) {
+        case KOEMI_F32: return by_out(static_cast<const float *>(rows));
+        case KOEMI_BF16: return by_out(static_cast<const __nv_bfloat16 *>(rows));
+        case KOEMI_F16: return by_out(static_cast<const __half *>(rows));
+        default: return fail(KOEMI_ERR_INVALID, "rows must be f32, f16 or bf16");
+    }
 }

@@ -812,12 +812,17 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
 
 // K splits of a dense projection: the largest S <= 8 whose tiles x S CTAs
 // are resident at once in clusters of S, with at least 4 K blocks per split.
-// A rows per tile: two 128-row halves share each B stage once there are
-// more than 128 rows (half the weight traffic per A row of a single tile).
-int64_t tile_rows(int64_t rows) { return rows > kBM ? 2 * kBM : kBM; }
+// A rows per surprise tile: 129..256 rows (a decode batch) run as one paired
+// tile per vocabulary slice, so every head byte crosses L2 -> SM once instead
+// of once per 128-row tile, in one wave. Longer inputs keep 128-row tiles
+// and the double-buffered accumulators (an epilogue overlaps the next tile's
+// MMAs), which measured faster there, as did 128-row tiles for the K-split
+// dense projections (their shorter main loops gain less than the paired
+// epilogue costs).
+int64_t surprise_tile_rows(int64_t rows) { return rows > kBM && rows <= 2 * kBM ? 2 * kBM : kBM; }
 
 int64_t dense_splits(int64_t rows, int64_t n, int64_t k) {
-    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * ((n + kBN - 1) / kBN);
+    const int64_t tiles = ((rows + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
     const int64_t k_blocks = (k + kBK - 1) / kBK;
     for (int64_t splits = 8; splits > 1; --splits) {
         if (k_blocks < 4 * splits) continue;
@@ -856,9 +861,9 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
     a.targets = targets;
     a.status = device_status_word();
     a.idesc = make_idesc(dtype);
-    const bool pair = tile_rows(rows) > kBM;
-    a.band = pair ? 8 : 16;  // 2048 rows per band either way
-    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * slices;
+    const bool pair = surprise_tile_rows(rows) > kBM;
+    a.band = 16;
+    const int64_t tiles = ((rows + surprise_tile_rows(rows) - 1) / surprise_tile_rows(rows)) * slices;
     rc = pair ? launch<kSurprise, true>(a, dtype, tiles, stream) : launch<kSurprise, false>(a, dtype, tiles, stream);
     if (rc != KOEMI_OK) return rc;
     *handled = true;
@@ -930,13 +935,8 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     args.partials = nullptr;
     args.status = device_status_word();
     args.idesc = make_idesc(dtype);
-    const bool pair = tile_rows(rows) > kBM;
-    const int64_t tiles = ((rows + tile_rows(rows) - 1) / tile_rows(rows)) * args.n_tiles * plan.splits;
-    if (plan.splits > 1) {
-        const int cluster = static_cast<int>(plan.splits);
-        return pair ? launch_clustered<kDenseCluster, true>(args, dtype, tiles, cluster, s)
-                    : launch_clustered<kDenseCluster, false>(args, dtype, tiles, cluster, s);
-    }
-    return pair ? launch<kDense, true>(args, dtype, tiles, s) : launch<kDense, false>(args, dtype, tiles, s);
+    const int64_t tiles = ((rows + kBM - 1) / kBM) * args.n_tiles * plan.splits;
+    if (plan.splits > 1) return launch_clustered<kDenseCluster>(args, dtype, tiles, static_cast<int>(plan.splits), s);
+    return launch<kDense>(args, dtype, tiles, s);
 }
 

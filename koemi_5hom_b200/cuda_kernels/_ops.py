@@ -413,3 +413,49 @@ def ep_unpack(slab: Tensor, sorted_experts: Tensor, segment_offsets: Tensor, ran
 @ep_unpack.register_fake
 def _(slab, sorted_experts, segment_offsets, ranks, local_experts, capacity):
     return slab.new_empty(sorted_experts.shape[0], slab.shape[1])
+
+
+@torch.library.custom_op("koemi_b200::combine_residual_rmsnorm_next", mutates_args=())
+def combine_residual_rmsnorm_next(context: Tensor, expert_out: Tensor, pair_positions: Tensor,
+                                  segment_offsets: Tensor, weights: Tensor | None, valid: Tensor,
+                                  norm_weight: Tensor, next_norm_weight: Tensor | None, top_k: int, eps: float,
+                                  out_dtype: torch.dtype) -> Tensor:
+    """``combine_residual_rmsnorm`` whose stored row is the next block's
+    input RMSNorm(x) * next_norm_weight (or x itself without a next norm), in
+    ``out_dtype``."""
+    (context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight,
+     next_norm_weight) = _dense(context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight,
+                                next_norm_weight)
+    stream = _prepare(context)
+    tokens, width = context.shape
+    experts = segment_offsets.shape[0] - 1
+    out = torch.empty(tokens, width, dtype=out_dtype, device=context.device)
+    call("koemi_moe_combine_residual_rmsnorm_next", ptr(context), ptr(expert_out), ptr(pair_positions),
+         ptr(segment_offsets), ptr(weights), ptr(valid), ptr(norm_weight), ptr(next_norm_weight), ptr(out),
+         dtype_code(out_dtype), tokens, width, top_k, experts, eps, dtype_code(expert_out.dtype), stream)
+    return out
+
+
+@combine_residual_rmsnorm_next.register_fake
+def _(context, expert_out, pair_positions, segment_offsets, weights, valid, norm_weight, next_norm_weight, top_k, eps,
+      out_dtype):
+    return context.new_empty(context.shape, dtype=out_dtype)
+
+
+@torch.library.custom_op("koemi_b200::gather_rows", mutates_args=())
+def gather_rows(rows: Tensor, sorted_rows: Tensor, segment_offsets: Tensor, out_dtype: torch.dtype) -> Tensor:
+    """Rows of an existing permutation (``sorted_rows`` from ``permute_topk``)
+    in ``out_dtype``, zero past the valid pairs."""
+    rows, sorted_rows, segment_offsets = _dense(rows, sorted_rows, segment_offsets)
+    stream = _prepare(rows)
+    pairs = sorted_rows.shape[0]
+    width = rows.shape[1]
+    out = torch.empty(pairs, width, dtype=out_dtype, device=rows.device)
+    call("koemi_moe_gather_rows", ptr(rows), dtype_code(rows.dtype), ptr(sorted_rows), ptr(segment_offsets),
+         segment_offsets.shape[0] - 1, ptr(out), dtype_code(out_dtype), pairs, width, stream)
+    return out
+
+
+@gather_rows.register_fake
+def _(rows, sorted_rows, segment_offsets, out_dtype):
+    return rows.new_empty(sorted_rows.shape[0], rows.shape[1], dtype=out_dtype)

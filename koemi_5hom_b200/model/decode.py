@@ -9,12 +9,14 @@ tensor of the state at a fixed address and updates it in place:
 - salient rings are circular per stream (head + count of admitted entries);
 - working state, associative bases and normalisers are overwritten in place.
 
-A step is then: per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
+A step is then: the hash route and its stable permutation once (the route
+depends only on the ids); per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
 -> surprise (tcgen05 head GEMM + online LSE) -> one local|assoc GEMM ->
 ``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` (with the
 feature projection of key and query fused in) -> fusion GEMM
 (its input rows are written in place by the three kernels) -> rms_norm ->
-route / permute / grouped expert MLP / combine; then the head GEMM. With fixed
+row gather through the shared permutation -> grouped expert MLP -> combine,
+which also writes the next block's normalised input; then the head GEMM. With fixed
 addresses the whole step is one CUDA graph with no copy-back of the state.
 
 ``to_koemi_state`` restores the reference layout (rings oldest first, salient
@@ -178,10 +180,22 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         targets = None
     else:
         targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
+    # the hash route depends only on the ids, so one permutation serves every
+    # block (each block gathers its own rows through it)
+    shared_route = s.expert_count > 0 and s.expert_routing != "learned"
+    if shared_route:
+        assignments = _ops.route_topk(ids, dstate.last_token_ids, valid, s.expert_count, s.expert_top_k)
+        _, sorted_tokens, sorted_experts, offsets, positions = _ops.permute_topk(
+            x, assignments, valid, s.expert_count, False)
+        weights = None
+    # the combine of block i also writes block i + 1's normalised input
+    fused_combine = s.expert_count > 0 and d % 4 == 0 and d <= 2048 and s.expert_top_k <= 8
+    u = None
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
         st = dstate.blocks[index]
-        u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, model.compute_dtype)
+        if u is None:
+            u = _ops.rms_norm(x, None, bc["input_norm"], None, NORM_EPSILON, model.compute_dtype)
         pre = model._linear(u, block.gates_weight, block.gates_bias)
         # fusion input rows, written in place by the step kernels: h | memory | local | salient
         concat = torch.empty(batch, 4 * d, dtype=concat_dtype, device=device)
@@ -209,20 +223,31 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
              ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d, s.memory_features, out_code, stream)
         fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
+        u = None
         if s.expert_count == 0:
             x = context
             continue
-        if s.expert_routing == "learned":
+        if shared_route:
+            sorted_context = _ops.gather_rows(context, sorted_tokens, offsets, model.compute_dtype)
+        else:
             gate_logits = model._linear(torch.where(valid.unsqueeze(-1), context, 0.0), block.router_weight, None)
             assignments, weights, _ = _ops.learned_topk(gate_logits, valid, s.expert_top_k, bool(s.router_renormalize))
-        else:
-            assignments = _ops.route_topk(ids, dstate.last_token_ids, valid, s.expert_count, s.expert_top_k)
-            weights = None
-        sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
-            context.to(model.compute_dtype), assignments, valid, s.expert_count, True)
+            sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
+                context.to(model.compute_dtype), assignments, valid, s.expert_count, True)
         expert_out = model.expert_mlp(block, sorted_context, sorted_experts, offsets, mode="padded")
-        x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid, bc["expert_norm"],
-                                          s.expert_top_k, NORM_EPSILON)
+        if fused_combine:
+            last = index + 1 == len(model.blocks)
+            next_norm = None if last else cache["blocks"][index + 1]["input_norm"]
+            y = _ops.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, weights, valid,
+                                                   bc["expert_norm"], next_norm, s.expert_top_k, NORM_EPSILON,
+                                                   model.compute_dtype)
+            if last:
+                x = y
+            else:
+                u = y
+        else:
+            x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid,
+                                              bc["expert_norm"], s.expert_top_k, NORM_EPSILON)
     logits = model._linear(x, model.head_weight, model.head_bias)
     dstate.last_token_ids.copy_(torch.where(valid, ids, dstate.last_token_ids))
     dstate.local_head.add_(1).remainder_(dstate.blocks[0].local_keys.shape[1])

@@ -268,3 +268,35 @@ def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
     torch.testing.assert_close(out.double(), expected, rtol=1e-4, atol=1e-4)
     again = _ops.dense_projection(a, w, b)
     assert torch.equal(out, again)  # fixed-order split-K reduction
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gather_rows_equals_permute_gather(out_dtype, cuda):
+    g = torch.Generator().manual_seed(11)
+    tokens, experts, width = 300, 16, 128
+    context = torch.randn(tokens, width, generator=g).to(cuda)
+    assignments = torch.randint(-1, experts + 1, (tokens, 2), generator=g).to(cuda)
+    valid = (torch.rand(tokens, generator=g) > 0.1).to(cuda)
+    sorted_ctx, rows, _, offsets, _ = _ops.permute_topk(context.to(out_dtype), assignments, valid, experts, True)
+    got = _ops.gather_rows(context, rows, offsets, out_dtype)
+    assert torch.equal(got, sorted_ctx)
+
+
+@pytest.mark.parametrize("with_next", [True, False])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_combine_with_next_norm_equals_two_ops(with_next, out_dtype, cuda):
+    from koemi_5hom_b200.cuda_kernels import _ops as ops_
+    g = torch.Generator().manual_seed(12)
+    tokens, experts, width, k = 256, 8, 2048, 2
+    context = torch.randn(tokens, width, generator=g).to(cuda)
+    assignments = torch.randint(0, experts, (tokens, k), generator=g).to(cuda)
+    valid = (torch.rand(tokens, generator=g) > 0.1).to(cuda)
+    _, rows, _, offsets, positions = ops_.permute_topk(context, assignments, valid, experts, False)
+    expert_out = torch.randn(tokens * k, width, generator=g).bfloat16().to(cuda)
+    norm = (1 + 0.1 * torch.randn(width, generator=g)).to(cuda)
+    nxt = (1 + 0.1 * torch.randn(width, generator=g)).to(cuda) if with_next else None
+    x = ops_.combine_residual_rmsnorm(context, expert_out, positions, offsets, None, valid, norm, k, 1e-6)
+    expected = ops_.rms_norm(x, None, nxt, None, 1e-6, out_dtype) if with_next else x.to(out_dtype)
+    got = ops_.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, None, valid, norm, nxt, k, 1e-6,
+                                             out_dtype)
+    assert torch.equal(got, expected)
