@@ -302,6 +302,225 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     if (threadIdx.x == 0) (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
 }
 
+// The same step with each (stream, ring) split over a thread-block cluster of
+// gridDim.z CTAs, for batches too small to fill the GPU with one CTA per
+// ring: CTA p scores slots [p S / P, (p + 1) S / P) and sums their weighted
+// values into a partial row; the softmax maximum, the best cosine, the
+// weight totals and the partial rows are combined across the cluster through
+// distributed shared memory (in CTA order, so the result is deterministic);
+// CTA p writes output columns [p d / P, (p + 1) d / P). The ring write and the
+// admission bookkeeping are done by the cluster's first CTA after every CTA
+// has read the ring.
+__device__ __forceinline__ float ld_dsmem_f32(const float *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename TR, typename TO>
+__global__ __launch_bounds__(kRingThreads) void ring_decode_split_kernel(RingArgs a) {
+    using P = RingPacket<TR>;
+    constexpr int W = P::kWidth;
+    extern __shared__ float shared[];
+    const bool local = blockIdx.y == 0;
+    const int64_t b = blockIdx.x;
+    const int64_t d = a.width;
+    const int64_t slots = local ? a.local_slots : a.salient_slots;
+    const uint32_t parts = gridDim.z;
+    const uint32_t part = blockIdx.z;  // == rank in the cluster (cluster dims (1, 1, parts))
+    const int64_t slot_begin = slots * part / parts;
+    const int64_t slot_end = slots * (part + 1) / parts;
+    const int64_t own = slot_end - slot_begin;
+    float *q = shared;                 // [d]
+    float *partial = q + d;            // [d] this CTA's weighted value sums
+    float *score = partial + d;        // [own]
+    float *cosine = score + own;       // [own]
+    float *scratch = cosine + own;     // [kRingWarps]
+    __shared__ float cl_max, cl_cos, cl_total;
+    __shared__ int32_t write_slot;
+    __shared__ int32_t live_count;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float *query = a.queries + b * a.query_stride;
+    float qq = 0.0f;
+    for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
+        const float v = query[c];
+        q[c] = v;
+        qq += v * v;
+    }
+    const float q_norm = sqrtf(block_reduce(qq, scratch, false));
+    TR *keys = static_cast<TR *>(local ? a.local_keys : a.salient_keys) + b * slots * d;
+    TR *values = static_cast<TR *>(local ? a.local_values : a.salient_values) + b * slots * d;
+    const uint8_t *flags = (local ? a.local_valid : a.salient_valid) + b * slots;
+    const float scale = rsqrtf(static_cast<float>(d));
+    const int64_t packets = d / W;
+
+    for (int64_t i = warp; i < own; i += kRingWarps) {
+        const int64_t s = slot_begin + i;
+        if (!flags[s]) {
+            if (lane == 0) {
+                score[i] = -INFINITY;
+                cosine[i] = -INFINITY;
+            }
+            continue;
+        }
+        const TR *row = keys + s * d;
+        float dot = 0.0f, kk = 0.0f;
+#pragma unroll 8
+        for (int64_t c = lane; c < packets; c += 32) {
+            float k[W];
+            P::load(row + c * W, k);
+#pragma unroll
+            for (int e = 0; e < W; ++e) {
+                dot = fmaf(k[e], q[c * W + e], dot);
+                kk = fmaf(k[e], k[e], kk);
+            }
+        }
+        dot = warp_sum(dot);
+        kk = warp_sum(kk);
+        if (lane == 0) {
+            score[i] = dot * scale;
+            cosine[i] = dot / (fmaxf(sqrtf(kk), 1e-12f) * fmaxf(q_norm, 1e-12f));
+        }
+    }
+    __syncthreads();
+    float m = -INFINITY, best = -INFINITY;
+    for (int64_t i = threadIdx.x; i < own; i += kRingThreads) {
+        m = fmaxf(m, score[i]);
+        best = fmaxf(best, cosine[i]);
+    }
+    m = block_reduce(m, scratch, true);
+    best = block_reduce(best, scratch, true);
+    if (threadIdx.x == 0) {
+        cl_max = m;
+        cl_cos = best;
+    }
+    cluster_barrier();  // 1: every CTA's maximum and best cosine are visible
+    m = -INFINITY;
+    best = -INFINITY;
+    for (uint32_t r = 0; r < parts; ++r) {
+        m = fmaxf(m, ld_dsmem_f32(&cl_max, r));
+        best = fmaxf(best, ld_dsmem_f32(&cl_cos, r));
+    }
+    const bool any = m != -INFINITY;
+    float total = 0.0f;
+    for (int64_t i = threadIdx.x; i < own; i += kRingThreads) {
+        const float w = any && score[i] != -INFINITY ? expf(score[i] - m) : 0.0f;
+        score[i] = w;
+        total += w;
+    }
+    total = block_reduce(total, scratch, false);
+    if (threadIdx.x == 0) cl_total = total;
+    int32_t *live = reinterpret_cast<int32_t *>(cosine);
+    if (warp == 0) {
+        int32_t base = 0;
+        for (int64_t i0 = 0; i0 < own; i0 += 32) {
+            const int64_t i = i0 + lane;
+            const bool nonzero = i < own && score[i] != 0.0f;
+            const unsigned mask = __ballot_sync(0xffffffffu, nonzero);
+            if (nonzero) live[base + __popc(mask & ((1u << lane) - 1u))] = static_cast<int32_t>(i);
+            base += __popc(mask);
+        }
+        if (lane == 0) live_count = base;
+    }
+    __syncthreads();
+    const int32_t n_live = live_count;
+    constexpr int kValueUnroll = 8;
+    for (int64_t c = threadIdx.x; c < packets; c += kRingThreads) {
+        float acc[W];
+#pragma unroll
+        for (int e = 0; e < W; ++e) acc[e] = 0.0f;
+        int32_t i = 0;
+        for (; i + kValueUnroll <= n_live; i += kValueUnroll) {
+            float v[kValueUnroll][W], w[kValueUnroll];
+#pragma unroll
+            for (int u = 0; u < kValueUnroll; ++u) {
+                const int32_t li = live[i + u];
+                w[u] = score[li];
+                P::load(values + (slot_begin + li) * d + c * W, v[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < kValueUnroll; ++u) {
+#pragma unroll
+                for (int e = 0; e < W; ++e) acc[e] = fmaf(w[u], v[u][e], acc[e]);
+            }
+        }
+        for (; i < n_live; ++i) {
+            const int32_t li = live[i];
+            const float w = score[li];
+            float v[W];
+            P::load(values + (slot_begin + li) * d + c * W, v);
+#pragma unroll
+            for (int e = 0; e < W; ++e) acc[e] = fmaf(w, v[e], acc[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < W; ++e) partial[c * W + e] = acc[e];
+    }
+    cluster_barrier();  // 2: partial rows and totals are visible; every ring read is done
+    float all_total = 0.0f;
+    for (uint32_t r = 0; r < parts; ++r) all_total += ld_dsmem_f32(&cl_total, r);
+    const float inv_total = any ? 1.0f / all_total : 0.0f;
+    TO *out = static_cast<TO *>(local ? a.local_out : a.salient_out) + b * a.out_stride;
+    const int64_t col_begin = d * part / parts, col_end = d * (part + 1) / parts;
+    for (int64_t c = col_begin + threadIdx.x; c < col_end; c += kRingThreads) {
+        float sum = 0.0f;
+        for (uint32_t r = 0; r < parts; ++r) sum += ld_dsmem_f32(partial + c, r);
+        out[c] = from_acc<TO>(sum * inv_total);
+    }
+    const bool token_valid = a.valid == nullptr || a.valid[b] != 0;
+    if (part == 0) {
+        if (local && threadIdx.x == 0 && a.novelty_out != nullptr) {
+            a.novelty_out[b] = any ? fminf(fmaxf(1.0f - best, 0.0f), 1.0f) : 1.0f;
+        }
+        if (threadIdx.x == 0) {
+            if (local) {
+                write_slot = static_cast<int32_t>(*a.local_head);
+            } else {
+                const bool admitted = token_valid && a.surprise[b] > a.threshold;
+                if (a.admission_out != nullptr) a.admission_out[b] = admitted;
+                write_slot = -1;
+                if (admitted) {
+                    const int32_t head = a.salient_head[b];
+                    const int32_t count = a.salient_count[b];
+                    if (count < slots) {
+                        write_slot = static_cast<int32_t>((head + count) % slots);
+                        a.salient_count[b] = count + 1;
+                    } else {
+                        write_slot = head;
+                        a.salient_head[b] = static_cast<int32_t>((head + 1) % slots);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        const int32_t slot = write_slot;
+        if (slot >= 0) {
+            TR *key_dst = keys + slot * d;
+            TR *value_dst = values + slot * d;
+            const float *entry = a.entries + b * a.entry_stride;
+            for (int64_t c = threadIdx.x; c < packets; c += kRingThreads) {
+                float k[W], v[W];
+#pragma unroll
+                for (int e = 0; e < W; ++e) {
+                    k[e] = token_valid ? entry[c * W + e] : 0.0f;
+                    v[e] = token_valid ? entry[d + c * W + e] : 0.0f;
+                }
+                P::store(key_dst + c * W, k);
+                P::store(value_dst + c * W, v);
+            }
+            if (threadIdx.x == 0) {
+                (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
+            }
+        }
+    }
+    cluster_barrier();  // 3: no CTA leaves while another still reads its shared memory
+}
+
 // ----------------------------------------------------------- associative
 constexpr int kAssocThreads = 512;
 
@@ -347,11 +566,14 @@ __device__ void assoc_feature_logits(const float *__restrict__ proj, const TW *_
     }
 }
 
-// One CTA per stream. The memory row i (m features) is read as m/4 float4
-// packets by m/4 adjacent threads, which combine their partial dot products
-// with the query features by shuffles; the decayed write goes back in place.
-// feature_logits ([2, batch, m]) may be NULL, in which case the logits come
-// from feature_weight / feature_bias in the kernel.
+// gridDim.y CTAs per stream (one thread-block cluster) split the d memory
+// rows; each recomputes the features. The memory row i (m features) is read
+// as m/4 float4 packets by m/4 adjacent threads, which combine their partial
+// dot products with the query features by shuffles; the decayed write goes
+// back in place. The normaliser is updated by the cluster's first CTA after
+// a cluster barrier, once every CTA has read it. feature_logits ([2, batch,
+// m]) may be NULL, in which case the logits come from feature_weight /
+// feature_bias in the kernel.
 template <typename TO, typename TW>
 __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float *__restrict__ projections, int64_t proj_stride, const float *__restrict__ feature_logits,
@@ -403,6 +625,8 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float reg = den + 1.0f / 256.0f;
     const float confidence = den / reg;
     float *rows = basis + b * d * m;
+    const int64_t row_begin = d * blockIdx.y / gridDim.y;
+    const int64_t row_end = d * (blockIdx.y + 1) / gridDim.y;
     if (m % 4 == 0 && m <= 128 && (kAssocThreads % (m / 4)) == 0 && 32 % (m / 4) == 0) {
         const int parts = static_cast<int>(m / 4);
         const int part = static_cast<int>(threadIdx.x) % parts;
@@ -412,13 +636,13 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
         // uniform trip count: every lane reaches the shuffles; kPasses rows
         // per thread are loaded before any is used, to keep loads in flight
         constexpr int kPasses = 4;
-        for (int64_t base = 0; base < d; base += kPasses * rows_per_pass) {
+        for (int64_t base = row_begin; base < row_end; base += kPasses * rows_per_pass) {
             float4 x[kPasses];
             float value[kPasses];
 #pragma unroll
             for (int u = 0; u < kPasses; ++u) {
                 const int64_t i = base + u * rows_per_pass + threadIdx.x / parts;
-                const bool live = i < d;
+                const bool live = i < row_end;
                 x[u] = live ? *(reinterpret_cast<const float4 *>(rows + i * m) + part) : make_float4(0.f, 0.f, 0.f, 0.f);
                 value[u] = live ? proj[2 * d + i] : 0.0f;
             }
@@ -427,7 +651,7 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
                 const int64_t i = base + u * rows_per_pass + threadIdx.x / parts;
                 float num = x[u].x * qv.x + x[u].y * qv.y + x[u].z * qv.z + x[u].w * qv.w;
                 for (int o = 1; o < parts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
-                if (i >= d) continue;
+                if (i >= row_end) continue;
                 const float v = write * tanhf(value[u]);
                 float4 y;
                 y.x = decay * x[u].x + v * fv.x;
@@ -439,7 +663,7 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
             }
         }
     } else {
-        for (int64_t i = threadIdx.x; i < d; i += kAssocThreads) {
+        for (int64_t i = row_begin + threadIdx.x; i < row_end; i += kAssocThreads) {
             float *row = rows + i * m;
             const float v = tanhf(proj[2 * d + i]);
             float num = 0.0f;
@@ -451,8 +675,9 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
             read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
         }
     }
-    __syncthreads();
-    if (threadIdx.x < m) {
+    // every CTA of the stream has read the normaliser (den) before this
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (blockIdx.y == 0 && threadIdx.x < m) {
         const int64_t j = threadIdx.x;
         normalizer[b * m + j] = decay * normalizer[b * m + j] + write * f[j];
     }
@@ -509,6 +734,42 @@ extern "C" int koemi_think_ring_decode_step(
     if (smem > 200 * 1024) return fail(KOEMI_ERR_UNSUPPORTED, "ring decode shared memory too large");
     const dim3 grid(static_cast<unsigned>(batch), 2);
     cudaStream_t s = as_stream(stream);
+    // few streams: split every ring over a cluster of CTAs (>= 16 slots each)
+    int64_t parts = static_cast<int64_t>(sm_count()) / batch;
+    const int64_t min_slots = local_slots < salient_slots ? local_slots : salient_slots;
+    parts = parts > 8 ? 8 : parts;
+    while (parts > 1 && min_slots / parts < 16) --parts;
+    if (parts >= 2) {
+        const int64_t own = (slots + parts - 1) / parts;
+        const size_t split_smem = (2 * static_cast<size_t>(width) + 2 * own + kRingWarps) * sizeof(float);
+        auto run_split = [&](auto kernel) -> int {
+            if (split_smem > 48 * 1024) {
+                KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(split_smem)));
+            }
+            cudaLaunchConfig_t config{};
+            config.gridDim = dim3(static_cast<unsigned>(batch), 2, static_cast<unsigned>(parts));
+            config.blockDim = dim3(kRingThreads, 1, 1);
+            config.dynamicSmemBytes = split_smem;
+            config.stream = s;
+            cudaLaunchAttribute attribute[1];
+            attribute[0].id = cudaLaunchAttributeClusterDimension;
+            attribute[0].val.clusterDim.x = 1;
+            attribute[0].val.clusterDim.y = 1;
+            attribute[0].val.clusterDim.z = static_cast<unsigned>(parts);
+            config.attrs = attribute;
+            config.numAttrs = 1;
+            KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, kernel, args));
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
+        };
+        const bool bf16_ring = ring_dtype == KOEMI_BF16;
+        switch (out_dtype) {
+            case KOEMI_F32: return bf16_ring ? run_split(ring_decode_split_kernel<__nv_bfloat16, float>) : run_split(ring_decode_split_kernel<float, float>);
+            case KOEMI_BF16: return bf16_ring ? run_split(ring_decode_split_kernel<__nv_bfloat16, __nv_bfloat16>) : run_split(ring_decode_split_kernel<float, __nv_bfloat16>);
+            case KOEMI_F16: return bf16_ring ? run_split(ring_decode_split_kernel<__nv_bfloat16, __half>) : run_split(ring_decode_split_kernel<float, __half>);
+            default: return fail(KOEMI_ERR_INVALID, "ring outputs must be f32, f16 or bf16");
+        }
+    }
     auto run = [&](auto kernel) -> int {
         if (smem > 48 * 1024) {
             KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -540,15 +801,32 @@ extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_st
     if (features % 4 == 0 && !aligned(basis, 16)) return fail(KOEMI_ERR_UNSUPPORTED, "basis must be 16-byte aligned");
     const bool vector = width % 8 == 0 && aligned(feature_weight, 16) && aligned(projections, 8) && proj_stride % 2 == 0;
     const size_t smem = 4 * static_cast<size_t>(features) * sizeof(float);
-    const unsigned grid = static_cast<unsigned>(batch);
+    // few streams: split each stream's rows over a cluster of up to 8 CTAs so
+    // the grid covers the SMs (at least 64 rows per CTA)
+    int64_t parts = 2 * static_cast<int64_t>(sm_count()) / batch;
+    parts = parts < 1 ? 1 : (parts > 8 ? 8 : parts);
+    while (parts > 1 && width / parts < 64) --parts;
     cudaStream_t s = as_stream(stream);
     auto run = [&](auto *out_type, auto *weight_type) -> int {
         using TO = std::remove_pointer_t<decltype(out_type)>;
         using TW = std::remove_pointer_t<decltype(weight_type)>;
-        assoc_decode_kernel<TO, TW><<<grid, kAssocThreads, smem, s>>>(
-            projections, proj_stride, feature_logits, static_cast<const TW *>(feature_weight),
-            static_cast<const TW *>(feature_bias), vector, surprise, valid, basis, normalizer,
-            static_cast<TO *>(read_out), read_stride, batch, width, features);
+        cudaLaunchConfig_t config{};
+        config.gridDim = dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts), 1);
+        config.blockDim = dim3(kAssocThreads, 1, 1);
+        config.dynamicSmemBytes = smem;
+        config.stream = s;
+        cudaLaunchAttribute attribute[1];
+        attribute[0].id = cudaLaunchAttributeClusterDimension;
+        attribute[0].val.clusterDim.x = 1;
+        attribute[0].val.clusterDim.y = static_cast<unsigned>(parts);
+        attribute[0].val.clusterDim.z = 1;
+        config.attrs = attribute;
+        config.numAttrs = 1;
+        KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, assoc_decode_kernel<TO, TW>, projections, proj_stride,
+                                          feature_logits, static_cast<const TW *>(feature_weight),
+                                          static_cast<const TW *>(feature_bias), vector, surprise, valid, basis,
+                                          normalizer, static_cast<TO *>(read_out), read_stride, batch, width,
+                                          features));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };

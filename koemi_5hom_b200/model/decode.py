@@ -208,8 +208,12 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         else:
             surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
                                                     torch.float32)
-        local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
-        local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
+        if batch <= 128:  # one row tile: a single wider GEMM fills the GPU better than two
+            local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
+            local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
+        else:
+            local = model._linear(h, block.local_weight, block.local_bias)
+            assoc = model._linear(h, block.assoc_weight, block.assoc_bias)
         scored = surprise if surprise is not None else torch.zeros(batch, device=device)
         # ring queries read the fp32 working state (the new h) directly
         call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), local.stride(0), ptr(valid), ptr(scored),
