@@ -444,7 +444,12 @@ def run_b200(args) -> None:
         "roofline": {"kernel": "koemi_moe_grouped_expert_mlp (decode step, one block)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm_peak,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s",
-                     "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                     "unit": "GB/s", "frac": achieved / hbm_peak,
+                     # dram__bytes_read.sum + dram__bytes_write.sum of both expert GEMMs for one call at this
+                     # workload's pair distribution, from one ncu capture of `--op expert_decode`; none was taken
+                     # of an expert-parallel owner's share
+                     "traffic": 3.249e9 if not expert_parallel(args, world) else None,
+                     "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
                      "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},
         "prefill_s": prefill_seconds,

@@ -607,6 +607,11 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
             for (int64_t j = lane; j < m; j += 32) dst[j] = expf(logits[j] - mx) / sum;
         }
         __syncwarp();
+        // den = normaliser . query features, one feature per lane (a serial
+        // loop of dependent-latency loads in one thread would dominate here)
+        float den = 0.0f;
+        for (int64_t j = lane; j < m; j += 32) den += normalizer[b * m + j] * qf[j];
+        den = warp_sum(den);
         if (lane == 0) {
             const bool ok = valid == nullptr || valid[b] != 0;
             const float lo = 1.0f / 4096.0f, hi = 1.0f - 1.0f / 4096.0f;
@@ -615,8 +620,6 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
             const float write = sigmoidf_(proj[3 * d + 1]) * (0.25f + 0.75f * s);
             s_decay = ok ? decay : 1.0f;
             s_write = ok ? write : 0.0f;
-            float den = 0.0f;
-            for (int64_t j = 0; j < m; ++j) den += normalizer[b * m + j] * qf[j];
             s_den = den;
         }
     }
