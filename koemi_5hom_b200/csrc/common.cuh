@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 #include "../../include/koemi_b200.h"
 
@@ -55,6 +56,35 @@ inline cudaStream_t as_stream(void *stream) { return reinterpret_cast<cudaStream
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while the previous kernel of the stream is finishing (its CTAs take SMs as
+// they free up and run their prologue), so every kernel launched this way
+// calls pdl_wait() before it touches global memory written or read by earlier
+// work. `cluster_y` / `cluster_z` > 1 also set thread-block cluster dims.
+template <typename... KernelArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, dim3 cluster, Args &&...args) {
+    cudaLaunchConfig_t config{};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attributes[2];
+    attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[0].val.programmaticStreamSerializationAllowed = 1;
+    unsigned count = 1;
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attributes[1].id = cudaLaunchAttributeClusterDimension;
+        attributes[1].val.clusterDim.x = cluster.x;
+        attributes[1].val.clusterDim.y = cluster.y;
+        attributes[1].val.clusterDim.z = cluster.z;
+        count = 2;
+    }
+    config.attrs = attributes;
+    config.numAttrs = count;
+    return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
 #define KOEMI_CUDA_TRY(expr)                                                                      \
     do {                                                                                          \
         cudaError_t koemi_error_ = (expr);                                                        \
@@ -67,6 +97,13 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 #define KOEMI_LAUNCH_CHECK() KOEMI_CUDA_TRY(cudaGetLastError())
 
 // ---------------------------------------------------------------- device side
+
+// Programmatic dependent launch: pdl_trigger lets the next kernel of the
+// stream be scheduled; pdl_wait blocks until the previous kernel has finished
+// and its memory is visible (a no-op for kernels launched without the
+// attribute).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <typename T>
 struct Accum {

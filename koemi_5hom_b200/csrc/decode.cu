@@ -32,6 +32,8 @@ template <typename TP>
 __global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t *__restrict__ valid,
                                     float *__restrict__ working, TP *__restrict__ prior, TP *__restrict__ h_out,
                                     int64_t h_stride, int64_t batch, int64_t features, float lo, float hi) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= batch * features) return;
     const int64_t row = i / features;
@@ -132,6 +134,8 @@ struct RingPacket<__nv_bfloat16> {
 // scores[slots], cosines[slots], reduction scratch.
 template <typename TR, typename TO>
 __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
+    pdl_trigger();
+    pdl_wait();
     using P = RingPacket<TR>;
     constexpr int W = P::kWidth;
     extern __shared__ float shared[];
@@ -325,6 +329,8 @@ __device__ __forceinline__ void cluster_barrier() {
 
 template <typename TR, typename TO>
 __global__ __launch_bounds__(kRingThreads) void ring_decode_split_kernel(RingArgs a) {
+    pdl_trigger();
+    pdl_wait();
     using P = RingPacket<TR>;
     constexpr int W = P::kWidth;
     extern __shared__ float shared[];
@@ -581,6 +587,8 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float *__restrict__ surprise, const uint8_t *__restrict__ valid, float *__restrict__ basis,
     float *__restrict__ normalizer, TO *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
     int64_t m) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float shared[];
     float *f = shared;       // [m] write features
     float *qf = shared + m;  // [m] query features
@@ -702,9 +710,9 @@ extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *
     const unsigned blocks = static_cast<unsigned>(ceil_div(total, 256));
     cudaStream_t s = as_stream(stream);
     switch (prior_dtype) {
-        case KOEMI_F32: decode_gates_kernel<float><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<float *>(prior_out), static_cast<float *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
-        case KOEMI_BF16: decode_gates_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), static_cast<__nv_bfloat16 *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
-        case KOEMI_F16: decode_gates_kernel<__half><<<blocks, 256, 0, s>>>(projections, valid, working, static_cast<__half *>(prior_out), static_cast<__half *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<float *>(prior_out), static_cast<float *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
+        case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), static_cast<__nv_bfloat16 *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__half *>(prior_out), static_cast<__half *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
         default: return fail(KOEMI_ERR_INVALID, "prior dtype must be f32, f16 or bf16");
     }
     KOEMI_LAUNCH_CHECK();
@@ -749,19 +757,8 @@ extern "C" int koemi_think_ring_decode_step(
             if (split_smem > 48 * 1024) {
                 KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(split_smem)));
             }
-            cudaLaunchConfig_t config{};
-            config.gridDim = dim3(static_cast<unsigned>(batch), 2, static_cast<unsigned>(parts));
-            config.blockDim = dim3(kRingThreads, 1, 1);
-            config.dynamicSmemBytes = split_smem;
-            config.stream = s;
-            cudaLaunchAttribute attribute[1];
-            attribute[0].id = cudaLaunchAttributeClusterDimension;
-            attribute[0].val.clusterDim.x = 1;
-            attribute[0].val.clusterDim.y = 1;
-            attribute[0].val.clusterDim.z = static_cast<unsigned>(parts);
-            config.attrs = attribute;
-            config.numAttrs = 1;
-            KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, kernel, args));
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(batch), 2, static_cast<unsigned>(parts)),
+                                      dim3(kRingThreads), split_smem, s, dim3(1, 1, static_cast<unsigned>(parts)), args));
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
         };
@@ -777,7 +774,7 @@ extern "C" int koemi_think_ring_decode_step(
         if (smem > 48 * 1024) {
             KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         }
-        kernel<<<grid, kRingThreads, smem, s>>>(args);
+        KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(grid), dim3(kRingThreads), smem, s, dim3(1, 1, 1), args));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };
@@ -813,23 +810,11 @@ extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_st
     auto run = [&](auto *out_type, auto *weight_type) -> int {
         using TO = std::remove_pointer_t<decltype(out_type)>;
         using TW = std::remove_pointer_t<decltype(weight_type)>;
-        cudaLaunchConfig_t config{};
-        config.gridDim = dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts), 1);
-        config.blockDim = dim3(kAssocThreads, 1, 1);
-        config.dynamicSmemBytes = smem;
-        config.stream = s;
-        cudaLaunchAttribute attribute[1];
-        attribute[0].id = cudaLaunchAttributeClusterDimension;
-        attribute[0].val.clusterDim.x = 1;
-        attribute[0].val.clusterDim.y = static_cast<unsigned>(parts);
-        attribute[0].val.clusterDim.z = 1;
-        config.attrs = attribute;
-        config.numAttrs = 1;
-        KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, assoc_decode_kernel<TO, TW>, projections, proj_stride,
-                                          feature_logits, static_cast<const TW *>(feature_weight),
-                                          static_cast<const TW *>(feature_bias), vector, surprise, valid, basis,
-                                          normalizer, static_cast<TO *>(read_out), read_stride, batch, width,
-                                          features));
+        KOEMI_CUDA_TRY(launch_pdl(assoc_decode_kernel<TO, TW>, dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts)),
+                                  dim3(kAssocThreads), smem, s, dim3(1, static_cast<unsigned>(parts), 1), projections,
+                                  proj_stride, feature_logits, static_cast<const TW *>(feature_weight),
+                                  static_cast<const TW *>(feature_bias), vector, surprise, valid, basis, normalizer,
+                                  static_cast<TO *>(read_out), read_stride, batch, width, features));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };

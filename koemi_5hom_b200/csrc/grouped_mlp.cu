@@ -28,6 +28,8 @@ size_t grouped_mlp_umma_workspace(int64_t pairs, int64_t input_width, int64_t hi
 // Shared by both paths: tile_prefix[e] = row tiles of experts < e (E + 1 entries).
 __global__ void tile_prefix_kernel(const int64_t *__restrict__ offsets, int64_t experts, int64_t tile_rows,
                                    int32_t *__restrict__ prefix) {
+    pdl_trigger();
+    pdl_wait();
     // one warp: 32 experts per round, inclusive shuffle scan plus a carry
     const int lane = threadIdx.x & 31;
     if (blockIdx.x != 0 || threadIdx.x >= 32) return;
@@ -59,6 +61,8 @@ __device__ __forceinline__ int64_t find_expert(const int32_t *prefix, int64_t ex
 
 __global__ void zero_tail_rows_kernel(void *out, const int64_t *__restrict__ offsets, int64_t experts,
                                       int64_t pairs, int64_t row_bytes) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t valid_rows = offsets[experts];
     char *base = static_cast<char *>(out);
     const int64_t begin = valid_rows * row_bytes;
@@ -157,7 +161,7 @@ int grouped_mlp_simt(const void *x, const int64_t *offsets, const void *gw, cons
                      int64_t h, int64_t experts, char *ws, cudaStream_t stream) {
     int32_t *prefix = reinterpret_cast<int32_t *>(ws);
     float *hidden = reinterpret_cast<float *>(ws + (((experts + 1) * sizeof(int32_t) + 255) & ~size_t(255)));
-    tile_prefix_kernel<<<1, 32, 0, stream>>>(offsets, experts, kBM, prefix);
+    KOEMI_CUDA_TRY(launch_pdl(tile_prefix_kernel, dim3(1), dim3(32), 0, stream, dim3(1, 1, 1), offsets, experts, kBM, prefix));
     KOEMI_LAUNCH_CHECK();
     const unsigned max_tiles = static_cast<unsigned>(ceil_div(pairs, kBM) + experts);
     grouped_gemm_simt_kernel<T, T, float, true><<<dim3(max_tiles, static_cast<unsigned>(ceil_div(h, kBN))), kThreads, 0, stream>>>(
@@ -168,7 +172,7 @@ int grouped_mlp_simt(const void *x, const int64_t *offsets, const void *gw, cons
         hidden, offsets, prefix, static_cast<const T *>(ow), static_cast<const T *>(ob), nullptr, nullptr,
         static_cast<T *>(output), experts, h, d);
     KOEMI_LAUNCH_CHECK();
-    zero_tail_rows_kernel<<<256, 256, 0, stream>>>(output, offsets, experts, pairs, d * sizeof(T));
+    KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, offsets, experts, pairs, d * sizeof(T)));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }

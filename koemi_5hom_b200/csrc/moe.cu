@@ -35,6 +35,8 @@ template <typename Index>
 __global__ void route_topk_kernel(const Index *__restrict__ tokens, const Index *__restrict__ previous,
                                   const uint8_t *__restrict__ valid, int64_t *__restrict__ out,
                                   int64_t count, int64_t experts, int64_t top_k) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= count) return;
     const bool ok = valid == nullptr || valid[t] != 0;
@@ -260,6 +262,8 @@ __global__ __launch_bounds__(kSmallThreads) void small_permute_kernel(
     int64_t experts, int64_t *__restrict__ segment_offsets, int64_t *__restrict__ sorted_rows,
     int64_t *__restrict__ sorted_experts, int64_t *__restrict__ pair_positions,
     int32_t *__restrict__ sorted_pairs_out) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ int32_t shared[];
     const int buckets = static_cast<int>(experts) + 1;  // keys in [0, experts]; experts = dropped
     const int n = static_cast<int>(pairs);
@@ -638,6 +642,8 @@ __global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__
                                                        const float *__restrict__ next_norm, TO *__restrict__ out,
                                                        int64_t tokens, int64_t width, int64_t top_k, int64_t experts,
                                                        float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= tokens) return;
@@ -754,11 +760,11 @@ extern "C" int koemi_moe_route_topk(const void *token_ids, const void *previous_
     const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 256));
     cudaStream_t s = as_stream(stream);
     if (index_dtype == KOEMI_I64) {
-        route_topk_kernel<int64_t><<<blocks, 256, 0, s>>>(static_cast<const int64_t *>(token_ids),
-            static_cast<const int64_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k);
+        KOEMI_CUDA_TRY(launch_pdl(route_topk_kernel<int64_t>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const int64_t *>(token_ids),
+            static_cast<const int64_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k));
     } else if (index_dtype == KOEMI_I32) {
-        route_topk_kernel<int32_t><<<blocks, 256, 0, s>>>(static_cast<const int32_t *>(token_ids),
-            static_cast<const int32_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k);
+        KOEMI_CUDA_TRY(launch_pdl(route_topk_kernel<int32_t>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const int32_t *>(token_ids),
+            static_cast<const int32_t *>(previous_token_ids), valid, assignments, tokens, expert_count, top_k));
     } else {
         return fail(KOEMI_ERR_INVALID, "token ids must be int32 or int64");
     }
@@ -827,8 +833,8 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
                 KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                     static_cast<int>(smem)));
             }
-            kernel<<<1, kSmallThreads, smem, s>>>(typed, valid, pairs, top_k, expert_count, segment_offsets,
-                                                  sorted_rows, sorted_experts, pair_positions, values_a);
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(1), dim3(kSmallThreads), smem, s, dim3(1, 1, 1), typed, valid, pairs, top_k, expert_count, segment_offsets,
+                                                  sorted_rows, sorted_experts, pair_positions, values_a));
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
         };
@@ -940,8 +946,8 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
     const int64_t quads_per_lane = ceil_div(width / 4, 32);
     if (vector && quads_per_lane <= 16) {
         auto run = [&](auto kernel, const auto *typed) -> int {
-            kernel<<<blocks, threads, 0, s>>>(context, typed, pair_positions, segment_offsets, weights, valid,
-                                              norm_weight, nullptr, out, tokens, width, top_k, expert_count, eps);
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), context, typed, pair_positions, segment_offsets, weights, valid,
+                                              norm_weight, nullptr, out, tokens, width, top_k, expert_count, eps));
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
         };
@@ -1112,9 +1118,9 @@ extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, con
         using T = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
         using TO = std::remove_pointer_t<decltype(out_typed)>;
         auto launch = [&](auto kernel) -> int {
-            kernel<<<blocks, threads, 0, s>>>(context, typed, pair_positions, segment_offsets, weights, valid,
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), context, typed, pair_positions, segment_offsets, weights, valid,
                                               norm_weight, next_norm_weight, out_typed, tokens, width, top_k,
-                                              expert_count, eps);
+                                              expert_count, eps));
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
         };
@@ -1147,6 +1153,8 @@ template <typename TI, typename TO>
 __global__ void gather_convert_kernel(const TI *__restrict__ rows, const int64_t *__restrict__ sorted_rows,
                                       const int64_t *__restrict__ valid_count, TO *__restrict__ out, int64_t pairs,
                                       int64_t width) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (i >= pairs) return;
@@ -1181,7 +1189,7 @@ extern "C" int koemi_moe_gather_rows(const void *rows, int rows_dtype, const int
     auto run = [&](const auto *in, auto *typed_out) -> int {
         using TI = std::remove_cv_t<std::remove_pointer_t<decltype(in)>>;
         using TO = std::remove_pointer_t<decltype(typed_out)>;
-        gather_convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(in, sorted_rows, valid_count, typed_out, pairs, width);
+        KOEMI_CUDA_TRY(launch_pdl(gather_convert_kernel<TI, TO>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), in, sorted_rows, valid_count, typed_out, pairs, width));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };

@@ -118,6 +118,8 @@ template <typename T>
 __global__ void ep_dispatch_kernel(ExchangeArgs a, const T *__restrict__ sorted_rows,
                                    const int64_t *__restrict__ sorted_experts, const int64_t *__restrict__ offsets,
                                    bool vector) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(a.own)[kEpochSlot] + 1;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
@@ -141,6 +143,8 @@ __global__ void ep_dispatch_kernel(ExchangeArgs a, const T *__restrict__ sorted_
 
 // Owner: wait until every sender's rows of this exchange have landed.
 __global__ void ep_wait_dispatch_kernel(const uint8_t *own, int64_t ranks, int *status) {
+    pdl_trigger();
+    pdl_wait();
     wait_flags(own, 0, ranks, status);
 }
 
@@ -149,6 +153,8 @@ __global__ void ep_wait_dispatch_kernel(const uint8_t *own, int64_t ranks, int *
 template <typename T>
 __global__ void ep_return_kernel(ExchangeArgs a, const T *__restrict__ local_out,
                                  const int64_t *__restrict__ local_positions, bool vector) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(a.own)[kEpochSlot];
     const int32_t *ids = reinterpret_cast<const int32_t *>(a.own + a.ids);
@@ -170,6 +176,8 @@ template <typename T>
 __global__ void ep_collect_kernel(ExchangeArgs a, const int64_t *__restrict__ sorted_experts,
                                   const int64_t *__restrict__ offsets, T *__restrict__ sorted_out, int64_t pairs,
                                   bool vector) {
+    pdl_trigger();
+    pdl_wait();
     if (!wait_flags(a.own, 1, a.ranks, a.status)) return;
     const int lane = threadIdx.x & 31;
     const T *ret = reinterpret_cast<const T *>(a.own + a.ret);
@@ -284,9 +292,9 @@ extern "C" int koemi_ep_dispatch(const void *sorted_rows, const int64_t *sorted_
     const unsigned blocks = exchange_blocks(ranks * capacity);
     cudaStream_t s = as_stream(stream);
     switch (dtype) {
-        case KOEMI_F32: ep_dispatch_kernel<float><<<blocks, 256, 0, s>>>(a, static_cast<const float *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
-        case KOEMI_F16: ep_dispatch_kernel<__half><<<blocks, 256, 0, s>>>(a, static_cast<const __half *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
-        default: ep_dispatch_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, static_cast<const __nv_bfloat16 *>(sorted_rows), sorted_experts, segment_offsets, vector); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(ep_dispatch_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const float *>(sorted_rows), sorted_experts, segment_offsets, vector)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(ep_dispatch_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const __half *>(sorted_rows), sorted_experts, segment_offsets, vector)); break;
+        default: KOEMI_CUDA_TRY(launch_pdl(ep_dispatch_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const __nv_bfloat16 *>(sorted_rows), sorted_experts, segment_offsets, vector)); break;
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
@@ -295,7 +303,7 @@ extern "C" int koemi_ep_dispatch(const void *sorted_rows, const int64_t *sorted_
 extern "C" int koemi_ep_wait_dispatch(const void *own, int64_t ranks, void *stream) {
     clear_error();
     if (own == nullptr || ranks < 1 || ranks > kMaxPeerRanks) return fail(KOEMI_ERR_INVALID, "bad exchange wait arguments");
-    ep_wait_dispatch_kernel<<<1, 32, 0, as_stream(stream)>>>(static_cast<const uint8_t *>(own), ranks, device_status_word());
+    KOEMI_CUDA_TRY(launch_pdl(ep_wait_dispatch_kernel, dim3(1), dim3(32), 0, as_stream(stream), dim3(1, 1, 1), static_cast<const uint8_t *>(own), ranks, device_status_word()));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -311,9 +319,9 @@ extern "C" int koemi_ep_return(const void *local_out, const int64_t *local_posit
     const unsigned blocks = exchange_blocks(ranks * capacity);
     cudaStream_t s = as_stream(stream);
     switch (dtype) {
-        case KOEMI_F32: ep_return_kernel<float><<<blocks, 256, 0, s>>>(a, static_cast<const float *>(local_out), local_positions, vector); break;
-        case KOEMI_F16: ep_return_kernel<__half><<<blocks, 256, 0, s>>>(a, static_cast<const __half *>(local_out), local_positions, vector); break;
-        default: ep_return_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, static_cast<const __nv_bfloat16 *>(local_out), local_positions, vector); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(ep_return_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const float *>(local_out), local_positions, vector)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(ep_return_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const __half *>(local_out), local_positions, vector)); break;
+        default: KOEMI_CUDA_TRY(launch_pdl(ep_return_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, static_cast<const __nv_bfloat16 *>(local_out), local_positions, vector)); break;
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
@@ -331,9 +339,9 @@ extern "C" int koemi_ep_collect(const int64_t *sorted_experts, const int64_t *se
     const unsigned blocks = exchange_blocks(pairs);
     cudaStream_t s = as_stream(stream);
     switch (dtype) {
-        case KOEMI_F32: ep_collect_kernel<float><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<float *>(sorted_out), pairs, vector); break;
-        case KOEMI_F16: ep_collect_kernel<__half><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<__half *>(sorted_out), pairs, vector); break;
-        default: ep_collect_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a, sorted_experts, segment_offsets, static_cast<__nv_bfloat16 *>(sorted_out), pairs, vector); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(ep_collect_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, sorted_experts, segment_offsets, static_cast<float *>(sorted_out), pairs, vector)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(ep_collect_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, sorted_experts, segment_offsets, static_cast<__half *>(sorted_out), pairs, vector)); break;
+        default: KOEMI_CUDA_TRY(launch_pdl(ep_collect_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, sorted_experts, segment_offsets, static_cast<__nv_bfloat16 *>(sorted_out), pairs, vector)); break;
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;

@@ -77,6 +77,8 @@ __device__ __forceinline__ void store_converted(TO *dst, const float (&v)[W]) {
 // output may be another floating type TO.
 template <typename T, typename TO, int kMode, int NV>
 __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int W = Pack<T>::kWidth;
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -145,6 +147,8 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
 // Scalar two-pass path for any width, alignment and in/out dtype pair.
 template <typename T, typename TO, int kMode>
 __global__ __launch_bounds__(kThreads) void rms_rows_scalar(RowArgs args) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= args.rows) return;
@@ -199,15 +203,15 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
     if (vector_ok) {
         const int64_t per_lane = ceil_div(args.hidden / W, 32);
         if (per_lane <= 1) {
-            rms_rows_cached<T, TO, kMode, 1><<<blocks, threads, 0, stream>>>(args);
+            KOEMI_CUDA_TRY(launch_pdl(rms_rows_cached<T, TO, kMode, 1>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
         } else if (per_lane <= 2) {
-            rms_rows_cached<T, TO, kMode, 2><<<blocks, threads, 0, stream>>>(args);
+            KOEMI_CUDA_TRY(launch_pdl(rms_rows_cached<T, TO, kMode, 2>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
         } else if (per_lane <= 4) {
-            rms_rows_cached<T, TO, kMode, 4><<<blocks, threads, 0, stream>>>(args);
+            KOEMI_CUDA_TRY(launch_pdl(rms_rows_cached<T, TO, kMode, 4>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
         } else if (per_lane <= 8) {
-            rms_rows_cached<T, TO, kMode, 8><<<blocks, threads, 0, stream>>>(args);
+            KOEMI_CUDA_TRY(launch_pdl(rms_rows_cached<T, TO, kMode, 8>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
         } else if (per_lane <= 16 && sizeof(T) == 4 && kMode == kPlain) {
-            rms_rows_cached<T, TO, kMode, 16><<<blocks, threads, 0, stream>>>(args);
+            KOEMI_CUDA_TRY(launch_pdl(rms_rows_cached<T, TO, kMode, 16>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
         } else {
             vector_ok = false;
         }
@@ -216,7 +220,7 @@ int launch_rows(const RowArgs &args, cudaStream_t stream) {
             return KOEMI_OK;
         }
     }
-    rms_rows_scalar<T, TO, kMode><<<blocks, threads, 0, stream>>>(args);
+    KOEMI_CUDA_TRY(launch_pdl(rms_rows_scalar<T, TO, kMode>, dim3(blocks), dim3(threads), 0, stream, dim3(1, 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }

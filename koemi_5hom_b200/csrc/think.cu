@@ -118,6 +118,8 @@ __global__ void surprise_finish_kernel(const float *__restrict__ partials, int64
                                        const int64_t *__restrict__ targets, const uint8_t *__restrict__ valid,
                                        TO *__restrict__ out, float *__restrict__ nll_out, int64_t rows,
                                        float log_vocab) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -261,9 +263,9 @@ int surprise_finish(const float *partials, int64_t slices, const int64_t *target
     const float log_vocab = std::log(static_cast<float>(content_vocab));
     const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
     switch (out_dtype) {
-        case KOEMI_F32: surprise_finish_kernel<float><<<blocks, 256, 0, stream>>>(partials, slices, targets, valid, static_cast<float *>(out), nll_out, rows, log_vocab); break;
-        case KOEMI_F16: surprise_finish_kernel<__half><<<blocks, 256, 0, stream>>>(partials, slices, targets, valid, static_cast<__half *>(out), nll_out, rows, log_vocab); break;
-        case KOEMI_BF16: surprise_finish_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(partials, slices, targets, valid, static_cast<__nv_bfloat16 *>(out), nll_out, rows, log_vocab); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(surprise_finish_kernel<float>, dim3(blocks), dim3(256), 0, stream, dim3(1, 1, 1), partials, slices, targets, valid, static_cast<float *>(out), nll_out, rows, log_vocab)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(surprise_finish_kernel<__half>, dim3(blocks), dim3(256), 0, stream, dim3(1, 1, 1), partials, slices, targets, valid, static_cast<__half *>(out), nll_out, rows, log_vocab)); break;
+        case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(surprise_finish_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream, dim3(1, 1, 1), partials, slices, targets, valid, static_cast<__nv_bfloat16 *>(out), nll_out, rows, log_vocab)); break;
         default: return fail(KOEMI_ERR_INVALID, "unsupported surprise output dtype %d", out_dtype);
     }
     KOEMI_LAUNCH_CHECK();

@@ -276,9 +276,9 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
+    pdl_trigger();
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t tiles = total_tiles<kProblem, kTileRows>(args);
     const int64_t k_blocks = (args.k + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
@@ -302,6 +302,10 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the prologue above touched no global memory; everything below may read
+    // what the previous kernel of the stream wrote
+    pdl_wait();
+    const int64_t tiles = total_tiles<kProblem, kTileRows>(args);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -664,7 +668,7 @@ int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stre
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-    kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(args);
+    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), kSmemBytes, stream, dim3(1, 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -675,19 +679,8 @@ int launch_clustered(const UmmaArgs &args, int dtype, int64_t ctas, int cluster,
     auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
                                       : umma_gemm_kernel<kProblem, __half, kPair>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
-    cudaLaunchConfig_t config{};
-    config.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
-    config.blockDim = dim3(kThreads, 1, 1);
-    config.dynamicSmemBytes = kSmemBytes;
-    config.stream = stream;
-    cudaLaunchAttribute attribute[1];
-    attribute[0].id = cudaLaunchAttributeClusterDimension;
-    attribute[0].val.clusterDim.x = static_cast<unsigned>(cluster);
-    attribute[0].val.clusterDim.y = 1;
-    attribute[0].val.clusterDim.z = 1;
-    config.attrs = attribute;
-    config.numAttrs = 1;
-    KOEMI_CUDA_TRY(cudaLaunchKernelEx(&config, kernel, args));
+    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(kThreads), kSmemBytes, stream,
+                              dim3(static_cast<unsigned>(cluster), 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -759,7 +752,7 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     char *ws = static_cast<char *>(workspace);
     int32_t *prefix = reinterpret_cast<int32_t *>(ws);
     void *hidden = ws + align256((expert_count + 1) * sizeof(int32_t));
-    tile_prefix_kernel<<<1, 32, 0, stream>>>(segment_offsets, expert_count, kBM, prefix);
+    KOEMI_CUDA_TRY(launch_pdl(tile_prefix_kernel, dim3(1), dim3(32), 0, stream, dim3(1, 1, 1), segment_offsets, expert_count, kBM, prefix));
     KOEMI_LAUNCH_CHECK();
     const int64_t max_m_tiles = (pairs + kBM - 1) / kBM + expert_count;
 
@@ -804,7 +797,7 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     g2.idesc = g1.idesc;
     rc = launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
     if (rc != KOEMI_OK) return rc;
-    zero_tail_rows_kernel<<<256, 256, 0, stream>>>(output, segment_offsets, expert_count, pairs, d * 2);
+    KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, segment_offsets, expert_count, pairs, d * 2));
     KOEMI_LAUNCH_CHECK();
     *handled = true;
     return KOEMI_OK;
