@@ -56,11 +56,15 @@ inline cudaStream_t as_stream(void *stream) { return reinterpret_cast<cudaStream
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-// Launch with programmatic dependent launch allowed: the kernel may start
-// while the previous kernel of the stream is finishing (its CTAs take SMs as
-// they free up and run their prologue), so every kernel launched this way
-// calls pdl_wait() before it touches global memory written or read by earlier
-// work. `cluster_y` / `cluster_z` > 1 also set thread-block cluster dims.
+// Launch helper for the decode-path kernels. With kProgrammaticLaunch the
+// kernel may start while the previous kernel of the stream is finishing (its
+// CTAs take SMs as they free up and run their prologue); every kernel
+// launched through here therefore calls pdl_wait() before it touches global
+// memory written or read by earlier work. Measured on the config-5 decode
+// step it gained nothing (consecutive kernels are already ~0.35 us apart) and
+// cost ~5% at 32 streams, so it is off; the waits are then no-ops. `cluster`
+// with more than one CTA also sets thread-block cluster dims.
+constexpr bool kProgrammaticLaunch = false;
 template <typename... KernelArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t stream, dim3 cluster, Args &&...args) {
@@ -71,7 +75,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 blo
     config.stream = stream;
     cudaLaunchAttribute attributes[2];
     attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attributes[0].val.programmaticStreamSerializationAllowed = 1;
+    attributes[0].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch ? 1 : 0;
     unsigned count = 1;
     if (cluster.x * cluster.y * cluster.z > 1) {
         attributes[1].id = cudaLaunchAttributeClusterDimension;
