@@ -151,10 +151,18 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float *query = a.queries + b * a.query_stride;
     float qq = 0.0f;
-    for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
-        const float v = query[c];
-        q[c] = v;
-        qq += v * v;
+    if ((reinterpret_cast<uintptr_t>(query) & 15) == 0) {  // d % 4 == 0 (the host checks it)
+        for (int64_t c = threadIdx.x; c < d / 4; c += kRingThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(query) + c);
+            reinterpret_cast<float4 *>(q)[c] = v;
+            qq += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
+            const float v = query[c];
+            q[c] = v;
+            qq += v * v;
+        }
     }
     const float q_norm = sqrtf(block_reduce(qq, scratch, false));
     TR *keys = static_cast<TR *>(local ? a.local_keys : a.salient_keys) + b * slots * d;
@@ -354,10 +362,18 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_split_kernel(RingArg
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float *query = a.queries + b * a.query_stride;
     float qq = 0.0f;
-    for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
-        const float v = query[c];
-        q[c] = v;
-        qq += v * v;
+    if ((reinterpret_cast<uintptr_t>(query) & 15) == 0) {  // d % 4 == 0 (the host checks it)
+        for (int64_t c = threadIdx.x; c < d / 4; c += kRingThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(query) + c);
+            reinterpret_cast<float4 *>(q)[c] = v;
+            qq += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (int64_t c = threadIdx.x; c < d; c += kRingThreads) {
+            const float v = query[c];
+            q[c] = v;
+            qq += v * v;
+        }
     }
     const float q_norm = sqrtf(block_reduce(qq, scratch, false));
     TR *keys = static_cast<TR *>(local ? a.local_keys : a.salient_keys) + b * slots * d;
@@ -746,7 +762,7 @@ extern "C" int koemi_think_ring_decode_step(
     const dim3 grid(static_cast<unsigned>(batch), 2);
     cudaStream_t s = as_stream(stream);
     // few streams: split every ring over a cluster of CTAs (>= 16 slots each)
-    int64_t parts = static_cast<int64_t>(sm_count()) / batch;
+    int64_t parts = 2 * static_cast<int64_t>(sm_count()) / batch;  // about two CTAs per SM over both rings
     const int64_t min_slots = local_slots < salient_slots ? local_slots : salient_slots;
     parts = parts > 8 ? 8 : parts;
     while (parts > 1 && min_slots / parts < 16) --parts;
