@@ -520,14 +520,14 @@ def run_op(args) -> None:
         a = torch.sigmoid(torch.randn(8, 4096, 1024, device=device, generator=g)).bfloat16()
         b = torch.randn(8, 4096, 1024, device=device, generator=g).bfloat16()
         h0 = torch.zeros(8, 1024, device=device, dtype=torch.bfloat16)
-        seconds = _time_op(lambda: _ops.affine_scan_forward(a, b, h0, False), args.steps, args.warmup)
+        seconds = _time_op(lambda: _ops.affine_scan_forward(a, b, h0, False), args.steps, args.warmup, graph=True)
         work, unit, peak, bound = 3 * a.numel() * 2 / seconds / 1e9, "GB/s", hbm, "hbm"
         shape = "B=8 T=4096 D=1024 bf16 (201 MB per launch > L2)"
     elif args.op == "rmsnorm":  # config 3: 65536 x 2048 bf16, gated form silu(gate) * rmsnorm(x) * w
         x = torch.randn(65536, 2048, device=device, generator=g).bfloat16()
         gate = torch.randn(65536, 2048, device=device, generator=g).bfloat16()
         w = (1.0 + 0.02 * torch.randn(2048, device=device, generator=g)).bfloat16()
-        seconds = _time_op(lambda: _ops.gated_rmsnorm_silu(x, gate, w, 1e-6), args.steps, args.warmup)
+        seconds = _time_op(lambda: _ops.gated_rmsnorm_silu(x, gate, w, 1e-6), args.steps, args.warmup, graph=True)
         work, unit, peak, bound = 3 * x.numel() * 2 / seconds / 1e9, "GB/s", hbm, "hbm"
         shape = "65536 x 2048 bf16, gated (805 MB per launch > L2)"
     elif args.op in ("moe", "expert_decode"):

@@ -83,12 +83,20 @@ KOEMI_API int koemi_device_init(int device);
  * `retention` is [batch, length, features], or [batch, length] when
  * `broadcast_retention` is nonzero (one coefficient per position).
  * Accumulates in fp32 (fp64 for KOEMI_F64); `states` gets every h_t in dtype.
+ * With a workspace of koemi_dense_affine_scan_workspace() bytes (16-byte
+ * aligned) the sequence is split into segments scanned by separate CTAs that
+ * pass carries by decoupled look-back; with workspace NULL one CTA walks each
+ * (batch row, 32 features) lane group through the whole sequence. Both give
+ * the same recurrence in fp32; the association order differs.
  * Replaces dense/affine_scan.cu:119-167 (`forward` behind
  * dense_affine_scan, dense/affine_scan.py:51-82). */
+KOEMI_API size_t koemi_dense_affine_scan_workspace(int64_t batch, int64_t length, int64_t features,
+                                         int dtype);
 KOEMI_API int koemi_dense_affine_scan_forward(const void *retention, const void *increment,
                                     const void *initial, void *states,
                                     int64_t batch, int64_t length, int64_t features,
-                                    int broadcast_retention, int dtype, void *stream);
+                                    int broadcast_retention, int dtype, void *workspace,
+                                    size_t workspace_bytes, void *stream);
 
 /* Reverse-time adjoint of the scan: grad_increment, grad_retention (full
  * [batch, length, features] even when broadcast; the caller reduces) and

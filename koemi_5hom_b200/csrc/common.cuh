@@ -140,6 +140,9 @@ __device__ __forceinline__ T from_acc(double v) {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
+// SiLU through the fast exponential and divide intrinsics (relative error
+// ~1e-6); for streaming kernels whose issue rate would otherwise bound them.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

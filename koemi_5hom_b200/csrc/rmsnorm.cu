@@ -40,9 +40,9 @@ __device__ __forceinline__ void finish_pack(float (&v)[Pack<T>::kWidth], const f
     for (int e = 0; e < Pack<T>::kWidth; ++e) {
         const float n = v[e] * inv * w[e];
         if (kMode == kSilu) {
-            v[e] = siluf_(n);
+            v[e] = silu_fast(n);
         } else if (kMode == kGated) {
-            v[e] = siluf_(g[e]) * n;
+            v[e] = silu_fast(g[e]) * n;
         } else {
             v[e] = n;
         }
@@ -189,12 +189,191 @@ __global__ __launch_bounds__(kThreads) void rms_rows_scalar(RowArgs args) {
     }
 }
 
+// Streamed path for many rows (the front at prefill and benchmark sizes):
+// a persistent CTA per SM whose producer warp moves groups of 8 consecutive
+// rows -- one contiguous block of x and one of the gate -- into a ring of
+// shared-memory stages with 1D bulk copies (cp.async.bulk, completion on an
+// mbarrier), while 8 consumer warps each normalise one row of the group
+// from shared memory and store the result straight to HBM. Loads for later
+// groups are in flight while earlier ones are computed, so HBM sees a steady
+// stream instead of the load/compute/store bursts of one-shot row blocks.
+// Two groups of 8 consumer warps take alternate stages, so each scheduler
+// has four warps to hide the latency of the per-row reduction.
+constexpr int kStreamWarps = 8;
+constexpr int kStreamGroups = 2;
+constexpr int kStreamThreads = (kStreamGroups * kStreamWarps + 1) * 32;
+constexpr int kStreamMaxStages = 8;
+constexpr size_t kStreamSmemBudget = 200 * 1024;
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+template <typename T, int kMode, int NV>
+__global__ __launch_bounds__(kStreamThreads) void rms_rows_streamed(RowArgs args, int stages, int *status) {
+    constexpr int W = Pack<T>::kWidth;
+    constexpr int kArrays = kMode == kGated ? 2 : 1;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int64_t row_bytes = args.hidden * static_cast<int64_t>(sizeof(T));
+    const int64_t stage_bytes = kStreamWarps * row_bytes * kArrays;
+    unsigned char *ring = smem_raw;
+    T *weight_s = reinterpret_cast<T *>(ring + stages * stage_bytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + stages * stage_bytes + ((row_bytes + 15) / 16) * 16);
+    uint64_t *empty = full + kStreamMaxStages;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t groups = (args.rows + kStreamWarps - 1) / kStreamWarps;
+    const int64_t packets = args.hidden / W;
+    for (int64_t p = threadIdx.x; p < packets; p += kStreamThreads) {
+        reinterpret_cast<uint4 *>(weight_s)[p] = load_cached(static_cast<const T *>(args.weight) + p * W);
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStreamWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kStreamGroups * kStreamWarps) {
+        if (lane == 0) {
+            // Stage s, its fill count `round` (phase parity = round & 1).
+            int s = 0, round = 0, issued = 0;
+            for (int64_t g = blockIdx.x; g < groups; g += gridDim.x, ++issued) {
+                if (round > 0 && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>((round - 1) & 1), status)) break;
+                const int64_t first = g * kStreamWarps;
+                const int64_t count = args.rows - first < kStreamWarps ? args.rows - first : kStreamWarps;
+                const uint32_t bytes = static_cast<uint32_t>(count * row_bytes);
+                mbar_arrive_expect_tx(&full[s], bytes * kArrays);
+                unsigned char *dst = ring + s * stage_bytes;
+                bulk_load(dst, static_cast<const T *>(args.x) + first * args.hidden, bytes, &full[s]);
+                if (kMode == kGated) {
+                    bulk_load(dst + kStreamWarps * row_bytes, static_cast<const T *>(args.gate) + first * args.hidden,
+                              bytes, &full[s]);
+                }
+                if (++s == stages) {
+                    s = 0;
+                    ++round;
+                }
+            }
+            // Drain: the newest copy of every stage has landed before the CTA
+            // leaves (stage t was last filled in round `round` if t < s, else
+            // in round - 1).
+            for (int t = 0; t < stages && t < issued; ++t) {
+                const int last_round = t < s ? round : round - 1;
+                mbar_wait_bounded(&full[t], static_cast<uint32_t>(last_round & 1), nullptr);
+            }
+        }
+        return;
+    }
+
+    // Consumer group `team` takes the block's groups k = team, team + 2, ...
+    const int team = warp / kStreamWarps;
+    const int member = warp % kStreamWarps;
+    int s = team % stages, round = team / stages;
+    for (int64_t g = blockIdx.x + int64_t(team) * gridDim.x; g < groups; g += int64_t(kStreamGroups) * gridDim.x) {
+        if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(round & 1), status)) break;
+        const int64_t row = g * kStreamWarps + member;
+        if (row < args.rows) {
+            const unsigned char *base = ring + s * stage_bytes + member * row_bytes;
+            const uint4 *xs = reinterpret_cast<const uint4 *>(base);
+            const uint4 *gs = reinterpret_cast<const uint4 *>(base + kStreamWarps * row_bytes);
+            uint4 raw[NV];
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int64_t p = lane + 32 * i;
+                if (p < packets) {
+                    raw[i] = xs[p];
+                    float v[W];
+                    unpack(raw[i], v, T());
+#pragma unroll
+                    for (int e = 0; e < W; ++e) sum = fmaf(v[e], v[e], sum);
+                }
+            }
+            sum = warp_sum(sum);
+            const float inv = rsqrtf(sum / static_cast<float>(args.hidden) + args.eps);
+            if (lane == 0 && args.inv_rms != nullptr) args.inv_rms[row] = inv;
+            T *yr = static_cast<T *>(args.y) + row * args.hidden;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int64_t p = lane + 32 * i;
+                if (p < packets) {
+                    float v[W], w[W], gv[W];
+                    unpack(raw[i], v, T());
+                    unpack(reinterpret_cast<const uint4 *>(weight_s)[p], w, T());
+                    if (kMode == kGated) unpack(gs[p], gv, T());
+                    finish_pack<T, kMode>(v, w, gv, inv);
+                    store_stream(yr + p * W, pack(v, T()));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        s += kStreamGroups;
+        while (s >= stages) {
+            s -= stages;
+            ++round;
+        }
+    }
+}
+
+template <typename T, int kMode>
+size_t streamed_smem(int64_t hidden, int *stages_out) {
+    const size_t row_bytes = static_cast<size_t>(hidden) * sizeof(T);
+    const size_t stage_bytes = kStreamWarps * row_bytes * (kMode == kGated ? 2 : 1);
+    const size_t fixed = ((row_bytes + 15) / 16) * 16 + 2 * kStreamMaxStages * sizeof(uint64_t);
+    int stages = static_cast<int>((kStreamSmemBudget - fixed) / stage_bytes);
+    if (stages > kStreamMaxStages) stages = kStreamMaxStages;
+    *stages_out = stages;
+    return stages * stage_bytes + fixed;
+}
+
+// Streamed path when: same in/out dtype, SiLU or gated mode, 16-byte aligned
+// rows of at most 8 packets per lane, and at least four groups per SM.
+template <typename T, typename TO, int kMode>
+bool try_launch_streamed(const RowArgs &args, cudaStream_t stream, int *rc) {
+    if constexpr (!std::is_same<T, TO>::value || kMode == kPlain) {
+        return false;
+    } else {
+        constexpr int W = Pack<T>::kWidth;
+        const int64_t packets = args.hidden / W;
+        if (args.hidden % W != 0 || packets > 32 * 8 || !aligned(args.x, 16) || !aligned(args.weight, 16) ||
+            !aligned(args.y, 16) || (kMode == kGated && !aligned(args.gate, 16))) {
+            return false;
+        }
+        const int64_t groups = ceil_div(args.rows, kStreamWarps);
+        const int64_t sms = sm_count();
+        if (groups < 4 * sms) return false;
+        int stages = 0;
+        const size_t smem = streamed_smem<T, kMode>(args.hidden, &stages);
+        if (stages < 2) return false;
+        auto kernel = packets > 32 * 4 ? rms_rows_streamed<T, kMode, 8> : rms_rows_streamed<T, kMode, 4>;
+        *rc = KOEMI_OK;
+        cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (err == cudaSuccess) {
+            kernel<<<static_cast<unsigned>(sms), kStreamThreads, smem, stream>>>(args, stages, device_status_word());
+            err = cudaGetLastError();
+        }
+        if (err != cudaSuccess) *rc = fail(KOEMI_ERR_CUDA, "streamed RMSNorm launch failed: %s", cudaGetErrorString(err));
+        return true;
+    }
+}
+
 template <typename T, typename TO, int kMode>
 int launch_rows(const RowArgs &args, cudaStream_t stream) {
     // few rows (decode steps): 2 rows per block so the rows spread over the SMs
     const int rows_per_block = args.rows >= static_cast<int64_t>(sm_count()) * 32 ? kRowsPerBlock : 2;
     const int threads = rows_per_block * 32;
     const unsigned blocks = static_cast<unsigned>(ceil_div(args.rows, rows_per_block));
+    int streamed_rc = KOEMI_OK;
+    if (try_launch_streamed<T, TO, kMode>(args, stream, &streamed_rc)) return streamed_rc;
     constexpr int W = Pack<T>::kWidth;
     bool vector_ok = args.hidden % W == 0 && aligned(args.x, 16) &&
                      aligned(args.weight, 16) && aligned(args.y, 16) &&

@@ -38,8 +38,11 @@ def affine_scan_forward(retention: Tensor, increment: Tensor, initial: Tensor, b
     batch, length = increment.shape[0], increment.shape[1]
     features = increment.numel() // max(batch * length, 1) if batch * length else 0
     states = torch.empty_like(increment)
+    code = dtype_code(increment.dtype)
+    workspace_bytes = _native.library().koemi_dense_affine_scan_workspace(batch, length, features, code)
+    workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=increment.device) if workspace_bytes else None
     call("koemi_dense_affine_scan_forward", ptr(retention), ptr(increment), ptr(initial), ptr(states),
-         batch, length, features, int(broadcast), dtype_code(increment.dtype), stream)
+         batch, length, features, int(broadcast), code, ptr(workspace), workspace_bytes, stream)
     return states
 
 

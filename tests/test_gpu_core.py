@@ -84,3 +84,35 @@ def test_plain_norm_with_residual_keep_and_cast(cuda):
     yb = rms_norm(x.to(cuda), w.to(cuda), out_dtype=torch.bfloat16)
     assert yb.dtype == torch.bfloat16
     torch.testing.assert_close(yb.cpu().float(), ops.rms_norm(x, w).bfloat16().float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("shape", [(5003, 2048), (4741, 1024), (9000, 520)])
+def test_streamed_rows_match_oracle(dtype, shape, cuda):
+    """Row counts large enough for the persistent bulk-copy kernel, including
+    a ragged last group of rows; every row is checked for both the SiLU front
+    (with its inv_rms output) and the gated form."""
+    rows, hidden = shape
+    if dtype == torch.float32 and hidden > 1024:
+        hidden = 1024
+    g = torch.Generator().manual_seed(rows)
+    x = (torch.randn(rows, hidden, generator=g) * 2.0).to(dtype)
+    gate = torch.randn(rows, hidden, generator=g).to(dtype)
+    w = (1.0 + 0.02 * torch.randn(hidden, generator=g)).to(dtype)
+    rtol, atol = TOL[dtype]
+    y = fused_rmsnorm_silu(x.to(cuda), w.to(cuda))
+    expected, _ = ops.rmsnorm_silu(x, w)
+    torch.testing.assert_close(y.cpu().double(), expected.to(dtype).double(), rtol=rtol, atol=atol)
+    yg = gated_rmsnorm_silu(x.to(cuda), gate.to(cuda), w.to(cuda))
+    torch.testing.assert_close(yg.cpu().double(), ops.gated_rmsnorm_silu(x, gate, w).to(dtype).double(),
+                               rtol=rtol, atol=atol)
+
+
+def test_streamed_rows_return_inv_rms(cuda):
+    from koemi_5hom_b200.cuda_kernels import _ops
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(6000, 2048, generator=g).bfloat16()
+    w = torch.ones(2048).bfloat16()
+    y, inv = _ops.rmsnorm_silu_forward(x.to(cuda), w.to(cuda), 1e-6)
+    expected = torch.rsqrt(x.double().pow(2).mean(-1) + 1e-6)
+    torch.testing.assert_close(inv.cpu().double(), expected, rtol=1e-5, atol=1e-6)

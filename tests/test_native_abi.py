@@ -45,7 +45,7 @@ def test_invalid_arguments_fail_before_touching_the_device():
     status = lib.koemi_core_rmsnorm_silu_forward(None, None, None, None, 4, 8, -1.0, _native.F32, None)
     assert status == _native.KOEMI_ERR_INVALID
     assert "eps" in _native.last_error()
-    status = lib.koemi_dense_affine_scan_forward(None, None, None, None, 1, 4, 8, 0, 99, None)
+    status = lib.koemi_dense_affine_scan_forward(None, None, None, None, 1, 4, 8, 0, 99, None, 0, None)
     assert status == _native.KOEMI_ERR_INVALID
     with pytest.raises(_native.KoemiNativeError, match="status -1"):
         _native.call("koemi_moe_learned_topk", None, None, None, None, None, 3, 4, 9, 0, None)
@@ -53,7 +53,7 @@ def test_invalid_arguments_fail_before_touching_the_device():
 
 def test_empty_work_is_a_no_op():
     lib = _native.library()
-    assert lib.koemi_dense_affine_scan_forward(None, None, None, None, 0, 5, 8, 0, _native.F32, None) == 0
+    assert lib.koemi_dense_affine_scan_forward(None, None, None, None, 0, 5, 8, 0, _native.F32, None, 0, None) == 0
     assert lib.koemi_moe_route_topk(None, None, None, None, 0, 4, 2, _native.I64, None) == 0
 
 
