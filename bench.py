@@ -70,6 +70,8 @@ def parse_args(argv=None):
     p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "expert_decode", "surprise_decode", "surprise_prefill",
                                     "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
+    p.add_argument("--op-tokens", type=int, default=None,
+                   help="token count of --op moe (default: config 4's 131072; smaller for profiler captures)")
     return p.parse_args(argv)
 
 
@@ -531,7 +533,7 @@ def run_op(args) -> None:
         work, unit, peak, bound = 3 * x.numel() * 2 / seconds / 1e9, "GB/s", hbm, "hbm"
         shape = "65536 x 2048 bf16, gated (805 MB per launch > L2)"
     elif args.op in ("moe", "expert_decode"):
-        tokens, d, e = (131072, 1024, 64) if args.op == "moe" else (256, 2048, 64)
+        tokens, d, e = (args.op_tokens or 131072, 1024, 64) if args.op == "moe" else (256, 2048, 64)
         h = 2 * d
         x = torch.randn(tokens, d, device=device, generator=g).bfloat16()
         ids = torch.randint(0, 256, (tokens,), device=device, generator=g)

@@ -9,9 +9,10 @@
 //               (M=128, N=256, K=16, fp32 accumulate) into one of two
 //               256-column accumulators and commits stage/accumulator
 //               completion to mbarriers;
-//   warps 2..5  epilogue: tcgen05.ld each accumulator row (one TMEM lane per
+//   warps 2..   epilogue: tcgen05.ld each accumulator row (one TMEM lane per
 //               thread), apply the fused epilogue, store to global memory,
-//               release the accumulator.
+//               release the accumulator (four warps; eight for the gated
+//               problem, two per lane quarter splitting the columns).
 // The epilogue of tile i overlaps the MMAs of tile i+1.
 //
 // Problems:
@@ -42,7 +43,19 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;  // problems with four epilogue warps
+
+// The gated problem's SwiGLU epilogue (two TMEM reads, bias adds and a SiLU
+// per output) takes longer than the MMAs of a tile with four warps, so it
+// runs eight: two per TMEM lane quarter, each on half of the columns.
+template <int kProblem>
+constexpr int epilogue_warps() {
+    return kProblem == 0 ? 8 : 4;
+}
+template <int kProblem>
+constexpr int threads_for() {
+    return (2 + epilogue_warps<kProblem>()) * 32;
+}
 constexpr uint32_t kABytes = kBM * kBK * 2;
 constexpr uint32_t kBBytes = kBN * kBK * 2;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -252,8 +265,28 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
 
 // ---------------------------------------------------------------- kernel
 
+// 32 bias values starting at column col0 as fp32 (zero past n_out): four
+// 16-byte loads when the run is whole and aligned (every lane of a warp reads
+// the same addresses), else element by element.
+template <typename T>
+__device__ __forceinline__ void load_bias32(const T *bias, int64_t col0, int64_t n_out, float (&out)[32]) {
+    const T *src = bias + col0;
+    if (col0 + 32 <= n_out && aligned16(src)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float part[8];
+            unpack(load_cached(src + q * 8), part, T());
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[q * 8 + e] = part[e];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) out[j] = col0 + j < n_out ? to_acc(src[j]) : 0.0f;
+    }
+}
+
 template <int kProblem, typename T, bool kPair>
-__global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
+__global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
     // paired tiles: 256 A rows (two 128-row halves) per tile, stages of
     // A0 | A1 | B (64 KB, 3 of them), both 256-column accumulators in use
     constexpr int kPipe = kPair ? 3 : kStages;
@@ -288,7 +321,7 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
         }
         for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], epilogue_warps<kProblem>());
         }
         *abort = 0;
         fence_barrier_init();
@@ -388,8 +421,11 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
         }
         __syncwarp();
     } else {
-        // epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31
+        // epilogue warps: warp w reads TMEM lanes 32*(w%4) .. +31; with eight
+        // warps, warps 2..5 take the first half of the columns, 6..9 the second
         const int quarter = warp & 3;
+        constexpr int kParts = epilogue_warps<kProblem>() / 4;
+        const int part = (warp - 2) / 4;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -406,30 +442,32 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                 const T *bg = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
                 const T *bv = static_cast<const T *>(args.bias1) + tile.group * args.b_rows_per_group;
                 T *out = static_cast<T *>(args.out);
+                constexpr int kChunks = 4 / kParts;
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int cc = 0; cc < kChunks; ++cc) {
+                    const int c = part * kChunks + cc;
                     uint32_t g[32], v[32];
                     KOEMI_TMEM_LD32(taddr + c * 32, g);
                     KOEMI_TMEM_LD32(taddr + 128 + c * 32, v);
                     tmem_wait_ld();
                     const int64_t col0 = tile.n * 128 + c * 32;
                     if (row_ok && col0 < args.n_out) {
+                        float gb[32], vb[32];
+                        load_bias32(bg, col0, args.n_out, gb);
+                        load_bias32(bv, col0, args.n_out, vb);
                         float h[32];
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            const int64_t col = col0 + j;
-                            const float gb = col < args.n_out ? to_acc(bg[col]) : 0.0f;
-                            const float vb = col < args.n_out ? to_acc(bv[col]) : 0.0f;
-                            h[j] = siluf_(__uint_as_float(g[j]) + gb) * (__uint_as_float(v[j]) + vb);
+                            h[j] = silu_fast(__uint_as_float(g[j]) + gb[j]) * (__uint_as_float(v[j]) + vb[j]);
                         }
                         T *dst = out + row * args.out_stride + col0;
                         if (col0 + 32 <= args.n_out) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
-                                float part[8];
+                                float part8[8];
 #pragma unroll
-                                for (int e = 0; e < 8; ++e) part[e] = h[q * 8 + e];
-                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part, T());
+                                for (int e = 0; e < 8; ++e) part8[e] = h[q * 8 + e];
+                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part8, T());
                             }
                         } else {
                             for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = from_acc<T>(h[j]);
@@ -447,19 +485,17 @@ __global__ __launch_bounds__(kThreads, 1) void umma_gemm_kernel(const __grid_con
                     const int64_t col0 = tile.n * kBN + c * 32;
                     if (row_ok && col0 < args.n_out) {
                         float o[32];
+                        load_bias32(bo, col0, args.n_out, o);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int64_t col = col0 + j;
-                            o[j] = __uint_as_float(y[j]) + (col < args.n_out ? to_acc(bo[col]) : 0.0f);
-                        }
+                        for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(y[j]);
                         T *dst = out + row * args.out_stride + col0;
                         if (col0 + 32 <= args.n_out) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
-                                float part[8];
+                                float part8[8];
 #pragma unroll
-                                for (int e = 0; e < 8; ++e) part[e] = o[q * 8 + e];
-                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part, T());
+                                for (int e = 0; e < 8; ++e) part8[e] = o[q * 8 + e];
+                                *reinterpret_cast<uint4 *>(dst + q * 8) = pack(part8, T());
                             }
                         } else {
                             for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = from_acc<T>(o[j]);
@@ -668,7 +704,8 @@ int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stre
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), kSmemBytes, stream, dim3(1, 1, 1), args));
+    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads_for<kProblem>()), kSmemBytes, stream,
+                              dim3(1, 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -679,7 +716,7 @@ int launch_clustered(const UmmaArgs &args, int dtype, int64_t ctas, int cluster,
     auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
                                       : umma_gemm_kernel<kProblem, __half, kPair>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
-    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(kThreads), kSmemBytes, stream,
+    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(threads_for<kProblem>()), kSmemBytes, stream,
                               dim3(static_cast<unsigned>(cluster), 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
