@@ -10,8 +10,12 @@ tensor of the state at a fixed address and updates it in place:
 - working state, associative bases and normalisers are overwritten in place.
 
 A step is then: the hash route and its stable permutation once (the route
-depends only on the ids); per block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step``
--> surprise (tcgen05 head GEMM + online LSE) -> one local|assoc GEMM ->
+depends only on the ids); the surprise of every block at once -- block l
+scores the token against the shared head from its working state before the
+update, which is known for all blocks when the step starts, so one tcgen05
+head GEMM + online LSE over [blocks x streams] rows reads the head once per
+step instead of once per block; per block, rms_norm -> gate GEMM ->
+``koemi_dense_decode_step`` -> one local|assoc GEMM ->
 ``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` (with the
 feature projection of key and query fused in) -> fusion GEMM
 (its input rows are written in place by the three kernels) -> rms_norm ->
@@ -188,6 +192,17 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         _, sorted_tokens, sorted_experts, offsets, positions = _ops.permute_topk(
             x, assignments, valid, s.expert_count, False)
         weights = None
+    # surprise of every block from its prior (the working state before this
+    # step's update), one pass over the content head for the whole stack;
+    # each row's result is independent of the others, so this equals the
+    # per-block computation bit for bit
+    all_surprise = None
+    if targets is not None:
+        count = len(model.blocks)
+        priors = torch.stack([st.working for st in dstate.blocks]).to(model.compute_dtype)
+        all_surprise = _ops.causal_surprise_forward(
+            priors.view(count * batch, d), cache["content_w"], cache["content_b"], targets.repeat(count),
+            valid.repeat(count), torch.float32).view(count, batch)
     # the combine of block i also writes block i + 1's normalised input
     fused_combine = s.expert_count > 0 and d % 4 == 0 and d <= 2048 and s.expert_top_k <= 8
     u = None
@@ -199,15 +214,10 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         pre = model._linear(u, block.gates_weight, block.gates_bias)
         # fusion input rows, written in place by the step kernels: h | memory | local | salient
         concat = torch.empty(batch, 4 * d, dtype=concat_dtype, device=device)
-        prior = torch.empty(batch, d, dtype=model.compute_dtype, device=device)
-        call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), ptr(prior), ptr(concat), 4 * d,
+        call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), None, ptr(concat), 4 * d,
              batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
         h = concat[:, :d]
-        if targets is None:
-            surprise = None
-        else:
-            surprise = _ops.causal_surprise_forward(prior, cache["content_w"], cache["content_b"], targets, valid,
-                                                    torch.float32)
+        surprise = None if all_surprise is None else all_surprise[index]
         if batch <= 128:  # one row tile: a single wider GEMM fills the GPU better than two
             local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
             local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
