@@ -630,40 +630,56 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
             const int valid_rows = have_tile ? static_cast<int>(max(static_cast<int64_t>(0),
                                                                     min(static_cast<int64_t>(kBM), args.rows - half_row0)))
                                              : 0;
-            for (int idx = threadIdx.x; idx < valid_rows * q_count; idx += kThreads) {
-                const int r = idx / q_count;
-                const int q = q_begin + (idx - r * q_count);
-                const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
-                // every split's value is requested before any is added (the
-                // remote loads overlap), then summed in split order
-                float4 v[kMaxClusterSplits];
-#pragma unroll
-                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                    if (sp < splits) v[sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
-                }
-                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                    if (sp < splits) {
-                        acc.x += v[sp].x;
-                        acc.y += v[sp].y;
-                        acc.z += v[sp].z;
-                        acc.w += v[sp].w;
-                    }
-                }
-                const int64_t row = half_row0 + r;
-                const int64_t col = tile.n * kBN + q * 4;
-                if (col >= args.n_out) continue;
-                float o[4] = {acc.x, acc.y, acc.z, acc.w};
+            // Thread t owns column quad q_begin + t % q_count (its bias read
+            // once) and rows t / q_count + j * row_step. Four rows' loads from
+            // every split are requested before any is summed, so the remote
+            // latency is paid once per four rows; sums run in split order.
+            const int row_step = kThreads / q_count;
+            const int my_row = threadIdx.x / q_count;
+            const int q = q_begin + threadIdx.x % q_count;
+            const int64_t col = tile.n * kBN + q * 4;
+            if (my_row < row_step && col < args.n_out) {
+                float bias4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 if (bias != nullptr) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) o[e] += col + e < args.n_out ? to_acc(bias[col + e]) : 0.0f;
+                    for (int e = 0; e < 4; ++e) bias4[e] = col + e < args.n_out ? to_acc(bias[col + e]) : 0.0f;
                 }
-                float *dst = out + row * args.out_stride + col;
-                if (col + 4 <= args.n_out && aligned16(dst)) {
-                    *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-                } else {
-                    for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
+                constexpr int kRowsInFlight = 4;
+                for (int r0 = my_row; r0 < valid_rows; r0 += kRowsInFlight * row_step) {
+                    float4 v[kRowsInFlight][kMaxClusterSplits];
+#pragma unroll
+                    for (int u = 0; u < kRowsInFlight; ++u) {
+                        const int r = r0 + u * row_step;
+                        if (r < valid_rows) {
+                            const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
+#pragma unroll
+                            for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+                                if (sp < splits) v[u][sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < kRowsInFlight; ++u) {
+                        const int r = r0 + u * row_step;
+                        if (r >= valid_rows) continue;
+                        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                        for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+                            if (sp < splits) {
+                                acc.x += v[u][sp].x;
+                                acc.y += v[u][sp].y;
+                                acc.z += v[u][sp].z;
+                                acc.w += v[u][sp].w;
+                            }
+                        }
+                        const float o[4] = {acc.x + bias4[0], acc.y + bias4[1], acc.z + bias4[2], acc.w + bias4[3]};
+                        float *dst = out + (half_row0 + r) * args.out_stride + col;
+                        if (col + 4 <= args.n_out && aligned16(dst)) {
+                            *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                        } else {
+                            for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
+                        }
+                    }
                 }
             }
             cluster_sync_all();

@@ -255,7 +255,9 @@ def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
 
 @pytest.mark.parametrize("rows,n,k,stride,bias", [(256, 4096, 2048, 2048, True), (256, 2048, 8192, 8192, True),
                                                   (3000, 1000, 512, 512, False), (256, 16, 2048, 8192, True),
-                                                  (7, 300, 64, 64, True)])
+                                                  (7, 300, 64, 64, True), (32, 10242, 2048, 2048, True),
+                                                  (200, 1030, 4096, 4096, True), (129, 2048, 8192, 8192, False),
+                                                  (256, 6146, 2048, 2048, True)])
 def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
     """tcgen05 projection (split-K or direct) against fp64 on the same bf16 operands."""
     g = torch.Generator(device=cuda).manual_seed(rows + n)
@@ -300,3 +302,4 @@ def test_combine_with_next_norm_equals_two_ops(with_next, out_dtype, cuda):
     got = ops_.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, None, valid, norm, nxt, k, 1e-6,
                                              out_dtype)
     assert torch.equal(got, expected)
+
