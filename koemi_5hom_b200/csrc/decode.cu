@@ -588,6 +588,67 @@ __device__ void assoc_feature_logits(const float *__restrict__ proj, const TW *_
     }
 }
 
+// The same logits with the key and query rows staged in shared memory first
+// (rounded to TW) and each warp's weight packets loaded eight at a time
+// before any is used, so a feature costs one L2 round trip per 2048 columns
+// instead of one per 256. Warp w takes features w, w + 16, ... for both rows
+// (they share the weight row). Per-lane summation order is that of
+// assoc_feature_logits, so the results are identical. Needs d % 8 == 0,
+// 16-byte aligned weight rows and 8-byte aligned projection rows.
+template <typename TW>
+__device__ void assoc_feature_logits_staged(const float *__restrict__ proj, const TW *__restrict__ weight,
+                                            const TW *__restrict__ bias, float *__restrict__ logits,
+                                            float *__restrict__ xs, int64_t d, int64_t m) {
+    for (int64_t c = 2 * static_cast<int64_t>(threadIdx.x); c < 2 * d; c += 2 * kAssocThreads) {
+        const float2 v = *reinterpret_cast<const float2 *>(proj + c);
+        xs[c] = to_acc(from_acc<TW>(v.x));
+        xs[c + 1] = to_acc(from_acc<TW>(v.y));
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kGroup = 8;
+    constexpr int kWords = std::is_same_v<TW, float> ? 2 : 1;  // 16-byte words per 8 weights
+    for (int64_t j = warp; j < m; j += kAssocThreads / 32) {
+        const TW *w = weight + j * d;
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int64_t g0 = 0; g0 < d; g0 += 256 * kGroup) {
+            uint4 raw[kGroup][kWords];
+#pragma unroll
+            for (int i = 0; i < kGroup; ++i) {
+                const int64_t c = g0 + lane * 8 + 256 * i;
+                if (c < d) {
+#pragma unroll
+                    for (int h = 0; h < kWords; ++h) raw[i][h] = __ldg(reinterpret_cast<const uint4 *>(w + c) + h);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kGroup; ++i) {
+                const int64_t c = g0 + lane * 8 + 256 * i;
+                if (c >= d) continue;
+                float wv[8];
+                if constexpr (std::is_same_v<TW, float>) {
+                    unpack(raw[i][0], *reinterpret_cast<float(*)[4]>(wv), float{});
+                    unpack(raw[i][1], *reinterpret_cast<float(*)[4]>(wv + 4), float{});
+                } else {
+                    unpack(raw[i][0], wv, TW{});
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    acc0 = fmaf(xs[c + e], wv[e], acc0);
+                    acc1 = fmaf(xs[d + c + e], wv[e], acc1);
+                }
+            }
+        }
+        acc0 = warp_sum(acc0);
+        acc1 = warp_sum(acc1);
+        if (lane == 0) {
+            const float bj = bias != nullptr ? to_acc(bias[j]) : 0.0f;
+            logits[j] = acc0 + bj;
+            logits[m + j] = acc1 + bj;
+        }
+    }
+}
+
 // gridDim.y CTAs per stream (one thread-block cluster) split the d memory
 // rows; each recomputes the features. The memory row i (m features) is read
 // as m/4 float4 packets by m/4 adjacent threads, which combine their partial
@@ -600,7 +661,8 @@ template <typename TO, typename TW>
 __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     const float *__restrict__ projections, int64_t proj_stride, const float *__restrict__ feature_logits,
     const TW *__restrict__ feature_weight, const TW *__restrict__ feature_bias, bool vector_features,
-    const float *__restrict__ surprise, const uint8_t *__restrict__ valid, float *__restrict__ basis,
+    bool stage_features, const float *__restrict__ surprise, const uint8_t *__restrict__ valid,
+    float *__restrict__ basis,
     float *__restrict__ normalizer, TO *__restrict__ read_out, int64_t read_stride, int64_t batch, int64_t d,
     int64_t m) {
     pdl_trigger();
@@ -609,11 +671,16 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     float *f = shared;       // [m] write features
     float *qf = shared + m;  // [m] query features
     float *own_logits = shared + 2 * m;  // [2, m] when computed here
+    float *staged_rows = shared + 4 * m;  // [2, d] when staging (stage_features)
     __shared__ float s_decay, s_write, s_den;
     const int64_t b = blockIdx.x;
     const float *proj = projections + b * proj_stride;
     if (feature_logits == nullptr) {
-        assoc_feature_logits(proj, feature_weight, feature_bias, own_logits, d, m, vector_features);
+        if (stage_features) {
+            assoc_feature_logits_staged(proj, feature_weight, feature_bias, own_logits, staged_rows, d, m);
+        } else {
+            assoc_feature_logits(proj, feature_weight, feature_bias, own_logits, d, m, vector_features);
+        }
         __syncthreads();
     }
     if (threadIdx.x < 32) {
@@ -816,7 +883,10 @@ extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_st
     }
     if (features % 4 == 0 && !aligned(basis, 16)) return fail(KOEMI_ERR_UNSUPPORTED, "basis must be 16-byte aligned");
     const bool vector = width % 8 == 0 && aligned(feature_weight, 16) && aligned(projections, 8) && proj_stride % 2 == 0;
-    const size_t smem = 4 * static_cast<size_t>(features) * sizeof(float);
+    // key and query rows staged in shared memory for the fused feature
+    // projection when they fit in 32 KB
+    const bool stage = vector && feature_logits == nullptr && width <= 4096;
+    const size_t smem = (4 * static_cast<size_t>(features) + (stage ? 2 * static_cast<size_t>(width) : 0)) * sizeof(float);
     // few streams: split each stream's rows over a cluster of up to 8 CTAs so
     // the grid covers the SMs (at least 64 rows per CTA)
     int64_t parts = 2 * static_cast<int64_t>(sm_count()) / batch;
@@ -829,7 +899,7 @@ extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_st
         KOEMI_CUDA_TRY(launch_pdl(assoc_decode_kernel<TO, TW>, dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts)),
                                   dim3(kAssocThreads), smem, s, dim3(1, static_cast<unsigned>(parts), 1), projections,
                                   proj_stride, feature_logits, static_cast<const TW *>(feature_weight),
-                                  static_cast<const TW *>(feature_bias), vector, surprise, valid, basis, normalizer,
+                                  static_cast<const TW *>(feature_bias), vector, stage, surprise, valid, basis, normalizer,
                                   static_cast<TO *>(read_out), read_stride, batch, width, features));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
