@@ -93,12 +93,14 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
 
     uint4 raw[NV];
     uint4 graw[NV];
+    uint4 wraw[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int64_t p = lane + 32 * i;
         if (p < packets) {
             raw[i] = load_stream(xr + p * W);
             if (kMode == kGated) graw[i] = load_stream(gr + p * W);
+            wraw[i] = load_cached(wr + p * W);  // all loads in flight before the first use
         }
     }
     float v[NV][W];
@@ -136,7 +138,7 @@ __global__ __launch_bounds__(kThreads) void rms_rows_cached(RowArgs args) {
                 continue;
             }
             float w[W], g[W];
-            unpack(load_cached(wr + p * W), w, T());
+            unpack(wraw[i], w, T());
             if (kMode == kGated) unpack(graw[i], g, T());
             finish_pack<T, kMode>(v[i], w, g, inv);
             store_converted(yr + p * W, v[i]);

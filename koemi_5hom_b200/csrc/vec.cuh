@@ -67,10 +67,10 @@ __device__ __forceinline__ uint4 load_cached(const void *p) {
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
-__device__ __forceinline__ void store_stream(void *p, const uint4 &v) {
-    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x),
-                 "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
+// A plain 16-byte store (global stores do not allocate in L1). Written as C++
+// rather than inline asm so the compiler may schedule later loads ahead of
+// it: a volatile asm store with a memory clobber serialised every
+// load-after-store of a loop into one L2 round trip per iteration.
+__device__ __forceinline__ void store_stream(void *p, const uint4 &v) { *reinterpret_cast<uint4 *>(p) = v; }
 
 }  // namespace koemi
