@@ -29,6 +29,7 @@
 // Every mbarrier wait is bounded; a wait that runs out raises a CTA abort
 // flag, records KOEMI_ERR_TIMEOUT in the device status word and every role
 // leaves its loop, so the CTA frees its TMEM and exits. No multicast loads.
+#include <algorithm>
 #include <mutex>
 
 #include "vec.cuh"
@@ -285,13 +286,18 @@ __device__ __forceinline__ void load_bias32(const T *bias, int64_t col0, int64_t
     }
 }
 
-template <int kProblem, typename T, bool kPair>
+// kNarrow (output problem only): N = 128 tiles, for decode-sized pair counts
+// whose 256-wide tiles would leave SMs idle (e.g. 8 experts x 8 tiles).
+template <int kProblem, typename T, bool kPair, bool kNarrow = false>
 __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
     // paired tiles: 256 A rows (two 128-row halves) per tile, stages of
     // A0 | A1 | B (64 KB, 3 of them), both 256-column accumulators in use
     constexpr int kPipe = kPair ? 3 : kStages;
     constexpr uint32_t kAStage = kPair ? 2 * kABytes : kABytes;
-    constexpr uint32_t kStage = kAStage + kBBytes;
+    constexpr int kTileN = kNarrow ? kBN / 2 : kBN;
+    constexpr uint32_t kBStage = kNarrow ? kBBytes / 2 : kBBytes;
+    constexpr uint32_t kStage = kAStage + kBStage;
+    static_assert(!kNarrow || kProblem == kOutput, "narrow tiles are for the expert output GEMM");
     constexpr int kTileRows = kPair ? 2 * kBM : kBM;
     constexpr int kHalves = kPair ? 2 : 1;
     constexpr int kAccBufs = kPair ? 1 : 2;
@@ -365,7 +371,7 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
                         tma_load_2d(b_dst + kBBytes / 2, &args.map_b1, &full[stage], kc, r);
                     } else {
-                        const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kBN);
+                        const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kTileN);
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
                     }
                     if (++stage == kPipe) {
@@ -478,11 +484,11 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                 const T *bo = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
                 T *out = static_cast<T *>(args.out);
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < kTileN / 32; ++c) {
                     uint32_t y[32];
                     KOEMI_TMEM_LD32(taddr + c * 32, y);
                     tmem_wait_ld();
-                    const int64_t col0 = tile.n * kBN + c * 32;
+                    const int64_t col0 = tile.n * kTileN + c * 32;
                     if (row_ok && col0 < args.n_out) {
                         float o[32];
                         load_bias32(bo, col0, args.n_out, o);
@@ -694,13 +700,13 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
 
 // ------------------------------------------------------------------- host
 
-uint32_t make_idesc(int dtype) {
+uint32_t make_idesc(int dtype, int n = kBN) {
     const uint32_t ab = dtype == KOEMI_BF16 ? 1u : 0u;  // 0 = f16, 1 = bf16
     uint32_t idesc = 0;
     idesc |= 1u << 4;                       // D format: f32
     idesc |= ab << 7;                       // A format
     idesc |= ab << 10;                      // B format
-    idesc |= static_cast<uint32_t>(kBN >> 3) << 17;
+    idesc |= static_cast<uint32_t>(n >> 3) << 17;
     idesc |= static_cast<uint32_t>(kBM >> 4) << 24;
     return idesc;
 }
@@ -713,10 +719,10 @@ int encode_kmajor(CUtensorMap *map, int dtype, const void *base, int64_t rows, i
     return encode_tensor_map(map, type, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int kProblem, bool kPair = false>
+template <int kProblem, bool kPair = false, bool kNarrow = false>
 int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stream) {
-    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
-                                      : umma_gemm_kernel<kProblem, __half, kPair>;
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair, kNarrow>
+                                      : umma_gemm_kernel<kProblem, __half, kPair, kNarrow>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
@@ -831,13 +837,19 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     rc = launch<kGated>(g1, dtype, max_m_tiles * g1.n_tiles, stream);
     if (rc != KOEMI_OK) return rc;
 
+    // Narrow (N = 128) output tiles when the 256-wide ones cannot fill the
+    // SMs: with few pairs every touched expert has about one row tile, so the
+    // row tiles are estimated by the number of experts the pairs can touch.
+    const int64_t est_m_tiles = std::min(max_m_tiles, std::max((pairs + kBM - 1) / kBM, std::min(pairs, expert_count)));
+    const bool narrow = est_m_tiles * ((d + kBN - 1) / kBN) < sm_count();
+    const int64_t tile_n = narrow ? kBN / 2 : kBN;
     UmmaArgs g2{};
     rc = encode_kmajor(&g2.map_a, dtype, hidden, pairs, h, kBM);
-    if (rc == KOEMI_OK) rc = encode_kmajor(&g2.map_b0, dtype, out_w, expert_count * d, h, kBN);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g2.map_b0, dtype, out_w, expert_count * d, h, static_cast<uint32_t>(tile_n));
     if (rc != KOEMI_OK) return rc;
     g2.k = h;
     g2.rows = pairs;
-    g2.n_tiles = (d + kBN - 1) / kBN;
+    g2.n_tiles = (d + tile_n - 1) / tile_n;
     g2.b_rows_per_group = d;
     g2.n_out = d;
     g2.out_stride = d;
@@ -847,8 +859,9 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     g2.bias0 = out_b;
     g2.out = output;
     g2.status = g1.status;
-    g2.idesc = g1.idesc;
-    rc = launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
+    g2.idesc = make_idesc(dtype, static_cast<int>(tile_n));
+    rc = narrow ? launch<kOutput, false, true>(g2, dtype, max_m_tiles * g2.n_tiles, stream)
+                : launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
     if (rc != KOEMI_OK) return rc;
     KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, segment_offsets, expert_count, pairs, d * 2));
     KOEMI_LAUNCH_CHECK();

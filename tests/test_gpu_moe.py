@@ -227,11 +227,13 @@ def _sampled_rows_check(sc, se, offsets, y, weights, rows, dtype, tol):
         torch.testing.assert_close(got / scale, expected[0].to(dtype).double() / scale, rtol=tol, atol=tol)
 
 
-@pytest.mark.parametrize("tokens,d,h,e,k", [(131072, 1024, 2048, 64, 2), (256, 2048, 4096, 64, 2)])
+@pytest.mark.parametrize("tokens,d,h,e,k", [(131072, 1024, 2048, 64, 2), (256, 2048, 4096, 64, 2),
+                                             (32, 2048, 4096, 8, 2)])
 def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
-    """Config 4 (131072 tokens, d=1024, d_ff=2048, 64 experts, top-2) and the
-    config-5 decode step (256 streams, d=2048, d_ff=4096): sampled rows of
-    every segment position class against the fp64 oracle."""
+    """Config 4 (131072 tokens, d=1024, d_ff=2048, 64 experts, top-2), the
+    config-5 decode step (256 streams, d=2048, d_ff=4096) and one rank's share
+    of it at 8 GPUs (32 streams, 8 experts: the narrow output tiles): sampled
+    rows of every segment position class against the fp64 oracle."""
     g = torch.Generator(device=cuda).manual_seed(tokens)
     x = torch.randn(tokens, d, generator=g, device=cuda).bfloat16()
     scores = torch.rand(tokens, e, generator=g, device=cuda)
