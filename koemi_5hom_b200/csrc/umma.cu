@@ -613,7 +613,9 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
         const uint32_t parked_base = smem_addr(stages);
         for (int h = 0; h < kHalves; ++h) {
             const int64_t half_row0 = tile.row0 + h * kBM;
-            if (have_tile && warp >= 2) {
+            // only the warps holding valid rows park them (a 32-row decode
+            // batch fills one of the four lane quarters)
+            if (have_tile && warp >= 2 && half_row0 + (warp & 3) * 32 < args.rows) {
                 tc_fence_after();
                 const int quarter = warp & 3;
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
