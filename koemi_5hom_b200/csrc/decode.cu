@@ -777,6 +777,189 @@ __global__ __launch_bounds__(kAssocThreads) void assoc_decode_kernel(
     }
 }
 
+// The same step for kM = 16 features with the key/query rows staged (the
+// config-5 shape), latency-ordered: every global load that does not depend
+// on another -- this warp's feature-weight row, the normaliser, the decay /
+// write / surprise / validity scalars, the first pass of basis rows and the
+// staged key/query rows -- is issued at entry, so a CTA waits for one memory
+// round trip before it computes instead of one per phase. Arithmetic and its
+// order are those of assoc_decode_kernel (bit-identical results).
+template <typename TO, typename TW, int kM>
+__global__ __launch_bounds__(kAssocThreads, 2) void assoc_decode_prefetch_kernel(
+    const float *__restrict__ projections, int64_t proj_stride, const TW *__restrict__ feature_weight,
+    const TW *__restrict__ feature_bias, const float *__restrict__ surprise, const uint8_t *__restrict__ valid,
+    float *__restrict__ basis, float *__restrict__ normalizer, TO *__restrict__ read_out, int64_t read_stride,
+    int64_t d) {
+    static_assert(kM % 4 == 0 && kM <= kAssocThreads / 32 && 32 % (kM / 4) == 0, "feature count");
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float shared[];
+    float *f = shared;                   // [m] write features
+    float *qf = shared + kM;             // [m] query features
+    float *own_logits = shared + 2 * kM; // [2, m]
+    float *xs = shared + 4 * kM;         // [2, d] staged key | query rows, rounded to TW
+    __shared__ float s_decay, s_write, s_den;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t b = blockIdx.x;
+    const float *proj = projections + b * proj_stride;
+    float *rows = basis + b * d * kM;
+    const int64_t row_begin = d * blockIdx.y / gridDim.y;
+    const int64_t row_end = d * (blockIdx.y + 1) / gridDim.y;
+    constexpr int kParts = kM / 4;
+    constexpr int kPasses = 4;
+    constexpr int64_t kRowsPerPass = kAssocThreads / kParts;
+    const int part = static_cast<int>(threadIdx.x) % kParts;
+
+    // ---- every independent load, issued before any is used
+    float pre_decay = 0.0f, pre_write = 0.0f, s_value = 0.0f;
+    bool ok = true;
+    if (threadIdx.x == 0) {
+        pre_decay = proj[3 * d];
+        pre_write = proj[3 * d + 1];
+        s_value = surprise != nullptr ? surprise[b] : 0.0f;
+        ok = valid == nullptr || valid[b] != 0;
+    }
+    const float nrm = threadIdx.x < kM ? normalizer[b * kM + threadIdx.x] : 0.0f;
+    constexpr int kGroup = 8;
+    constexpr int kWords = std::is_same_v<TW, float> ? 2 : 1;
+    uint4 wraw[kGroup][kWords];
+    const TW *wrow = feature_weight + static_cast<int64_t>(warp < kM ? warp : 0) * d;
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) {
+        const int64_t c = lane * 8 + 256 * i;
+        if (warp < kM && c < d) {
+#pragma unroll
+            for (int h = 0; h < kWords; ++h) wraw[i][h] = __ldg(reinterpret_cast<const uint4 *>(wrow + c) + h);
+        }
+    }
+    float4 x0[kPasses];
+    float value0[kPasses];
+#pragma unroll
+    for (int u = 0; u < kPasses; ++u) {
+        const int64_t i = row_begin + u * kRowsPerPass + threadIdx.x / kParts;
+        const bool live = i < row_end;
+        x0[u] = live ? *(reinterpret_cast<const float4 *>(rows + i * kM) + part) : make_float4(0.f, 0.f, 0.f, 0.f);
+        value0[u] = live ? proj[2 * d + i] : 0.0f;
+    }
+    for (int64_t c = 2 * static_cast<int64_t>(threadIdx.x); c < 2 * d; c += 2 * kAssocThreads) {
+        const float2 v = *reinterpret_cast<const float2 *>(proj + c);
+        xs[c] = to_acc(from_acc<TW>(v.x));
+        xs[c + 1] = to_acc(from_acc<TW>(v.y));
+    }
+    __syncthreads();
+
+    // ---- feature logits: warp j, both rows, summed as assoc_feature_logits_staged does
+    if (warp < kM) {
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int64_t g0 = 0; g0 < d; g0 += 256 * kGroup) {
+            if (g0 > 0) {  // rows wider than 2048: later groups load here
+#pragma unroll
+                for (int i = 0; i < kGroup; ++i) {
+                    const int64_t c = g0 + lane * 8 + 256 * i;
+                    if (c < d) {
+#pragma unroll
+                        for (int h = 0; h < kWords; ++h) wraw[i][h] = __ldg(reinterpret_cast<const uint4 *>(wrow + c) + h);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kGroup; ++i) {
+                const int64_t c = g0 + lane * 8 + 256 * i;
+                if (c >= d) continue;
+                float wv[8];
+                if constexpr (std::is_same_v<TW, float>) {
+                    unpack(wraw[i][0], *reinterpret_cast<float(*)[4]>(wv), float{});
+                    unpack(wraw[i][1], *reinterpret_cast<float(*)[4]>(wv + 4), float{});
+                } else {
+                    unpack(wraw[i][0], wv, TW{});
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    acc0 = fmaf(xs[c + e], wv[e], acc0);
+                    acc1 = fmaf(xs[d + c + e], wv[e], acc1);
+                }
+            }
+        }
+        acc0 = warp_sum(acc0);
+        acc1 = warp_sum(acc1);
+        if (lane == 0) {
+            const float bj = feature_bias != nullptr ? to_acc(feature_bias[warp]) : 0.0f;
+            own_logits[warp] = acc0 + bj;
+            own_logits[kM + warp] = acc1 + bj;
+        }
+    }
+    __syncthreads();
+
+    // ---- feature softmaxes, the normaliser read and the gates (warp 0)
+    if (warp == 0) {
+        for (int which = 0; which < 2; ++which) {
+            const float *logits = own_logits + which * kM;
+            float mx = -INFINITY;
+            for (int j = lane; j < kM; j += 32) mx = fmaxf(mx, logits[j]);
+            mx = warp_max(mx);
+            float sum = 0.0f;
+            for (int j = lane; j < kM; j += 32) sum += expf(logits[j] - mx);
+            sum = warp_sum(sum);
+            float *dst = which == 0 ? f : qf;
+            for (int j = lane; j < kM; j += 32) dst[j] = expf(logits[j] - mx) / sum;
+        }
+        __syncwarp();
+        float den = lane < kM ? nrm * qf[lane] : 0.0f;
+        den = warp_sum(den);
+        if (lane == 0) {
+            const float lo = 1.0f / 4096.0f, hi = 1.0f - 1.0f / 4096.0f;
+            const float decay = lo + (hi - lo) * sigmoidf_(pre_decay);
+            const float sv = surprise != nullptr ? fminf(fmaxf(s_value, 0.0f), 1.0f) : 0.0f;
+            const float write = sigmoidf_(pre_write) * (0.25f + 0.75f * sv);
+            s_decay = ok ? decay : 1.0f;
+            s_write = ok ? write : 0.0f;
+            s_den = den;
+        }
+    }
+    __syncthreads();
+    const float decay = s_decay, write = s_write, den = s_den;
+    const float reg = den + 1.0f / 256.0f;
+    const float confidence = den / reg;
+    const float4 qv = reinterpret_cast<const float4 *>(qf)[part];
+    const float4 fv = reinterpret_cast<const float4 *>(f)[part];
+    for (int64_t base = row_begin; base < row_end; base += kPasses * kRowsPerPass) {
+        float4 x[kPasses];
+        float value[kPasses];
+#pragma unroll
+        for (int u = 0; u < kPasses; ++u) {
+            if (base == row_begin) {
+                x[u] = x0[u];
+                value[u] = value0[u];
+            } else {
+                const int64_t i = base + u * kRowsPerPass + threadIdx.x / kParts;
+                const bool live = i < row_end;
+                x[u] = live ? *(reinterpret_cast<const float4 *>(rows + i * kM) + part) : make_float4(0.f, 0.f, 0.f, 0.f);
+                value[u] = live ? proj[2 * d + i] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kPasses; ++u) {
+            const int64_t i = base + u * kRowsPerPass + threadIdx.x / kParts;
+            float num = x[u].x * qv.x + x[u].y * qv.y + x[u].z * qv.z + x[u].w * qv.w;
+            for (int o = 1; o < kParts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
+            if (i >= row_end) continue;
+            const float v = write * tanhf(value[u]);
+            float4 y;
+            y.x = decay * x[u].x + v * fv.x;
+            y.y = decay * x[u].y + v * fv.y;
+            y.z = decay * x[u].z + v * fv.z;
+            y.w = decay * x[u].w + v * fv.w;
+            *(reinterpret_cast<float4 *>(rows + i * kM) + part) = y;
+            if (part == 0) read_out[b * read_stride + i] = from_acc<TO>(confidence * num / reg);
+        }
+    }
+    // every CTA of the stream has read the normaliser (den) before this
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (blockIdx.y == 0 && threadIdx.x < kM) {
+        normalizer[b * kM + threadIdx.x] = decay * nrm + write * f[threadIdx.x];
+    }
+}
+
 }  // namespace
 }  // namespace koemi
 
@@ -896,6 +1079,16 @@ extern "C" int koemi_assoc_decode_step(const float *projections, int64_t proj_st
     auto run = [&](auto *out_type, auto *weight_type) -> int {
         using TO = std::remove_pointer_t<decltype(out_type)>;
         using TW = std::remove_pointer_t<decltype(weight_type)>;
+        if (stage && features == 16) {  // the config-5 shape: latency-ordered kernel
+            KOEMI_CUDA_TRY(launch_pdl(assoc_decode_prefetch_kernel<TO, TW, 16>,
+                                      dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts)),
+                                      dim3(kAssocThreads), smem, s, dim3(1, static_cast<unsigned>(parts), 1), projections,
+                                      proj_stride, static_cast<const TW *>(feature_weight),
+                                      static_cast<const TW *>(feature_bias), surprise, valid, basis, normalizer,
+                                      static_cast<TO *>(read_out), read_stride, width));
+            KOEMI_LAUNCH_CHECK();
+            return KOEMI_OK;
+        }
         KOEMI_CUDA_TRY(launch_pdl(assoc_decode_kernel<TO, TW>, dim3(static_cast<unsigned>(batch), static_cast<unsigned>(parts)),
                                   dim3(kAssocThreads), smem, s, dim3(1, static_cast<unsigned>(parts), 1), projections,
                                   proj_stride, feature_logits, static_cast<const TW *>(feature_weight),

@@ -119,10 +119,13 @@ def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slot
         assert torch.equal(new_k, old_k) and torch.equal(new_v, old_v)
 
 
+@pytest.mark.parametrize("batch,d", [(9, 256), (5, 2048), (300, 2048)])
 @pytest.mark.parametrize("feature_source", ["logits", "f32_weight", "bf16_weight"])
-def test_assoc_decode_step_matches_oracle(feature_source, cuda):
+def test_assoc_decode_step_matches_oracle(feature_source, batch, d, cuda):
+    """Rows split over a cluster of CTAs (few streams) or one CTA per stream
+    walking the rows in several passes (many streams)."""
     g = torch.Generator().manual_seed(3)
-    batch, d, m = 9, 256, 16
+    m = 16
     proj = torch.randn(batch, 3 * d + 2, generator=g)
     feats = torch.randn(2, batch, m, generator=g)
     feature_weight = torch.randn(m, d, generator=g) * 0.1
