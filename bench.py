@@ -270,6 +270,18 @@ def emit(line: dict, args) -> None:
 
 
 # ----------------------------------------------------------------- GPU side
+class GreedyTokens:
+    """The greedy sampler of the decode loop: TokenSampler's greedy path (PAD
+    masked, first index among equal maxima) as one native pass over the
+    logits."""
+
+    def __call__(self, logits):
+        from koemi_5hom_b200.cuda_kernels import _ops
+        from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
+        return _ops.greedy_tokens(logits.reshape(-1, logits.shape[-1]).float(), PAD_TOKEN_ID)
+
+
+
 def count_native_kernels(model, decoder, token) -> int:
     """Kernels of libkoemi_b200 launched by one eager decode step (on a copy of
     the decoder's state, so the measured run is not advanced)."""
@@ -370,12 +382,13 @@ def run_b200(args) -> None:
     progress(rank, f"prefill done in {prefill_seconds:.1f} s")
     del prompts
 
-    token = logits.argmax(dim=-1, keepdim=True)
+    greedy = GreedyTokens()
+    token = greedy(logits)
     eager_kernels = count_native_kernels(model, decoder, token)
     progress(rank, f"eager step counted {eager_kernels} native launches")
     for _ in range(max(args.warmup, 1)):
         logits = decoder.step(token)
-        token = logits.argmax(dim=-1, keepdim=True)
+        token = greedy(logits)
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream(device)
@@ -389,7 +402,7 @@ def run_b200(args) -> None:
         start.record(stream)
         for _ in range(args.steps):
             logits = decoder.step(token)
-            token = logits.argmax(dim=-1, keepdim=True)
+            token = greedy(logits)
         stop.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -417,7 +430,7 @@ def run_b200(args) -> None:
     for _ in range(args.steps):
         device_ids.copy_(host_in, non_blocking=True)
         logits = decoder.step(device_ids)
-        host_out.copy_(logits.argmax(dim=-1, keepdim=True), non_blocking=True)
+        host_out.copy_(greedy(logits), non_blocking=True)
         stream.synchronize()
         host_in.copy_(host_out)
     e2e_seconds = time.perf_counter() - e2e_start

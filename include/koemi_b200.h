@@ -76,6 +76,17 @@ KOEMI_API int koemi_device_status(int device, int *status_out);
  * these kernels into a CUDA graph; compute calls otherwise do it lazily. */
 KOEMI_API int koemi_device_init(int device);
 
+/* ------------------------------------------------------------- sampling */
+
+/* Greedy decode tokens: out[r] = argmax over c of logits[r * row_stride + c]
+ * with column pad_id scored as -inf (pass -1 for no mask), ties to the first
+ * index and NaN ranked above every number, as torch.argmax does on the
+ * masked row. logits fp32 [rows, vocab] (row stride in elements), out int64
+ * [rows]. Replaces the greedy path of TokenSampler
+ * (src/koemi/runtime/fast_decode.py:40-87). */
+KOEMI_API int koemi_sampler_greedy(const float *logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                   int64_t pad_id, int64_t *out, void *stream);
+
 /* ------------------------------------------------------------ dense front */
 
 /* Affine recurrent scan h_t = a_t * h_{t-1} + b_t over [batch, length,

@@ -462,3 +462,22 @@ def gather_rows(rows: Tensor, sorted_rows: Tensor, segment_offsets: Tensor, out_
 @gather_rows.register_fake
 def _(rows, sorted_rows, segment_offsets, out_dtype):
     return rows.new_empty(sorted_rows.shape[0], rows.shape[1], dtype=out_dtype)
+
+
+# ------------------------------------------------------------------ sampling
+
+@torch.library.custom_op("koemi_b200::greedy_tokens", mutates_args=())
+def greedy_tokens(logits: Tensor, pad_id: int) -> Tensor:
+    """[rows, vocab] fp32 logits -> int64 [rows, 1]: argmax with column
+    pad_id masked (TokenSampler's greedy path, fast_decode.py:40-87)."""
+    (logits,) = _dense(logits)
+    stream = _prepare(logits)
+    rows, vocab = logits.shape
+    out = torch.empty(rows, 1, dtype=torch.int64, device=logits.device)
+    call("koemi_sampler_greedy", ptr(logits), rows, vocab, vocab, pad_id, ptr(out), stream)
+    return out
+
+
+@greedy_tokens.register_fake
+def _(logits, pad_id):
+    return logits.new_empty(logits.shape[0], 1, dtype=torch.int64)

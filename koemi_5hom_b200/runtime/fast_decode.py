@@ -20,6 +20,7 @@ from dataclasses import dataclass, replace
 import torch
 from torch import Tensor
 
+from koemi_5hom_b200.cuda_kernels import _ops
 from koemi_5hom_b200.model.decode import (RING_DTYPES, decode_step, from_koemi_state, supports_decode_path,
                                            to_koemi_state)
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
@@ -55,6 +56,9 @@ class TokenSampler:
     def __call__(self, logits: Tensor) -> Tensor:
         if logits.ndim != 2:
             raise ValueError("sampling requires logits with shape [batch, vocabulary]")
+        if self.policy.greedy and logits.is_cuda and logits.dtype == torch.float32:
+            # one native pass: PAD scored as -inf, torch.argmax tie and NaN order
+            return _ops.greedy_tokens(logits, PAD_TOKEN_ID)
         scores = self.content_scores(logits)
         if self.policy.greedy:
             return scores.argmax(dim=-1, keepdim=True)
