@@ -142,6 +142,21 @@ KOEMI_API int koemi_dense_decode_step(const float *projections, const uint8_t *v
                             int64_t features, float minimum_retention, float maximum_retention,
                             int prior_dtype, void *stream);
 
+/* Associative memory over a window of `length` positions (prefill), in place:
+ * for t = 0..length-1 of every stream, den = n . q_t, reg = den + 2^-8,
+ * read_t[i] = (den / reg) (basis[i] . q_t) / reg, then
+ * basis[i] = decay_t basis[i] + write_t value_t[i] f_t and
+ * n = decay_t n + write_t f_t. decay, write fp32 [batch, length]; value,
+ * read_out fp32 [batch, length, width]; features, query_features fp32
+ * [batch, length, feature_count]; basis fp32 [batch, width, feature_count]
+ * (16-byte aligned), normaliser fp32 [batch, feature_count]. feature_count
+ * must be 16. Replaces the window read of
+ * HierarchicalAssociativeMemory.scan_and_read (model/memory.py:97-144,146-242). */
+KOEMI_API int koemi_assoc_window_scan_read(const float *decay, const float *write, const float *value,
+                                           const float *features, const float *query_features, float *basis,
+                                           float *normalizer, float *read_out, int64_t batch, int64_t length,
+                                           int64_t width, int64_t feature_count, void *stream);
+
 /* Dense projection out = a W^T + bias on tcgen05 tensor cores, fp32 output:
  * a [rows, k] (row stride a_stride elements, bf16/f16), W [n, k] (same dtype,
  * contiguous), bias [n] (same dtype, may be NULL), out fp32 rows of

@@ -38,12 +38,25 @@ __global__ __launch_bounds__(kSamplerThreads) void greedy_kernel(const float *__
     Best best{-INFINITY, vocab};  // ranks after every real entry
     const bool vector = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const int64_t quads = vector ? vocab / 4 : 0;
-    for (int64_t q = threadIdx.x; q < quads; q += kSamplerThreads) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + q);
-        take(best, v.x, 4 * q, pad);
-        take(best, v.y, 4 * q + 1, pad);
-        take(best, v.z, 4 * q + 2, pad);
-        take(best, v.w, 4 * q + 3, pad);
+    // eight packets per thread requested before any is compared
+    constexpr int kInFlight = 8;
+    for (int64_t q0 = threadIdx.x; q0 < quads; q0 += kInFlight * kSamplerThreads) {
+        float4 v[kInFlight];
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+            const int64_t q = q0 + u * kSamplerThreads;
+            v[u] = q < quads ? __ldg(reinterpret_cast<const float4 *>(x) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+            const int64_t q = q0 + u * kSamplerThreads;
+            if (q < quads) {
+                take(best, v[u].x, 4 * q, pad);
+                take(best, v[u].y, 4 * q + 1, pad);
+                take(best, v[u].z, 4 * q + 2, pad);
+                take(best, v[u].w, 4 * q + 3, pad);
+            }
+        }
     }
     for (int64_t i = 4 * quads + threadIdx.x; i < vocab; i += kSamplerThreads) take(best, x[i], i, pad);
 #pragma unroll

@@ -481,3 +481,27 @@ def greedy_tokens(logits: Tensor, pad_id: int) -> Tensor:
 @greedy_tokens.register_fake
 def _(logits, pad_id):
     return logits.new_empty(logits.shape[0], 1, dtype=torch.int64)
+
+
+# -------------------------------------------------------- associative memory
+
+@torch.library.custom_op("koemi_b200::assoc_window_scan_read", mutates_args=())
+def assoc_window_scan_read(basis: Tensor, normalizer: Tensor, decay: Tensor, value: Tensor, features: Tensor,
+                           write: Tensor, query_features: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """Window read and update of the rank-one associative memory (fp32):
+    returns (read [B, T, d], new basis [B, d, m], new normaliser [B, m])."""
+    decay, write, value, features, query_features = _dense(
+        decay.float(), write.float(), value.float(), features.float(), query_features.float())
+    stream = _prepare(value)
+    batch, length, width = value.shape
+    new_basis = basis.float().contiguous().clone()
+    new_normalizer = normalizer.float().contiguous().clone()
+    read = torch.empty_like(value)
+    call("koemi_assoc_window_scan_read", ptr(decay), ptr(write), ptr(value), ptr(features), ptr(query_features),
+         ptr(new_basis), ptr(new_normalizer), ptr(read), batch, length, width, features.shape[-1], stream)
+    return read, new_basis, new_normalizer
+
+
+@assoc_window_scan_read.register_fake
+def _(basis, normalizer, decay, value, features, write, query_features):
+    return torch.empty_like(value), torch.empty_like(basis), torch.empty_like(normalizer)

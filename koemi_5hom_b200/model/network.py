@@ -632,6 +632,15 @@ def _salient_read(carried_keys, carried_values, carried_valid, keys, values, adm
 
 
 def _associative_scan_read(basis, normalizer, decay, value, features, write, query_features):
+    """Rank-one decayed memory over one window: the native sequential kernel
+    (koemi_assoc_window_scan_read) for 16 memory features on CUDA, else the
+    closed form below."""
+    if value.is_cuda and features.shape[-1] == 16:
+        return _ops.assoc_window_scan_read(basis, normalizer, decay, value, features, write, query_features)
+    return _associative_scan_read_closed_form(basis, normalizer, decay, value, features, write, query_features)
+
+
+def _associative_scan_read_closed_form(basis, normalizer, decay, value, features, write, query_features):
     """Rank-one decayed memory over one window, in closed form.
 
     With D_t = prod_{j<=t} decay_j, the read at t sees the carried memory scaled
