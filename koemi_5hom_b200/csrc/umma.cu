@@ -61,7 +61,9 @@ constexpr uint32_t kABytes = kBM * kBK * 2;
 constexpr uint32_t kBBytes = kBN * kBK * 2;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemColumns = 512;
+constexpr int kMaxPipe = 8;  // barrier slots: the deepest ring (narrow tiles)
 constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+static_assert((2 * kMaxPipe + 4) * 8 + 8 <= 256, "barrier area");
 
 enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3, kDenseCluster = 4 };
 
@@ -286,18 +288,21 @@ __device__ __forceinline__ void load_bias32(const T *bias, int64_t col0, int64_t
     }
 }
 
-// kNarrow (output problem only): N = 128 tiles, for decode-sized pair counts
-// whose 256-wide tiles would leave SMs idle (e.g. 8 experts x 8 tiles).
-template <int kProblem, typename T, bool kPair, bool kNarrow = false>
+// kTileN < 256 (output and direct dense problems): N = 128 or 64 tiles, for
+// decode-sized problems whose 256-wide tiles would leave SMs idle or need a
+// split-K reduction; the smaller stages run a deeper ring.
+template <int kProblem, typename T, bool kPair, int kTileN = kBN>
 __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(const __grid_constant__ UmmaArgs args) {
     // paired tiles: 256 A rows (two 128-row halves) per tile, stages of
     // A0 | A1 | B (64 KB, 3 of them), both 256-column accumulators in use
-    constexpr int kPipe = kPair ? 3 : kStages;
     constexpr uint32_t kAStage = kPair ? 2 * kABytes : kABytes;
-    constexpr int kTileN = kNarrow ? kBN / 2 : kBN;
-    constexpr uint32_t kBStage = kNarrow ? kBBytes / 2 : kBBytes;
+    constexpr uint32_t kBStage = static_cast<uint32_t>(kTileN) * kBK * 2;
     constexpr uint32_t kStage = kAStage + kBStage;
-    static_assert(!kNarrow || kProblem == kOutput, "narrow tiles are for the expert output GEMM");
+    constexpr int kDeepPipe = static_cast<int>((kStages * kStageBytes) / kStage);
+    constexpr int kPipe = kPair ? 3 : (kTileN < kBN ? (kDeepPipe < kMaxPipe ? kDeepPipe : kMaxPipe) : kStages);
+    static_assert(kTileN == kBN || kProblem == kOutput || kProblem == kDense,
+                  "narrow tiles are for the expert output and direct dense problems");
+    static_assert(kTileN == kBN || kTileN == kBN / 2 || kTileN == kBN / 4, "tile width 256, 128 or 64");
     constexpr int kTileRows = kPair ? 2 * kBM : kBM;
     constexpr int kHalves = kPair ? 2 : 1;
     constexpr int kAccBufs = kPair ? 1 : 2;
@@ -309,8 +314,8 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
     uint8_t *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
     uint8_t *stages = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-    uint64_t *empty = full + kStages;
-    uint64_t *acc_full = empty + kStages;
+    uint64_t *empty = full + kMaxPipe;
+    uint64_t *acc_full = empty + kMaxPipe;
     uint64_t *acc_empty = acc_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -518,11 +523,11 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                 float *dst_row = direct ? static_cast<float *>(args.out) + row * args.out_stride
                                         : args.partials + (tile.split * args.rows + row) * args.n_out;
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < kTileN / 32; ++c) {
                     uint32_t y[32];
                     KOEMI_TMEM_LD32(taddr + c * 32, y);
                     tmem_wait_ld();
-                    const int64_t col0 = tile.n * kBN + c * 32;
+                    const int64_t col0 = tile.n * kTileN + c * 32;
                     if (row_ok && col0 < args.n_out) {
                         float o[32];
 #pragma unroll
@@ -721,10 +726,10 @@ int encode_kmajor(CUtensorMap *map, int dtype, const void *base, int64_t rows, i
     return encode_tensor_map(map, type, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int kProblem, bool kPair = false, bool kNarrow = false>
+template <int kProblem, bool kPair = false, int kTileN = kBN>
 int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stream) {
-    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair, kNarrow>
-                                      : umma_gemm_kernel<kProblem, __half, kPair, kNarrow>;
+    auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair, kTileN>
+                                      : umma_gemm_kernel<kProblem, __half, kPair, kTileN>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
@@ -862,7 +867,7 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     g2.out = output;
     g2.status = g1.status;
     g2.idesc = make_idesc(dtype, static_cast<int>(tile_n));
-    rc = narrow ? launch<kOutput, false, true>(g2, dtype, max_m_tiles * g2.n_tiles, stream)
+    rc = narrow ? launch<kOutput, false, kBN / 2>(g2, dtype, max_m_tiles * g2.n_tiles, stream)
                 : launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
     if (rc != KOEMI_OK) return rc;
     KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, segment_offsets, expert_count, pairs, d * 2));
@@ -940,6 +945,10 @@ struct DensePlan {
     int64_t splits;
     int64_t k_per_split;
 };
+// Measured alternatives that lost at decode sizes: full-K N = 64 / 128 tiles
+// without a reduction (every narrow tile re-reads all activation rows from L2:
+// gates 13.8 -> 17.0 us at 256 rows) and a push-style reduction through
+// distributed shared memory (13.8 -> 24.7 us).
 DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
     const int64_t k_blocks = (k + kBK - 1) / kBK;
     const int64_t wanted = dense_splits(rows, n, k);
