@@ -1,18 +1,21 @@
 // Dense front: affine recurrent scan h_t = a_t * h_{t-1} + b_t.
 //
 // Layout: retention/increment/states are [batch, length, features] row-major
-// (features contiguous). One CTA owns 32 features of one batch row and walks
-// the whole sequence in chunks of 64 positions. Each chunk is staged into
-// shared memory by TMA (3D tensor map, box {32 features, 64 positions, 1})
-// through a multi-stage mbarrier pipeline, so HBM streams while the previous
-// chunks are being combined. Inside a chunk, warp w owns positions
-// [8w, 8w + 8) and lane l owns feature l: every thread first composes its 8
-// affine maps into one (A, B) pair, the 8 per-warp pairs are exchanged through
-// shared memory to form each warp's carry-in from the running fp32 state, and
-// the thread then replays its 8 steps from that carry to produce h_t, which is
-// stored straight from registers (32 consecutive features per warp store).
+// (features contiguous), fp32 state. Three kernels:
+//   - scan_segment_kernel (with a caller workspace): the sequence is cut into
+//     segments scanned by separate CTAs that pass carries by decoupled
+//     look-back (described at the kernel); thousands of CTAs at prefill sizes.
+//   - scan_forward_kernel (no workspace): one CTA owns 32 features of one
+//     batch row and walks the whole sequence in chunks of 64 positions staged
+//     by TMA (3D tensor map, box {32 features, 64 positions, 1}) through a
+//     multi-stage mbarrier pipeline. Inside a chunk, warp w owns positions
+//     [8w, 8w + 8) and lane l owns feature l: each thread composes its 8
+//     affine maps into one (A, B) pair, the per-warp pairs are exchanged
+//     through shared memory to form each warp's carry-in from the running
+//     state, and the thread replays its 8 steps to produce h_t.
+//   - scan_forward_short_kernel: T <= 8 (decode steps), one thread per lane.
 // Reference behaviour: dense/affine_scan.cu:18-56 (sequential per lane) and
-// model/scan.py:17-30 (log-step doubling); both compute the same recurrence.
+// model/scan.py:17-30 (log-step doubling); all compute the same recurrence.
 #include "common.cuh"
 
 namespace koemi {
