@@ -273,12 +273,25 @@ def emit(line: dict, args) -> None:
 class GreedyTokens:
     """The greedy sampler of the decode loop: TokenSampler's greedy path (PAD
     masked, first index among equal maxima) as one native pass over the
-    logits."""
+    logits, called through the C ABI into a reused output (no op dispatch on
+    the host between steps)."""
+
+    def __init__(self):
+        self._out = None
 
     def __call__(self, logits):
-        from koemi_5hom_b200.cuda_kernels import _ops
+        import torch
+        from koemi_5hom_b200 import _native
         from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
-        return _ops.greedy_tokens(logits.reshape(-1, logits.shape[-1]).float(), PAD_TOKEN_ID)
+        flat = logits.reshape(-1, logits.shape[-1])
+        if flat.dtype != torch.float32 or not flat.is_contiguous():
+            flat = flat.float().contiguous()
+        rows, vocab = flat.shape
+        if self._out is None or self._out.shape[0] != rows or self._out.device != flat.device:
+            self._out = torch.empty(rows, 1, dtype=torch.int64, device=flat.device)
+        _native.call("koemi_sampler_greedy", flat.data_ptr(), rows, vocab, vocab, PAD_TOKEN_ID,
+                     self._out.data_ptr(), torch.cuda.current_stream(flat.device).cuda_stream)
+        return self._out
 
 
 

@@ -67,10 +67,16 @@ __global__ void zero_tail_rows_kernel(void *out, const int64_t *__restrict__ off
     char *base = static_cast<char *>(out);
     const int64_t begin = valid_rows * row_bytes;
     const int64_t end = pairs * row_bytes;
-    for (int64_t i = begin + (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x); i < end;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        base[i] = 0;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (((reinterpret_cast<uintptr_t>(base) | static_cast<uintptr_t>(row_bytes)) & 15) == 0) {
+        // whole rows of 16-byte packets: begin and end are multiples of 16
+        uint4 *packets = reinterpret_cast<uint4 *>(base + begin);
+        const int64_t count = (end - begin) / 16;
+        for (int64_t i = first; i < count; i += stride) packets[i] = make_uint4(0, 0, 0, 0);
+        return;
     }
+    for (int64_t i = begin + first; i < end; i += stride) base[i] = 0;
 }
 
 namespace {
