@@ -64,6 +64,26 @@ def test_workspace_queries_are_host_only():
     assert lib.koemi_moe_grouped_mlp_workspace(512, 2048, 4096, 64, _native.BF16) > 0
 
 
+def test_scan_workspace_query():
+    lib = _native.library()
+    # bf16: tiles of 128 positions x 64 features, 768 B of records each after a 256 B head
+    assert lib.koemi_dense_affine_scan_workspace(8, 4096, 1024, _native.BF16) == 256 + 8 * 16 * 32 * 768
+    # fp32 tiles are 64 positions long
+    assert lib.koemi_dense_affine_scan_workspace(8, 4096, 1024, _native.F32) == 256 + 8 * 16 * 64 * 768
+    # decode steps (length <= 8) and fp64 take the workspace-free kernels
+    assert lib.koemi_dense_affine_scan_workspace(256, 1, 2048, _native.BF16) == 0
+    assert lib.koemi_dense_affine_scan_workspace(8, 4096, 1024, _native.F64) == 0
+
+
+def test_sampler_and_window_memory_reject_bad_arguments_on_the_host():
+    lib = _native.library()
+    assert lib.koemi_sampler_greedy(None, 4, 0, 0, 256, None, None) == _native.KOEMI_ERR_INVALID
+    assert lib.koemi_sampler_greedy(None, 0, 10, 10, 256, None, None) == _native.KOEMI_OK  # no rows
+    status = lib.koemi_assoc_window_scan_read(None, None, None, None, None, None, None, None, 2, 5, 64, 8, None)
+    assert status == _native.KOEMI_ERR_UNSUPPORTED
+    assert "16 memory features" in _native.last_error()
+
+
 def test_last_error_is_truncated_safely():
     lib = _native.library()
     lib.koemi_moe_route_topk(None, None, None, None, 4, 0, 1, _native.I64, None)
