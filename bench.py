@@ -6,18 +6,20 @@ Workload (config 5): HERM stack with vocabulary 32768, d_model 2048, 24
 blocks, memory features 16, 128 local + 128 salient ring slots, 64 experts
 top-2 (d_ff 4096), bf16 weights, fp32 state, bf16 ring storage; 256 streams
 in total, each with a 2048-token prompt of uniform random ids (PAD excluded),
-prefilled untimed, then greedy decode. Weights are seeded random
-(N(0, 0.02)), inputs synthetic. One step = one decode step of every stream
-(256 tokens). The timed region is K CUDA-graph replays of that step between
-barriers, timed with CUDA events on the decode stream, max over ranks; every
-step reads far more than the 126 MB L2, so no flush is needed.
+prefilled untimed, then greedy decode (the native greedy sampler, PAD
+masked). Weights are seeded random (N(0, 0.02)), inputs synthetic. One step =
+one decode step of every stream (256 tokens) plus its sampler. The timed
+region is K CUDA-graph replays of that step between barriers, timed with CUDA
+events on the decode stream, max over ranks; every step reads far more than
+the 126 MB L2, so no flush is needed.
 
 Multi-GPU (config 5): one process per GPU (torchrun); the 256 streams are
 split data-parallel (256/N per rank) and the 64 experts expert-parallel
-(64/N per rank, two NCCL all-to-alls of the token rows per MoE block and
-step, captured in the step's CUDA graph): the total work is fixed, so
+(64/N per rank): per MoE block and step the expert rows go to their owners
+and the outputs come back through peer-memory stores (CUDA IPC buffers and
+epoch flags, inside the step's CUDA graph). The total work is fixed, so
 ``scaling`` is "strong". ``--weak`` keeps 256 streams per GPU with a full
-replica per rank instead (no collective on the step).
+replica per rank instead (no exchange on the step).
 
 ``--impl reference`` times the CPU oracle port of the same decode step on the
 host cores (rank 0 only; the reference is Python and does not travel to the
