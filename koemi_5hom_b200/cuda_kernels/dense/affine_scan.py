@@ -3,8 +3,10 @@
 ``dense_affine_scan(retention, increment, initial=None)`` keeps the reference
 signature, broadcasting rule, dtype set {f16, bf16, f32, f64}, validation
 order/messages and exception types (src/koemi/cuda_kernels/dense/affine_scan.py:33-255).
-The forward is ``koemi_dense_affine_scan_forward`` (TMA-staged chunked scan
-with an fp32 running state; fp64 for f64 input) and the backward is
+The forward is ``koemi_dense_affine_scan_forward`` with a workspace from the
+caching allocator: segments of the sequence scanned by separate CTAs from
+TMA-staged tiles, carries passed by decoupled look-back, fp32 state (f64 input
+takes a per-lane fp64 kernel). The backward is
 ``koemi_dense_affine_scan_backward`` (reverse-time adjoint). There is no CPU
 fallback.
 """
