@@ -6,7 +6,7 @@ order/messages and exception types (src/koemi/cuda_kernels/dense/affine_scan.py:
 The forward is ``koemi_dense_affine_scan_forward`` with a workspace from the
 caching allocator: segments of the sequence scanned by separate CTAs from
 TMA-staged tiles, carries passed by decoupled look-back, fp32 state (f64 input
-takes a per-lane fp64 kernel). The backward is
+takes the workspace-free kernel, one CTA walking each lane group in fp64). The backward is
 ``koemi_dense_affine_scan_backward`` (reverse-time adjoint). There is no CPU
 fallback.
 """
