@@ -332,12 +332,16 @@ KOEMI_API int koemi_moe_permute_topk(const void *context, const void *assignment
  * flight). It has no counterpart in the reference. Arguments and outputs are
  * those of koemi_moe_permute_topk minus the workspace: the scratch is a fixed
  * 2 MiB device array inside the library, held by every GPU that loads it
- * until the process exits, enough for 65536 token-expert pairs; larger
- * requests fail with KOEMI_ERR_UNSUPPORTED and a message. The first call on a
- * device looks up that array's address with the device current, so make that
- * first call before any stream capture. All calls share the array: calls that
- * can overlap on the GPU (different streams, different host threads) race and
- * must be serialised by the caller. Allocates nothing. */
+ * until the process exits. A request fits when
+ * koemi_moe_permute_workspace(tokens, top_k, expert_count) <= 2 MiB: 65536
+ * token-expert pairs always fit, at any expert count, and more fit when there
+ * are few experts; larger requests fail with KOEMI_ERR_UNSUPPORTED and a
+ * message that gives the bytes needed. The first call in a context looks up
+ * that array's address with the device current (again after the context
+ * changes, e.g. after cudaDeviceReset), so make that first call before any
+ * stream capture. All calls share the array: calls that can overlap on the
+ * GPU (different streams, different host threads) race and must be
+ * serialised by the caller. Allocates nothing. */
 KOEMI_API int koemi_moe_permute_topk_static(const void *context, const void *assignments, const uint8_t *valid,
                                   void *sorted_context, int64_t *sorted_rows, int64_t *sorted_experts,
                                   int64_t *segment_offsets, int64_t *pair_positions, int64_t tokens,

@@ -196,6 +196,15 @@ def device_status(device: torch.device) -> int:
     return value.value
 
 
+def raise_for_device_status(device: torch.device) -> None:
+    """Read (and clear) the device status word; raise if a bounded
+    device-side wait gave up since the last read. Synchronises the device."""
+    status = device_status(device)
+    if status != KOEMI_OK:
+        raise KoemiNativeError("device status", status,
+                               "a bounded device-side wait gave up (a peer or producer never signalled)")
+
+
 def stream_of(tensor: torch.Tensor) -> int:
     """Raw handle of the current stream of ``tensor``'s device."""
     return torch.cuda.current_stream(tensor.device).cuda_stream

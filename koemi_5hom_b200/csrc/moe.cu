@@ -993,28 +993,80 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
 namespace {
 constexpr size_t kStaticPermuteScratchBytes = size_t(2) << 20;  // 2 MiB on every device that loads the library
 constexpr int kStaticScratchDevices = 64;
+
+// A cached address is only valid in the context it was looked up in: after
+// cudaDeviceReset, or when a host drives the device through another context,
+// the array lives at a different address. Each cache entry therefore carries
+// the driver's unique id of its context (cuCtxGetId, resolved through the
+// runtime's driver entry point, so the library still needs no -lcuda).
+struct StaticScratchEntry {
+    unsigned long long context_id;
+    void *address;
+};
 std::mutex g_static_scratch_mutex;
-void *g_static_scratch[kStaticScratchDevices] = {};
+StaticScratchEntry g_static_scratch[kStaticScratchDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+std::once_flag g_ctx_entry_once;
+
+// Unique id of the calling thread's current context; 0 when there is none yet.
+int current_context_id(unsigned long long *id) {
+    std::call_once(g_ctx_entry_once, [] {
+        void *entry = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &entry, cudaEnableDefault, &query) == cudaSuccess &&
+            query == cudaDriverEntryPointSuccess) {
+            g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(entry);
+        }
+        entry = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &entry, cudaEnableDefault, &query) == cudaSuccess &&
+            query == cudaDriverEntryPointSuccess) {
+            g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(entry);
+        }
+    });
+    if (g_ctx_get_current == nullptr || g_ctx_get_id == nullptr) {
+        return fail(KOEMI_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are unavailable from the driver");
+    }
+    CUcontext context = nullptr;
+    if (g_ctx_get_current(&context) != CUDA_SUCCESS) return fail(KOEMI_ERR_CUDA, "cuCtxGetCurrent failed");
+    *id = 0;
+    if (context != nullptr && g_ctx_get_id(context, id) != CUDA_SUCCESS) {
+        return fail(KOEMI_ERR_CUDA, "cuCtxGetId failed");
+    }
+    return KOEMI_OK;
+}
 }  // namespace
 
 static __device__ __align__(256) unsigned char koemi_permute_static_scratch[kStaticPermuteScratchBytes];
 
 namespace {
-// Device address of the scratch array for the current device, looked up once
-// per device (with that device current) and cached.
+// Device address of the scratch array in the current device's current
+// context. The lookup (cudaGetSymbolAddress with that device current) runs
+// on the first call in a context and again whenever the context changed;
+// later calls in the same context reuse the cached address.
 int static_permute_scratch(void **out) {
     int device = 0;
     KOEMI_CUDA_TRY(cudaGetDevice(&device));
     if (device < 0 || device >= kStaticScratchDevices) {
         return fail(KOEMI_ERR_UNSUPPORTED, "device %d is beyond the static-scratch device table", device);
     }
+    unsigned long long context_id = 0;
+    int rc = current_context_id(&context_id);
+    if (rc != KOEMI_OK) return rc;
     std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-    if (g_static_scratch[device] == nullptr) {
+    StaticScratchEntry &entry = g_static_scratch[device];
+    if (context_id == 0 || entry.address == nullptr || entry.context_id != context_id) {
         void *address = nullptr;
         KOEMI_CUDA_TRY(cudaGetSymbolAddress(&address, koemi_permute_static_scratch));
-        g_static_scratch[device] = address;
+        rc = current_context_id(&context_id);  // the lookup may have created the primary context
+        if (rc != KOEMI_OK) return rc;
+        entry.context_id = context_id;
+        entry.address = address;
     }
-    *out = g_static_scratch[device];
+    *out = entry.address;
     return KOEMI_OK;
 }
 }  // namespace
@@ -1031,9 +1083,11 @@ extern "C" int koemi_moe_permute_topk_static(const void *context, const void *as
     const size_t need = koemi_moe_permute_workspace(tokens, top_k, expert_count);
     if (need > kStaticPermuteScratchBytes) {
         return fail(KOEMI_ERR_UNSUPPORTED,
-                    "allocation-free permute: %lld tokens x top_k %lld over %lld experts needs %zu scratch bytes, "
-                    "more than the fixed %zu (at most 65536 pairs); use koemi_moe_permute_topk with a workspace",
-                    (long long)tokens, (long long)top_k, (long long)expert_count, need, kStaticPermuteScratchBytes);
+                    "allocation-free permute: %lld tokens x top_k %lld over %lld experts needs %zu scratch bytes "
+                    "(koemi_moe_permute_workspace), more than the fixed %zu-byte array; 65536 token-expert pairs "
+                    "always fit at any expert count, more fit with fewer experts; use koemi_moe_permute_topk with "
+                    "a workspace", (long long)tokens, (long long)top_k, (long long)expert_count, need,
+                    kStaticPermuteScratchBytes);
     }
     void *scratch = nullptr;
     const int rc = static_permute_scratch(&scratch);

@@ -50,46 +50,56 @@ def load_native_extension() -> Any:
     return handle
 
 
+# Per-tensor rules, checked in order for every tensor a front receives: the
+# first rule a tensor breaks raises (exception type, message with its name).
+_TENSOR_RULES = (
+    (lambda t: not isinstance(t, Tensor), TypeError, "{} must be a torch.Tensor"),
+    (lambda t: not t.is_cuda, CudaMoeValidationError, "{} must be a CUDA tensor"),
+    (lambda t: not t.is_contiguous(), CudaMoeValidationError, "{} must be contiguous"),
+)
+_FLOAT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+# Upper limits of the positive integer arguments (the kernels' index widths).
+_COUNT_LIMITS = {"expert_count": 1 << 20, "top_k": 256, "token_count": 1 << 31}
+
+
 def _check_tensors(tensors: dict[str, Tensor]) -> None:
     for name, tensor in tensors.items():
-        if not isinstance(tensor, Tensor):
-            raise TypeError(f"{name} must be a torch.Tensor")
-        if not tensor.is_cuda:
-            raise CudaMoeValidationError(f"{name} must be a CUDA tensor")
-        if not tensor.is_contiguous():
-            raise CudaMoeValidationError(f"{name} must be contiguous")
-    devices = {tensor.device for tensor in tensors.values()}
-    if len(devices) != 1:
-        raise CudaMoeValidationError(
-            f"all MoE tensors must use one CUDA device, found {', '.join(sorted(str(d) for d in devices))}"
-        )
+        for broken, error, message in _TENSOR_RULES:
+            if broken(tensor):
+                raise error(message.format(name))
+    devices = sorted({str(tensor.device) for tensor in tensors.values()})
+    if len(devices) > 1:
+        raise CudaMoeValidationError(f"all MoE tensors must use one CUDA device, found {', '.join(devices)}")
 
 
 def _check_float(tensor: Tensor, name: str) -> None:
-    if tensor.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+    if tensor.dtype not in _FLOAT_DTYPES:
         raise CudaMoeValidationError(f"{name} must use float32, float16, or bfloat16; found {tensor.dtype}")
 
 
-def _bounded(value: int, name: str, upper: int) -> int:
-    if isinstance(value, bool) or not isinstance(value, int) or value < 1:
+def _count(name: str, value: int) -> int:
+    """``value`` if it is a positive int within ``_COUNT_LIMITS[name]``."""
+    if type(value) is not int or value < 1:
         raise CudaMoeValidationError(f"{name} must be a positive integer")
-    if value > upper:
-        raise CudaMoeValidationError(f"{name} exceeds the CUDA MoE limit of {upper}")
+    if value > _COUNT_LIMITS[name]:
+        raise CudaMoeValidationError(f"{name} exceeds the CUDA MoE limit of {_COUNT_LIMITS[name]}")
     return value
 
 
 def _inference_only(tensors: dict[str, Tensor]) -> None:
-    needing = [name for name, tensor in tensors.items() if tensor.requires_grad]
-    if needing:
-        raise RuntimeError("the native MoE path is inference-only; tensors require gradients: " + ", ".join(needing))
+    tracked = [name for name in tensors if tensors[name].requires_grad]
+    if tracked:
+        raise RuntimeError("the native MoE path is inference-only; tensors require gradients: " + ", ".join(tracked))
 
 
 def _reject_duplicates(assignments: Tensor, valid_mask: Tensor, message: str) -> None:
+    """A valid token may not name one expert twice: after sorting its k
+    slots, equal neighbours mark a repeat."""
     if assignments.shape[-1] < 2:
         return
-    equal = assignments.unsqueeze(-1).eq(assignments.unsqueeze(-2))
-    later_repeat = torch.triu(equal, diagonal=1).any(dim=-1)
-    if bool((later_repeat & valid_mask.unsqueeze(-1)).any().item()):
+    ordered = assignments.sort(dim=-1).values
+    repeated = (ordered[..., 1:] == ordered[..., :-1]).any(dim=-1)
+    if bool((repeated & valid_mask).any().item()):
         raise CudaMoeValidationError(message)
 
 
@@ -106,8 +116,8 @@ def route_topk_valid(token_ids: Tensor, previous_token_ids: Tensor, valid_mask: 
         raise CudaMoeValidationError("valid_mask must use boolean dtype")
     if token_ids.shape != previous_token_ids.shape or token_ids.shape != valid_mask.shape:
         raise CudaMoeValidationError("routing tensors must have equal shapes")
-    expert_count = _bounded(expert_count, "expert_count", 1 << 20)
-    top_k = _bounded(top_k, "top_k", 256)
+    expert_count = _count("expert_count", expert_count)
+    top_k = _count("top_k", top_k)
     if top_k > expert_count:
         raise CudaMoeValidationError("top_k must not exceed expert_count")
     load_native_extension()
@@ -135,8 +145,8 @@ def permute_topk(context: Tensor, assignments: Tensor, valid_mask: Tensor, *,
         raise CudaMoeValidationError("assignments must use int32 or int64")
     if valid_mask.ndim != 1 or valid_mask.shape[0] != assignments.shape[0]:
         raise CudaMoeValidationError("valid_mask must have shape [token_count]")
-    expert_count = _bounded(expert_count, "expert_count", 1 << 20)
-    top_k = _bounded(int(assignments.shape[1]), "top_k", 256)
+    expert_count = _count("expert_count", expert_count)
+    top_k = _count("top_k", int(assignments.shape[1]))
     if top_k > expert_count:
         raise CudaMoeValidationError("top_k must not exceed expert_count")
     out_of_range = ((assignments < 0) | (assignments >= expert_count)) & valid_mask.unsqueeze(-1)
@@ -226,8 +236,8 @@ def combine_topk(expert_outputs: Tensor, sorted_rows: Tensor, segment_offsets: T
         raise CudaMoeValidationError("sorted_rows must match expert_outputs pair_count")
     if segment_offsets.dtype != torch.int64 or segment_offsets.ndim != 1:
         raise CudaMoeValidationError("segment_offsets must be a one-dimensional int64 tensor")
-    token_count = _bounded(token_count, "token_count", 1 << 31)
-    top_k = _bounded(top_k, "top_k", 256)
+    token_count = _count("token_count", token_count)
+    top_k = _count("top_k", top_k)
     valid_pairs = int(segment_offsets[-1].item())
     if valid_pairs < 0 or valid_pairs > expert_outputs.shape[0]:
         raise CudaMoeValidationError("segment_offsets final value is outside pair_count")

@@ -18,9 +18,10 @@ Per window of ``scan_chunk`` positions each block runs:
 
 Parameters are held in a packed layout (all projections that read the same
 input are one GEMM) in ``compute_dtype``; memories, reductions and the state
-stay fp32. Dense projections are cuBLAS GEMMs with fp32 outputs; every other
-step is a koemi_b200 kernel or a small torch elementwise/batched op on the
-current stream. Nothing reads device values on the host unless
+stay fp32. Dense projections run the tcgen05 projection kernel
+(``koemi_dense_projection``: bf16 operands, fused bias, fp32 out) for bf16
+models and cuBLAS (addmm) for fp32 models; every other step is a koemi_b200
+kernel or a small torch elementwise/batched op on the current stream. Nothing reads device values on the host unless
 ``trusted_inputs`` is False (token counting and id validation, as the
 reference does), so decode steps can be captured in CUDA graphs.
 
@@ -284,6 +285,13 @@ class KoemiModel(nn.Module):
         if mode == "padded" and self.exchange == "peer":
             return self.peer_exchange(sorted_rows.shape[0], sorted_rows.shape[1], sorted_rows.dtype).run(
                 sorted_rows, sorted_experts, offsets, block.expert_weights())
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            # A 2-rank config-5 decode with these all-to-alls captured in the
+            # step graph stalled once without a cause found (no fault; the
+            # small 2-rank graph tests passed), so the NCCL exchange is kept
+            # out of CUDA graphs: use exchange="peer" or an eager decoder.
+            raise RuntimeError("the NCCL expert exchange is not allowed inside CUDA graph capture; "
+                               "use model.exchange = 'peer' or BatchDecoder(capture_graph=False)")
         return expert_parallel_mlp(self.expert_shard, sorted_rows, sorted_experts, offsets, block.expert_weights(),
                                    mode)
 

@@ -128,6 +128,9 @@ class BatchDecoder:
         device = model.device
         if capture_graph and device.type != "cuda":
             raise RuntimeError("CUDA graph capture requires a model on a CUDA device")
+        if capture_graph and getattr(model, "expert_shard", None) is not None and model.exchange == "nccl":
+            raise RuntimeError("the NCCL expert exchange is not captured in CUDA graphs; use model.exchange = "
+                               "'peer' or capture_graph=False")
         self.model = model
         self.device = device
         self._capture_graph = capture_graph
@@ -247,33 +250,43 @@ class BatchDecoder:
         self._static_ids = None
         self._static_logits = None
 
+    def _rows(self) -> int:
+        return self._dstate.last_token_ids.shape[0] if self._dstate is not None else _rows(self._state)
+
     def _normalize_step_input(self, token_ids: Tensor) -> Tensor:
-        if not isinstance(token_ids, Tensor):
-            raise TypeError("step token ids must be a torch.Tensor")
-        if token_ids.ndim == 1:
-            token_ids = token_ids.unsqueeze(-1)
-        if token_ids.ndim != 2 or token_ids.shape[1] != 1:
-            raise ValueError("step requires exactly one token id per row")
-        rows = self._dstate.last_token_ids.shape[0] if self._dstate is not None else _rows(self._state)
-        if token_ids.shape[0] != rows:
-            raise ValueError("step token ids must carry one row per decoded sequence")
-        if token_ids.dtype != torch.long:
-            raise TypeError("step token ids must use torch.long")
-        if token_ids.device != self.device:
-            raise ValueError("step token ids must live on the model device")
-        return token_ids
+        _enforce(_STEP_TYPE_RULE, token_ids, self)
+        ids = token_ids.unsqueeze(-1) if token_ids.ndim == 1 else token_ids
+        _enforce(_STEP_RULES, ids, self)
+        return ids
 
     def _validate_prompt(self, input_ids: Tensor) -> None:
-        if not isinstance(input_ids, Tensor):
-            raise TypeError("prompt ids must be a torch.Tensor")
-        if input_ids.ndim != 2 or input_ids.shape[0] == 0 or input_ids.shape[1] == 0:
-            raise ValueError("prompt ids must have shape [batch, sequence]")
-        if input_ids.dtype != torch.long:
-            raise TypeError("prompt ids must use torch.long")
-        if input_ids.device != self.device:
-            raise ValueError("prompt ids must live on the model device")
-        if int(input_ids.min()) < 0 or int(input_ids.max()) >= self.model.settings.vocabulary_size:
-            raise ValueError("prompt ids contain values outside the model vocabulary")
+        _enforce(_PROMPT_RULES, input_ids, self)
+
+
+# Input contracts of BatchDecoder (the reference's messages, in its order of
+# checks, fast_decode.py:304-330): (broken(ids, decoder), exception, message).
+_STEP_TYPE_RULE = ((lambda ids, dec: not isinstance(ids, Tensor), TypeError, "step token ids must be a torch.Tensor"),)
+_STEP_RULES = (
+    (lambda ids, dec: ids.ndim != 2 or ids.shape[1] != 1, ValueError, "step requires exactly one token id per row"),
+    (lambda ids, dec: ids.shape[0] != dec._rows(), ValueError,
+     "step token ids must carry one row per decoded sequence"),
+    (lambda ids, dec: ids.dtype != torch.long, TypeError, "step token ids must use torch.long"),
+    (lambda ids, dec: ids.device != dec.device, ValueError, "step token ids must live on the model device"),
+)
+_PROMPT_RULES = (
+    (lambda ids, dec: not isinstance(ids, Tensor), TypeError, "prompt ids must be a torch.Tensor"),
+    (lambda ids, dec: ids.ndim != 2 or 0 in ids.shape, ValueError, "prompt ids must have shape [batch, sequence]"),
+    (lambda ids, dec: ids.dtype != torch.long, TypeError, "prompt ids must use torch.long"),
+    (lambda ids, dec: ids.device != dec.device, ValueError, "prompt ids must live on the model device"),
+    (lambda ids, dec: int(ids.min()) < 0 or int(ids.max()) >= dec.model.settings.vocabulary_size, ValueError,
+     "prompt ids contain values outside the model vocabulary"),
+)
+
+
+def _enforce(rules, ids, decoder) -> None:
+    for broken, error, message in rules:
+        if broken(ids, decoder):
+            raise error(message)
 
 
 def generate_tokens(model, prompt_ids: Tensor, max_new_tokens: int, *, policy: SamplingPolicy | None = None,

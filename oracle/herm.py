@@ -96,7 +96,11 @@ class HermOracle:
         out["state"] = state
         return out
 
-    def window(self, ids: torch.Tensor, state: dict) -> dict:
+    def window(self, ids: torch.Tensor, state: dict, context: torch.Tensor | None = None,
+               logits: bool = True) -> dict:
+        """One window of the block. ``context`` (an extension for stacked
+        blocks) replaces the embedding rows of ``ids`` as the block input;
+        ``logits=False`` skips the head (blocks below the top of a stack)."""
         c = self.config
         batch, length = ids.shape
         width = c.embedding_size
@@ -104,7 +108,8 @@ class HermOracle:
         v3 = valid.unsqueeze(-1)
 
         # embedding + input norm (network.py:703-707), bounded gates (memory.py:22-26)
-        u = self.norm("input_normalizer.weight", self.p["embedding.weight"][ids])
+        inputs = self.p["embedding.weight"][ids] if context is None else context
+        u = self.norm("input_normalizer.weight", inputs)
         lo, hi = 2.0 ** -8, 1.0 - 2.0 ** -8
         a = lo + (hi - lo) * torch.sigmoid(self.linear("recurrent_state.retention_projection", u))
         b = (1.0 - a) * torch.tanh(self.linear("recurrent_state.candidate_projection", u))
@@ -204,7 +209,7 @@ class HermOracle:
                           self.linear("fusion_projection", torch.cat((h, memory_value, local_value, salient_value), -1)))
         previous = self._previous_ids(ids, valid, state["last_token_ids"])
         final, expert_indices, active = self._experts(fused, ids, previous, valid)
-        logits = self.linear("token_predictor", final)
+        head = self.linear("token_predictor", final) if logits else None
 
         local_keep = all_keys.shape[1] - min(all_keys.shape[1], c.local_memory_size)
         sk, sv, svalid = ops.salient_tail(s_keys, s_values, s_valid, keys, values, admission, c.salience_memory_size)
@@ -216,7 +221,7 @@ class HermOracle:
             "salient_keys": sk, "salient_values": sv, "salient_valid": svalid,
             "last_token_ids": last_ids,
         }
-        return {"logits": logits, "surprise": surprise, "expert_indices": expert_indices,
+        return {"logits": head, "final": final, "surprise": surprise, "expert_indices": expert_indices,
                 "active_expert_indices": active, "valid_positions": valid, "state": new_state}
 
     def _scan_read(self, basis, normalizer, decay, value, features, write, query_features):

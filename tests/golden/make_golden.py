@@ -1,10 +1,11 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Runs only where the Koemi-5HOM sources are available (default
-``/root/reference/src``, override with ``KOEMI_REFERENCE_SRC``); the fixtures
-it writes are committed, so nothing else ever imports the reference.
+Runs only where the Koemi-5HOM sources are available: ``KOEMI_REFERENCE_SRC``
+must name the reference's ``src`` directory (the one holding ``koemi/``); the
+fixtures it writes are committed, so nothing else ever imports the reference.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    KOEMI_REFERENCE_SRC=<reference checkout>/src PYTHONDONTWRITEBYTECODE=1 \
+        python tests/golden/make_golden.py
 
 Fixtures:
 - ``ops.pt``: per-operator inputs and the reference's outputs (scan, norms,
@@ -26,7 +27,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 from herm_weights import HermShape, herm_parameters  # noqa: E402
 
-REFERENCE_SRC = os.environ.get("KOEMI_REFERENCE_SRC", "/root/reference/src")
+REFERENCE_SRC = os.environ.get("KOEMI_REFERENCE_SRC")
+if not REFERENCE_SRC or not (Path(REFERENCE_SRC) / "koemi").is_dir():
+    raise SystemExit("set KOEMI_REFERENCE_SRC to the reference's src directory (the one that holds koemi/)")
 sys.path.insert(0, REFERENCE_SRC)
 
 from koemi.configuration.settings import ModelSettings  # noqa: E402

@@ -86,3 +86,23 @@ def _rank_main(rank: int, world: int, port: int, experts: int, top_k: int) -> No
 @pytest.mark.parametrize("world,experts,top_k", [(2, 8, 2), (4, 8, 3), (2, 2, 1)])
 def test_exchange_equals_single_rank_mlp(world, experts, top_k):
     mp.spawn(_rank_main, args=(world, _free_port(), experts, top_k), nprocs=world, join=True)
+
+
+def test_nccl_exchange_is_refused_inside_graph_capture(monkeypatch):
+    """The NCCL all-to-all exchange stays out of CUDA graphs: expert_mlp
+    refuses it while the stream is capturing, before any collective, and the
+    decoder refuses to capture a model that uses it."""
+    from koemi_5hom_b200.runtime import BatchDecoder
+    settings = ModelSettings(vocabulary_size=300, embedding_size=64, memory_features=8, expert_count=8,
+                             expert_top_k=2)
+    model = KoemiModel(settings, expert_shard=ExpertShard(2, 0, 8))
+    model.exchange = "nccl"
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    block = model.blocks[0]
+    rows = torch.zeros(4, 64)
+    with pytest.raises(RuntimeError, match="not allowed inside CUDA graph capture"):
+        model.expert_mlp(block, rows, torch.zeros(4, dtype=torch.long), torch.zeros(9, dtype=torch.long))
+    monkeypatch.setattr(type(model), "device", property(lambda self: torch.device("cuda", 0)))
+    with pytest.raises(RuntimeError, match="not captured in CUDA graphs"):
+        BatchDecoder(model, capture_graph=True, cache_expert_weights=False)

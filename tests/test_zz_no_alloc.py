@@ -55,7 +55,11 @@ def _permute(static: bool, context, assignments, valid, experts):
 def test_static_permute_matches_workspace_permute_on_consecutive_calls(call):
     device = torch.device("cuda", 0)
     results = []
-    for seed, (tokens, experts, top_k, width) in enumerate(((4000, 64, 2, 96), (777, 300, 3, 40))):
+    # the radix path (8000 pairs at 64 experts; 300 experts) and the one-CTA
+    # path (2000 pairs at 16 experts), whose keys and counts live in the
+    # scratch too
+    shapes = ((4000, 64, 2, 96), (777, 300, 3, 40), (1000, 16, 2, 64))
+    for seed, (tokens, experts, top_k, width) in enumerate(shapes):
         g = torch.Generator().manual_seed(100 * call + seed)
         assignments = torch.randint(-1, experts + 1, (tokens, top_k), generator=g).to(device)
         valid = (torch.rand(tokens, generator=g) > 0.1).to(device)
@@ -65,7 +69,7 @@ def test_static_permute_matches_workspace_permute_on_consecutive_calls(call):
         for name in expected:
             assert torch.equal(got[name], expected[name]), (seed, name)  # bit-exact, like the permute tests
         results.append(got["segment_offsets"][-1].item())
-    assert results[0] != results[1]  # the two calls really were different problems
+    assert len(set(results)) == len(results)  # the calls really were different problems
 
 
 def test_static_permute_refuses_oversized_requests():
@@ -73,4 +77,12 @@ def test_static_permute_refuses_oversized_requests():
     status = lib.koemi_moe_permute_topk_static(None, None, None, None, None, None, None, None, 200000, 64, 2, 64,
                                               _native.BF16, _native.I64, None)
     assert status == _native.KOEMI_ERR_UNSUPPORTED
-    assert "65536 pairs" in _native.last_error()
+    message = _native.last_error()
+    need = lib.koemi_moe_permute_workspace(200000, 2, 64)
+    assert f"needs {need} scratch bytes" in message and "65536 token-expert pairs always fit" in message
+
+
+def test_static_permute_accepts_65536_pairs_at_any_expert_count():
+    lib = _native.library()
+    for experts in (1, 64, 255, 256, 2048, 1 << 20):
+        assert lib.koemi_moe_permute_workspace(65536, 1, experts) <= 2 << 20
