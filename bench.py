@@ -69,8 +69,8 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
-    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "expert_decode", "surprise_decode", "surprise_prefill",
-                                    "dense_decode"),
+    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "expert_decode", "surprise_decode",
+                                    "surprise_prefill", "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
     p.add_argument("--op-tokens", type=int, default=None,
                    help="token count of --op moe (default: config 4's 131072; smaller for profiler captures)")
@@ -642,8 +642,123 @@ def run_op(args) -> None:
     emit(line, args)
 
 
+def run_op_moe_parallel(args) -> None:
+    """Config 4 (MoE dispatch + experts) over N ranks: 131072 tokens in total
+    split data-parallel (131072 / N per rank), the 64 experts split
+    expert-parallel (64 / N per rank, 8 per GPU at N = 8). One step per rank =
+    hash route -> stable permutation -> NCCL all-to-all of the rows to their
+    experts' owners (exact per-owner counts) -> grouped expert MLP of the
+    owner's experts -> all-to-all back -> combine (sum / k). Before timing,
+    every rank checks its step's output bit for bit against the grouped MLP
+    of all 64 experts on one GPU (each rank also draws the full expert set,
+    805 MB, for that check). Timed with CUDA events over K steps between
+    barriers, max over ranks; the job's rate counts every rank's pairs."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from koemi_5hom_b200 import _native
+    from koemi_5hom_b200.cuda_kernels import _ops
+    from koemi_5hom_b200.model.expert_parallel import ExpertShard, expert_parallel_mlp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    _native.ensure_device(device)
+    total_tokens = args.op_tokens or 131072
+    if total_tokens % world or 64 % world:
+        raise SystemExit(f"{total_tokens} tokens / 64 experts do not split over {world} ranks")
+    tokens, d, h, e, k = total_tokens // world, 1024, 2048, 64, 2
+    shard = ExpertShard.from_group(e) if world > 1 else None
+    first, held = (shard.first, shard.local_count) if shard is not None else (0, e)
+
+    def expert_tensors(lo: int, hi: int) -> tuple:
+        """Experts [lo, hi) in grouped-MLP order, each drawn from its own seed
+        (a shard holds exactly the rows of the full set)."""
+        shapes = ((h, d), (h,), (h, d), (h,), (d, h), (d,))
+        out = [torch.empty(hi - lo, *shape, dtype=torch.bfloat16, device=device) for shape in shapes]
+        for j, expert in enumerate(range(lo, hi)):
+            g = torch.Generator(device=device).manual_seed(4000 + expert)
+            for tensor, scale in zip(out, (0.02, 0.002, 0.02, 0.002, 0.02, 0.002)):
+                tensor[j].copy_(torch.randn(tensor.shape[1:], generator=g, device=device) * scale)
+        return tuple(out)
+
+    weights = expert_tensors(first, first + held)
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    x = torch.randn(tokens, d, device=device, generator=g).bfloat16()
+    ids = torch.randint(0, 256, (tokens,), device=device, generator=g)
+    prev = torch.randint(0, 256, (tokens,), device=device, generator=g)
+    valid = torch.ones(tokens, dtype=torch.bool, device=device)
+
+    def step(expert_set=weights, sharded=shard):
+        assignments = _ops.route_topk(ids, prev, valid, e, k)
+        sc, rows, se, offsets, _ = _ops.permute_topk(x, assignments, valid, e, True)
+        if sharded is not None:
+            y = expert_parallel_mlp(sharded, sc, se, offsets, expert_set, mode="exact")
+        else:
+            y = _ops.grouped_expert_mlp(sc, se, offsets, *expert_set)
+        return _ops.combine_topk(y, rows, offsets, tokens, k)
+
+    full = expert_tensors(0, e)
+    expected = step(full, None)
+    got = step()
+    exact = bool(torch.equal(got, expected))
+    del full, expected, got
+    torch.cuda.empty_cache()
+    for _ in range(max(args.warmup, 1)):
+        step()
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    seconds = start.elapsed_time(stop) / 1000.0 / args.steps
+    flags = torch.tensor([seconds, 0.0 if exact else 1.0], device=device)
+    if world > 1:
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    seconds, mismatch = float(flags[0]), bool(flags[1] > 0)
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    peak = peaks.get("bf16_tflops_sustained", 1409.6)
+    pairs_total = total_tokens * k
+    job_tflops = pairs_total * 6 * d * h / seconds / 1e12
+    line = {"op": "moe_ep", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "shape": f"config 4: {total_tokens} tokens x d={d} bf16, hash top-2 over {e} experts (d_ff {h}); "
+                     f"{tokens} tokens and {held} experts per GPU",
+            "parallelism": f"dp{world}+ep{world}" if world > 1 else "dp1",
+            "exchange": "NCCL all_to_all_single, exact per-owner counts" if world > 1 else "none",
+            "us_per_step": seconds * 1e6, "pairs_total": pairs_total, "job_tflops": job_tflops,
+            "parity": "bit-exact with the single-GPU grouped MLP of all experts on every rank's tokens"
+                      if not mismatch else "MISMATCH against the single-GPU grouped MLP",
+            "roofline": {"bound": "tensor", "achieved": job_tflops / world, "peak": peak, "unit": "TFLOP/s per GPU",
+                         "frac": job_tflops / world / peak,
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback",
+                         "work": "expert FLOPs only (6 d d_ff per pair); route, permutation, exchange and combine "
+                                 "are inside the timed step"}}
+    if rank == 0:
+        emit(line, args)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if mismatch:
+        raise SystemExit("expert-parallel MoE step differs from the single-GPU result")
+
+
 def main(argv=None) -> None:
     args = parse_args(argv)
+    if args.op == "moe_ep":
+        run_op_moe_parallel(args)
+        return
     if args.op is not None:
         run_op(args)
         return

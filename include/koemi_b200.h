@@ -133,12 +133,13 @@ KOEMI_API int koemi_dense_bounded_gates(const float *projections, const uint8_t 
  * a = lo + (hi - lo) sigmoid(pre_a), b = (1 - a) tanh(pre_c) (a = 1, b = 0 where
  * !valid); prior_out <- working (cast to prior_dtype, may be NULL);
  * working <- a * working + b; h_out[row * h_stride + f] <- the new working
- * (in prior_dtype, may be NULL).
+ * (in prior_dtype, may be NULL); h_copy[row * features + f] <- the same value
+ * again (may be NULL: the decode step's rows of the next head pass).
  * `projections` is [batch, 2*features] fp32 (pre_a | pre_c). Fuses
  * BoundedRecurrentState.gates (model/memory.py:22-26), the masks of
  * network.py:308-309 and the T == 1 affine scan (model/scan.py:17-30). */
 KOEMI_API int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
-                            void *prior_out, void *h_out, int64_t h_stride, int64_t batch,
+                            void *prior_out, void *h_out, int64_t h_stride, void *h_copy, int64_t batch,
                             int64_t features, float minimum_retention, float maximum_retention,
                             int prior_dtype, void *stream);
 
@@ -223,6 +224,37 @@ KOEMI_API int koemi_think_causal_surprise_forward(const void *prior, const void 
                                         void *out, float *nll_out, int64_t rows, int64_t width,
                                         int64_t content_vocab, int dtype, int out_dtype,
                                         void *workspace, size_t workspace_bytes, void *stream);
+
+/* Merged head pass of a decode step (one read of the head for two uses):
+ * rows [lse_rows + logit_rows, width] (bf16/f16, contiguous) against the full
+ * head W [vocab, width] + bias [vocab] on tcgen05 tensor cores.
+ *  - rows [0, lse_rows) (the working state of every block after this step,
+ *    i.e. the next step's surprise priors): per 256-wide vocabulary slice a
+ *    (max, sum exp, -inf) triple of the fp32 logits with column pad_id left
+ *    out, into partials [slices][lse_rows][3] (slices =
+ *    koemi_think_head_pass_slices(vocab)); the target is not known yet.
+ *  - rows [lse_rows, lse_rows + logit_rows) (the final contexts): fp32 logits
+ *    [logit_rows, vocab] = row W^T + bias, every column.
+ * Replaces the separate content-head surprise pass of the next step and this
+ * step's logits head (calculate_surprise and predict_tokens,
+ * model/network.py:677-701). */
+KOEMI_API int64_t koemi_think_head_pass_slices(int64_t vocab);
+KOEMI_API int koemi_think_head_pass(const void *rows, int64_t lse_rows, int64_t logit_rows, int64_t width,
+                                    const void *head_weight, const void *head_bias, int64_t vocab, int64_t pad_id,
+                                    float *partials, float *logits, int dtype, void *stream);
+
+/* Surprise of the head pass's rows once their targets are known (the next
+ * step's tokens): row r (block-major, stream r % batch) gets
+ * NLL = logsumexp(partials) - (prior_r . W[token] + b[token]) and
+ * s = 1 - exp(-NLL / ln C), C = vocab - 1 (PAD excluded), 0 where !valid.
+ * Tokens must lie in [0, vocab) (the sampler's output). fp32 surprise [rows].
+ * Same value as causal_surprise (think/surprise.py:91-128) up to the fp32
+ * summation order. */
+KOEMI_API int koemi_think_surprise_from_partials(const void *prior, const void *head_weight, const void *head_bias,
+                                                 const int64_t *token_ids, const uint8_t *valid,
+                                                 const float *partials, int64_t slices, int64_t rows, int64_t batch,
+                                                 int64_t width, int64_t vocab, int64_t pad_id, int dtype,
+                                                 float *surprise, void *stream);
 
 /* Salient admission and ring compaction (network.py:349 and
  * LocalKeyValueMemory.salient_tail, model/memory.py:431-455): admits

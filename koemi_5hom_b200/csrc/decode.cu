@@ -31,7 +31,8 @@ namespace {
 template <typename TP>
 __global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t *__restrict__ valid,
                                     float *__restrict__ working, TP *__restrict__ prior, TP *__restrict__ h_out,
-                                    int64_t h_stride, int64_t batch, int64_t features, float lo, float hi) {
+                                    int64_t h_stride, TP *__restrict__ h_copy, int64_t batch, int64_t features,
+                                    float lo, float hi) {
     pdl_trigger();
     pdl_wait();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -49,6 +50,7 @@ __global__ void decode_gates_kernel(const float *__restrict__ pre, const uint8_t
     const float h = a * previous + b;
     working[i] = h;
     if (h_out != nullptr) h_out[row * h_stride + f] = from_acc<TP>(h);
+    if (h_copy != nullptr) h_copy[i] = from_acc<TP>(h);
 }
 
 // ---------------------------------------------------------------- rings
@@ -966,7 +968,7 @@ __global__ __launch_bounds__(kAssocThreads, 2) void assoc_decode_prefetch_kernel
 using namespace koemi;
 
 extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *valid, float *working,
-                                       void *prior_out, void *h_out, int64_t h_stride, int64_t batch,
+                                       void *prior_out, void *h_out, int64_t h_stride, void *h_copy, int64_t batch,
                                        int64_t features, float minimum_retention, float maximum_retention,
                                        int prior_dtype, void *stream) {
     clear_error();
@@ -976,9 +978,9 @@ extern "C" int koemi_dense_decode_step(const float *projections, const uint8_t *
     const unsigned blocks = static_cast<unsigned>(ceil_div(total, 256));
     cudaStream_t s = as_stream(stream);
     switch (prior_dtype) {
-        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<float *>(prior_out), static_cast<float *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
-        case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), static_cast<__nv_bfloat16 *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
-        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__half *>(prior_out), static_cast<__half *>(h_out), h_stride, batch, features, minimum_retention, maximum_retention)); break;
+        case KOEMI_F32: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<float>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<float *>(prior_out), static_cast<float *>(h_out), h_stride, static_cast<float *>(h_copy), batch, features, minimum_retention, maximum_retention)); break;
+        case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__nv_bfloat16 *>(prior_out), static_cast<__nv_bfloat16 *>(h_out), h_stride, static_cast<__nv_bfloat16 *>(h_copy), batch, features, minimum_retention, maximum_retention)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(decode_gates_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), projections, valid, working, static_cast<__half *>(prior_out), static_cast<__half *>(h_out), h_stride, static_cast<__half *>(h_copy), batch, features, minimum_retention, maximum_retention)); break;
         default: return fail(KOEMI_ERR_INVALID, "prior dtype must be f32, f16 or bf16");
     }
     KOEMI_LAUNCH_CHECK();

@@ -12,7 +12,7 @@
 // 16-bit inputs take the tcgen05 path of umma.cu when the shape allows it.
 #include <cmath>
 
-#include "common.cuh"
+#include "vec.cuh"
 
 namespace koemi {
 
@@ -150,6 +150,70 @@ __global__ void surprise_finish_kernel(const float *__restrict__ partials, int64
         const float nll = logf(total) + m - target;
         out[row] = from_acc<TO>(ok ? 1.0f - expf(-nll / log_vocab) : 0.0f);
         if (nll_out != nullptr) nll_out[row] = ok ? nll : 0.0f;
+    }
+}
+
+// Surprise of the rows of a merged head pass, whose log-sum-exp partials were
+// folded without a target (the target was not known yet): one warp per row
+// computes the target logit prior . W[token] + b[token] in fp32 (16-byte
+// loads of the bf16/f16 prior row and head row), merges the row's (max, sum)
+// partials over the slices, and writes s = 1 - exp(-NLL / ln C); 0 where the
+// row's token is invalid. Row r belongs to stream r % batch (rows are
+// block-major: [block][stream]).
+template <typename T>
+__global__ void surprise_from_partials_kernel(const T *__restrict__ prior, const T *__restrict__ weight,
+                                              const T *__restrict__ bias, const int64_t *__restrict__ tokens,
+                                              const uint8_t *__restrict__ valid, const float *__restrict__ partials,
+                                              int64_t slices, int64_t rows, int64_t batch, int64_t width,
+                                              float log_vocab, float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int64_t stream = row % batch;
+    const bool ok = valid == nullptr || valid[stream] != 0;
+    if (!ok) {
+        if (lane == 0) out[row] = 0.0f;
+        return;
+    }
+    const int64_t token = tokens[stream];
+    constexpr int W = Pack<T>::kWidth;
+    const T *p = prior + row * width;
+    const T *w = weight + token * width;
+    float dot = 0.0f;
+    for (int64_t c = static_cast<int64_t>(lane) * W; c < width; c += 32 * W) {
+        float a[8], b[8];
+        unpack(load_cached(p + c), a, T());
+        unpack(load_cached(w + c), b, T());
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot = fmaf(a[e], b[e], dot);
+    }
+    dot = warp_sum(dot);
+    const float target = dot + to_acc(bias[token]);
+    float m = -INFINITY, total = 0.0f;
+    for (int64_t s = lane; s < slices; s += 32) {
+        const float *q = partials + (s * rows + row) * 3;
+        const float pm = q[0];
+        if (pm != -INFINITY) {
+            const float nm = fmaxf(m, pm);
+            total = total * expf(m - nm) + q[1] * expf(pm - nm);
+            m = nm;
+        }
+    }
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, offset);
+        const float ot = __shfl_xor_sync(0xffffffffu, total, offset);
+        const float nm = fmaxf(m, om);
+        if (nm != -INFINITY) {
+            total = (m == -INFINITY ? 0.0f : total * expf(m - nm)) + (om == -INFINITY ? 0.0f : ot * expf(om - nm));
+        }
+        m = nm;
+    }
+    if (lane == 0) {
+        const float nll = logf(total) + m - target;
+        out[row] = 1.0f - expf(-nll / log_vocab);
     }
 }
 
@@ -344,6 +408,35 @@ extern "C" int koemi_think_salient_admission(const float *carried_keys, const fl
     salient_admission_kernel<<<static_cast<unsigned>(batch), 256, smem, as_stream(stream)>>>(
         carried_keys, carried_values, carried_valid, keys, values, surprise, valid, threshold, out_keys,
         out_values, out_valid, admission_out, carried, length, width, capacity);
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_think_surprise_from_partials(const void *prior, const void *head_weight, const void *head_bias,
+                                                  const int64_t *token_ids, const uint8_t *valid,
+                                                  const float *partials, int64_t slices, int64_t rows, int64_t batch,
+                                                  int64_t width, int64_t vocab, int64_t pad_id, int dtype,
+                                                  float *surprise, void *stream) {
+    clear_error();
+    if (rows < 0 || batch < 1 || width < 1 || vocab < 2 || slices < 1) return fail(KOEMI_ERR_INVALID, "bad surprise sizes");
+    if (rows == 0) return KOEMI_OK;
+    if (rows % batch != 0) return fail(KOEMI_ERR_INVALID, "rows must be a whole number of batches");
+    if (width % 8 != 0 || !aligned(prior, 16) || !aligned(head_weight, 16)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "width must be a multiple of 8 with 16-byte aligned prior and head");
+    }
+    if (head_bias == nullptr || token_ids == nullptr || partials == nullptr || surprise == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "head_bias, token_ids, partials and surprise must be non-NULL");
+    }
+    // the content vocabulary is the head without its PAD column
+    const int64_t content = pad_id >= 0 && pad_id < vocab ? vocab - 1 : vocab;
+    const float log_vocab = std::log(static_cast<float>(content));
+    const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
+    cudaStream_t s = as_stream(stream);
+    switch (dtype) {
+        case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(surprise_from_partials_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const __nv_bfloat16 *>(prior), static_cast<const __nv_bfloat16 *>(head_weight), static_cast<const __nv_bfloat16 *>(head_bias), token_ids, valid, partials, slices, rows, batch, width, log_vocab, surprise)); break;
+        case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(surprise_from_partials_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const __half *>(prior), static_cast<const __half *>(head_weight), static_cast<const __half *>(head_bias), token_ids, valid, partials, slices, rows, batch, width, log_vocab, surprise)); break;
+        default: return fail(KOEMI_ERR_INVALID, "the head-pass surprise takes bf16 or f16 rows");
+    }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }

@@ -97,7 +97,9 @@ struct UmmaArgs {
     const void *bias1;
     void *out;
     float *partials;
-    const int64_t *targets;
+    const int64_t *targets;   // surprise: target column per row, or NULL (no target logit)
+    int64_t lse_rows;         // surprise: rows below fold into partials; rows at or above write logits to out
+    int64_t pad_column;       // surprise: column left out of the log-sum-exp (-1: none)
     int *status;
     uint32_t idesc;
 };
@@ -547,8 +549,14 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                     }
                 }
             } else {
+                // rows below lse_rows fold into per-slice log-sum-exp
+                // partials; rows at or above (the head pass's logits rows)
+                // store acc + bias for every column (PAD included). The TMEM
+                // loads stay outside the row-dependent branches: tcgen05.ld
+                // is warp-aligned and a warp may hold both kinds of row.
                 const T *bias = static_cast<const T *>(args.bias0);
-                const int64_t target = row_ok ? args.targets[row] : -1;
+                const bool logit_row = row >= args.lse_rows;
+                const int64_t target = row_ok && !logit_row && args.targets != nullptr ? args.targets[row] : -1;
                 float run_max = -INFINITY, run_sum = 0.0f, target_logit = -INFINITY;
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) {
@@ -556,12 +564,32 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                     KOEMI_TMEM_LD32(taddr + c * 32, y);
                     tmem_wait_ld();
                     const int64_t col0 = tile.n * kBN + c * 32;
+                    if (logit_row) {
+                        if (row_ok && col0 < args.n_out) {
+                            float o[32];
+                            load_bias32(bias, col0, args.n_out, o);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(y[j]);
+                            float *dst = static_cast<float *>(args.out) + (row - args.lse_rows) * args.out_stride + col0;
+                            if (col0 + 32 <= args.n_out && aligned16(dst)) {
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    reinterpret_cast<float4 *>(dst)[q] =
+                                        make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                                }
+                            } else {
+                                for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = o[j];
+                            }
+                        }
+                        continue;
+                    }
                     float l[32];
                     float chunk_max = -INFINITY;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int64_t col = col0 + j;
-                        l[j] = col < args.n_out ? __uint_as_float(y[j]) + to_acc(bias[col]) : -INFINITY;
+                        l[j] = col < args.n_out && col != args.pad_column ? __uint_as_float(y[j]) + to_acc(bias[col])
+                                                                          : -INFINITY;
                         chunk_max = fmaxf(chunk_max, l[j]);
                     }
                     if (target >= col0 && target < col0 + 32) {
@@ -579,8 +607,8 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         run_sum = s;
                     }
                 }
-                if (row_ok) {
-                    float *p = args.partials + (tile.n * args.rows + row) * 3;
+                if (row_ok && !logit_row) {
+                    float *p = args.partials + (tile.n * args.lse_rows + row) * 3;
                     p[0] = run_max;
                     p[1] = run_sum;
                     p[2] = target_logit;
@@ -925,6 +953,8 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
     a.bias0 = bias;
     a.partials = partials;
     a.targets = targets;
+    a.lse_rows = rows;
+    a.pad_column = -1;
     a.status = device_status_word();
     a.idesc = make_idesc(dtype);
     const bool pair = surprise_tile_rows(rows) > kBM;
@@ -936,9 +966,58 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
     return KOEMI_OK;
 }
 
+int head_pass_umma(const void *rows_in, int64_t lse_rows, int64_t logit_rows, int64_t width, const void *weight,
+                   const void *bias, int64_t vocab, int64_t pad_id, float *partials, float *logits, int dtype,
+                   cudaStream_t stream) {
+    const int64_t rows = lse_rows + logit_rows;
+    UmmaArgs a{};
+    int rc = encode_kmajor(&a.map_a, dtype, rows_in, rows, width, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&a.map_b0, dtype, weight, vocab, width, kBN);
+    if (rc != KOEMI_OK) return rc;
+    const int64_t slices = (vocab + kBN - 1) / kBN;
+    a.k = width;
+    a.rows = rows;
+    a.n_tiles = slices;
+    a.n_out = vocab;
+    a.out_stride = vocab;
+    a.experts = 1;
+    a.bias0 = bias;
+    a.out = logits;
+    a.partials = partials;
+    a.targets = nullptr;
+    a.lse_rows = lse_rows;
+    a.pad_column = pad_id;
+    a.status = device_status_word();
+    a.idesc = make_idesc(dtype);
+    a.band = 16;
+    const bool pair = surprise_tile_rows(rows) > kBM;
+    const int64_t tiles = ((rows + surprise_tile_rows(rows) - 1) / surprise_tile_rows(rows)) * slices;
+    return pair ? launch<kSurprise, true>(a, dtype, tiles, stream) : launch<kSurprise, false>(a, dtype, tiles, stream);
+}
+
 }  // namespace koemi
 
 using namespace koemi;
+
+extern "C" int64_t koemi_think_head_pass_slices(int64_t vocab) { return vocab < 1 ? 0 : (vocab + kBN - 1) / kBN; }
+
+extern "C" int koemi_think_head_pass(const void *rows, int64_t lse_rows, int64_t logit_rows, int64_t width,
+                                     const void *head_weight, const void *head_bias, int64_t vocab, int64_t pad_id,
+                                     float *partials, float *logits, int dtype, void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "the head pass takes bf16 or f16 operands");
+    if (lse_rows < 0 || logit_rows < 0 || width < 1 || vocab < 2) return fail(KOEMI_ERR_INVALID, "bad head pass sizes");
+    if (lse_rows + logit_rows == 0) return KOEMI_OK;
+    if (width % 8 != 0 || !aligned(rows, 16) || !aligned(head_weight, 16) || head_bias == nullptr ||
+        lse_rows + logit_rows >= (int64_t(1) << 31) || vocab >= (int64_t(1) << 31)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the head pass needs width a multiple of 8, 16-byte aligned rows and head, and a bias");
+    }
+    if ((lse_rows > 0 && partials == nullptr) || (logit_rows > 0 && logits == nullptr)) {
+        return fail(KOEMI_ERR_INVALID, "partials (surprise rows) and logits (logit rows) must be non-NULL");
+    }
+    return head_pass_umma(rows, lse_rows, logit_rows, width, head_weight, head_bias, vocab, pad_id, partials, logits,
+                          dtype, as_stream(stream));
+}
 
 namespace {
 struct DensePlan {

@@ -12,15 +12,20 @@ tensor of the state at a fixed address and updates it in place:
 A step is then: the hash route and its stable permutation once (the route
 depends only on the ids); the surprise of every block at once -- block l
 scores the token against the shared head from its working state before the
-update, which is known for all blocks when the step starts, so one tcgen05
-head GEMM + online LSE over [blocks x streams] rows reads the head once per
-step instead of once per block; per block, rms_norm -> gate GEMM ->
-``koemi_dense_decode_step`` -> one local|assoc GEMM ->
+update, which is known for all blocks when the previous step ends. For 16-bit
+models the previous step's head pass already folded the log-sum-exp of those
+rows (the merged head pass: one tcgen05 read of the head per step gives this
+step's logits and the next step's surprise partials), so only the target
+logits remain; otherwise one tcgen05 head GEMM + online LSE over [blocks x
+streams] rows reads the head once per step instead of once per block; per
+block, rms_norm -> gate GEMM -> ``koemi_dense_decode_step`` -> one
+local|assoc GEMM ->
 ``koemi_think_ring_decode_step`` -> ``koemi_assoc_decode_step`` (with the
 feature projection of key and query fused in) -> fusion GEMM
 (its input rows are written in place by the three kernels) -> rms_norm ->
 row gather through the shared permutation -> grouped expert MLP -> combine,
-which also writes the next block's normalised input; then the head GEMM. With fixed
+which also writes the next block's normalised input; then the head pass (or
+the logits GEMM). With fixed
 addresses the whole step is one CUDA graph with no copy-back of the state.
 
 ``to_koemi_state`` restores the reference layout (rings oldest first, salient
@@ -66,6 +71,13 @@ class DecodeState:
     last_token_ids: Tensor  # int64 [B]
     step_index: int
     layered: bool
+    # merged head pass (16-bit models): rows [blocks * B + B, d] in the compute
+    # dtype -- every block's working state (the next step's surprise priors)
+    # then the final contexts -- and the log-sum-exp partials
+    # [slices, blocks * B, 3] of the prior rows, written at the end of a step
+    # and read at the start of the next one
+    head_rows: Tensor | None = None
+    head_partials: Tensor | None = None
 
     @property
     def ring_dtype(self) -> torch.dtype:
@@ -75,7 +87,9 @@ class DecodeState:
         """A deep copy at new addresses (same ring layout and dtype)."""
         blocks = [DecodeBlockState(**{f: getattr(b, f).clone() for f in DecodeBlockState.__dataclass_fields__})
                   for b in self.blocks]
-        return DecodeState(blocks, self.local_head.clone(), self.last_token_ids.clone(), self.step_index, self.layered)
+        copy = lambda t: None if t is None else t.clone()  # noqa: E731
+        return DecodeState(blocks, self.local_head.clone(), self.last_token_ids.clone(), self.step_index, self.layered,
+                           copy(self.head_rows), copy(self.head_partials))
 
 
 def supports_decode_path(settings) -> bool:
@@ -163,6 +177,37 @@ def to_koemi_state(dstate: DecodeState):
     return layers[0]
 
 
+def supports_head_pass(model) -> bool:
+    """The merged head pass runs on the tcgen05 path: 16-bit weights, a
+    surprise to score, and a width of whole 16-byte packets."""
+    s = model.settings
+    return (model.compute_dtype in (torch.bfloat16, torch.float16) and s.ablation != "no_surprise"
+            and s.embedding_size % 8 == 0)
+
+
+def attach_head_pass(model, dstate: DecodeState) -> None:
+    """Give ``dstate`` the buffers of the merged head pass and fold the
+    log-sum-exp partials of its current priors (every block's working state),
+    which the next decode step reads. Call again whenever the working states
+    were replaced (a new or adopted state); a no-op for models without the
+    merged pass."""
+    if not supports_head_pass(model):
+        dstate.head_rows = dstate.head_partials = None
+        return
+    s = model.settings
+    blocks, batch, d = len(dstate.blocks), dstate.last_token_ids.shape[0], s.embedding_size
+    device = dstate.last_token_ids.device
+    lib = _native.library()
+    slices = lib.koemi_think_head_pass_slices(s.vocabulary_size)
+    rows = torch.zeros((blocks + 1) * batch, d, dtype=model.compute_dtype, device=device)
+    rows[:blocks * batch].view(blocks, batch, d).copy_(torch.stack([st.working for st in dstate.blocks]))
+    partials = torch.empty(slices, blocks * batch, 3, dtype=torch.float32, device=device)
+    _native.call("koemi_think_head_pass", _native.ptr(rows), blocks * batch, 0, d, _native.ptr(model.head_weight),
+                 _native.ptr(model.head_bias), s.vocabulary_size, PAD_TOKEN_ID, _native.ptr(partials), None,
+                 _native.dtype_code(model.compute_dtype), torch.cuda.current_stream(device).cuda_stream)
+    dstate.head_rows, dstate.head_partials = rows, partials
+
+
 def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     """Advance every stream by one token in place; return fp32 logits [B, V]."""
     s = model.settings
@@ -180,7 +225,9 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     concat_dtype = model.compute_dtype
     out_code = _native.dtype_code(concat_dtype)
     ring_code = _native.dtype_code(dstate.ring_dtype)
-    if s.ablation == "no_surprise":
+    scoring = s.ablation != "no_surprise"
+    merged = scoring and dstate.head_rows is not None
+    if not scoring or merged:
         targets = None
     else:
         targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
@@ -193,12 +240,18 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             x, assignments, valid, s.expert_count, False)
         weights = None
     # surprise of every block from its prior (the working state before this
-    # step's update), one pass over the content head for the whole stack;
-    # each row's result is independent of the others, so this equals the
-    # per-block computation bit for bit
+    # step's update). With the merged head pass its log-sum-exp partials were
+    # folded by the previous step's head read; only the target logits remain.
+    # Otherwise one pass over the content head for the whole stack. Each
+    # row's result is independent of the others.
     all_surprise = None
-    if targets is not None:
-        count = len(model.blocks)
+    count = len(model.blocks)
+    if merged:
+        all_surprise = torch.empty(count, batch, dtype=torch.float32, device=device)
+        call("koemi_think_surprise_from_partials", ptr(dstate.head_rows), ptr(model.head_weight),
+             ptr(model.head_bias), ptr(ids), ptr(valid), ptr(dstate.head_partials), dstate.head_partials.shape[0],
+             count * batch, batch, d, s.vocabulary_size, PAD_TOKEN_ID, prior_dtype, ptr(all_surprise), stream)
+    elif targets is not None:
         priors = torch.stack([st.working for st in dstate.blocks]).to(model.compute_dtype)
         all_surprise = _ops.causal_surprise_forward(
             priors.view(count * batch, d), cache["content_w"], cache["content_b"], targets.repeat(count),
@@ -214,8 +267,10 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         pre = model._linear(u, block.gates_weight, block.gates_bias)
         # fusion input rows, written in place by the step kernels: h | memory | local | salient
         concat = torch.empty(batch, 4 * d, dtype=concat_dtype, device=device)
+        # the new working state is also the next step's prior row of the head pass
+        next_prior = ptr(dstate.head_rows[index * batch:(index + 1) * batch]) if merged else None
         call("koemi_dense_decode_step", ptr(pre), ptr(valid), ptr(st.working), None, ptr(concat), 4 * d,
-             batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
+             next_prior, batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
         h = concat[:, :d]
         surprise = None if all_surprise is None else all_surprise[index]
         if batch <= 128:  # one row tile: a single wider GEMM fills the GPU better than two
@@ -262,7 +317,16 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         else:
             x = _ops.combine_residual_rmsnorm(context, expert_out, positions, offsets, weights, valid,
                                               bc["expert_norm"], s.expert_top_k, NORM_EPSILON)
-    logits = model._linear(x, model.head_weight, model.head_bias)
+    if merged:
+        # one read of the head: this step's logits and the next step's
+        # surprise partials of every block's new working state
+        dstate.head_rows[count * batch:].copy_(x)
+        logits = torch.empty(batch, s.vocabulary_size, dtype=torch.float32, device=device)
+        call("koemi_think_head_pass", ptr(dstate.head_rows), count * batch, batch, d, ptr(model.head_weight),
+             ptr(model.head_bias), s.vocabulary_size, PAD_TOKEN_ID, ptr(dstate.head_partials), ptr(logits),
+             prior_dtype, stream)
+    else:
+        logits = model._linear(x, model.head_weight, model.head_bias)
     dstate.last_token_ids.copy_(torch.where(valid, ids, dstate.last_token_ids))
     dstate.local_head.add_(1).remainder_(dstate.blocks[0].local_keys.shape[1])
     return logits

@@ -21,8 +21,8 @@ import torch
 from torch import Tensor
 
 from koemi_5hom_b200.cuda_kernels import _ops
-from koemi_5hom_b200.model.decode import (RING_DTYPES, decode_step, from_koemi_state, supports_decode_path,
-                                           to_koemi_state)
+from koemi_5hom_b200.model.decode import (RING_DTYPES, attach_head_pass, decode_step, from_koemi_state,
+                                           supports_decode_path, to_koemi_state)
 from koemi_5hom_b200.model.settings import PAD_TOKEN_ID
 from koemi_5hom_b200.model.state import KOEMI_STATE_FIELDS, KoemiState, LayeredKoemiState
 
@@ -167,6 +167,7 @@ class BatchDecoder:
         static = to_static_state(state, s.local_memory_size, s.salience_memory_size)
         if self._in_place:
             self._dstate = from_koemi_state(static, s.local_memory_size, s.salience_memory_size, self._ring_dtype)
+            attach_head_pass(self.model, self._dstate)
             self._state = None
         else:
             self._state = static

@@ -186,7 +186,18 @@ CASES = {
     "c5_small": dict(settings=dict(vocabulary_size=1024, embedding_size=128, memory_features=16,
                                    local_memory_size=48, salience_memory_size=40, expert_count=16,
                                    expert_top_k=2, salience_threshold=0.6, scan_chunk=64),
-                     batch=3, length=150, decode=32, seed=11, init="normal", pad_rows=1, bf16=True),
+                     batch=3, length=150, decode=64, seed=11, init="normal", pad_rows=1, bf16=True),
+    # config 5 at full width for one block: vocabulary 32768 (hybrid), d=2048,
+    # 16 features, 128 + 128 slots, 64 experts top-2 (d_ff 4096), bf16-rounded
+    # N(0, 0.02) weights, the bench's fixed threshold 0.64; two streams with a
+    # short prompt (the reference's static dispatch gathers 100 MB of fp32
+    # expert weights per token-expert pair). Rings are not stored (8 MB);
+    # the admitted positions are, through the surprise values.
+    "c5_width": dict(settings=dict(vocabulary_size=32768, embedding_size=2048, memory_features=16,
+                                   local_memory_size=128, salience_memory_size=128, expert_count=64,
+                                   expert_top_k=2, salience_threshold=0.64, scan_chunk=128),
+                     batch=2, length=40, decode=64, seed=21, init="normal", pad_rows=0, bf16=True,
+                     compact=True),
 }
 
 
@@ -212,17 +223,27 @@ def herm_fixture(case: dict) -> dict:
         decoder = BatchDecoder(model, cache_expert_weights=True)
         sampler = TokenSampler(SamplingPolicy(greedy=True), torch.device("cpu"))
         logits = decoder.prefill(ids)
-        tokens, step_logits = [], []
+        tokens, step_logits, top_values, top_ids = [], [], [], []
         for step in range(case["decode"]):
             nxt = sampler(logits)
             tokens.append(nxt)
             if step < 4:
                 step_logits.append(logits.clone())
+            # every step: the eight best content logits (PAD masked) and their ids
+            scores = logits.clone()
+            scores[:, PAD] = float("-inf")
+            best = scores.topk(8, dim=-1)
+            top_values.append(best.values)
+            top_ids.append(best.indices)
             logits = decoder.step(nxt)
         final_state = decoder.state
     state = {name: getattr(output.state, name) for name in output.state.__dataclass_fields__ if name != "step_index"}
     decode_state = {name: getattr(final_state, name) for name in final_state.__dataclass_fields__
                     if name != "step_index"}
+    if case.get("compact"):  # small state fields only; rings and bases summarised
+        small = ("working_state", "memory_normalizer", "local_valid", "salient_valid", "last_token_ids")
+        state = {name: value for name, value in state.items() if name in small}
+        decode_state = {name: value for name, value in decode_state.items() if name in small}
     return {
         "case": {k: v for k, v in case.items()},
         "ids": ids,
@@ -234,6 +255,8 @@ def herm_fixture(case: dict) -> dict:
         "state": state,
         "decode_tokens": torch.cat(tokens, dim=1),
         "decode_logits": torch.stack(step_logits, dim=1),
+        "decode_top_values": torch.stack(top_values, dim=1),
+        "decode_top_ids": torch.stack(top_ids, dim=1),
         "decode_state": decode_state,
     }
 
@@ -249,9 +272,15 @@ def _compact(value):
 
 
 def main() -> None:
+    """``make_golden.py [case ...]`` regenerates the named herm cases only
+    (``ops`` names the per-operator fixture); no argument regenerates all."""
+    wanted = set(sys.argv[1:]) or {"ops", *CASES}
     torch.manual_seed(0)
-    torch.save(_compact(ops_fixture()), HERE / "ops.pt")
+    if "ops" in wanted:
+        torch.save(_compact(ops_fixture()), HERE / "ops.pt")
     for name, case in CASES.items():
+        if name not in wanted:
+            continue
         fixture = herm_fixture(case)
         # keep the fixture small: logits at every 8th position, the window
         # edges and the last position

@@ -138,3 +138,46 @@ def test_surprise_tensor_core_decode_shape(cuda):
     pick = [0, 1, 127, 128, 200, 255]
     expected = ops.causal_surprise(prior[:, pick], weight, bias, targets[:, pick], valid[:, pick])
     torch.testing.assert_close(got[:, pick].cpu().double(), expected.bfloat16().double(), rtol=1.6e-2, atol=4e-3)
+
+
+@pytest.mark.parametrize("blocks,batch,width,vocab,dtype", [(3, 100, 256, 1000, torch.bfloat16),
+                                                            (2, 37, 128, 300, torch.float16),
+                                                            (24, 32, 2048, 32768, torch.bfloat16)])
+def test_merged_head_pass_gives_logits_and_next_surprise(blocks, batch, width, vocab, dtype, cuda):
+    """The decode step's merged head pass against the oracle: the logits rows
+    equal row W^T + b over the full head, and the surprise finished from the
+    prior rows' partials once the tokens are known equals causal_surprise over
+    the content head (PAD column removed, targets remapped). Row counts that
+    are not multiples of 32 put prior rows and logits rows in one warp."""
+    from koemi_5hom_b200 import _native
+    pad = 256
+    g = torch.Generator().manual_seed(vocab + batch)
+    lse_rows = blocks * batch
+    rows = torch.randn(lse_rows + batch, width, generator=g).to(dtype)
+    weight = (torch.randn(vocab, width, generator=g) * width ** -0.5).to(dtype)
+    bias = (torch.randn(vocab, generator=g) * 0.1).to(dtype)
+    tokens = torch.randint(0, vocab, (batch,), generator=g)
+    tokens[::7] = pad  # invalid streams score 0
+    valid = tokens != pad
+    d_rows, d_w, d_b = rows.to(cuda), weight.to(cuda), bias.to(cuda)
+    lib = _native.library()
+    slices = lib.koemi_think_head_pass_slices(vocab)
+    partials = torch.empty(slices, lse_rows, 3, device=cuda)
+    logits = torch.empty(batch, vocab, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    code = _native.dtype_code(dtype)
+    _native.call("koemi_think_head_pass", d_rows.data_ptr(), lse_rows, batch, width, d_w.data_ptr(), d_b.data_ptr(),
+                 vocab, pad, partials.data_ptr(), logits.data_ptr(), code, stream)
+    surprise = torch.empty(lse_rows, device=cuda)
+    d_tokens, d_valid = tokens.to(cuda), valid.to(cuda)
+    _native.call("koemi_think_surprise_from_partials", d_rows.data_ptr(), d_w.data_ptr(), d_b.data_ptr(),
+                 d_tokens.data_ptr(), d_valid.data_ptr(), partials.data_ptr(), slices, lse_rows, batch, width, vocab,
+                 pad, code, surprise.data_ptr(), stream)
+    torch.cuda.synchronize()
+    expected_logits = rows[lse_rows:].double() @ weight.double().T + bias.double()
+    torch.testing.assert_close(logits.cpu().double(), expected_logits, rtol=1e-5, atol=1e-4)
+    keep = [i for i in range(vocab) if i != pad]
+    content = torch.where(tokens > pad, tokens - 1, tokens).repeat(blocks)
+    expected = ops.causal_surprise(rows[:lse_rows], weight[keep], bias[keep], content, valid.repeat(blocks))
+    torch.testing.assert_close(surprise.cpu().double(), expected, rtol=1e-5, atol=2e-6)
+    assert bool((surprise.cpu()[~valid.repeat(blocks)] == 0).all())
