@@ -87,6 +87,21 @@ KOEMI_API int koemi_device_init(int device);
 KOEMI_API int koemi_sampler_greedy(const float *logits, int64_t rows, int64_t vocab, int64_t row_stride,
                                    int64_t pad_id, int64_t *out, void *stream);
 
+/* Temperature sampling of one token per row from softmax(logits / T), PAD
+ * (pad_id) excluded, as a counter-based Gumbel-max: out[r] = argmax_v of
+ * logit_v / T - log(-log(u_v)), u_v drawn from (seed, stream_offset + r,
+ * *step, v) by SplitMix64 (the formula is in sampler.cu; the oracle restates
+ * it bit for bit), so each stream's draws are its own and reproducible.
+ * `step` is a device int64 the caller advances between calls (graph
+ * capturable). `thresholds` (fp32 [rows], may be NULL) drops logits below the
+ * row's value (the top-k filter of the reference). NaN logits are never
+ * chosen. Replaces TokenSampler's sampled path (runtime/fast_decode.py:72-80:
+ * softmax(scores / T) then torch.multinomial with a generator): the same
+ * distribution from a different random stream. */
+KOEMI_API int koemi_sampler_temperature(const float *logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                        int64_t pad_id, float temperature, uint64_t seed, int64_t stream_offset,
+                                        const int64_t *step, const float *thresholds, int64_t *out, void *stream);
+
 /* ------------------------------------------------------------ dense front */
 
 /* Affine recurrent scan h_t = a_t * h_{t-1} + b_t over [batch, length,

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_device_status": (_int, (_int, ctypes.POINTER(_int))),
     "koemi_device_init": (_int, (_int,)),
     "koemi_sampler_greedy": (_int, (_p, _i64, _i64, _i64, _i64, _p, _p)),
+    "koemi_sampler_temperature": (_int, (_p, _i64, _i64, _i64, _i64, _f, ctypes.c_uint64, _i64, _p, _p, _p, _p)),
     "koemi_assoc_window_scan_read": (_int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p)),
     "koemi_dense_affine_scan_workspace": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_dense_affine_scan_forward": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _int, _int, _p, _sz, _p)),

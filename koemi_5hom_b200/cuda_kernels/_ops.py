@@ -478,6 +478,21 @@ def greedy_tokens(logits: Tensor, pad_id: int) -> Tensor:
     return out
 
 
+def temperature_tokens(logits: Tensor, pad_id: int, temperature: float, seed: int, stream_offset: int,
+                       step: Tensor, thresholds: Tensor | None = None) -> Tensor:
+    """[rows, vocab] fp32 logits -> int64 [rows, 1] drawn from
+    softmax(logits / temperature) with column pad_id masked (and logits below
+    ``thresholds[row]`` dropped), by the native counter-based Gumbel-max
+    keyed by (seed, stream_offset + row, step[0], column)."""
+    (logits,) = _dense(logits)
+    stream = _prepare(logits)
+    rows, vocab = logits.shape
+    out = torch.empty(rows, 1, dtype=torch.int64, device=logits.device)
+    call("koemi_sampler_temperature", ptr(logits), rows, vocab, vocab, pad_id, float(temperature),
+         int(seed) & ((1 << 64) - 1), stream_offset, ptr(step), ptr(thresholds), ptr(out), stream)
+    return out
+
+
 @greedy_tokens.register_fake
 def _(logits, pad_id):
     return logits.new_empty(logits.shape[0], 1, dtype=torch.int64)

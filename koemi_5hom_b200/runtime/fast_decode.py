@@ -43,12 +43,24 @@ class SamplingPolicy:
 
 
 class TokenSampler:
-    """Select decode tokens on the device (no host reads)."""
+    """Select decode tokens on the device (no host reads).
 
-    def __init__(self, policy: SamplingPolicy, device: torch.device, generator: torch.Generator | None = None):
+    Greedy runs the native argmax. Temperature sampling follows the reference
+    (softmax + ``torch.multinomial`` with ``generator``) unless ``stream_seed``
+    is given: then one native pass per row draws from the same distribution
+    by counter-based Gumbel-max, seeded per stream (stream id
+    ``stream_offset + row``) and per call (a device step counter advanced
+    after every call, so the sampler can live inside a CUDA graph); a stream's
+    tokens then do not depend on the batch it is decoded in."""
+
+    def __init__(self, policy: SamplingPolicy, device: torch.device, generator: torch.Generator | None = None,
+                 *, stream_seed: int | None = None, stream_offset: int = 0):
         self.policy = policy
         self.generator = generator
         self._padding = torch.tensor([PAD_TOKEN_ID], dtype=torch.long, device=device)
+        self.stream_seed = stream_seed
+        self.stream_offset = stream_offset
+        self._step = torch.zeros(1, dtype=torch.int64, device=device) if stream_seed is not None else None
 
     def content_scores(self, logits: Tensor) -> Tensor:
         return logits.float().index_fill(-1, self._padding, float("-inf"))
@@ -59,6 +71,15 @@ class TokenSampler:
         if self.policy.greedy and logits.is_cuda and logits.dtype == torch.float32:
             # one native pass: PAD scored as -inf, torch.argmax tie and NaN order
             return _ops.greedy_tokens(logits, PAD_TOKEN_ID)
+        if self.stream_seed is not None and not self.policy.greedy and logits.is_cuda and logits.dtype == torch.float32:
+            thresholds = None
+            if self.policy.top_k is not None:
+                kept = min(self.policy.top_k, logits.shape[-1])
+                thresholds = torch.topk(self.content_scores(logits), kept, dim=-1).values[:, -1].contiguous()
+            tokens = _ops.temperature_tokens(logits, PAD_TOKEN_ID, float(self.policy.temperature), self.stream_seed,
+                                             self.stream_offset, self._step, thresholds)
+            self._step.add_(1)
+            return tokens
         scores = self.content_scores(logits)
         if self.policy.greedy:
             return scores.argmax(dim=-1, keepdim=True)

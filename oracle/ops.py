@@ -262,3 +262,41 @@ def permute_rows(rows, assignments, valid, expert_count: int, gather: bool = Tru
     sorted_rows[:n_valid] = rows[torch.from_numpy(sorted_tokens[:n_valid])]
     return (sorted_rows, torch.from_numpy(sorted_tokens), torch.from_numpy(keys), torch.from_numpy(offsets),
             torch.from_numpy(positions))
+
+
+_GOLDEN_GAMMA = np.uint64(0x9E3779B97F4A7C15)
+
+
+def _splitmix64(z):
+    """SplitMix64 finaliser (Steele, Lea and Flood, OOPSLA 2014) on uint64
+    arrays, wrapping modulo 2^64 like the kernel's unsigned arithmetic."""
+    with np.errstate(over="ignore"):
+        z = np.asarray(z, dtype=np.uint64) + _GOLDEN_GAMMA
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def gumbel_sample(logits, temperature, seed, stream_offset, step, pad, thresholds=None):
+    """Counter-based Gumbel-max sampling from softmax(logits / T) with PAD,
+    NaN and below-threshold columns excluded (the kernel of
+    koemi_sampler_temperature; the reference samples the same distribution
+    with torch.multinomial, runtime/fast_decode.py:72-80). Returns
+    (ids [rows], scores [rows, vocab] in float64)."""
+    x = np.asarray(logits, dtype=np.float64)
+    rows, vocab = x.shape
+    with np.errstate(over="ignore"):
+        streams = np.arange(rows, dtype=np.uint64) + np.uint64(stream_offset)
+        key = _splitmix64(np.uint64(seed) ^ _splitmix64(streams ^ _splitmix64(np.uint64(step))))
+        columns = np.arange(vocab, dtype=np.uint64) * _GOLDEN_GAMMA
+        bits = _splitmix64(key[:, None] + columns[None, :])
+    u = ((bits >> np.uint64(40)).astype(np.float64) + 0.5) / 16777216.0
+    scores = x / temperature - np.log(-np.log(u))
+    dropped = np.isnan(x)
+    if 0 <= pad < vocab:
+        dropped[:, pad] = True
+    if thresholds is not None:
+        dropped |= x < np.asarray(thresholds, dtype=np.float64)[:, None]
+    scores = np.where(dropped, -np.inf, scores)
+    ids = np.where(np.isneginf(scores).all(axis=1), 0, scores.argmax(axis=1))
+    return ids, scores

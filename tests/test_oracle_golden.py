@@ -137,3 +137,32 @@ def test_herm_block_matches_reference_forward_and_decode(name):
 def test_threshold_065_exercises_admission():
     fx = load_golden("c1_t065")
     assert int(fx["state"]["salient_valid"].sum()) > 0
+
+
+def test_splitmix64_known_answers():
+    """SplitMix64 from state 0: the first two outputs of the published
+    generator (Steele, Lea and Flood, 2014)."""
+    import numpy as np
+    assert int(ops._splitmix64(np.uint64(0))) == 0xE220A8397B1DCDAF
+    assert int(ops._splitmix64(np.uint64(0x9E3779B97F4A7C15))) == 0x6E789E6AA1B965F4
+
+
+def test_gumbel_sampler_oracle_follows_softmax():
+    """The counter-based Gumbel-max draws of the oracle (one per stream) have
+    softmax(logits / T) frequencies, never PAD, never below a threshold."""
+    import numpy as np
+    rows, vocab, temperature = 40000, 300, 0.8
+    base = np.full(vocab, -3.0)
+    base[:4] = [1.0, 0.0, 2.0, -0.5]
+    base[ops.PAD_TOKEN_ID] = 9.0
+    ids, _ = ops.gumbel_sample(np.broadcast_to(base, (rows, vocab)), temperature, 99, 0, 0, ops.PAD_TOKEN_ID)
+    counts = np.bincount(ids, minlength=vocab).astype(np.float64)
+    masked = base.copy()
+    masked[ops.PAD_TOKEN_ID] = -np.inf
+    p = np.exp(masked / temperature - np.max(masked / temperature))
+    p /= p.sum()
+    assert counts[ops.PAD_TOKEN_ID] == 0
+    assert (np.abs(counts - rows * p) <= 5 * np.sqrt(rows * p * (1 - p)) + 1).all()
+    kept, _ = ops.gumbel_sample(np.broadcast_to(base, (64, vocab)), temperature, 99, 0, 1, ops.PAD_TOKEN_ID,
+                                thresholds=np.full(64, 0.5))
+    assert set(kept.tolist()) <= {0, 2}
