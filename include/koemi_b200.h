@@ -240,6 +240,24 @@ KOEMI_API int koemi_think_causal_surprise_forward(const void *prior, const void 
                                         int64_t content_vocab, int dtype, int out_dtype,
                                         void *workspace, size_t workspace_bytes, void *stream);
 
+/* Backward of the causal surprise: dlogits [rows, content_vocab] fp32 =
+ * dL/dNLL_r * (softmax(prior_r W^T + b) - onehot(target_r)), with
+ * dL/dNLL_r = grad_r * exp(-NLL_r / ln C) / ln C and zero rows where !valid
+ * (valid may be NULL). `nll` is the forward's per-row NLL (nll_out of
+ * koemi_think_causal_surprise_forward); grad_surprise has the prior's dtype.
+ * The logits are recomputed tile by tile (tcgen05 for bf16/f16, FMA tiles for
+ * f32) and never stored; the caller forms dprior = dlogits W,
+ * dW = dlogits^T prior and db = column sums (fp32 library GEMMs, as the
+ * reference does). Workspace: koemi_think_surprise_backward_workspace(rows).
+ * Replaces think/surprise_kernel.cu:137-261 (an fp32 logits at::mm, then
+ * the logits-gradient kernel). */
+KOEMI_API size_t koemi_think_surprise_backward_workspace(int64_t rows);
+KOEMI_API int koemi_think_causal_surprise_backward(const void *prior, const void *weight, const void *bias,
+                                                   const int64_t *target_ids, const uint8_t *valid,
+                                                   const void *grad_surprise, const float *nll, float *dlogits,
+                                                   int64_t rows, int64_t width, int64_t content_vocab, int dtype,
+                                                   void *workspace, size_t workspace_bytes, void *stream);
+
 /* Merged head pass of a decode step (one read of the head for two uses):
  * rows [lse_rows + logit_rows, width] (bf16/f16, contiguous) against the full
  * head W [vocab, width] + bias [vocab] on tcgen05 tensor cores.

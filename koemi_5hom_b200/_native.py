@@ -57,6 +57,9 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int, (_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int, _p)),
     "koemi_dense_bounded_gates": (_int, (_p, _p, _p, _p, _i64, _i64, _f, _f, _p)),
     "koemi_dense_decode_step": (_int, (_p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _f, _f, _int, _p)),
+    "koemi_think_surprise_backward_workspace": (_sz, (_i64,)),
+    "koemi_think_causal_surprise_backward": (
+        _int, (_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p)),
     "koemi_think_head_pass_slices": (_i64, (_i64,)),
     "koemi_think_head_pass": (_int, (_p, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _int, _p)),
     "koemi_think_surprise_from_partials": (

@@ -24,6 +24,9 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
                           int64_t rows, int64_t width, int64_t content_vocab, int dtype, float *partials,
                           int64_t slices, cudaStream_t stream, bool *handled);
 int64_t surprise_umma_slices(int64_t rows, int64_t width, int64_t content_vocab, int dtype);
+int surprise_grad_umma(const void *prior, const void *weight, const void *bias, const int64_t *targets,
+                       const float *row_lse, const float *row_scale, float *dlogits, int64_t rows, int64_t width,
+                       int64_t content_vocab, int dtype, cudaStream_t stream, bool *handled);
 
 namespace {
 
@@ -214,6 +217,98 @@ __global__ void surprise_from_partials_kernel(const T *__restrict__ prior, const
     if (lane == 0) {
         const float nll = logf(total) + m - target;
         out[row] = 1.0f - expf(-nll / log_vocab);
+    }
+}
+
+// Backward, per row: the target logit prior . W[t] + b[t] (fp32), the
+// row's log-sum-exp lse = NLL + target logit (NLL saved by the forward) and
+// dL/dNLL = grad * exp(-NLL / ln C) / ln C (zero on invalid rows), one warp
+// per row.
+template <typename T>
+__global__ void surprise_grad_rows_kernel(const T *__restrict__ prior, const T *__restrict__ weight,
+                                          const T *__restrict__ bias, const int64_t *__restrict__ targets,
+                                          const uint8_t *__restrict__ valid, const T *__restrict__ grad,
+                                          const float *__restrict__ nll, float *__restrict__ row_lse,
+                                          float *__restrict__ row_scale, int64_t rows, int64_t width,
+                                          float log_vocab) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const bool ok = valid == nullptr || valid[row] != 0;
+    if (!ok) {
+        if (lane == 0) {
+            row_lse[row] = 0.0f;
+            row_scale[row] = 0.0f;
+        }
+        return;
+    }
+    const int64_t t = targets[row];
+    const T *p = prior + row * width;
+    const T *w = weight + t * width;
+    float dot = 0.0f;
+    for (int64_t c = lane; c < width; c += 32) dot = fmaf(to_acc(p[c]), to_acc(w[c]), dot);
+    dot = warp_sum(dot);
+    if (lane == 0) {
+        const float n = nll[row];
+        row_lse[row] = n + dot + to_acc(bias[t]);
+        row_scale[row] = to_acc(grad[row]) * expf(-n / log_vocab) / log_vocab;
+    }
+}
+
+// Backward on FMA tiles (fp32 inputs and shapes TMA cannot take): a CTA
+// forms a [32 x 64] logit tile as the forward kernel does and stores
+// dlogits = scale * (exp(l - lse) - onehot(target)) for it.
+template <typename T>
+__global__ __launch_bounds__(kThreads) void surprise_grad_kernel(
+    const T *__restrict__ prior, const T *__restrict__ weight, const T *__restrict__ bias,
+    const int64_t *__restrict__ targets, const float *__restrict__ row_lse, const float *__restrict__ row_scale,
+    float *__restrict__ dlogits, int64_t rows, int64_t width, int64_t vocab) {
+    __shared__ float a_tile[kKTile][kRowsTile + 1];
+    __shared__ float b_tile[kKTile][kVocabTile + 1];
+    const int tid = threadIdx.x;
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRowsTile;
+    const int64_t v0 = static_cast<int64_t>(blockIdx.y) * kVocabTile;
+    const int tr = tid / 16;
+    const int tc = tid % 16;
+    float acc[2][4] = {};
+    for (int64_t k0 = 0; k0 < width; k0 += kKTile) {
+        for (int i = tid; i < kRowsTile * kKTile; i += kThreads) {
+            const int r = i / kKTile, k = i % kKTile;
+            const int64_t gr = row0 + r, gk = k0 + k;
+            a_tile[k][r] = (gr < rows && gk < width) ? to_acc(prior[gr * width + gk]) : 0.0f;
+        }
+        for (int i = tid; i < kVocabTile * kKTile; i += kThreads) {
+            const int c = i / kKTile, k = i % kKTile;
+            const int64_t gc = v0 + c, gk = k0 + k;
+            b_tile[k][c] = (gc < vocab && gk < width) ? to_acc(weight[gc * width + gk]) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kKTile; ++k) {
+            const float a0 = a_tile[k][tr * 2], a1 = a_tile[k][tr * 2 + 1];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float b = b_tile[k][tc * 4 + j];
+                acc[0][j] = fmaf(a0, b, acc[0][j]);
+                acc[1][j] = fmaf(a1, b, acc[1][j]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int64_t r = row0 + tr * 2 + i;
+        if (r >= rows) continue;
+        const float lse = row_lse[r], scale = row_scale[r];
+        const int64_t t = targets[r];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t c = v0 + tc * 4 + j;
+            if (c < vocab) {
+                const float l = acc[i][j] + to_acc(bias[c]);
+                dlogits[r * vocab + c] = scale * (expf(l - lse) - (c == t ? 1.0f : 0.0f));
+            }
+        }
     }
 }
 
@@ -436,6 +531,51 @@ extern "C" int koemi_think_surprise_from_partials(const void *prior, const void 
         case KOEMI_BF16: KOEMI_CUDA_TRY(launch_pdl(surprise_from_partials_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const __nv_bfloat16 *>(prior), static_cast<const __nv_bfloat16 *>(head_weight), static_cast<const __nv_bfloat16 *>(head_bias), token_ids, valid, partials, slices, rows, batch, width, log_vocab, surprise)); break;
         case KOEMI_F16: KOEMI_CUDA_TRY(launch_pdl(surprise_from_partials_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), static_cast<const __half *>(prior), static_cast<const __half *>(head_weight), static_cast<const __half *>(head_bias), token_ids, valid, partials, slices, rows, batch, width, log_vocab, surprise)); break;
         default: return fail(KOEMI_ERR_INVALID, "the head-pass surprise takes bf16 or f16 rows");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" size_t koemi_think_surprise_backward_workspace(int64_t rows) {
+    return rows <= 0 ? 256 : static_cast<size_t>(2 * rows) * sizeof(float) + 256;
+}
+
+extern "C" int koemi_think_causal_surprise_backward(const void *prior, const void *weight, const void *bias,
+                                                    const int64_t *target_ids, const uint8_t *valid,
+                                                    const void *grad_surprise, const float *nll, float *dlogits,
+                                                    int64_t rows, int64_t width, int64_t content_vocab, int dtype,
+                                                    void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (rows < 0 || width < 1 || content_vocab < 2) return fail(KOEMI_ERR_INVALID, "need rows >= 0, width >= 1, content_vocab >= 2");
+    if (rows == 0) return KOEMI_OK;
+    if (workspace_bytes < koemi_think_surprise_backward_workspace(rows)) {
+        return fail(KOEMI_ERR_WORKSPACE, "surprise backward needs %zu workspace bytes", koemi_think_surprise_backward_workspace(rows));
+    }
+    if (prior == nullptr || weight == nullptr || bias == nullptr || target_ids == nullptr || grad_surprise == nullptr ||
+        nll == nullptr || dlogits == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "surprise backward pointers must be non-NULL (valid may be NULL)");
+    }
+    float *row_lse = static_cast<float *>(workspace);
+    float *row_scale = row_lse + rows;
+    const float log_vocab = std::log(static_cast<float>(content_vocab));
+    cudaStream_t s = as_stream(stream);
+    const unsigned row_blocks = static_cast<unsigned>(ceil_div(rows, 8));
+    switch (dtype) {
+        case KOEMI_F32: surprise_grad_rows_kernel<float><<<row_blocks, 256, 0, s>>>(static_cast<const float *>(prior), static_cast<const float *>(weight), static_cast<const float *>(bias), target_ids, valid, static_cast<const float *>(grad_surprise), nll, row_lse, row_scale, rows, width, log_vocab); break;
+        case KOEMI_F16: surprise_grad_rows_kernel<__half><<<row_blocks, 256, 0, s>>>(static_cast<const __half *>(prior), static_cast<const __half *>(weight), static_cast<const __half *>(bias), target_ids, valid, static_cast<const __half *>(grad_surprise), nll, row_lse, row_scale, rows, width, log_vocab); break;
+        case KOEMI_BF16: surprise_grad_rows_kernel<__nv_bfloat16><<<row_blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(prior), static_cast<const __nv_bfloat16 *>(weight), static_cast<const __nv_bfloat16 *>(bias), target_ids, valid, static_cast<const __nv_bfloat16 *>(grad_surprise), nll, row_lse, row_scale, rows, width, log_vocab); break;
+        default: return fail(KOEMI_ERR_INVALID, "surprise backward supports f32, f16 and bf16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    bool handled = false;
+    int rc = surprise_grad_umma(prior, weight, bias, target_ids, row_lse, row_scale, dlogits, rows, width, content_vocab,
+                                dtype, s, &handled);
+    if (rc != KOEMI_OK || handled) return rc;
+    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRowsTile)), static_cast<unsigned>(ceil_div(content_vocab, kVocabTile)));
+    switch (dtype) {
+        case KOEMI_F32: surprise_grad_kernel<float><<<grid, kThreads, 0, s>>>(static_cast<const float *>(prior), static_cast<const float *>(weight), static_cast<const float *>(bias), target_ids, row_lse, row_scale, dlogits, rows, width, content_vocab); break;
+        case KOEMI_F16: surprise_grad_kernel<__half><<<grid, kThreads, 0, s>>>(static_cast<const __half *>(prior), static_cast<const __half *>(weight), static_cast<const __half *>(bias), target_ids, row_lse, row_scale, dlogits, rows, width, content_vocab); break;
+        default: surprise_grad_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(static_cast<const __nv_bfloat16 *>(prior), static_cast<const __nv_bfloat16 *>(weight), static_cast<const __nv_bfloat16 *>(bias), target_ids, row_lse, row_scale, dlogits, rows, width, content_vocab); break;
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;

@@ -100,6 +100,9 @@ struct UmmaArgs {
     const int64_t *targets;   // surprise: target column per row, or NULL (no target logit)
     int64_t lse_rows;         // surprise: rows below fold into partials; rows at or above write logits to out
     int64_t pad_column;       // surprise: column left out of the log-sum-exp (-1: none)
+    const float *row_lse;     // surprise gradient: per-row log-sum-exp (NULL: forward modes)
+    const float *row_scale;   // surprise gradient: per-row dL/dNLL (0 on invalid rows)
+    float *grad_out;          // surprise gradient: fp32 dlogits [rows, n_out]
     int *status;
     uint32_t idesc;
 };
@@ -564,6 +567,30 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                     KOEMI_TMEM_LD32(taddr + c * 32, y);
                     tmem_wait_ld();
                     const int64_t col0 = tile.n * kBN + c * 32;
+                    if (args.grad_out != nullptr) {
+                        // gradient mode: dlogits = scale * (softmax - onehot(target))
+                        if (row_ok && col0 < args.n_out) {
+                            const float lse = args.row_lse[row];
+                            const float scale = args.row_scale[row];
+                            float g[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const int64_t col = col0 + j;
+                                const float l = __uint_as_float(y[j]) + (col < args.n_out ? to_acc(bias[col]) : 0.0f);
+                                g[j] = scale * (expf(l - lse) - (col == target ? 1.0f : 0.0f));
+                            }
+                            float *dst = args.grad_out + row * args.n_out + col0;
+                            if (col0 + 32 <= args.n_out && aligned16(dst)) {
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    reinterpret_cast<float4 *>(dst)[q] = make_float4(g[4 * q], g[4 * q + 1], g[4 * q + 2], g[4 * q + 3]);
+                                }
+                            } else {
+                                for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = g[j];
+                            }
+                        }
+                        continue;
+                    }
                     if (logit_row) {
                         if (row_ok && col0 < args.n_out) {
                             float o[32];
@@ -607,7 +634,7 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         run_sum = s;
                     }
                 }
-                if (row_ok && !logit_row) {
+                if (row_ok && !logit_row && args.grad_out == nullptr) {
                     float *p = args.partials + (tile.n * args.lse_rows + row) * 3;
                     p[0] = run_max;
                     p[1] = run_sum;
@@ -964,6 +991,45 @@ int surprise_umma_forward(const void *prior, const void *weight, const void *bia
     if (rc != KOEMI_OK) return rc;
     *handled = true;
     return KOEMI_OK;
+}
+
+// dlogits of the causal surprise on tensor cores: the logits tile recomputed
+// by the MMAs, then scale_r * (exp(l - lse_r) - onehot(target_r)) stored as
+// fp32 [rows, content_vocab]. False in *handled when TMA cannot describe the
+// operands (the FMA kernel takes those).
+int surprise_grad_umma(const void *prior, const void *weight, const void *bias, const int64_t *targets,
+                       const float *row_lse, const float *row_scale, float *dlogits, int64_t rows, int64_t width,
+                       int64_t content_vocab, int dtype, cudaStream_t stream, bool *handled) {
+    *handled = false;
+    if ((dtype != KOEMI_BF16 && dtype != KOEMI_F16) || !umma_shape_ok(prior, width) || !umma_shape_ok(weight, width) ||
+        rows >= (int64_t(1) << 31) || content_vocab >= (int64_t(1) << 31)) {
+        return KOEMI_OK;
+    }
+    UmmaArgs a{};
+    int rc = encode_kmajor(&a.map_a, dtype, prior, rows, width, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&a.map_b0, dtype, weight, content_vocab, width, kBN);
+    if (rc != KOEMI_OK) return rc;
+    const int64_t slices = (content_vocab + kBN - 1) / kBN;
+    a.k = width;
+    a.rows = rows;
+    a.n_tiles = slices;
+    a.n_out = content_vocab;
+    a.experts = 1;
+    a.bias0 = bias;
+    a.targets = targets;
+    a.lse_rows = rows;
+    a.pad_column = -1;
+    a.row_lse = row_lse;
+    a.row_scale = row_scale;
+    a.grad_out = dlogits;
+    a.status = device_status_word();
+    a.idesc = make_idesc(dtype);
+    a.band = 16;
+    const bool pair = surprise_tile_rows(rows) > kBM;
+    const int64_t tiles = ((rows + surprise_tile_rows(rows) - 1) / surprise_tile_rows(rows)) * slices;
+    rc = pair ? launch<kSurprise, true>(a, dtype, tiles, stream) : launch<kSurprise, false>(a, dtype, tiles, stream);
+    if (rc == KOEMI_OK) *handled = true;
+    return rc;
 }
 
 int head_pass_umma(const void *rows_in, int64_t lse_rows, int64_t logit_rows, int64_t width, const void *weight,

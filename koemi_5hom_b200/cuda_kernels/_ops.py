@@ -210,6 +210,55 @@ def _(prior, weight, bias, targets, valid, out_dtype):
     return prior.new_empty(prior.shape[:-1], dtype=out_dtype)
 
 
+@torch.library.custom_op("koemi_b200::causal_surprise_forward_nll", mutates_args=())
+def causal_surprise_forward_nll(prior: Tensor, weight: Tensor, bias: Tensor, targets: Tensor, valid: Tensor,
+                                out_dtype: torch.dtype) -> tuple[Tensor, Tensor]:
+    """The surprise and the per-row fp32 NLL (kept for the backward)."""
+    prior, weight, bias, targets, valid = _dense(prior, weight, bias, targets, valid)
+    stream = _prepare(prior)
+    width = prior.shape[-1]
+    rows = prior.numel() // width
+    vocab = weight.shape[0]
+    out = torch.empty(prior.shape[:-1], dtype=out_dtype, device=prior.device)
+    nll = torch.empty(prior.shape[:-1], dtype=torch.float32, device=prior.device)
+    size = _native.library().koemi_think_surprise_workspace(rows, width, vocab, dtype_code(prior.dtype))
+    scratch = _native.workspace(size, prior.device)
+    call("koemi_think_causal_surprise_forward", ptr(prior), ptr(weight), ptr(bias), ptr(targets), ptr(valid),
+         ptr(out), ptr(nll), rows, width, vocab, dtype_code(prior.dtype), dtype_code(out_dtype), ptr(scratch),
+         scratch.numel(), stream)
+    return out, nll
+
+
+@causal_surprise_forward_nll.register_fake
+def _(prior, weight, bias, targets, valid, out_dtype):
+    return (prior.new_empty(prior.shape[:-1], dtype=out_dtype),
+            prior.new_empty(prior.shape[:-1], dtype=torch.float32))
+
+
+@torch.library.custom_op("koemi_b200::causal_surprise_dlogits", mutates_args=())
+def causal_surprise_dlogits(prior: Tensor, weight: Tensor, bias: Tensor, targets: Tensor, valid: Tensor,
+                            grad: Tensor, nll: Tensor) -> Tensor:
+    """fp32 [rows, content_vocab] gradient of the loss with respect to the
+    surprise logits (koemi_think_causal_surprise_backward)."""
+    prior, weight, bias, targets, valid, grad, nll = _dense(prior, weight, bias, targets, valid, grad, nll)
+    stream = _prepare(prior)
+    width = prior.shape[-1]
+    rows = prior.numel() // width
+    vocab = weight.shape[0]
+    dlogits = torch.empty(rows, vocab, dtype=torch.float32, device=prior.device)
+    scratch = _native.workspace(_native.library().koemi_think_surprise_backward_workspace(rows), prior.device)
+    call("koemi_think_causal_surprise_backward", ptr(prior), ptr(weight), ptr(bias), ptr(targets), ptr(valid),
+         ptr(grad), ptr(nll), ptr(dlogits), rows, width, vocab, dtype_code(prior.dtype), ptr(scratch),
+         scratch.numel(), stream)
+    return dlogits
+
+
+@causal_surprise_dlogits.register_fake
+def _(prior, weight, bias, targets, valid, grad, nll):
+    width = prior.shape[-1]
+    return prior.new_empty(prior.numel() // width, weight.shape[0], dtype=torch.float32)
+
+
 @torch.library.custom_op("koemi_b200::salient_admission", mutates_args=())
 def salient_admission(carried_keys: Tensor, carried_values: Tensor, carried_valid: Tensor, keys: Tensor,
                       values: Tensor, surprise: Tensor, valid: Tensor, threshold: float,

@@ -4,8 +4,10 @@
 validation contract (src/koemi/cuda_kernels/think/surprise.py:91-251). The
 forward is ``koemi_think_causal_surprise_forward``: the head contraction and
 the log-sum-exp/NLL reduction run fused, so the ``[rows, content_vocab]``
-logits are never written to memory. The backward recomputes the logits in
-vocabulary chunks with torch CUDA ops (no native backward kernel yet).
+logits are never written to memory. The backward is
+``koemi_think_causal_surprise_backward``: the logits recomputed tile by tile
+(tcgen05 for 16-bit inputs) and turned into dlogits in the same kernel; the
+three contractions with dlogits are fp32 library GEMMs, as in the reference.
 ``salient_admission`` exposes the admission + ring compaction kernel the HERM
 block uses after the surprise.
 """
@@ -31,7 +33,6 @@ __all__ = [
 ]
 
 _SUPPORTED_DTYPES: tuple[torch.dtype, ...] = (torch.float16, torch.bfloat16, torch.float32)
-_BACKWARD_VOCAB_CHUNK = 8192
 
 
 class CudaThinkUnavailableError(RuntimeError):
@@ -129,41 +130,24 @@ class _CausalSurpriseFunction(torch.autograd.Function):
     @staticmethod
     def forward(context, prior_states, content_weight, content_bias, target_ids, valid_mask):
         inputs = tuple(t.contiguous() for t in (prior_states, content_weight, content_bias, target_ids, valid_mask))
-        surprise = _ops.causal_surprise_forward(*inputs, prior_states.dtype)
-        context.save_for_backward(*inputs, surprise)
+        surprise, nll = _ops.causal_surprise_forward_nll(*inputs, prior_states.dtype)
+        context.save_for_backward(*inputs, nll)
         return surprise
 
     @staticmethod
     def backward(context, gradient):
-        prior, weight, bias, targets, valid, surprise = context.saved_tensors
-        # ds/dNLL = (1 - s) / ln C; dNLL/dlogit = softmax - onehot(target).
-        vocab = weight.shape[0]
-        rows = prior.reshape(-1, prior.shape[-1]).float()
-        scale = (gradient.float() * (1.0 - surprise.float()) / math.log(vocab)) * valid
-        scale = scale.reshape(-1)
-        flat_targets = targets.reshape(-1)
-        w = weight.float()
-        b = bias.float()
-        lse = torch.full((rows.shape[0],), float("-inf"), device=rows.device)
-        for start in range(0, vocab, _BACKWARD_VOCAB_CHUNK):
-            chunk = rows @ w[start:start + _BACKWARD_VOCAB_CHUNK].T + b[start:start + _BACKWARD_VOCAB_CHUNK]
-            lse = torch.logaddexp(lse, torch.logsumexp(chunk, dim=-1))
-        grad_rows = torch.zeros_like(rows)
-        grad_w = torch.zeros_like(w)
-        grad_b = torch.zeros_like(b)
-        for start in range(0, vocab, _BACKWARD_VOCAB_CHUNK):
-            stop = min(vocab, start + _BACKWARD_VOCAB_CHUNK)
-            chunk = rows @ w[start:stop].T + b[start:stop]
-            dlogits = torch.exp(chunk - lse.unsqueeze(-1))
-            inside = (flat_targets >= start) & (flat_targets < stop)
-            hit = torch.nonzero(inside, as_tuple=False).squeeze(-1)
-            dlogits[hit, flat_targets[hit] - start] -= 1.0
-            dlogits *= scale.unsqueeze(-1)
-            grad_rows += dlogits @ w[start:stop]
-            grad_w[start:stop] = dlogits.T @ rows
-            grad_b[start:stop] = dlogits.sum(dim=0)
-        return (grad_rows.reshape(prior.shape).to(prior.dtype), grad_w.to(weight.dtype), grad_b.to(bias.dtype),
-                None, None)
+        """The native kernel forms dlogits = dL/dNLL (softmax - onehot) from
+        recomputed logits (never stored); the three contractions run in fp32
+        as the reference's (think/surprise_kernel.cu:248-251)."""
+        prior, weight, bias, targets, valid, nll = context.saved_tensors
+        width = prior.shape[-1]
+        dlogits = _ops.causal_surprise_dlogits(prior, weight, bias, targets, valid,
+                                               gradient.to(prior.dtype).contiguous(), nll)
+        rows = prior.reshape(-1, width).float()
+        grad_prior = (dlogits @ weight.float()).reshape(prior.shape)
+        grad_weight = dlogits.T @ rows
+        grad_bias = dlogits.sum(dim=0)
+        return grad_prior.to(prior.dtype), grad_weight.to(weight.dtype), grad_bias.to(bias.dtype), None, None
 
 
 def _validate_inputs(prior_states, content_weight, content_bias, target_ids, valid_mask, validate_targets) -> int:
