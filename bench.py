@@ -72,6 +72,8 @@ def parse_args(argv=None):
     p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "expert_decode", "surprise_decode",
                                     "surprise_prefill", "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
+    p.add_argument("--op-rows", type=int, default=None,
+                   help="activation rows of --op dense_decode (default 256; 32 is one rank's share at 8 GPUs)")
     p.add_argument("--op-tokens", type=int, default=None,
                    help="token count of --op moe (default: config 4's 131072; smaller for profiler captures)")
     return p.parse_args(argv)
@@ -595,14 +597,17 @@ def run_op(args) -> None:
             moved = touched * 3 * d * h * 2 + pairs * (2 * d + 4 * h) * 2
             work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
             shape = f"config 5 decode step: {pairs} pairs, {touched} experts touched, d={d}, d_ff={h} (3.2 GB weights > L2)"
-    elif args.op == "dense_decode":  # the four dense projections of one config-5 decode block, 256 rows
+    elif args.op == "dense_decode":  # the four dense projections of one config-5 decode block
         shapes = {"gates": (4096, 2048), "local": (4096, 2048), "assoc": (6146, 2048), "fusion": (2048, 8192),
                   "local_assoc": (10242, 2048)}  # the last: local and assoc as one GEMM (not in the block total)
         sets = 4  # weight sets cycled so each launch reads its weights from HBM (4 x 75 MB > L2)
         layers = [{name: ((torch.randn(n, k, device=device, generator=g) * 0.02).bfloat16(),
                           torch.zeros(n, device=device, dtype=torch.bfloat16)) for name, (n, k) in shapes.items()}
                   for _ in range(sets)]
-        inputs = {k: torch.randn(256, k, device=device, generator=g).bfloat16() for k in (2048, 8192)}
+        rows = args.op_rows or 256
+        inputs = {k: torch.randn(rows, k, device=device, generator=g).bfloat16() for k in (2048, 8192)}
+        from koemi_5hom_b200 import _native as native
+        stream_handle = torch.cuda.current_stream().cuda_stream
         per = {}
         for name, (n, k) in shapes.items():
             counter = iter(range(1 << 30))
@@ -613,13 +618,23 @@ def run_op(args) -> None:
             library = lambda name=name, k=k: torch.mm(  # noqa: E731
                 inputs[k], layers[next(counter_lib) % sets][name][0].t(), out_dtype=torch.float32)
             t_lib = _time_op(library, args.steps, args.warmup, graph=True)
-            per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + 256 * k * 2 + 256 * n * 4) / t / 1e9,
-                         "cublas_us_no_bias": t_lib * 1e6}
+            out = torch.empty(rows, n, device=device)
+            swapped = {}
+            for splits in (0, 1, 2, 4, 8):
+                counter_swap = iter(range(1 << 30))
+
+                def swap(name=name, k=k, n=n, splits=splits, counter_swap=counter_swap):
+                    weight, bias = layers[next(counter_swap) % sets][name]
+                    native.call("koemi_dense_projection_swap", inputs[k].data_ptr(), k, weight.data_ptr(),
+                                bias.data_ptr(), out.data_ptr(), n, rows, n, k, native.BF16, splits, stream_handle)
+                swapped[f"splits_{splits or 'auto'}"] = _time_op(swap, args.steps, args.warmup, graph=True) * 1e6
+            per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + rows * k * 2 + rows * n * 4) / t / 1e9,
+                         "cublas_us_no_bias": t_lib * 1e6, "swapped_us": swapped}
         block = ("gates", "local", "assoc", "fusion")
         seconds = sum(per[name]["us"] for name in block) / 1e6
-        moved = sum(n * k * 2 + 256 * k * 2 + 256 * n * 4 for name, (n, k) in shapes.items() if name in block)
+        moved = sum(n * k * 2 + rows * k * 2 + rows * n * 4 for name, (n, k) in shapes.items() if name in block)
         work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
-        shape = "config 5 decode block: 256 rows; gates 4096x2048, local 4096x2048, assoc 6146x2048, " \
+        shape = f"config 5 decode block: {rows} rows; gates 4096x2048, local 4096x2048, assoc 6146x2048, " \
                 "fusion 2048x8192 bf16 -> fp32"
         extra = {"per_projection": per}
     else:  # surprise head: decode (256 rows) or one prefill window (32768 rows) of config 5
