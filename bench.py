@@ -69,7 +69,7 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
-    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "expert_decode", "surprise_decode",
+    p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "permute", "expert_decode", "surprise_decode",
                                     "surprise_prefill", "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
     p.add_argument("--op-rows", type=int, default=None,
@@ -597,6 +597,20 @@ def run_op(args) -> None:
             moved = touched * 3 * d * h * 2 + pairs * (2 * d + 4 * h) * 2
             work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
             shape = f"config 5 decode step: {pairs} pairs, {touched} experts touched, d={d}, d_ff={h} (3.2 GB weights > L2)"
+    elif args.op == "permute":  # config 4's stable permutation with the row gather (262144 pairs, d=1024 bf16)
+        tokens, d, e = args.op_tokens or 131072, 1024, 64
+        x = torch.randn(tokens, d, device=device, generator=g).bfloat16()
+        ids = torch.randint(0, 256, (tokens,), device=device, generator=g)
+        prev = torch.randint(0, 256, (tokens,), device=device, generator=g)
+        valid = torch.ones(tokens, dtype=torch.bool, device=device)
+        assignments = _ops.route_topk(ids, prev, valid, e, 2)
+        seconds = _time_op(lambda: _ops.permute_topk(x, assignments, valid, e, True), args.steps, args.warmup,
+                           graph=True)
+        pairs = tokens * 2
+        # context read once, sorted rows written, assignments read, sorted rows / experts / positions written
+        moved = tokens * d * 2 + pairs * d * 2 + pairs * 8 + 3 * pairs * 8 + (e + 1) * 8
+        work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = f"config 4: {tokens} tokens x d={d} bf16, hash top-2 over {e} experts ({moved / 1e6:.0f} MB per call)"
     elif args.op == "dense_decode":  # the four dense projections of one config-5 decode block
         shapes = {"gates": (4096, 2048), "local": (4096, 2048), "assoc": (6146, 2048), "fusion": (2048, 8192),
                   "local_assoc": (10242, 2048)}  # the last: local and assoc as one GEMM (not in the block total)
@@ -607,7 +621,6 @@ def run_op(args) -> None:
         rows = args.op_rows or 256
         inputs = {k: torch.randn(rows, k, device=device, generator=g).bfloat16() for k in (2048, 8192)}
         from koemi_5hom_b200 import _native as native
-        stream_handle = torch.cuda.current_stream().cuda_stream
         per = {}
         for name, (n, k) in shapes.items():
             counter = iter(range(1 << 30))
@@ -626,7 +639,8 @@ def run_op(args) -> None:
                 def swap(name=name, k=k, n=n, splits=splits, counter_swap=counter_swap):
                     weight, bias = layers[next(counter_swap) % sets][name]
                     native.call("koemi_dense_projection_swap", inputs[k].data_ptr(), k, weight.data_ptr(),
-                                bias.data_ptr(), out.data_ptr(), n, rows, n, k, native.BF16, splits, stream_handle)
+                                bias.data_ptr(), out.data_ptr(), n, rows, n, k, native.BF16, splits,
+                                torch.cuda.current_stream().cuda_stream)
                 swapped[f"splits_{splits or 'auto'}"] = _time_op(swap, args.steps, args.warmup, graph=True) * 1e6
             per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + rows * k * 2 + rows * n * 4) / t / 1e9,
                          "cublas_us_no_bias": t_lib * 1e6, "swapped_us": swapped}

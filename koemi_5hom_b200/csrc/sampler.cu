@@ -85,7 +85,7 @@ __global__ __launch_bounds__(kSamplerThreads) void greedy_kernel(const float *__
 // number and a stream's draws do not depend on the batch it decodes in:
 //   key  = splitmix64(seed ^ splitmix64(stream ^ splitmix64(step)))
 //   bits = splitmix64(key + v * 0x9E3779B97F4A7C15)
-//   u    = ((bits >> 40) + 0.5) / 2^24
+//   u    = ((bits >> 41) + 0.5) / 2^23   (exact in fp32, never 0 or 1)
 // splitmix64 is Steele, Lea and Flood's SplitMix finaliser (OOPSLA 2014):
 //   z += 0x9E3779B97F4A7C15; z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9;
 //   z = (z ^ (z >> 27)) * 0x94D049BB133111EB; return z ^ (z >> 31).
@@ -103,7 +103,7 @@ __device__ __forceinline__ void take_sample(Best &best, float logit, int64_t i, 
                                             float threshold, uint64_t key) {
     if (i == pad || isnan(logit) || logit < threshold) return;
     const uint64_t bits = splitmix64(key + static_cast<uint64_t>(i) * 0x9E3779B97F4A7C15ull);
-    const float u = (static_cast<float>(bits >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u = (static_cast<float>(bits >> 41) + 0.5f) * (1.0f / 8388608.0f);
     const float score = logit * inv_t - logf(-logf(u));
     if (score > best.value || (score == best.value && i < best.index)) best = Best{score, i};
 }

@@ -290,7 +290,7 @@ def gumbel_sample(logits, temperature, seed, stream_offset, step, pad, threshold
         key = _splitmix64(np.uint64(seed) ^ _splitmix64(streams ^ _splitmix64(np.uint64(step))))
         columns = np.arange(vocab, dtype=np.uint64) * _GOLDEN_GAMMA
         bits = _splitmix64(key[:, None] + columns[None, :])
-    u = ((bits >> np.uint64(40)).astype(np.float64) + 0.5) / 16777216.0
+    u = ((bits >> np.uint64(41)).astype(np.float64) + 0.5) / 8388608.0
     scores = x / temperature - np.log(-np.log(u))
     dropped = np.isnan(x)
     if 0 <= pad < vocab:
