@@ -469,6 +469,27 @@ def run_b200(args) -> None:
         e2e_seconds = float(t.item())
     e2e_value = per_rank * world * args.steps / e2e_seconds
 
+    # the config's sampled variant: temperature 0.8, seeded per stream (the
+    # native counter-based sampler; stream ids are global across ranks)
+    from koemi_5hom_b200.runtime import SamplingPolicy, TokenSampler
+    sampler = TokenSampler(SamplingPolicy(temperature=0.8), device, stream_seed=2024, stream_offset=rank * per_rank)
+    token = sampler(logits)
+    for _ in range(max(args.warmup, 1)):
+        token = sampler(decoder.step(token))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        token = sampler(decoder.step(token))
+    stop.record(stream)
+    torch.cuda.synchronize()
+    sampled_seconds = start.elapsed_time(stop) / 1000.0
+    if world > 1:
+        t = torch.tensor([sampled_seconds], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sampled_seconds = float(t.item())
+
     progress(rank, "end-to-end done; expert kernel roofline")
     mlp = measure_expert_mlp(model, args, world)
     peaks_path = ROOT / "MEASURED_PEAKS.json"
@@ -497,6 +518,9 @@ def run_b200(args) -> None:
                      "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
                      "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},
         "prefill_s": prefill_seconds,
+        "sampled": {"policy": "temperature 0.8, seeded per stream (native Gumbel-max)",
+                    "value": per_rank * world * args.steps / sampled_seconds,
+                    "ms_per_step": sampled_seconds / args.steps * 1000.0},
     }
     # the step graph (which may hold collectives) and the peer buffers go
     # before the process group
@@ -620,7 +644,6 @@ def run_op(args) -> None:
                   for _ in range(sets)]
         rows = args.op_rows or 256
         inputs = {k: torch.randn(rows, k, device=device, generator=g).bfloat16() for k in (2048, 8192)}
-        from koemi_5hom_b200 import _native as native
         per = {}
         for name, (n, k) in shapes.items():
             counter = iter(range(1 << 30))
@@ -631,19 +654,8 @@ def run_op(args) -> None:
             library = lambda name=name, k=k: torch.mm(  # noqa: E731
                 inputs[k], layers[next(counter_lib) % sets][name][0].t(), out_dtype=torch.float32)
             t_lib = _time_op(library, args.steps, args.warmup, graph=True)
-            out = torch.empty(rows, n, device=device)
-            swapped = {}
-            for splits in (0, 1, 2, 4, 8):
-                counter_swap = iter(range(1 << 30))
-
-                def swap(name=name, k=k, n=n, splits=splits, counter_swap=counter_swap):
-                    weight, bias = layers[next(counter_swap) % sets][name]
-                    native.call("koemi_dense_projection_swap", inputs[k].data_ptr(), k, weight.data_ptr(),
-                                bias.data_ptr(), out.data_ptr(), n, rows, n, k, native.BF16, splits,
-                                torch.cuda.current_stream().cuda_stream)
-                swapped[f"splits_{splits or 'auto'}"] = _time_op(swap, args.steps, args.warmup, graph=True) * 1e6
             per[name] = {"us": t * 1e6, "gbs": (n * k * 2 + rows * k * 2 + rows * n * 4) / t / 1e9,
-                         "cublas_us_no_bias": t_lib * 1e6, "swapped_us": swapped}
+                         "cublas_us_no_bias": t_lib * 1e6}
         block = ("gates", "local", "assoc", "fusion")
         seconds = sum(per[name]["us"] for name in block) / 1e6
         moved = sum(n * k * 2 + rows * k * 2 + rows * n * 4 for name, (n, k) in shapes.items() if name in block)

@@ -186,15 +186,6 @@ KOEMI_API int koemi_dense_projection(const void *a, int64_t a_stride, const void
                            float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
                            void *workspace, size_t workspace_bytes, void *stream);
 
-/* The same projection for 1..256 rows with the operands swapped (weight rows
- * as the tcgen05 M = 128 operand, the rows as N = rows rounded up to 16):
- * `splits` K splits per 128 weight rows reduced in a thread-block cluster
- * (0 picks the largest of 8 / 4 / 2 that fits one wave; 1 stores straight
- * from TMEM). Deterministic; no workspace. */
-KOEMI_API int koemi_dense_projection_swap(const void *a, int64_t a_stride, const void *weight, const void *bias,
-                                          float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k,
-                                          int dtype, int splits, void *stream);
-
 /* ------------------------------------------------------------- core front */
 
 /* y = silu(x * rsqrt(mean(x^2) + eps) * w), inv_rms[row] = rsqrt(...).

@@ -760,216 +760,6 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
     }
 }
 
-// ------------------------------------------------------- swapped projection
-// Decode-sized projections (rows <= 256) with the operands swapped: the
-// weight rows are the MMA's M = 128 operand and the activation rows its N
-// operand (N = rows rounded up to 16), so a 32-row batch costs a 128 x 32
-// accumulator instead of a 128 x 256 one, and no MMA work is spent on padding
-// rows. One CTA per (128 weight rows, K split); the K splits of a weight tile
-// form one thread-block cluster and reduce through distributed shared memory
-// in split order (deterministic); a single split stores straight from TMEM.
-// The stage ring holds W [128 x 64] + X [n_tile x 64] per stage, as many
-// stages as fit (4 at 256 rows, 8 at 64 rows or fewer).
-constexpr int kSwapThreads = 192;
-constexpr uint32_t kSwapRingBytes = kStages * kStageBytes;
-constexpr uint32_t kSwapTmemColumns = 256;
-
-struct SwapArgs {
-    CUtensorMap map_w;   // weights [n, k], box {64, 128}
-    CUtensorMap map_x;   // activation rows [rows, k] (row stride a_stride), box {64, n_tile}
-    int64_t k, rows, n, out_stride;
-    int n_tile;          // activation rows per MMA (multiple of 16, >= rows)
-    int splits;          // K splits (cluster size)
-    int k_per_split;     // K blocks per split
-    int pipe;            // stages in the ring
-    uint32_t stage_bytes;
-    const void *bias;
-    float *out;
-    int *status;
-    uint32_t idesc;
-};
-
-template <typename T>
-__global__ __launch_bounds__(kSwapThreads, 1) void dense_swap_kernel(const __grid_constant__ SwapArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw_addr = smem_addr(smem_raw);
-    uint8_t *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-    uint8_t *stages = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kSwapRingBytes);
-    uint64_t *empty = full + kMaxPipe;
-    uint64_t *acc_full = empty + kMaxPipe;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
-    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    pdl_trigger();
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int split = static_cast<int>(blockIdx.x % a.splits);
-    const int64_t m_tile = blockIdx.x / a.splits;
-    const int64_t k_blocks = (a.k + kBK - 1) / kBK;
-    const int64_t k_begin = static_cast<int64_t>(split) * a.k_per_split;
-    const int64_t k_end = min(k_blocks, k_begin + a.k_per_split);
-    constexpr uint32_t kWBytes = kBM * kBK * 2;
-
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < a.pipe; ++st) {
-            mbar_init(&full[st], 1);
-            mbar_init(&empty[st], 1);
-        }
-        mbar_init(&acc_full[0], 1);
-        *abort = 0;
-        fence_barrier_init();
-    }
-    if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(kSwapTmemColumns));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();  // the prologue above touched no global memory
-
-    if (warp == 0) {
-        if (lane == 0) {
-            prefetch_tensor_map(&a.map_w);
-            prefetch_tensor_map(&a.map_x);
-            int stage = 0;
-            uint32_t phase = 0;
-            for (int64_t kb = k_begin; kb < k_end; ++kb) {
-                if (!wait_or_abort(&empty[stage], phase ^ 1, abort, a.status)) break;
-                uint8_t *w_dst = stages + stage * a.stage_bytes;
-                mbar_arrive_expect_tx(&full[stage], a.stage_bytes);
-                const int32_t kc = static_cast<int32_t>(kb * kBK);
-                tma_load_2d(w_dst, &a.map_w, &full[stage], kc, static_cast<int32_t>(m_tile * kBM));
-                tma_load_2d(w_dst + kWBytes, &a.map_x, &full[stage], kc, 0);
-                if (++stage == a.pipe) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int64_t kb = k_begin; kb < k_end; ++kb) {
-                if (!wait_or_abort(&full[stage], phase, abort, a.status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t w_addr = smem_addr(stages + stage * a.stage_bytes);
-                const uint32_t x_addr = w_addr + kWBytes;
-#pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    umma_f16(tmem_base, sw128_kmajor_desc(w_addr + kk * 32), sw128_kmajor_desc(x_addr + kk * 32), a.idesc,
-                             (kb > k_begin || kk > 0) ? 1u : 0u);
-                }
-                umma_commit(&empty[stage]);
-                if (++stage == a.pipe) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-            }
-            if (ok) umma_commit(&acc_full[0]);
-        }
-        __syncwarp();
-    } else {
-        // warp w reads TMEM lanes 32 (w % 4) ..: weight row m of the tile;
-        // TMEM column r holds activation row r
-        const int quarter = warp & 3;
-        const int m = quarter * 32 + lane;
-        const int64_t col = m_tile * kBM + m;
-        if (wait_or_abort(&acc_full[0], 0, abort, a.status)) {
-            tc_fence_after();
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-            if (a.splits == 1) {
-                const float b = (a.bias != nullptr && col < a.n) ? to_acc(static_cast<const T *>(a.bias)[col]) : 0.0f;
-#pragma unroll 1
-                for (int c = 0; c * 32 < a.n_tile && c * 32 < a.rows; ++c) {
-                    uint32_t y[32];
-                    KOEMI_TMEM_LD32(taddr + c * 32, y);
-                    tmem_wait_ld();
-                    if (col < a.n) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int64_t r = c * 32 + j;
-                            if (r < a.rows) a.out[r * a.out_stride + col] = __uint_as_float(y[j]) + b;
-                        }
-                    }
-                }
-            } else {
-                float *parked = reinterpret_cast<float *>(stages) + m * (a.n_tile + 4);
-#pragma unroll 1
-                for (int c = 0; c * 32 < a.n_tile; ++c) {
-                    uint32_t y[32];
-                    KOEMI_TMEM_LD32(taddr + c * 32, y);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        // the parked row holds n_tile values (a chunk may run past them)
-                        if (c * 32 + 4 * q < a.n_tile) {
-                            reinterpret_cast<float4 *>(parked + c * 32)[q] =
-                                make_float4(__uint_as_float(y[4 * q]), __uint_as_float(y[4 * q + 1]),
-                                            __uint_as_float(y[4 * q + 2]), __uint_as_float(y[4 * q + 3]));
-                        }
-                    }
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (a.splits > 1) {
-        // every thread of every CTA reaches both cluster barriers, aborted or not
-        cluster_sync_all();
-        if (!*abort) {
-            const int64_t per = ((a.rows + a.splits - 1) / a.splits + 3) / 4 * 4;  // rows per split, whole quads
-            const int64_t r0 = split * per;
-            const int64_t r1 = min(a.rows, r0 + per);
-            const int64_t quads = r1 > r0 ? (r1 - r0 + 3) / 4 : 0;
-            const uint32_t parked_base = smem_addr(stages);
-            const uint32_t stride = static_cast<uint32_t>(a.n_tile + 4);
-            for (int64_t item = threadIdx.x; item < kBM * quads; item += kSwapThreads) {
-                const int mm = static_cast<int>(item % kBM);
-                const int64_t r = r0 + 4 * (item / kBM);
-                const int64_t c = m_tile * kBM + mm;
-                const uint32_t offset = parked_base + (static_cast<uint32_t>(mm) * stride + static_cast<uint32_t>(r)) * 4u;
-                float4 v[kMaxClusterSplits];
-#pragma unroll
-                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                    if (sp < a.splits) v[sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
-                }
-                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                    if (sp < a.splits) {
-                        acc.x += v[sp].x;
-                        acc.y += v[sp].y;
-                        acc.z += v[sp].z;
-                        acc.w += v[sp].w;
-                    }
-                }
-                if (c < a.n) {
-                    const float b = a.bias != nullptr ? to_acc(static_cast<const T *>(a.bias)[c]) : 0.0f;
-                    const float o[4] = {acc.x + b, acc.y + b, acc.z + b, acc.w + b};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (r + e < r1) a.out[(r + e) * a.out_stride + c] = o[e];
-                    }
-                }
-            }
-        }
-        cluster_sync_all();
-    }
-    if (warp == 1) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kSwapTmemColumns));
-    }
-}
-
 // ------------------------------------------------------------------- host
 
 uint32_t make_idesc(int dtype, int n = kBN) {
@@ -1302,8 +1092,12 @@ struct DensePlan {
 };
 // Measured alternatives that lost at decode sizes: full-K N = 64 / 128 tiles
 // without a reduction (every narrow tile re-reads all activation rows from L2:
-// gates 13.8 -> 17.0 us at 256 rows) and a push-style reduction through
-// distributed shared memory (13.8 -> 24.7 us).
+// gates 13.8 -> 17.0 us at 256 rows), a push-style reduction through
+// distributed shared memory (13.8 -> 24.7 us), and swapped operands (weight
+// rows as M = 128, activation rows as N): without K splits only n / 128 SMs
+// run the MMAs (gates 22.2 us at 256 rows), with splits the parked
+// accumulator is as large as here (gates 19.6 us at 256 rows, 9.0 us vs
+// 8.8 us at 32 rows).
 DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
     const int64_t k_blocks = (k + kBK - 1) / kBK;
     const int64_t wanted = dense_splits(rows, n, k);
@@ -1311,77 +1105,6 @@ DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
     return DensePlan{(k_blocks + per - 1) / per, per};
 }
 }  // namespace
-
-namespace {
-// K splits of the swapped projection: the largest S in {8, 4, 2} whose
-// m_tiles x S CTAs are resident in one wave of clusters of S and leave each
-// split at least four K blocks; else no split.
-int swap_splits(int64_t n, int64_t k) {
-    const int64_t m_tiles = (n + kBM - 1) / kBM;
-    const int64_t k_blocks = (k + kBK - 1) / kBK;
-    for (int splits : {8, 4, 2}) {
-        if (k_blocks < 4 * splits) continue;
-        if (m_tiles * splits <= resident_cluster_ctas(splits)) return splits;
-    }
-    return 1;
-}
-
-int launch_dense_swap(const void *a, int64_t a_stride, const void *weight, const void *bias, float *out,
-                      int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype, int splits,
-                      cudaStream_t stream) {
-    SwapArgs args{};
-    const CUtensorMapDataType type = dtype == KOEMI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const int n_tile = static_cast<int>((rows + 15) / 16 * 16);
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(rows)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(a_stride) * 2};
-        const uint32_t box[2] = {kBK, static_cast<uint32_t>(n_tile)};
-        int rc = encode_tensor_map(&args.map_x, type, 2, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (rc != KOEMI_OK) return rc;
-    }
-    int rc = encode_kmajor(&args.map_w, dtype, weight, n, k, kBM);
-    if (rc != KOEMI_OK) return rc;
-    const int64_t k_blocks = (k + kBK - 1) / kBK;
-    if (splits < 1) splits = swap_splits(n, k);
-    const int64_t per = (k_blocks + splits - 1) / splits;
-    splits = static_cast<int>((k_blocks + per - 1) / per);  // every split non-empty
-    args.k = k;
-    args.rows = rows;
-    args.n = n;
-    args.out_stride = out_stride;
-    args.n_tile = n_tile;
-    args.splits = splits;
-    args.k_per_split = static_cast<int>(per);
-    args.stage_bytes = static_cast<uint32_t>(kBM * kBK * 2 + n_tile * kBK * 2);
-    args.pipe = static_cast<int>(std::min<uint32_t>(kMaxPipe, kSwapRingBytes / args.stage_bytes));
-    args.bias = bias;
-    args.out = out;
-    args.status = device_status_word();
-    args.idesc = make_idesc(dtype, n_tile);
-    auto kernel = dtype == KOEMI_BF16 ? dense_swap_kernel<__nv_bfloat16> : dense_swap_kernel<__half>;
-    KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
-    const int64_t ctas = ((n + kBM - 1) / kBM) * splits;
-    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(kSwapThreads), kSmemBytes, stream,
-                              dim3(static_cast<unsigned>(splits), 1, 1), args));
-    KOEMI_LAUNCH_CHECK();
-    return KOEMI_OK;
-}
-}  // namespace
-
-extern "C" int koemi_dense_projection_swap(const void *a, int64_t a_stride, const void *weight, const void *bias,
-                                           float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k,
-                                           int dtype, int splits, void *stream) {
-    clear_error();
-    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "dense projection takes bf16 or f16 operands");
-    if (rows < 0 || rows > 256 || n < 1 || k < 1) return fail(KOEMI_ERR_INVALID, "the swapped projection takes 0..256 rows and positive n, k");
-    if (splits < 0 || splits > kMaxClusterSplits) return fail(KOEMI_ERR_INVALID, "splits must be 0 (automatic) .. %d", kMaxClusterSplits);
-    if (rows == 0) return KOEMI_OK;
-    if (k % 8 != 0 || a_stride < k || a_stride % 8 != 0 || !aligned(a, 16) || !aligned(weight, 16) ||
-        n >= (int64_t(1) << 31)) {
-        return fail(KOEMI_ERR_UNSUPPORTED, "dense projection needs K and the A row stride to be multiples of 8 and 16-byte aligned operands");
-    }
-    return launch_dense_swap(a, a_stride, weight, bias, out, out_stride, rows, n, k, dtype, splits, as_stream(stream));
-}
 
 extern "C" size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64_t k, int dtype) {
     // the K splits are reduced in distributed shared memory: no scratch

@@ -103,22 +103,47 @@ def test_fp32_greedy_decode_matches_reference(name, capture_graph):
 # fp32 reference's by ~1e-5, so positions whose reference surprise lies within
 # this distance of the threshold are left out of the exact admitted-set check.
 ADMISSION_MARGIN = 2e-4
+BF16_LOGIT_GATE = 2e-2
+
+
+def forced_decode(model, ids, forced, ring_dtype, watch_ids):
+    """Prefill, then one CUDA-graph step per column of ``forced`` fed with
+    the reference's tokens (teacher forcing): our greedy choice and the
+    logits at ``watch_ids`` [B, steps, n] at every step."""
+    decoder = BatchDecoder(model, capture_graph=True, ring_dtype=ring_dtype)
+    sampler = TokenSampler(SamplingPolicy(greedy=True), model.device)
+    logits = decoder.prefill(ids)
+    chosen, watched = [], []
+    for step in range(forced.shape[1]):
+        chosen.append(sampler(logits))
+        watched.append(logits.gather(1, watch_ids[:, step].to(logits.device)))
+        logits = decoder.step(forced[:, step:step + 1].to(logits.device))
+    return torch.cat(chosen, dim=1).cpu(), torch.stack(watched, dim=1).cpu(), decoder.state
 
 
 @pytest.mark.parametrize("name,ring_dtype", [("c5_small", torch.float32), ("c5_small", torch.bfloat16),
                                              ("c5_width", torch.float32), ("c5_width", torch.bfloat16)])
 def test_bf16_model_within_logit_gate(name, ring_dtype):
-    """The bf16 gate of the north star against the fp32 reference on the same
-    bf16-rounded weights: prefill logits within 2e-2 max-abs, hash routing
-    and admitted positions exact, and 64 greedy decode steps (CUDA graph)
-    with identical tokens, every step's logits at the reference's eight best
-    ids within 2e-2. c5_width is one block at config-5 width (d=2048, 64
-    experts top-2, vocabulary 32768, 128 + 128 slots, threshold 0.64)."""
+    """The bf16 gate against the fp32 reference on the same bf16-rounded
+    weights, prefill plus 64 decode steps (CUDA graph). c5_width is one block
+    at config-5 width (d=2048, 64 experts top-2, vocabulary 32768, 128 + 128
+    slots, threshold 0.64).
+
+    - prefill logits within 2e-2 max-abs; hash routing and the admitted
+      positions exact;
+    - teacher forced (the reference's tokens fed back), all 64 steps: the
+      logits at the reference's eight best ids within 2e-2, and our greedy
+      choice equal to the reference's wherever its top-2 margin exceeds twice
+      the largest logit error measured (elsewhere the two may differ without
+      any error beyond that bound);
+    - free running (our own greedy tokens fed back): the reference's tokens
+      up to each stream's first such near tie, all 64 where there is none.
+    """
     fx, model = build(name, compute_dtype="bfloat16")
     out = model(fx["ids"].cuda())
     pos = fx["logit_positions"]
     error = (out.logits[:, pos].cpu() - fx["logits"]).abs().max().item()
-    assert error <= 2e-2, error
+    assert error <= BF16_LOGIT_GATE, error
     assert torch.equal(out.expert_indices.cpu(), fx["expert_indices"])  # hash routing on ids
     threshold = fx["case"]["settings"]["salience_threshold"]
     reference_surprise = fx["surprise"]
@@ -127,15 +152,25 @@ def test_bf16_model_within_logit_gate(name, ring_dtype):
     mine = (out.surprise_values.cpu() > threshold) & valid
     theirs = (reference_surprise > threshold) & valid
     assert torch.equal(mine[decided], theirs[decided])
-    steps = fx["case"]["decode"]
+
+    reference = fx["decode_tokens"]
+    steps = reference.shape[1]
     assert steps == 64
-    tokens, first_logits, state, watched = greedy_decode(model, fx["ids"].cuda(), steps, capture_graph=True,
-                                                         ring_dtype=ring_dtype, watch_ids=fx["decode_top_ids"])
-    assert (first_logits.cpu() - fx["decode_logits"]).abs().max().item() <= 2e-2
-    assert (watched.cpu() - fx["decode_top_values"]).abs().max().item() <= 2e-2
-    assert torch.equal(tokens.cpu(), fx["decode_tokens"])
+    chosen, watched, state = forced_decode(model, fx["ids"].cuda(), reference, ring_dtype, fx["decode_top_ids"])
+    logit_error = (watched - fx["decode_top_values"]).abs().max().item()
+    assert logit_error <= BF16_LOGIT_GATE, logit_error
+    margins = fx["decode_top_values"][..., 0] - fx["decode_top_values"][..., 1]
+    near_tie = margins <= 2 * logit_error
+    assert torch.equal(chosen[~near_tie], reference[~near_tie])
     assert torch.equal(state.salient_valid.sum(1).cpu(), fx["decode_state"]["salient_valid"].sum(1))
     assert torch.equal(state.last_token_ids.cpu(), fx["decode_state"]["last_token_ids"])
+
+    tokens, _, _ = greedy_decode(model, fx["ids"].cuda(), steps, capture_graph=True, ring_dtype=ring_dtype)
+    tokens = tokens.cpu()
+    for stream in range(reference.shape[0]):
+        ties = torch.nonzero(near_tie[stream]).flatten()
+        agree_until = int(ties[0]) + 1 if ties.numel() else steps
+        assert torch.equal(tokens[stream, :agree_until], reference[stream, :agree_until]), (stream, agree_until)
 
 
 def test_sequential_mode_matches_parallel():

@@ -306,29 +306,3 @@ def test_combine_with_next_norm_equals_two_ops(with_next, out_dtype, cuda):
     assert torch.equal(got, expected)
 
 
-
-@pytest.mark.parametrize("rows,n,k,stride", [(256, 4096, 2048, 2048), (32, 4096, 2048, 2048), (1, 300, 64, 64),
-                                             (7, 6146, 2048, 8192), (100, 2048, 8192, 8192), (16, 10242, 2048, 2048),
-                                             (250, 1030, 512, 512)])
-@pytest.mark.parametrize("splits", [0, 1, 2, 4, 8])
-def test_swapped_projection_matches_fp64(rows, n, k, stride, splits, cuda):
-    """The swapped tcgen05 projection (weight rows as M, activation rows as N)
-    at every split count against fp64 on the same bf16 operands; repeated
-    calls are bit-identical (fixed-order cluster reduction)."""
-    from koemi_5hom_b200 import _native
-    g = torch.Generator(device=cuda).manual_seed(rows * 7 + n)
-    wide = torch.randn(rows, stride, generator=g, device=cuda).bfloat16()
-    a = wide[:, :k]
-    w = (torch.randn(n, k, generator=g, device=cuda) * k ** -0.5).bfloat16()
-    b = (torch.randn(n, generator=g, device=cuda) * 0.1).bfloat16()
-
-    def run():
-        out = torch.full((rows, n), float("nan"), device=cuda)
-        _native.call("koemi_dense_projection_swap", a.data_ptr(), stride, w.data_ptr(), b.data_ptr(), out.data_ptr(),
-                     n, rows, n, k, _native.BF16, splits, torch.cuda.current_stream(cuda).cuda_stream)
-        return out
-
-    out = run()
-    expected = a.double() @ w.double().T + b.double()
-    torch.testing.assert_close(out.double(), expected, rtol=1e-4, atol=1e-4)
-    assert torch.equal(out, run())
