@@ -547,6 +547,31 @@ KOEMI_API int koemi_ep_dispatch(const void *sorted_rows, const int64_t *sorted_e
                       const int64_t *segment_offsets, const uint64_t *peers, void *own, int64_t pairs,
                       int64_t width, int64_t rank, int64_t ranks, int64_t local_experts,
                       int64_t capacity, int dtype, void *stream);
+
+/* koemi_ep_dispatch fused with the row gather: slab row (g, j) is
+ * context[sorted_tokens[i]] (context [tokens, width] in f32 or the exchange
+ * dtype, converted to the exchange dtype on the way), so the sorted rows are
+ * never written locally. 16-bit exchange rows, width a multiple of 8. */
+KOEMI_API int koemi_ep_dispatch_gather(const void *context, int context_dtype, const int64_t *sorted_tokens,
+                                       const int64_t *sorted_experts, const int64_t *segment_offsets,
+                                       const uint64_t *peers, void *own, int64_t pairs, int64_t width, int64_t rank,
+                                       int64_t ranks, int64_t local_experts, int64_t capacity, int dtype,
+                                       void *stream);
+
+/* Owner side of an exchange in one launch: the bounded wait for every
+ * sender's flag, then the stable sort of the received slots ([sender][j]) by
+ * local expert and the gather of the live rows into expert-major order:
+ * sorted_rows [ranks * capacity, width] (rows past the live count are left
+ * as they were), segment_offsets [local_experts + 1], sorted_experts
+ * [ranks * capacity] (local_experts for empty slots) and positions
+ * [ranks * capacity] (sorted index of every slot). A wait that gives up
+ * records KOEMI_ERR_TIMEOUT and yields empty segments. At most 4096 slots and
+ * 255 local experts. Replaces koemi_ep_wait_dispatch plus a general
+ * permutation of the received rows. */
+KOEMI_API int koemi_ep_owner_sort(const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
+                                  int64_t local_experts, int64_t capacity, int dtype, void *sorted_rows,
+                                  int64_t *segment_offsets, int64_t *sorted_experts, int64_t *positions,
+                                  void *stream);
 KOEMI_API int koemi_ep_wait_dispatch(const void *own, int64_t ranks, void *stream);
 KOEMI_API int koemi_ep_return(const void *local_out, const int64_t *local_positions, const uint64_t *peers,
                     void *own, int64_t width, int64_t rank, int64_t ranks, int64_t local_experts,

@@ -107,6 +107,9 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_peer_buffer_close": (_int, (_p,)),
     "koemi_peer_buffer_free": (_int, (_p,)),
     "koemi_ep_dispatch": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_ep_dispatch_gather": (
+        _int, (_p, _int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_ep_owner_sort": (_int, (_p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _p, _p, _p, _p)),
     "koemi_ep_wait_dispatch": (_int, (_p, _i64, _p)),
     "koemi_ep_return": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_ep_collect": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),

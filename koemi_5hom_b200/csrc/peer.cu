@@ -15,6 +15,7 @@
 //   recv_ids   [ranks][capacity] int32    rows' owner-local expert ids (-1 padding)
 //   recv_rows  [ranks][capacity][width]   rows dispatched to this rank, block = sender
 //   ret_rows   [ranks][capacity][width]   outputs returned to this rank, block = owner
+#include <algorithm>
 #include <cstring>
 
 #include "vec.cuh"
@@ -139,6 +140,149 @@ __global__ void ep_dispatch_kernel(ExchangeArgs a, const T *__restrict__ sorted_
                            vector, lane);
     }
     signal_peers(a.own, a.peers, 0, a.rank, a.ranks, epoch, true);
+}
+
+// Sender, fused with the row gather: slab row (g, j) is token row
+// sorted_tokens[i] of `context` (converted to the exchange dtype T), stored
+// straight into owner g's recv block `rank`. Saves the gathered copy of the
+// sorted rows that the plain dispatch reads.
+template <typename TI, typename T>
+__global__ void ep_dispatch_gather_kernel(ExchangeArgs a, const TI *__restrict__ context,
+                                          const int64_t *__restrict__ sorted_tokens,
+                                          const int64_t *__restrict__ sorted_experts,
+                                          const int64_t *__restrict__ offsets) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(a.own)[kEpochSlot] + 1;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    constexpr int W = 8;  // 8 elements per packet on both sides (16 B of T = 16-bit, 32 B of fp32)
+    for (int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+         q < a.ranks * a.capacity; q += warps) {
+        const int64_t g = q / a.capacity;
+        const int64_t j = q - g * a.capacity;
+        const int64_t i = offsets[g * a.local_experts] + j;
+        const bool live = i < offsets[(g + 1) * a.local_experts];
+        uint8_t *peer = reinterpret_cast<uint8_t *>(a.peers[g]);
+        const int64_t slot = a.rank * a.capacity + j;
+        if (lane == 0) {
+            reinterpret_cast<int32_t *>(peer + a.ids)[slot] =
+                live ? static_cast<int32_t>(sorted_experts[i] - g * a.local_experts) : -1;
+        }
+        if (!live) continue;
+        const TI *src = context + sorted_tokens[i] * a.width;
+        T *dst = reinterpret_cast<T *>(peer + a.rows) + slot * a.width;
+        for (int64_t c = static_cast<int64_t>(lane) * W; c < a.width; c += 32 * W) {
+            float v[8];
+            if constexpr (sizeof(TI) == 4) {
+                const float4 lo = *reinterpret_cast<const float4 *>(src + c);
+                const float4 hi = *reinterpret_cast<const float4 *>(src + c + 4);
+                v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+                v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+            } else {
+                unpack(load_cached(src + c), v, TI());
+            }
+            *reinterpret_cast<uint4 *>(dst + c) = pack(v, T());
+        }
+    }
+    signal_peers(a.own, a.peers, 0, a.rank, a.ranks, epoch, true);
+}
+
+// Owner, fused: wait for every sender's rows, then (every CTA redundantly, in
+// shared memory) the stable counting sort of the received slots by local
+// expert -- slot order [sender][j], dead slots (id -1) last -- and each CTA
+// gathers its share of the live rows into expert-major order. CTA 0 writes
+// the segment offsets [local + 1], the sorted expert ids (local for dead
+// slots) and each slot's sorted position. Replaces the wait kernel, the
+// validity mask and the general permutation of the received rows.
+constexpr int kOwnerThreads = 512;
+constexpr int kOwnerWarps = kOwnerThreads / 32;
+constexpr int64_t kOwnerMaxSlots = 4096;
+constexpr int64_t kOwnerMaxExperts = 255;
+
+template <typename T>
+__global__ __launch_bounds__(kOwnerThreads) void ep_owner_sort_kernel(ExchangeArgs a, T *__restrict__ sorted_rows,
+                                                                      int64_t *__restrict__ offsets_out,
+                                                                      int64_t *__restrict__ experts_out,
+                                                                      int64_t *__restrict__ positions_out,
+                                                                      bool vector) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ int32_t shared[];
+    // a wait that gives up (status word set) sorts every slot as dead, so the
+    // outputs stay well formed: empty segments, no rows
+    const bool arrived = wait_flags(a.own, 0, a.ranks, a.status);
+    const int n = static_cast<int>(a.ranks * a.capacity);
+    const int buckets = static_cast<int>(a.local_experts) + 1;
+    int32_t *keys = shared;                       // [n]
+    int32_t *order = keys + n;                    // [n] slot at each sorted position
+    int32_t *running = order + n;                 // [buckets]
+    int32_t *warp_counts = running + buckets;     // [kOwnerWarps][buckets]
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int32_t *ids = reinterpret_cast<const int32_t *>(a.own + a.ids);
+    for (int b = threadIdx.x; b < buckets; b += kOwnerThreads) running[b] = 0;
+    for (int i = threadIdx.x; i < kOwnerWarps * buckets; i += kOwnerThreads) warp_counts[i] = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < n; q += kOwnerThreads) {
+        const int32_t id = arrived ? ids[q] : -1;
+        const int32_t key = id < 0 || id >= a.local_experts ? static_cast<int32_t>(a.local_experts) : id;
+        keys[q] = key;
+        atomicAdd(&running[key], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive scan (at most 256 buckets)
+        int32_t carry = 0;
+        for (int b = 0; b < buckets; ++b) {
+            const int32_t v = running[b];
+            running[b] = carry;
+            if (blockIdx.x == 0) offsets_out[b] = carry;
+            carry += v;
+        }
+    }
+    __syncthreads();
+    const unsigned lower = (1u << lane) - 1u;
+    for (int base = 0; base < n; base += kOwnerThreads) {
+        const int q = base + static_cast<int>(threadIdx.x);
+        const bool live = q < n;
+        const int32_t key = live ? keys[q] : 0;
+        const int digit = live ? key : -1 - lane;
+        const unsigned same = __match_any_sync(0xffffffffu, digit);
+        const int rank = __popc(same & lower);
+        if (live && (same & lower) == 0) warp_counts[warp * buckets + digit] = __popc(same);
+        __syncthreads();
+        if (live) {
+            int32_t before = 0;
+            for (int w = 0; w < warp; ++w) before += warp_counts[w * buckets + digit];
+            order[running[digit] + before + rank] = q;
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < buckets; b += kOwnerThreads) {
+            int32_t total = 0;
+            for (int w = 0; w < kOwnerWarps; ++w) {
+                total += warp_counts[w * buckets + b];
+                warp_counts[w * buckets + b] = 0;
+            }
+            running[b] += total;
+        }
+        __syncthreads();
+    }
+    // after the scatter, running[b] is the end of bucket b: the live rows end
+    // where the last expert's bucket does
+    const int32_t live_rows = running[a.local_experts - 1];
+    if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < n; i += kOwnerThreads) {
+            const int32_t q = order[i];
+            experts_out[i] = keys[q];
+            positions_out[q] = i;
+        }
+    }
+    // rows of sorted positions [0, live_rows): one warp per row, CTAs strided
+    const T *recv = reinterpret_cast<const T *>(a.own + a.rows);
+    const int64_t warps_total = static_cast<int64_t>(gridDim.x) * kOwnerWarps;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kOwnerWarps + warp; i < live_rows; i += warps_total) {
+        copy_row(sorted_rows + i * a.width, recv + static_cast<int64_t>(order[i]) * a.width, a.width, vector, lane);
+    }
 }
 
 // Owner: wait until every sender's rows of this exchange have landed.
@@ -345,4 +489,69 @@ extern "C" int koemi_ep_collect(const int64_t *sorted_experts, const int64_t *se
     }
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_dispatch_gather(const void *context, int context_dtype, const int64_t *sorted_tokens,
+                                        const int64_t *sorted_experts, const int64_t *segment_offsets,
+                                        const uint64_t *peers, void *own, int64_t pairs, int64_t width, int64_t rank,
+                                        int64_t ranks, int64_t local_experts, int64_t capacity, int dtype,
+                                        void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    if (capacity < pairs) return fail(KOEMI_ERR_INVALID, "capacity %lld is below the %lld pairs one owner may receive", (long long)capacity, (long long)pairs);
+    if (dtype == KOEMI_F32 || width % 8 != 0 || !aligned(context, 16) || context == nullptr || sorted_tokens == nullptr) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the gathering dispatch takes 16-bit exchange rows, width a multiple of 8 and 16-byte aligned context");
+    }
+    const unsigned blocks = exchange_blocks(ranks * capacity);
+    cudaStream_t s = as_stream(stream);
+#define KOEMI_DISPATCH_GATHER(TI, T) \
+    KOEMI_CUDA_TRY(launch_pdl(ep_dispatch_gather_kernel<TI, T>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a, \
+                              static_cast<const TI *>(context), sorted_tokens, sorted_experts, segment_offsets))
+    if (context_dtype == KOEMI_F32 && dtype == KOEMI_BF16) KOEMI_DISPATCH_GATHER(float, __nv_bfloat16);
+    else if (context_dtype == KOEMI_F32 && dtype == KOEMI_F16) KOEMI_DISPATCH_GATHER(float, __half);
+    else if (context_dtype == KOEMI_BF16 && dtype == KOEMI_BF16) KOEMI_DISPATCH_GATHER(__nv_bfloat16, __nv_bfloat16);
+    else if (context_dtype == KOEMI_F16 && dtype == KOEMI_F16) KOEMI_DISPATCH_GATHER(__half, __half);
+    else return fail(KOEMI_ERR_INVALID, "context dtype must be f32 or the exchange dtype");
+#undef KOEMI_DISPATCH_GATHER
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_ep_owner_sort(const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
+                                   int64_t local_experts, int64_t capacity, int dtype, void *sorted_rows,
+                                   int64_t *segment_offsets, int64_t *sorted_experts, int64_t *positions,
+                                   void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    const int64_t n = ranks * capacity;
+    if (n > kOwnerMaxSlots || local_experts > kOwnerMaxExperts) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the owner sort takes at most %lld slots and %lld local experts",
+                    (long long)kOwnerMaxSlots, (long long)kOwnerMaxExperts);
+    }
+    if (sorted_rows == nullptr || segment_offsets == nullptr || sorted_experts == nullptr || positions == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "owner sort outputs must be non-NULL");
+    }
+    const bool vector = (width * static_cast<int64_t>(dtype_size(dtype))) % 16 == 0 && aligned(sorted_rows, 16);
+    const int64_t buckets = local_experts + 1;
+    const size_t smem = static_cast<size_t>(2 * n + buckets * (kOwnerWarps + 1)) * sizeof(int32_t);
+    const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(64, ceil_div(n, 64))));
+    cudaStream_t s = as_stream(stream);
+    auto go = [&](auto kernel, auto *typed) -> int {
+        if (smem > 48 * 1024) {
+            KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        }
+        KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(kOwnerThreads), smem, s, dim3(1, 1, 1), a, typed,
+                                  segment_offsets, sorted_experts, positions, vector));
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    };
+    switch (dtype) {
+        case KOEMI_F32: return go(ep_owner_sort_kernel<float>, static_cast<float *>(sorted_rows));
+        case KOEMI_F16: return go(ep_owner_sort_kernel<__half>, static_cast<__half *>(sorted_rows));
+        default: return go(ep_owner_sort_kernel<__nv_bfloat16>, static_cast<__nv_bfloat16 *>(sorted_rows));
+    }
 }

@@ -297,13 +297,13 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             x = context
             continue
         if shared_route:
-            sorted_context = _ops.gather_rows(context, sorted_tokens, offsets, model.compute_dtype)
+            expert_out = model.expert_mlp_of_tokens(block, context, sorted_tokens, sorted_experts, offsets)
         else:
             gate_logits = model._linear(torch.where(valid.unsqueeze(-1), context, 0.0), block.router_weight, None)
             assignments, weights, _ = _ops.learned_topk(gate_logits, valid, s.expert_top_k, bool(s.router_renormalize))
             sorted_context, _, sorted_experts, offsets, positions = _ops.permute_topk(
                 context.to(model.compute_dtype), assignments, valid, s.expert_count, True)
-        expert_out = model.expert_mlp(block, sorted_context, sorted_experts, offsets, mode="padded")
+            expert_out = model.expert_mlp(block, sorted_context, sorted_experts, offsets, mode="padded")
         if fused_combine:
             last = index + 1 == len(model.blocks)
             next_norm = None if last else cache["blocks"][index + 1]["input_norm"]

@@ -141,6 +141,12 @@ def expert_parallel_mlp(shard: ExpertShard, sorted_rows: Tensor, sorted_experts:
     return out
 
 
+# limits of the one-launch owner sort (koemi_ep_owner_sort); larger exchanges
+# wait, then run the general permutation
+OWNER_SORT_MAX_SLOTS = 4096
+OWNER_SORT_MAX_EXPERTS = 255
+
+
 class _DeviceArray:
     """A raw device allocation seen by torch through __cuda_array_interface__."""
 
@@ -219,24 +225,46 @@ class PeerExchange:
             _native.check("koemi_peer_buffer_free", lib.koemi_peer_buffer_free(self.own))
             self.own = 0
 
-    def run(self, sorted_rows: Tensor, sorted_experts: Tensor, offsets: Tensor, weights: tuple[Tensor, ...]) -> Tensor:
+    def run(self, sorted_rows: Tensor | None, sorted_experts: Tensor, offsets: Tensor, weights: tuple[Tensor, ...],
+            *, context: Tensor | None = None, sorted_tokens: Tensor | None = None) -> Tensor:
         """The expert MLP of the global experts over this rank's sorted pairs,
-        through the owners (same contract as ``expert_parallel_mlp``)."""
+        through the owners (same contract as ``expert_parallel_mlp``). With
+        ``context`` and ``sorted_tokens`` instead of ``sorted_rows``, pair i's
+        row is ``context[sorted_tokens[i]]``, gathered by the dispatch itself."""
         from koemi_5hom_b200 import _native
         from koemi_5hom_b200.cuda_kernels import _ops
         shard = self.shard
-        pairs, width = sorted_rows.shape
-        if pairs > self.capacity or width != self.width or sorted_rows.dtype != self.dtype:
+        pairs = sorted_experts.shape[0]
+        width = self.width if sorted_rows is None else sorted_rows.shape[1]
+        if pairs > self.capacity or width != self.width or (sorted_rows is not None and sorted_rows.dtype != self.dtype):
             raise ValueError("rows do not fit this exchange")
-        sorted_rows, sorted_experts, offsets = (t.contiguous() for t in (sorted_rows, sorted_experts, offsets))
+        sorted_experts, offsets = sorted_experts.contiguous(), offsets.contiguous()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         code = _native.dtype_code(self.dtype)
         ptr, call = _native.ptr, _native.call
-        call("koemi_ep_dispatch", ptr(sorted_rows), ptr(sorted_experts), ptr(offsets), ptr(self.peers), self.own, pairs,
-             width, shard.rank, shard.world, shard.local_count, self.capacity, code, stream)
-        call("koemi_ep_wait_dispatch", self.own, shard.world, stream)
-        local_sorted, _, local_experts, local_offsets, local_positions = _ops.permute_topk(
-            self.recv_rows, self.recv_ids.view(-1, 1), self.recv_ids >= 0, shard.local_count, True)
+        if sorted_rows is None:
+            context, sorted_tokens = context.contiguous(), sorted_tokens.contiguous()
+            call("koemi_ep_dispatch_gather", ptr(context), _native.dtype_code(context.dtype), ptr(sorted_tokens),
+                 ptr(sorted_experts), ptr(offsets), ptr(self.peers), self.own, pairs, width, shard.rank, shard.world,
+                 shard.local_count, self.capacity, code, stream)
+        else:
+            sorted_rows = sorted_rows.contiguous()
+            call("koemi_ep_dispatch", ptr(sorted_rows), ptr(sorted_experts), ptr(offsets), ptr(self.peers), self.own,
+                 pairs, width, shard.rank, shard.world, shard.local_count, self.capacity, code, stream)
+        slots = shard.world * self.capacity
+        if slots <= OWNER_SORT_MAX_SLOTS and shard.local_count <= OWNER_SORT_MAX_EXPERTS:
+            # wait, sort by local expert and gather the received rows in one launch
+            local_sorted = torch.empty(slots, width, dtype=self.dtype, device=self.device)
+            local_offsets = torch.empty(shard.local_count + 1, dtype=torch.int64, device=self.device)
+            local_experts = torch.empty(slots, dtype=torch.int64, device=self.device)
+            local_positions = torch.empty(slots, dtype=torch.int64, device=self.device)
+            call("koemi_ep_owner_sort", ptr(self.peers), self.own, width, shard.rank, shard.world, shard.local_count,
+                 self.capacity, code, ptr(local_sorted), ptr(local_offsets), ptr(local_experts), ptr(local_positions),
+                 stream)
+        else:
+            call("koemi_ep_wait_dispatch", self.own, shard.world, stream)
+            local_sorted, _, local_experts, local_offsets, local_positions = _ops.permute_topk(
+                self.recv_rows, self.recv_ids.view(-1, 1), self.recv_ids >= 0, shard.local_count, True)
         local_out = _ops.grouped_expert_mlp(local_sorted, local_experts, local_offsets, *weights)
         call("koemi_ep_return", ptr(local_out), ptr(local_positions), ptr(self.peers), self.own, width, shard.rank,
              shard.world, shard.local_count, self.capacity, code, stream)

@@ -295,6 +295,21 @@ class KoemiModel(nn.Module):
         return expert_parallel_mlp(self.expert_shard, sorted_rows, sorted_experts, offsets, block.expert_weights(),
                                    mode)
 
+    def expert_mlp_of_tokens(self, block: HermBlock, context: Tensor, sorted_tokens: Tensor, sorted_experts: Tensor,
+                             offsets: Tensor) -> Tensor:
+        """Grouped expert MLP of the sorted pairs whose rows are
+        ``context[sorted_tokens]`` (decode: the shared permutation). Under the
+        peer exchange the row gather runs inside the dispatch; otherwise the
+        rows are gathered in the compute dtype first."""
+        width = context.shape[1]
+        if (self.expert_shard is not None and self.exchange == "peer" and width % 8 == 0
+                and self.compute_dtype != torch.float32 and context.dtype in (torch.float32, self.compute_dtype)):
+            exchange = self.peer_exchange(sorted_tokens.shape[0], width, self.compute_dtype)
+            return exchange.run(None, sorted_experts, offsets, block.expert_weights(), context=context,
+                                sorted_tokens=sorted_tokens)
+        rows = _ops.gather_rows(context, sorted_tokens, offsets, self.compute_dtype)
+        return self.expert_mlp(block, rows, sorted_experts, offsets, mode="padded")
+
     def peer_exchange(self, capacity: int, width: int, dtype: torch.dtype) -> PeerExchange:
         """The peer-memory exchange for decode-sized pair counts (created by
         all ranks together on first use, then reused by every block)."""

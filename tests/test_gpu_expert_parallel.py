@@ -38,10 +38,13 @@ def test_slab_pack_and_unpack_match_oracle(ranks, local, tokens, top_k, dtype, c
     assert torch.equal(back.cpu(), ops.ep_unpack(returned, sorted_experts, offsets, ranks, local, capacity))
 
 
-@pytest.mark.parametrize("tokens,experts,steps", [(64, 8, 3), (256, 64, 2), (5, 4, 1)])
-def test_peer_exchange_with_itself_equals_grouped_mlp(tokens, experts, steps, cuda):
+@pytest.mark.parametrize("tokens,experts,steps", [(64, 8, 3), (256, 64, 2), (5, 4, 1), (2100, 8, 2)])
+@pytest.mark.parametrize("gathered", [False, True])
+def test_peer_exchange_with_itself_equals_grouped_mlp(tokens, experts, steps, gathered, cuda):
     """One rank exchanging with its own buffer runs every peer kernel
-    (dispatch, flag wait, return, collect) on one GPU, repeatedly (epochs)."""
+    (dispatch -- plain, or gathering fp32 token rows --, the one-launch owner
+    sort, or past 4096 slots the wait + general permutation, return, collect)
+    on one GPU, repeatedly (epochs)."""
     from koemi_5hom_b200 import _native
     from koemi_5hom_b200.model.expert_parallel import ExpertShard, PeerExchange
     g = torch.Generator().manual_seed(tokens)
@@ -52,12 +55,18 @@ def test_peer_exchange_with_itself_equals_grouped_mlp(tokens, experts, steps, cu
     exchange = PeerExchange(ExpertShard(1, 0, experts), tokens * 2, width, torch.bfloat16, cuda)
     try:
         for step in range(steps):
-            rows = torch.randn(tokens, width, generator=g).bfloat16().to(cuda)
+            context = torch.randn(tokens, width, generator=g).to(cuda)
+            rows = context.bfloat16()
             assignments = torch.randint(-1, experts, (tokens, 2), generator=g).to(cuda)
             valid = torch.ones(tokens, dtype=torch.bool, device=cuda)
-            sorted_rows, _, sorted_experts, offsets, _ = _ops.permute_topk(rows, assignments, valid, experts, True)
+            sorted_rows, sorted_tokens, sorted_experts, offsets, _ = _ops.permute_topk(rows, assignments, valid,
+                                                                                       experts, True)
             expected = _ops.grouped_expert_mlp(sorted_rows, sorted_experts, offsets, *weights)
-            got = exchange.run(sorted_rows, sorted_experts, offsets, weights)
+            if gathered:
+                got = exchange.run(None, sorted_experts, offsets, weights, context=context,
+                                   sorted_tokens=sorted_tokens)
+            else:
+                got = exchange.run(sorted_rows, sorted_experts, offsets, weights)
             torch.cuda.synchronize()
             assert _native.device_status(cuda) == 0
             assert torch.equal(got, expected), step
