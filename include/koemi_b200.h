@@ -166,7 +166,8 @@ KOEMI_API int koemi_dense_decode_step(const float *projections, const uint8_t *v
  * read_out fp32 [batch, length, width]; features, query_features fp32
  * [batch, length, feature_count]; basis fp32 [batch, width, feature_count]
  * (16-byte aligned), normaliser fp32 [batch, feature_count]. feature_count
- * must be 16. Replaces the window read of
+ * must be 4, 8, 16 or 32 (other counts up to 32 run zero-padded to the next
+ * of these: a zero feature never writes nor reads). Replaces the window read of
  * HierarchicalAssociativeMemory.scan_and_read (model/memory.py:97-144,146-242). */
 KOEMI_API int koemi_assoc_window_scan_read(const float *decay, const float *write, const float *value,
                                            const float *features, const float *query_features, float *basis,

@@ -23,14 +23,22 @@ namespace koemi {
 namespace {
 
 constexpr int kWindowThreads = 256;
-constexpr int kWindowChunk = 64;
 constexpr float kReadEpsilon = 1.0f / 256.0f;
+
+// Positions staged per chunk: 64, or 32 for 4 features (256 rows per CTA
+// then, and the staged values must stay within the static shared memory).
+template <int kM>
+constexpr int window_chunk() {
+    return kM >= 8 ? 64 : 32;
+}
 
 template <int kM>
 __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
     const float *__restrict__ decay, const float *__restrict__ write, const float *__restrict__ value,
     const float *__restrict__ features, const float *__restrict__ query_features, float *__restrict__ basis,
     float *__restrict__ normalizer, float *__restrict__ read_out, int64_t length, int64_t d) {
+    static_assert(kM % 4 == 0 && kM <= 32 && 32 % (kM / 4) == 0, "4, 8, 16 or 32 features");
+    constexpr int kWindowChunk = window_chunk<kM>();
     constexpr int kParts = kM / 4;
     constexpr int kRows = kWindowThreads / kParts;
     __shared__ __align__(16) float sf[kWindowChunk][kM];
@@ -109,18 +117,26 @@ extern "C" int koemi_assoc_window_scan_read(const float *decay, const float *wri
     clear_error();
     if (batch < 0 || length < 0 || width < 0) return fail(KOEMI_ERR_INVALID, "negative associative window sizes");
     if (batch == 0 || length == 0 || width == 0) return KOEMI_OK;
-    if (feature_count != 16) {
-        return fail(KOEMI_ERR_UNSUPPORTED, "the window associative kernel is built for 16 memory features (got %lld)",
-                    static_cast<long long>(feature_count));
+    if (feature_count != 4 && feature_count != 8 && feature_count != 16 && feature_count != 32) {
+        return fail(KOEMI_ERR_UNSUPPORTED,
+                    "the window associative kernel is built for 4, 8, 16 or 32 memory features (got %lld); "
+                    "pad the features with zeros to the next of these", static_cast<long long>(feature_count));
     }
     if (!aligned(basis, 16)) return fail(KOEMI_ERR_INVALID, "basis must be 16-byte aligned");
     if (batch > 2147483647) return fail(KOEMI_ERR_INVALID, "too many streams");
-    constexpr int kRows = kWindowThreads / (16 / 4);
-    const int64_t blocks_y = ceil_div(width, kRows);
-    if (blocks_y > 65535) return fail(KOEMI_ERR_INVALID, "width too large");
-    assoc_window_kernel<16><<<dim3(static_cast<unsigned>(batch), static_cast<unsigned>(blocks_y)), kWindowThreads, 0,
-                             as_stream(stream)>>>(decay, write, value, features, query_features, basis, normalizer,
-                                                  read_out, length, width);
-    KOEMI_LAUNCH_CHECK();
-    return KOEMI_OK;
+    auto run = [&](auto kernel, int rows_per_cta) -> int {
+        const int64_t blocks_y = ceil_div(width, rows_per_cta);
+        if (blocks_y > 65535) return fail(KOEMI_ERR_INVALID, "width too large");
+        kernel<<<dim3(static_cast<unsigned>(batch), static_cast<unsigned>(blocks_y)), kWindowThreads, 0,
+                 as_stream(stream)>>>(decay, write, value, features, query_features, basis, normalizer, read_out,
+                                      length, width);
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    };
+    switch (feature_count) {
+        case 4: return run(assoc_window_kernel<4>, kWindowThreads / 1);
+        case 8: return run(assoc_window_kernel<8>, kWindowThreads / 2);
+        case 16: return run(assoc_window_kernel<16>, kWindowThreads / 4);
+        default: return run(assoc_window_kernel<32>, kWindowThreads / 8);
+    }
 }

@@ -654,13 +654,27 @@ def _salient_read(carried_keys, carried_values, carried_valid, keys, values, adm
     return torch.einsum("bts,bsd->btd", weights, all_values)
 
 
+_WINDOW_FEATURE_COUNTS = (4, 8, 16, 32)
+
+
 def _associative_scan_read(basis, normalizer, decay, value, features, write, query_features):
     """Rank-one decayed memory over one window: the native sequential kernel
-    (koemi_assoc_window_scan_read) for 16 memory features on CUDA, else the
-    closed form below."""
-    if value.is_cuda and features.shape[-1] == 16:
+    (koemi_assoc_window_scan_read) on CUDA for up to 32 memory features, else
+    the closed form below. Feature counts between the kernel's sizes (4, 8,
+    16, 32) run zero-padded: a zero feature column never writes the basis or
+    the normaliser and adds nothing to a read, so the padded columns stay zero
+    and are dropped afterwards."""
+    m = features.shape[-1]
+    if not value.is_cuda or m > _WINDOW_FEATURE_COUNTS[-1]:
+        return _associative_scan_read_closed_form(basis, normalizer, decay, value, features, write, query_features)
+    size = next(c for c in _WINDOW_FEATURE_COUNTS if c >= m)
+    if size == m:
         return _ops.assoc_window_scan_read(basis, normalizer, decay, value, features, write, query_features)
-    return _associative_scan_read_closed_form(basis, normalizer, decay, value, features, write, query_features)
+    pad = (0, size - m)
+    read, padded_basis, padded_normalizer = _ops.assoc_window_scan_read(
+        torch.nn.functional.pad(basis, pad), torch.nn.functional.pad(normalizer, pad), decay, value,
+        torch.nn.functional.pad(features, pad), write, torch.nn.functional.pad(query_features, pad))
+    return read, padded_basis[..., :m].contiguous(), padded_normalizer[..., :m].contiguous()
 
 
 def _associative_scan_read_closed_form(basis, normalizer, decay, value, features, write, query_features):

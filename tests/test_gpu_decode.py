@@ -267,15 +267,16 @@ def test_state_round_trip_through_decode_state(cuda):
         assert torch.equal(mk, rk) and torch.equal(mv, rv)
 
 
-@pytest.mark.parametrize("batch,length,d", [(3, 70, 256), (2, 200, 100), (4, 1, 64), (5, 129, 2048)])
-def test_window_associative_kernel_matches_oracle(batch, length, d, cuda):
+@pytest.mark.parametrize("batch,length,d,m", [(3, 70, 256, 16), (2, 200, 100, 16), (4, 1, 64, 16), (5, 129, 2048, 16),
+                                              (3, 70, 256, 4), (2, 90, 300, 8), (2, 70, 256, 32), (3, 65, 128, 12),
+                                              (2, 40, 96, 20), (1, 33, 64, 5)])
+def test_window_associative_kernel_matches_oracle(batch, length, d, m, cuda):
     """Prefill (window) associative read and update, fp32, against the oracle's
     sequential form; padded positions carry decay 1 and write 0 as the model
     passes them."""
     from oracle.herm import HermOracle
     from koemi_5hom_b200.cuda_kernels import _ops
-    g = torch.Generator().manual_seed(batch * 1000 + length)
-    m = 16
+    g = torch.Generator().manual_seed(batch * 1000 + length + m)
     basis = torch.randn(batch, d, m, generator=g) * 0.1
     normalizer = torch.rand(batch, m, generator=g)
     decay = 2.0 ** -12 + (1 - 2.0 ** -11) * torch.sigmoid(torch.randn(batch, length, generator=g))
@@ -286,7 +287,10 @@ def test_window_associative_kernel_matches_oracle(batch, length, d, cuda):
     features = torch.softmax(torch.randn(batch, length, m, generator=g), -1)
     query = torch.softmax(torch.randn(batch, length, m, generator=g), -1)
     inputs = (basis, normalizer, decay, value, features, write, query)
-    read, new_basis, new_norm = _ops.assoc_window_scan_read(*(t.to(cuda) for t in inputs))
+    from koemi_5hom_b200.model.network import _associative_scan_read
+    # 4, 8, 16, 32 features run the kernel directly, other counts zero-padded
+    read, new_basis, new_norm = _associative_scan_read(*(t.to(cuda) for t in inputs))
+    assert new_basis.shape == basis.shape and new_norm.shape == normalizer.shape
     expected = HermOracle._scan_read(None, *(t.double() for t in inputs))
     torch.testing.assert_close(read.cpu().double(), expected[0], rtol=1e-4, atol=1e-6)
     torch.testing.assert_close(new_basis.cpu().double(), expected[1], rtol=1e-5, atol=1e-6)

@@ -79,9 +79,9 @@ def test_sampler_and_window_memory_reject_bad_arguments_on_the_host():
     lib = _native.library()
     assert lib.koemi_sampler_greedy(None, 4, 0, 0, 256, None, None) == _native.KOEMI_ERR_INVALID
     assert lib.koemi_sampler_greedy(None, 0, 10, 10, 256, None, None) == _native.KOEMI_OK  # no rows
-    status = lib.koemi_assoc_window_scan_read(None, None, None, None, None, None, None, None, 2, 5, 64, 8, None)
-    assert status == _native.KOEMI_ERR_UNSUPPORTED
-    assert "16 memory features" in _native.last_error()
+    status = lib.koemi_assoc_window_scan_read(None, None, None, None, None, None, None, None, 2, 5, 64, 12, None)
+    assert status == _native.KOEMI_ERR_UNSUPPORTED  # the model pads 12 features to 16 before calling
+    assert "4, 8, 16 or 32 memory features" in _native.last_error()
 
 
 def test_last_error_is_truncated_safely():
