@@ -370,6 +370,23 @@ def measure_expert_mlp(model, args, world: int, repeats: int = 20) -> dict:
     return {"seconds": seconds, "bytes": algorithmic, "touched_experts": touched, "pairs": pairs}
 
 
+def prefill_roofline(args, streams: int, seconds: float, world: int) -> dict:
+    """Prefill rate and its fraction of the tensor-core bound: per token and
+    block the surprise head (2 d C), the two expert pairs (2 x 6 d d_ff) and the
+    dense projections (gates 4 d^2, local 4 d^2, associative 2 (3d + 2) d,
+    fusion 8 d^2) in FLOPs, at the sustained bf16 peak of every GPU."""
+    d, c = args.width, args.vocab - 1
+    per_token_block = 2 * d * c + args.top_k * 6 * d * (2 * d) + (4 + 4 + 8) * d * d + 2 * (3 * d + 2) * d
+    tokens = streams * args.prompt_len
+    flop = per_token_block * args.layers * tokens
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    peak = peaks.get("bf16_tflops_sustained", 1409.6) * 1e12 * world
+    return {"tokens_per_s": tokens / seconds, "tensor_flop": flop, "bound_s": flop / peak,
+            "frac_of_tensor_bound": flop / peak / seconds,
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback 1409.6 TFLOP/s"}
+
+
 def progress(rank: int, message: str) -> None:
     """Timestamped, rank-tagged progress on stderr (the JSON line stays alone on stdout)."""
     print(f"[bench rank {rank} {time.strftime('%H:%M:%S')}] {message}", file=sys.stderr, flush=True)
@@ -518,6 +535,7 @@ def run_b200(args) -> None:
                      "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
                      "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},
         "prefill_s": prefill_seconds,
+        "prefill": prefill_roofline(args, per_rank * world, prefill_seconds, world),
         "sampled": {"policy": "temperature 0.8, seeded per stream (native Gumbel-max)",
                     "value": per_rank * world * args.steps / sampled_seconds,
                     "ms_per_step": sampled_seconds / args.steps * 1000.0},
