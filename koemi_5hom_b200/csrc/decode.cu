@@ -316,229 +316,6 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
     if (threadIdx.x == 0) (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
 }
 
-// One CTA per stream for batches that fill the GPU, both rings in turn, each
-// in ONE streaming pass: rounds of kBatch slots, every thread loading its
-// packets of the rounds' keys and values together, then an online softmax
-// (running maximum, rescaled sums) so no pass waits for the whole ring's
-// maximum. The two-pass kernel above stalls every CTA between its key and
-// value passes at the same moment (all CTAs run in lockstep), which leaves
-// HBM idle; here each round costs one block barrier and keeps 64 KB in
-// flight per CTA. Same results up to the fp32 summation order.
-constexpr int kStreamThreads = 256;
-constexpr int kStreamWarps = kStreamThreads / 32;
-
-template <typename TR>
-__device__ __forceinline__ void unpack_ring(const uint4 &raw, float (&v)[RingPacket<TR>::kWidth]);
-template <>
-__device__ __forceinline__ void unpack_ring<float>(const uint4 &raw, float (&v)[4]) {
-    v[0] = __uint_as_float(raw.x);
-    v[1] = __uint_as_float(raw.y);
-    v[2] = __uint_as_float(raw.z);
-    v[3] = __uint_as_float(raw.w);
-}
-template <>
-__device__ __forceinline__ void unpack_ring<__nv_bfloat16>(const uint4 &raw, float (&v)[8]) {
-    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-    }
-}
-
-template <typename TR, typename TO, int PPT>
-__global__ __launch_bounds__(kStreamThreads, 2) void ring_decode_stream_kernel(RingArgs a) {
-    pdl_trigger();
-    pdl_wait();
-    using P = RingPacket<TR>;
-    constexpr int W = P::kWidth;
-    constexpr int kBatch = 8 / PPT;  // slots per round (64 KB of keys and values per CTA at 2048 bf16 columns)
-    __shared__ float partial[2][kStreamWarps][2 * kBatch];  // per-warp dot and |k|^2, double buffered
-    __shared__ float scratch[kStreamWarps];
-    __shared__ int32_t write_slot;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t b = blockIdx.x;
-    const int64_t d = a.width;
-    const int64_t packets = d / W;
-    const float scale = rsqrtf(static_cast<float>(d));
-
-    // this thread's packets of the query (fp32) and |q|^2
-    const float *query = a.queries + b * a.query_stride;
-    float q[PPT][W];
-    float qq = 0.0f;
-#pragma unroll
-    for (int j = 0; j < PPT; ++j) {
-        const int64_t pk = threadIdx.x + static_cast<int64_t>(j) * kStreamThreads;
-#pragma unroll
-        for (int e = 0; e < W; ++e) {
-            q[j][e] = pk < packets ? query[pk * W + e] : 0.0f;
-            qq = fmaf(q[j][e], q[j][e], qq);
-        }
-    }
-    qq = warp_sum(qq);
-    if (lane == 0) scratch[warp] = qq;
-    __syncthreads();
-    float total_qq = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kStreamWarps; ++w) total_qq += scratch[w];
-    const float q_norm = fmaxf(sqrtf(total_qq), 1e-12f);
-    const bool token_valid = a.valid == nullptr || a.valid[b] != 0;
-    int round = 0;
-
-    for (int ring = 0; ring < 2; ++ring) {
-        const bool local = ring == 0;
-        const int64_t slots = local ? a.local_slots : a.salient_slots;
-        TR *keys = static_cast<TR *>(local ? a.local_keys : a.salient_keys) + b * slots * d;
-        TR *values = static_cast<TR *>(local ? a.local_values : a.salient_values) + b * slots * d;
-        const uint8_t *flags = (local ? a.local_valid : a.salient_valid) + b * slots;
-        float acc[PPT][W];
-#pragma unroll
-        for (int j = 0; j < PPT; ++j) {
-#pragma unroll
-            for (int e = 0; e < W; ++e) acc[j][e] = 0.0f;
-        }
-        float run_max = -INFINITY, run_sum = 0.0f, best_cos = -INFINITY;
-
-        for (int64_t s0 = 0; s0 < slots; s0 += kBatch, ++round) {
-            uint4 kraw[kBatch][PPT], vraw[kBatch][PPT];
-            bool on[kBatch];
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                const int64_t slot = s0 + u;
-                on[u] = slot < slots && flags[slot] != 0;
-#pragma unroll
-                for (int j = 0; j < PPT; ++j) {
-                    const int64_t pk = threadIdx.x + static_cast<int64_t>(j) * kStreamThreads;
-                    if (on[u] && pk < packets) {
-                        kraw[u][j] = __ldg(reinterpret_cast<const uint4 *>(keys + slot * d + pk * W));
-                        vraw[u][j] = __ldg(reinterpret_cast<const uint4 *>(values + slot * d + pk * W));
-                    } else {
-                        kraw[u][j] = make_uint4(0u, 0u, 0u, 0u);
-                        vraw[u][j] = make_uint4(0u, 0u, 0u, 0u);
-                    }
-                }
-            }
-            float red[2 * kBatch];
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                float dot = 0.0f, kk = 0.0f;
-#pragma unroll
-                for (int j = 0; j < PPT; ++j) {
-                    float k[W];
-                    unpack_ring<TR>(kraw[u][j], k);
-#pragma unroll
-                    for (int e = 0; e < W; ++e) {
-                        dot = fmaf(k[e], q[j][e], dot);
-                        kk = fmaf(k[e], k[e], kk);
-                    }
-                }
-                red[u] = warp_sum(dot);
-                red[kBatch + u] = warp_sum(kk);
-            }
-            float(*slot_partial)[2 * kBatch] = partial[round & 1];
-            if (lane == 0) {
-#pragma unroll
-                for (int i = 0; i < 2 * kBatch; ++i) slot_partial[warp][i] = red[i];
-            }
-            __syncthreads();
-            float score[kBatch];
-            float round_max = -INFINITY;
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                float dot = 0.0f, kk = 0.0f;
-#pragma unroll
-                for (int w = 0; w < kStreamWarps; ++w) {
-                    dot += slot_partial[w][u];
-                    kk += slot_partial[w][kBatch + u];
-                }
-                score[u] = on[u] ? dot * scale : -INFINITY;
-                if (on[u]) best_cos = fmaxf(best_cos, dot / (fmaxf(sqrtf(kk), 1e-12f) * q_norm));
-                round_max = fmaxf(round_max, score[u]);
-            }
-            if (round_max == -INFINITY) continue;  // no valid slot in this round
-            const float new_max = fmaxf(run_max, round_max);
-            const float rescale = run_max == -INFINITY ? 0.0f : expf(run_max - new_max);
-            run_sum *= rescale;
-#pragma unroll
-            for (int j = 0; j < PPT; ++j) {
-#pragma unroll
-                for (int e = 0; e < W; ++e) acc[j][e] *= rescale;
-            }
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                if (!on[u]) continue;
-                const float wgt = expf(score[u] - new_max);
-                run_sum += wgt;
-#pragma unroll
-                for (int j = 0; j < PPT; ++j) {
-                    float v[W];
-                    unpack_ring<TR>(vraw[u][j], v);
-#pragma unroll
-                    for (int e = 0; e < W; ++e) acc[j][e] = fmaf(wgt, v[e], acc[j][e]);
-                }
-            }
-            run_max = new_max;
-        }
-
-        const bool any = run_max != -INFINITY;
-        const float inv = any ? 1.0f / run_sum : 0.0f;
-        TO *out = static_cast<TO *>(local ? a.local_out : a.salient_out) + b * a.out_stride;
-#pragma unroll
-        for (int j = 0; j < PPT; ++j) {
-            const int64_t pk = threadIdx.x + static_cast<int64_t>(j) * kStreamThreads;
-            if (pk < packets) {
-#pragma unroll
-                for (int e = 0; e < W; ++e) out[pk * W + e] = from_acc<TO>(acc[j][e] * inv);
-            }
-        }
-        if (local && threadIdx.x == 0 && a.novelty_out != nullptr) {
-            a.novelty_out[b] = any ? fminf(fmaxf(1.0f - best_cos, 0.0f), 1.0f) : 1.0f;
-        }
-        // the ring write, after every thread's last read of this ring (each
-        // round's loads were consumed before that round's barrier)
-        if (threadIdx.x == 0) {
-            if (local) {
-                write_slot = static_cast<int32_t>(*a.local_head);
-            } else {
-                const bool admitted = token_valid && a.surprise[b] > a.threshold;
-                if (a.admission_out != nullptr) a.admission_out[b] = admitted;
-                write_slot = -1;
-                if (admitted) {
-                    const int32_t head = a.salient_head[b];
-                    const int32_t count = a.salient_count[b];
-                    if (count < slots) {
-                        write_slot = static_cast<int32_t>((head + count) % slots);
-                        a.salient_count[b] = count + 1;
-                    } else {
-                        write_slot = head;
-                        a.salient_head[b] = static_cast<int32_t>((head + 1) % slots);
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        const int32_t slot = write_slot;
-        if (slot >= 0) {
-            TR *key_dst = keys + slot * d;
-            TR *value_dst = values + slot * d;
-            const float *entry = a.entries + b * a.entry_stride;
-            for (int64_t c = threadIdx.x; c < packets; c += kStreamThreads) {
-                float k[W], v[W];
-#pragma unroll
-                for (int e = 0; e < W; ++e) {
-                    k[e] = token_valid ? entry[c * W + e] : 0.0f;
-                    v[e] = token_valid ? entry[d + c * W + e] : 0.0f;
-                }
-                P::store(key_dst + c * W, k);
-                P::store(value_dst + c * W, v);
-            }
-            if (threadIdx.x == 0) (local ? a.local_valid : a.salient_valid)[b * slots + slot] = local ? token_valid : 1;
-        }
-        __syncthreads();  // write_slot and the partial buffers are reused by the next ring
-    }
-}
-
 // The same step with each (stream, ring) split over a thread-block cluster of
 // gridDim.z CTAs, for batches too small to fill the GPU with one CTA per
 // ring: CTA p scores slots [p S / P, (p + 1) S / P) and sums their weighted
@@ -1260,31 +1037,6 @@ extern "C" int koemi_think_ring_decode_step(
             case KOEMI_F16: return bf16_ring ? run_split(ring_decode_split_kernel<__nv_bfloat16, __half>) : run_split(ring_decode_split_kernel<float, __half>);
             default: return fail(KOEMI_ERR_INVALID, "ring outputs must be f32, f16 or bf16");
         }
-    }
-    // enough streams to fill the GPU: one CTA per stream, one pass per ring
-    const int64_t packets = width / packet;
-    if (packets <= 2 * kStreamThreads && batch >= sm_count()) {
-        const bool wide = packets > kStreamThreads;
-        auto run_stream = [&](auto narrow_kernel, auto wide_kernel) -> int {
-            if (wide) {
-                KOEMI_CUDA_TRY(launch_pdl(wide_kernel, dim3(static_cast<unsigned>(batch)), dim3(kStreamThreads), 0, s,
-                                          dim3(1, 1, 1), args));
-            } else {
-                KOEMI_CUDA_TRY(launch_pdl(narrow_kernel, dim3(static_cast<unsigned>(batch)), dim3(kStreamThreads), 0, s,
-                                          dim3(1, 1, 1), args));
-            }
-            KOEMI_LAUNCH_CHECK();
-            return KOEMI_OK;
-        };
-        const bool bf16 = ring_dtype == KOEMI_BF16;
-#define KOEMI_RING_STREAM(TR, TO) run_stream(ring_decode_stream_kernel<TR, TO, 1>, ring_decode_stream_kernel<TR, TO, 2>)
-        switch (out_dtype) {
-            case KOEMI_F32: return bf16 ? KOEMI_RING_STREAM(__nv_bfloat16, float) : KOEMI_RING_STREAM(float, float);
-            case KOEMI_BF16: return bf16 ? KOEMI_RING_STREAM(__nv_bfloat16, __nv_bfloat16) : KOEMI_RING_STREAM(float, __nv_bfloat16);
-            case KOEMI_F16: return bf16 ? KOEMI_RING_STREAM(__nv_bfloat16, __half) : KOEMI_RING_STREAM(float, __half);
-            default: return fail(KOEMI_ERR_INVALID, "ring outputs must be f32, f16 or bf16");
-        }
-#undef KOEMI_RING_STREAM
     }
     auto run = [&](auto kernel) -> int {
         if (smem > 48 * 1024) {
