@@ -46,9 +46,12 @@ def _logical_salient(sk, sv, head, count, slots):
 
 
 @pytest.mark.parametrize("ring_dtype", [torch.float32, torch.bfloat16])
+# >= 148 streams take the one-CTA-per-(stream, ring) kernel, fewer the
+# cluster-split kernel
 @pytest.mark.parametrize("batch,width,local_slots,salient_slots", [(7, 64, 16, 12), (256, 2048, 128, 128),
                                                                    (3, 128, 5, 9), (16, 256, 128, 128),
-                                                                   (37, 512, 64, 128), (32, 2048, 128, 128)])
+                                                                   (37, 512, 64, 128), (32, 2048, 128, 128),
+                                                                   (160, 4096, 16, 8), (200, 1000, 24, 40)])
 def test_ring_decode_step_matches_oracle(batch, width, local_slots, salient_slots, ring_dtype, cuda):
     c = _ring_case(batch, width, local_slots, salient_slots, seed=width)
     # the kernel reads stored (possibly bf16) rows and computes in fp32, so the
