@@ -528,9 +528,10 @@ def run_b200(args) -> None:
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s",
                      "unit": "GB/s", "frac": achieved / hbm_peak,
                      # dram__bytes_read.sum + dram__bytes_write.sum of both expert GEMMs for one call at this
-                     # workload's pair distribution, from one ncu capture of `--op expert_decode`; none was taken
+                     # workload's pair distribution (512 pairs, 64 experts), from one ncu capture of
+                     # `bench.py --op expert_decode` (profiles/expert_mlp_decode_config5.md); none was taken
                      # of an expert-parallel owner's share
-                     "traffic": 3.249e9 if not expert_parallel(args, world) else None,
+                     "traffic": 3246450432 if not expert_parallel(args, world) else None,
                      "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
                      "touched_experts": mlp["touched_experts"], "pairs": mlp["pairs"]},

@@ -160,18 +160,31 @@ __global__ __launch_bounds__(kSortThreads) void digit_count_kernel(const int32_t
     }
 }
 
-// Exclusive scan of the bucket-major counts array in place (one CTA).
-__global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restrict__ data, int64_t n) {
+// Exclusive scan of the bucket-major counts array in place (one CTA, 16
+// consecutive counts per thread per round: two rounds for the config-4
+// permutation's 32768 counts). With `offsets` it also writes offsets[e] =
+// data[e * stride] for e < offsets_count: after a single-pass sort's scan that
+// is the number of keys below bucket e, i.e. the segment offsets.
+constexpr int kScanPerThread = 16;
+__global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restrict__ data, int64_t n,
+                                                              int64_t *__restrict__ offsets, int64_t stride,
+                                                              int64_t offsets_count) {
     __shared__ int32_t warp_totals[32];
     __shared__ int32_t carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    for (int64_t base = 0; base < n; base += 1024) {
-        const int64_t i = base + threadIdx.x;
-        const int32_t v = i < n ? data[i] : 0;
-        int32_t inclusive = v;
+    for (int64_t base = 0; base < n; base += 1024 * kScanPerThread) {
+        const int64_t start = base + static_cast<int64_t>(threadIdx.x) * kScanPerThread;
+        int32_t v[kScanPerThread];
+        int32_t sum = 0;
+#pragma unroll
+        for (int j = 0; j < kScanPerThread; ++j) {
+            v[j] = start + j < n ? data[start + j] : 0;
+            sum += v[j];
+        }
+        int32_t inclusive = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int32_t other = __shfl_up_sync(0xffffffffu, inclusive, o);
@@ -189,12 +202,18 @@ __global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restric
             warp_totals[lane] = t;
         }
         __syncthreads();
-        const int32_t warp_prefix = warp == 0 ? 0 : warp_totals[warp - 1];
-        const int32_t c = carry;
-        if (i < n) data[i] = c + warp_prefix + inclusive - v;
+        int32_t running = carry + (warp == 0 ? 0 : warp_totals[warp - 1]) + inclusive - sum;
+#pragma unroll
+        for (int j = 0; j < kScanPerThread; ++j) {
+            if (start + j < n) data[start + j] = running;
+            running += v[j];
+        }
         __syncthreads();
-        if (threadIdx.x == 0) carry = c + warp_totals[31];
+        if (threadIdx.x == 0) carry += warp_totals[31];
         __syncthreads();
+    }
+    if (offsets != nullptr) {
+        for (int64_t e = threadIdx.x; e < offsets_count; e += 1024) offsets[e] = data[e * stride];
     }
 }
 
@@ -387,6 +406,42 @@ __global__ void gather_rows_kernel(const T *__restrict__ context, const int32_t 
         }
     } else {
         for (int64_t c = lane; c < width; c += 32) dst[c] = live ? src[c] : from_acc<T>(0.0f);
+    }
+}
+
+// Token-major form of the row gather, used when the pair positions are
+// known: one warp per token reads its row once and writes it to the sorted
+// position of each of its top_k pairs (zeros for pairs past the valid count),
+// so a row routed to k experts is read once instead of k times.
+template <typename T>
+__global__ void scatter_rows_kernel(const T *__restrict__ context, const int64_t *__restrict__ pair_positions,
+                                    const int64_t *__restrict__ valid_count, T *__restrict__ out, int64_t tokens,
+                                    int64_t width, int64_t top_k, bool vector) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= tokens) return;
+    const int64_t valid = *valid_count;
+    bool any_live = false;
+    for (int64_t k = 0; k < top_k; ++k) any_live |= pair_positions[t * top_k + k] < valid;
+    const T *src = context + t * width;
+    if (vector) {
+        constexpr int W = 16 / sizeof(T);
+        const int64_t packets = width / W;
+        for (int64_t p = lane; p < packets; p += 32) {
+            const uint4 v = any_live ? load_stream(src + p * W) : make_uint4(0, 0, 0, 0);
+            for (int64_t k = 0; k < top_k; ++k) {
+                const int64_t pos = pair_positions[t * top_k + k];
+                store_stream(out + pos * width + p * W, pos < valid ? v : make_uint4(0, 0, 0, 0));
+            }
+        }
+    } else {
+        for (int64_t c = lane; c < width; c += 32) {
+            const T v = any_live ? src[c] : from_acc<T>(0.0f);
+            for (int64_t k = 0; k < top_k; ++k) {
+                const int64_t pos = pair_positions[t * top_k + k];
+                out[pos * width + c] = pos < valid ? v : from_acc<T>(0.0f);
+            }
+        }
     }
 }
 
@@ -858,7 +913,10 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
             const int shift = pass * kDigitBits;
             digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
             KOEMI_LAUNCH_CHECK();
-            exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets);
+            // a single pass's scan also yields the segment offsets (every key in its own bucket)
+            const bool last_single = l.passes == 1;
+            exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets, last_single ? segment_offsets : nullptr,
+                                                     l.blocks, expert_count + 1);
             KOEMI_LAUNCH_CHECK();
             digit_scatter_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, scatter_smem, s>>>(
                 keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b);
@@ -866,12 +924,26 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
             int32_t *t = keys_a; keys_a = keys_b; keys_b = t;
             t = values_a; values_a = values_b; values_b = t;
         }
-        segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
-        KOEMI_LAUNCH_CHECK();
+        if (l.passes > 1) {
+            segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
+            KOEMI_LAUNCH_CHECK();
+        }
         finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
         KOEMI_LAUNCH_CHECK();
     }
-    if (sorted_context != nullptr && width > 0) {
+    if (sorted_context != nullptr && width > 0 && pair_positions != nullptr) {
+        const size_t es = dtype_size(context_dtype);
+        const bool vector = (width * es) % 16 == 0 && aligned(context, 16) && aligned(sorted_context, 16);
+        const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
+        const int64_t *valid_count = segment_offsets + expert_count;
+        switch (context_dtype) {
+            case KOEMI_F32: scatter_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float *>(context), pair_positions, valid_count, static_cast<float *>(sorted_context), tokens, width, top_k, vector); break;
+            case KOEMI_F16: scatter_rows_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(context), pair_positions, valid_count, static_cast<__half *>(sorted_context), tokens, width, top_k, vector); break;
+            case KOEMI_BF16: scatter_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(context), pair_positions, valid_count, static_cast<__nv_bfloat16 *>(sorted_context), tokens, width, top_k, vector); break;
+            default: return fail(KOEMI_ERR_INVALID, "context must be f32, f16 or bf16");
+        }
+        KOEMI_LAUNCH_CHECK();
+    } else if (sorted_context != nullptr && width > 0) {
         const size_t es = dtype_size(context_dtype);
         const bool vector = (width * es) % 16 == 0 && aligned(context, 16) && aligned(sorted_context, 16);
         const unsigned blocks = static_cast<unsigned>(ceil_div(pairs, 8));

@@ -321,6 +321,26 @@ int64_t simt_slices(int64_t rows, int64_t vocab) {
     return s < 1 ? 1 : s;
 }
 
+// Row copy / fill of the admission kernel: one warp per row, 16-byte
+// packets when the row allows them.
+__device__ __forceinline__ void copy_row_f32(float *dst, const float *src, int64_t width, int lane) {
+    if (width % 4 == 0 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
+        for (int64_t c = lane; c < width / 4; c += 32) {
+            reinterpret_cast<float4 *>(dst)[c] = __ldg(reinterpret_cast<const float4 *>(src) + c);
+        }
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = src[c];
+    }
+}
+
+__device__ __forceinline__ void zero_row_f32(float *dst, int64_t width, int lane) {
+    if (width % 4 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        for (int64_t c = lane; c < width / 4; c += 32) reinterpret_cast<float4 *>(dst)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+        for (int64_t c = lane; c < width; c += 32) dst[c] = 0.0f;
+    }
+}
+
 // --------------------------------------------------------- salient admission
 // One CTA per batch row. Admission is valid && surprise > threshold
 // (network.py:349). When carried + length fits the capacity the ring is the
@@ -374,12 +394,8 @@ __global__ void salient_admission_kernel(const float *__restrict__ carried_keys,
         for (int64_t i = warp; i < total; i += warps) {
             const float *ks = i < carried ? carried_keys + (b * carried + i) * width : keys + (b * length + i - carried) * width;
             const float *vs = i < carried ? carried_values + (b * carried + i) * width : values + (b * length + i - carried) * width;
-            float *kd = out_keys + (b * total + i) * width;
-            float *vd = out_values + (b * total + i) * width;
-            for (int64_t c = lane; c < width; c += 32) {
-                kd[c] = ks[c];
-                vd[c] = vs[c];
-            }
+            copy_row_f32(out_keys + (b * total + i) * width, ks, width, lane);
+            copy_row_f32(out_values + (b * total + i) * width, vs, width, lane);
             if (lane == 0) out_valid[b * total + i] = flag_of(i);
         }
         return;
@@ -389,12 +405,8 @@ __global__ void salient_admission_kernel(const float *__restrict__ carried_keys,
     const int64_t lead = capacity - kept;
     // leading empty slots
     for (int64_t slot = warp; slot < lead; slot += warps) {
-        float *kd = out_keys + (b * capacity + slot) * width;
-        float *vd = out_values + (b * capacity + slot) * width;
-        for (int64_t c = lane; c < width; c += 32) {
-            kd[c] = 0.0f;
-            vd[c] = 0.0f;
-        }
+        zero_row_f32(out_keys + (b * capacity + slot) * width, width, lane);
+        zero_row_f32(out_values + (b * capacity + slot) * width, width, lane);
         if (lane == 0) out_valid[b * capacity + slot] = 0;
     }
     for (int64_t i = warp; i < total; i += warps) {
@@ -404,12 +416,8 @@ __global__ void salient_admission_kernel(const float *__restrict__ carried_keys,
         const int64_t slot = lead + (r - 1 - skip);
         const float *ks = i < carried ? carried_keys + (b * carried + i) * width : keys + (b * length + i - carried) * width;
         const float *vs = i < carried ? carried_values + (b * carried + i) * width : values + (b * length + i - carried) * width;
-        float *kd = out_keys + (b * capacity + slot) * width;
-        float *vd = out_values + (b * capacity + slot) * width;
-        for (int64_t c = lane; c < width; c += 32) {
-            kd[c] = ks[c];
-            vd[c] = vs[c];
-        }
+        copy_row_f32(out_keys + (b * capacity + slot) * width, ks, width, lane);
+        copy_row_f32(out_values + (b * capacity + slot) * width, vs, width, lane);
         if (lane == 0) out_valid[b * capacity + slot] = 1;
     }
 }
@@ -500,7 +508,7 @@ extern "C" int koemi_think_salient_admission(const float *carried_keys, const fl
     if (smem > 48 * 1024) {
         KOEMI_CUDA_TRY(cudaFuncSetAttribute(salient_admission_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     }
-    salient_admission_kernel<<<static_cast<unsigned>(batch), 256, smem, as_stream(stream)>>>(
+    salient_admission_kernel<<<static_cast<unsigned>(batch), 512, smem, as_stream(stream)>>>(
         carried_keys, carried_values, carried_valid, keys, values, surprise, valid, threshold, out_keys,
         out_values, out_valid, admission_out, carried, length, width, capacity);
     KOEMI_LAUNCH_CHECK();

@@ -589,19 +589,16 @@ class KoemiModel(nn.Module):
             active = assignments.reshape(batch, length, s.expert_top_k)
             expert_indices = active[..., 0]
 
-        all_keys = torch.cat((state.local_keys, keys), dim=1)
-        all_values = torch.cat((state.local_values, values), dim=1)
-        all_valid = torch.cat((state.local_valid, valid), dim=1)
-        cut = max(0, all_keys.shape[1] - s.local_memory_size)
+        keep = min(s.local_memory_size, state.local_keys.shape[1] + length)
         new_state = KoemiState(
             working_state=h[:, -1],
             memory_basis=basis,
             memory_normalizer=normalizer,
             refine_basis=refine_basis,
             refine_normalizer=refine_normalizer,
-            local_keys=all_keys[:, cut:],
-            local_values=all_values[:, cut:],
-            local_valid=all_valid[:, cut:],
+            local_keys=_ring_tail(state.local_keys, keys, keep),
+            local_values=_ring_tail(state.local_values, values, keep),
+            local_valid=_ring_tail(state.local_valid, valid, keep),
             salient_keys=salient_keys,
             salient_values=salient_values,
             salient_valid=salient_valid,
@@ -614,25 +611,37 @@ class KoemiModel(nn.Module):
 
 # ------------------------------------------------------------------ memories
 
-def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid, queries, window):
-    """Softmax read over the ``window`` slots strictly before each query plus
-    novelty = 1 - max cosine (memory.py:332-383); 0 / 1 when nothing is eligible."""
-    batch, length, width = queries.shape
+def _two_part_read(carried_keys, carried_values, keys, values, queries, eligible):
+    """Softmax read of ``queries`` [B, T, d] over the slots [carried ; window]
+    with ``eligible`` [B, T, S_c + T], without concatenating the two key or
+    value blocks: two score products are concatenated instead ([B, T, S]
+    rather than [B, S, d]) and the weighted sum is split the same way.
+    Returns (read [B, T, d], raw dot products [B, T, S], any eligible [B, T, 1])."""
     carried = carried_keys.shape[1]
-    all_keys = torch.cat((carried_keys, keys), dim=1)
-    all_values = torch.cat((carried_values, values), dim=1)
-    all_valid = torch.cat((carried_valid, valid), dim=1)
-    own = carried + torch.arange(length, device=queries.device).unsqueeze(1)
-    source = torch.arange(all_keys.shape[1], device=queries.device).unsqueeze(0)
-    eligible = ((source < own) & (source >= own - window)).unsqueeze(0) & all_valid.unsqueeze(1)
-    scores = torch.einsum("bsd,btd->bts", all_keys, queries) / math.sqrt(width)
-    scores = scores.masked_fill(~eligible, float("-inf"))
+    raw = torch.cat((torch.einsum("bsd,btd->bts", carried_keys, queries),
+                     torch.einsum("bsd,btd->bts", keys, queries)), dim=-1)
+    scores = (raw / math.sqrt(queries.shape[-1])).masked_fill(~eligible, float("-inf"))
     any_slot = eligible.any(dim=-1, keepdim=True)
     weights = torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0)
-    value = torch.einsum("bts,bsd->btd", weights, all_values)
-    nq = queries / queries.norm(dim=-1, keepdim=True).clamp_min(1e-12)
-    nk = all_keys / all_keys.norm(dim=-1, keepdim=True).clamp_min(1e-12)
-    similarity = torch.einsum("bsd,btd->bts", nk, nq).masked_fill(~eligible, float("-inf"))
+    read = torch.einsum("bts,bsd->btd", weights[..., :carried], carried_values)
+    read = read + torch.einsum("bts,bsd->btd", weights[..., carried:], values)
+    return read, raw, any_slot
+
+
+def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid, queries, window):
+    """Softmax read over the ``window`` slots strictly before each query plus
+    novelty = 1 - max cosine (memory.py:332-383); 0 / 1 when nothing is
+    eligible. The cosine reuses the score products: q.k / (|q| |k|)."""
+    batch, length, width = queries.shape
+    carried = carried_keys.shape[1]
+    all_valid = torch.cat((carried_valid, valid), dim=1)
+    own = carried + torch.arange(length, device=queries.device).unsqueeze(1)
+    source = torch.arange(carried + length, device=queries.device).unsqueeze(0)
+    eligible = ((source < own) & (source >= own - window)).unsqueeze(0) & all_valid.unsqueeze(1)
+    value, raw, any_slot = _two_part_read(carried_keys, carried_values, keys, values, queries, eligible)
+    key_norm = torch.cat((carried_keys.norm(dim=-1), keys.norm(dim=-1)), dim=1).clamp_min(1e-12)
+    query_norm = queries.norm(dim=-1).clamp_min(1e-12)
+    similarity = (raw / (query_norm.unsqueeze(-1) * key_norm.unsqueeze(1))).masked_fill(~eligible, float("-inf"))
     novelty = torch.where(any_slot.squeeze(-1), 1.0 - similarity.amax(dim=-1), 1.0)
     return value, novelty.clamp(0.0, 1.0)
 
@@ -641,17 +650,20 @@ def _salient_read(carried_keys, carried_values, carried_valid, keys, values, adm
     """Read over every valid carried slot plus earlier admitted window entries
     (memory.py:405-429)."""
     batch, length, width = queries.shape
-    all_keys = torch.cat((carried_keys, keys), dim=1)
-    all_values = torch.cat((carried_values, values), dim=1)
     position = torch.arange(length, device=queries.device)
     earlier = position.unsqueeze(1) > position.unsqueeze(0)
     eligible = torch.cat((carried_valid.unsqueeze(1).expand(batch, length, carried_keys.shape[1]),
                           admission.unsqueeze(1) & earlier.unsqueeze(0)), dim=-1)
-    scores = torch.einsum("bsd,btd->bts", all_keys, queries) / math.sqrt(width)
-    scores = scores.masked_fill(~eligible, float("-inf"))
-    any_slot = eligible.any(dim=-1, keepdim=True)
-    weights = torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0)
-    return torch.einsum("bts,bsd->btd", weights, all_values)
+    return _two_part_read(carried_keys, carried_values, keys, values, queries, eligible)[0]
+
+
+def _ring_tail(carried, window, keep: int):
+    """The last ``keep`` entries of [carried ; window] along dim 1, copying
+    only when the window alone does not cover them."""
+    length = window.shape[1]
+    if length >= keep:
+        return window[:, length - keep:]
+    return torch.cat((carried[:, carried.shape[1] - (keep - length):], window), dim=1)
 
 
 _WINDOW_FEATURE_COUNTS = (4, 8, 16, 32)
