@@ -389,18 +389,24 @@ class KoemiModel(nn.Module):
             self._validate_input_ids(input_ids)
         if self._cache is None:
             self.cache_inference_weights()
-        state = state if state is not None else self.initial_state(input_ids.shape[0], input_ids.device)
+        # The running state travels in a one-element list that the window call
+        # empties: a block's previous state is then released as soon as its
+        # new state exists, instead of every block's old and new states (27 GB
+        # each at config 5) living together for the whole window.
+        carried = [state if state is not None else self.initial_state(input_ids.shape[0], input_ids.device)]
+        del state
         window = 1 if getattr(execution_mode, "value", execution_mode) == "sequential" else self.settings.scan_chunk
         length = input_ids.shape[1]
         outputs = []
         with torch.no_grad():
             for start in range(0, length, window):
                 last = start + window >= length
-                piece = self._window(input_ids[:, start:start + window], state, trusted_inputs,
+                piece = self._window(input_ids[:, start:start + window], carried, trusted_inputs,
                                      logits=(not last_logits_only) or last, last_only=last_logits_only)
-                state = piece.state
+                carried = [piece.state]
                 # keep only per-position outputs: a window's state is superseded by the next
                 outputs.append(piece if last else dataclasses.replace(piece, state=None))
+                del piece
         if len(outputs) == 1:
             return outputs[0]
         return _concatenate(outputs, last_logits_only)
@@ -413,22 +419,29 @@ class KoemiModel(nn.Module):
         if int(input_ids.min()) < 0 or int(input_ids.max()) >= self.settings.vocabulary_size:
             raise ValueError("input_ids contain values outside the model vocabulary")
 
-    def _window(self, ids: Tensor, state, trusted: bool, logits: bool, last_only: bool) -> KoemiOutput:
+    def _window(self, ids: Tensor, carried: list, trusted: bool, logits: bool, last_only: bool) -> KoemiOutput:
+        """One window over every block; ``carried`` holds the running state
+        and is emptied, so each block's old state is dropped once replaced."""
         s = self.settings
+        state = carried.pop()
+        layered = isinstance(state, LayeredKoemiState)
+        layer_states = list(state.layers) if layered else [state]
+        step = layer_states[0].step_index + ids.shape[1]
+        del state
         ids = ids.contiguous()  # a window slice of the prompt is strided
         valid = ids != PAD_TOKEN_ID
-        layer_states = state.layers if isinstance(state, LayeredKoemiState) else (state,)
         x = self.embedding_weight.index_select(0, ids.reshape(-1)).float().reshape(*ids.shape, s.embedding_size)
         new_states, statistics = [], []
         result = None
         for index, block in enumerate(self.blocks):
-            result = self._block_window(block, self._cache["blocks"][index], x, ids, valid, layer_states[index])
+            previous, layer_states[index] = layer_states[index], None
+            result = self._block_window(block, self._cache["blocks"][index], x, ids, valid, previous)
+            del previous
             x = result["final"]
             new_states.append(result["state"])
             if result["statistics"] is not None:
                 statistics.append(result["statistics"])
-        step = layer_states[0].step_index + ids.shape[1]
-        if isinstance(state, LayeredKoemiState):
+        if layered:
             new_state = LayeredKoemiState(tuple(_with_step(st, step) for st in new_states), step)
         else:
             new_state = _with_step(new_states[0], step)
