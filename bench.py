@@ -69,6 +69,9 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-streams", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--out", type=str, default=None, help="also write the JSON line to this file")
+    p.add_argument("--breakdown", type=str, default=None,
+                   help="after the measurement, write per-kernel device times of 3 profiled decode steps "
+                        "(torch profiler, CUDA activity) to this JSON file")
     p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "permute", "expert_decode", "surprise_decode",
                                     "surprise_prefill", "dense_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
@@ -387,6 +390,31 @@ def prefill_roofline(args, streams: int, seconds: float, world: int) -> dict:
             "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback 1409.6 TFLOP/s"}
 
 
+def write_breakdown(path: str, rank: int, world: int, step, steps: int = 3) -> None:
+    """Per-kernel device time of ``steps`` decode steps under the torch
+    profiler (CUDA activity only), averaged per step, largest first; one file
+    per rank (``path`` gets ``.rank<r>`` inserted when world > 1)."""
+    import torch
+    from collections import defaultdict
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize()
+    totals = defaultdict(lambda: [0, 0.0])
+    for event in prof.events():
+        if event.device_type.name == "CUDA":
+            totals[event.name][0] += 1
+            totals[event.name][1] += event.device_time_total
+    rows = sorted(totals.items(), key=lambda kv: -kv[1][1])
+    out = {"steps": steps, "kernel_us_per_step": sum(v[1] for v in totals.values()) / steps,
+           "kernels": [{"name": name, "launches_per_step": count / steps, "us_per_step": us / steps}
+                       for name, (count, us) in rows]}
+    target = Path(path) if world == 1 else Path(path).with_suffix(f".rank{rank}{Path(path).suffix}")
+    target.write_text(json.dumps(out, indent=1))
+
+
 def progress(rank: int, message: str) -> None:
     """Timestamped, rank-tagged progress on stderr (the JSON line stays alone on stdout)."""
     print(f"[bench rank {rank} {time.strftime('%H:%M:%S')}] {message}", file=sys.stderr, flush=True)
@@ -506,6 +534,9 @@ def run_b200(args) -> None:
         t = torch.tensor([sampled_seconds], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         sampled_seconds = float(t.item())
+
+    if args.breakdown:
+        write_breakdown(args.breakdown, rank, world, lambda: greedy(decoder.step(token)))
 
     progress(rank, "end-to-end done; expert kernel roofline")
     mlp = measure_expert_mlp(model, args, world)
