@@ -517,9 +517,13 @@ class KoemiModel(nn.Module):
         if s.ablation == "no_surprise":
             surprise = torch.zeros(batch, length, device=h.device)
         else:
-            prior = torch.cat((state.working_state.unsqueeze(1), h[:, :-1]), dim=1)
+            # the prior (state before each position) built straight in the
+            # compute dtype: one converting copy per part, no fp32 concatenation
+            prior = torch.empty(batch, length, d, dtype=self.compute_dtype, device=h.device)
+            prior[:, 0].copy_(state.working_state)
+            prior[:, 1:].copy_(h[:, :-1])
             targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
-            surprise = _ops.causal_surprise_forward(prior.to(self.compute_dtype), self._cache["content_w"],
+            surprise = _ops.causal_surprise_forward(prior, self._cache["content_w"],
                                                     self._cache["content_b"], targets, valid, torch.float32)
 
         # local ring entries + sliding-window read: memory.py:297-361
@@ -567,8 +571,12 @@ class KoemiModel(nn.Module):
             refine_basis, refine_normalizer = state.refine_basis, state.refine_normalizer
 
         # fusion (cuBLAS + core rms_norm): network.py:723-732
-        fused = self._linear(torch.cat((h, memory_value, local_value, salient_value), dim=-1), block.fusion_weight,
-                             block.fusion_bias)
+        # fusion input [h | memory | local | salient] written part by part in
+        # the compute dtype (the GEMM's operand type), no fp32 concatenation
+        fusion_in = torch.empty(batch, length, 4 * d, dtype=self.compute_dtype, device=h.device)
+        for part, piece in enumerate((h, memory_value, local_value, salient_value)):
+            fusion_in[..., part * d:(part + 1) * d].copy_(piece)
+        fused = self._linear(fusion_in, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused.reshape(rows, d), None, cache["fusion_norm"], None, NORM_EPSILON, torch.float32)
 
         # experts (moe): experts.py:90-143; router.py:43-97
