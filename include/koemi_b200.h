@@ -187,6 +187,16 @@ KOEMI_API int koemi_dense_projection(const void *a, int64_t a_stride, const void
                            float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* A batch of small products on tcgen05 tensor cores, fp32 output:
+ * out[g * M + i, j] = sum_k A[g * M + i, k] B[g * N + j, k] for every group
+ * g < groups (M = rows_per_group), A [groups * M, k] and B [groups * N, k]
+ * bf16/f16 row-major, out fp32 [groups * M, N]. The prefill's ring reads use
+ * it per stream: the [C, L + C] scores (queries x ring keys) and the weighted
+ * sums (weights x transposed ring values) of LocalKeyValueMemory.read_window
+ * and the salient read (model/memory.py:332-361, 405-429). k a multiple of 8. */
+KOEMI_API int koemi_grouped_projection(const void *a, const void *b, float *out, int64_t groups,
+                                       int64_t rows_per_group, int64_t n, int64_t k, int dtype, void *stream);
+
 /* ------------------------------------------------------------- core front */
 
 /* y = silu(x * rsqrt(mean(x^2) + eps) * w), inv_rms[row] = rsqrt(...).

@@ -100,6 +100,7 @@ struct UmmaArgs {
     const int64_t *targets;   // surprise: target column per row, or NULL (no target logit)
     int64_t lse_rows;         // surprise: rows below fold into partials; rows at or above write logits to out
     int64_t pad_column;       // surprise: column left out of the log-sum-exp (-1: none)
+    int64_t group_rows;       // dense, uniform groups: A rows per group (0: one ungrouped problem)
     const float *row_lse;     // surprise gradient: per-row log-sum-exp (NULL: forward modes)
     const float *row_scale;   // surprise gradient: per-row dL/dNLL (0 on invalid rows)
     float *grad_out;          // surprise gradient: fp32 dlogits [rows, n_out]
@@ -205,6 +206,9 @@ struct Tile {
 template <int kProblem, int kTileRows>
 __device__ __forceinline__ int64_t total_tiles(const UmmaArgs &a) {
     if (kProblem == kSurprise) return ((a.rows + kTileRows - 1) / kTileRows) * a.n_tiles;
+    if (kProblem == kDense && a.group_rows > 0) {
+        return (a.rows / a.group_rows) * ((a.group_rows + kTileRows - 1) / kTileRows) * a.n_tiles;
+    }
     if (kProblem == kDense || kProblem == kDenseCluster) {
         return ((a.rows + kTileRows - 1) / kTileRows) * a.n_tiles * a.splits;
     }
@@ -228,6 +232,20 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
         tile.k_end = min(k_blocks, tile.k_begin + a.k_per_split);
         tile.row0 = tile.m_tile * kTileRows;
         tile.row_end = a.rows;
+        return tile;
+    }
+    if (kProblem == kDense && a.group_rows > 0) {
+        // uniform groups (a batch of small products): group g's A rows are
+        // [g * group_rows, (g + 1) * group_rows) and its B rows start at
+        // g * b_rows_per_group; N fastest, so a group's A tile is reused from L2
+        const int64_t per_group = (a.group_rows + kTileRows - 1) / kTileRows;
+        tile.n = t % a.n_tiles;
+        const int64_t rest = t / a.n_tiles;
+        tile.group = rest / per_group;
+        tile.m_tile = rest;
+        tile.row0 = tile.group * a.group_rows + (rest - tile.group * per_group) * kTileRows;
+        tile.row_end = (tile.group + 1) * a.group_rows;
+        tile.split = 0;
         return tile;
     }
     if (kProblem == kDense) {
@@ -1105,6 +1123,39 @@ DensePlan dense_plan(int64_t rows, int64_t n, int64_t k) {
     return DensePlan{(k_blocks + per - 1) / per, per};
 }
 }  // namespace
+
+extern "C" int koemi_grouped_projection(const void *a, const void *b, float *out, int64_t groups,
+                                        int64_t rows_per_group, int64_t n, int64_t k, int dtype, void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "grouped projection takes bf16 or f16 operands");
+    if (groups < 0 || rows_per_group < 1 || n < 1 || k < 1) return fail(KOEMI_ERR_INVALID, "bad grouped projection sizes");
+    if (groups == 0) return KOEMI_OK;
+    if (k % 8 != 0 || !aligned(a, 16) || !aligned(b, 16) || groups * rows_per_group >= (int64_t(1) << 31) ||
+        groups * n >= (int64_t(1) << 31)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "grouped projection needs K a multiple of 8 and 16-byte aligned operands");
+    }
+    UmmaArgs args{};
+    int rc = encode_kmajor(&args.map_a, dtype, a, groups * rows_per_group, k, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&args.map_b0, dtype, b, groups * n, k, kBN);
+    if (rc != KOEMI_OK) return rc;
+    const int64_t k_blocks = (k + kBK - 1) / kBK;
+    args.k = k;
+    args.rows = groups * rows_per_group;
+    args.group_rows = rows_per_group;
+    args.n_tiles = (n + kBN - 1) / kBN;
+    args.b_rows_per_group = n;
+    args.n_out = n;
+    args.out_stride = n;
+    args.experts = groups;
+    args.splits = 1;
+    args.k_per_split = k_blocks;
+    args.bias0 = nullptr;
+    args.out = out;
+    args.status = device_status_word();
+    args.idesc = make_idesc(dtype);
+    const int64_t tiles = groups * ((rows_per_group + kBM - 1) / kBM) * args.n_tiles;
+    return launch<kDense>(args, dtype, tiles, as_stream(stream));
+}
 
 extern "C" size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64_t k, int dtype) {
     // the K splits are reduced in distributed shared memory: no scratch

@@ -114,6 +114,25 @@ def _(a, weight, bias):
     return a.new_empty(a.shape[0], weight.shape[0], dtype=torch.float32)
 
 
+@torch.library.custom_op("koemi_b200::grouped_projection", mutates_args=())
+def grouped_projection(a: Tensor, b: Tensor, groups: int) -> Tensor:
+    """fp32 [G * M, N] with out[g] = a[g] @ b[g]^T for G uniform groups:
+    a [G * M, K], b [G * N, K] (bf16/f16, row-major) on tensor cores."""
+    a, b = _dense(a, b)
+    stream = _prepare(a)
+    rows, k = a.shape
+    n = b.shape[0] // groups
+    out = torch.empty(rows, n, dtype=torch.float32, device=a.device)
+    call("koemi_grouped_projection", ptr(a), ptr(b), ptr(out), groups, rows // groups, n, k, dtype_code(a.dtype),
+         stream)
+    return out
+
+
+@grouped_projection.register_fake
+def _(a, b, groups):
+    return a.new_empty(a.shape[0], b.shape[0] // groups, dtype=torch.float32)
+
+
 # ----------------------------------------------------------------- core front
 
 @torch.library.custom_op("koemi_b200::rmsnorm_silu_forward", mutates_args=())

@@ -531,8 +531,11 @@ class KoemiModel(nn.Module):
         keep = valid.unsqueeze(-1)
         keys = torch.where(keep, local[..., :d], 0.0)
         values = torch.where(keep, local[..., d:], 0.0)
+        # 16-bit models read the rings on tensor cores (bf16 operands, fp32 results)
+        low_queries = (h.to(self.compute_dtype) if self.compute_dtype != torch.float32 and h.is_cuda
+                       and d % 8 == 0 else None)
         local_value, novelty = _local_read(state.local_keys, state.local_values, state.local_valid, keys, values, valid,
-                                           h, s.local_memory_size)
+                                           h, s.local_memory_size, low_queries)
 
         # associative memory: memory.py:82-144,244-255
         assoc = self._linear(h, block.assoc_weight, block.assoc_bias)
@@ -553,7 +556,7 @@ class KoemiModel(nn.Module):
             keys.contiguous(), values.contiguous(), surprise, valid, float(s.salience_threshold),
             int(s.salience_memory_size))
         salient_value = _salient_read(state.salient_keys, state.salient_values, state.salient_valid, keys, values,
-                                      admission, h)
+                                      admission, h, low_queries)
 
         if s.ablation == "herm":  # memory.py:257-268; network.py:366-386,709-721
             refine_decay = (1.0 - (1.0 - decay) * s.refine_decay_rate).clamp(max=MAX_REFINE_DECAY)
@@ -632,16 +635,44 @@ class KoemiModel(nn.Module):
 
 # ------------------------------------------------------------------ memories
 
-def _two_part_read(carried_keys, carried_values, keys, values, queries, eligible):
+def _two_part_read(carried_keys, carried_values, keys, values, queries, eligible, low_queries=None):
     """Softmax read of ``queries`` [B, T, d] over the slots [carried ; window]
-    with ``eligible`` [B, T, S_c + T], without concatenating the two key or
-    value blocks: two score products are concatenated instead ([B, T, S]
-    rather than [B, S, d]) and the weighted sum is split the same way.
-    Returns (read [B, T, d], raw dot products [B, T, S], any eligible [B, T, 1])."""
+    with ``eligible`` [B, T, S_c + T]. Returns (read [B, T, d], raw dot
+    products [B, T, S], any eligible [B, T, 1]).
+
+    fp32 (``low_queries`` None): two score products concatenated instead of
+    the two key or value blocks ([B, T, S] rather than [B, S, d]), the weighted
+    sum split the same way. 16-bit (``low_queries``: the queries in the
+    model's compute dtype, on CUDA): per stream, one tcgen05 product of the
+    queries with the stacked keys and one of the softmax weights with the
+    stacked, transposed values, bf16 operands and fp32 results; the slot
+    count is padded to a multiple of 8 with ineligible zero slots."""
     carried = carried_keys.shape[1]
+    batch, length, width = queries.shape
+    if low_queries is not None:
+        dtype = low_queries.dtype
+        slots = carried + length
+        padded = (slots + 7) // 8 * 8
+        stacked = torch.empty(batch, padded, width, dtype=dtype, device=queries.device)
+        stacked[:, :carried].copy_(carried_keys)
+        stacked[:, carried:slots].copy_(keys)
+        stacked[:, slots:].zero_()
+        raw = _ops.grouped_projection(low_queries.reshape(batch * length, width), stacked.view(batch * padded, width),
+                                      batch).view(batch, length, padded)[..., :slots]
+        scores = (raw / math.sqrt(width)).masked_fill(~eligible, float("-inf"))
+        any_slot = eligible.any(dim=-1, keepdim=True)
+        weights = torch.zeros(batch, length, padded, dtype=dtype, device=queries.device)
+        weights[..., :slots].copy_(torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0))
+        transposed = torch.empty(batch, width, padded, dtype=dtype, device=queries.device)
+        transposed[:, :, :carried].copy_(carried_values.transpose(1, 2))
+        transposed[:, :, carried:slots].copy_(values.transpose(1, 2))
+        transposed[:, :, slots:].zero_()
+        read = _ops.grouped_projection(weights.view(batch * length, padded), transposed.view(batch * width, padded),
+                                       batch).view(batch, length, width)
+        return read, raw, any_slot
     raw = torch.cat((torch.einsum("bsd,btd->bts", carried_keys, queries),
                      torch.einsum("bsd,btd->bts", keys, queries)), dim=-1)
-    scores = (raw / math.sqrt(queries.shape[-1])).masked_fill(~eligible, float("-inf"))
+    scores = (raw / math.sqrt(width)).masked_fill(~eligible, float("-inf"))
     any_slot = eligible.any(dim=-1, keepdim=True)
     weights = torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0)
     read = torch.einsum("bts,bsd->btd", weights[..., :carried], carried_values)
@@ -649,7 +680,8 @@ def _two_part_read(carried_keys, carried_values, keys, values, queries, eligible
     return read, raw, any_slot
 
 
-def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid, queries, window):
+def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid, queries, window,
+                low_queries=None):
     """Softmax read over the ``window`` slots strictly before each query plus
     novelty = 1 - max cosine (memory.py:332-383); 0 / 1 when nothing is
     eligible. The cosine reuses the score products: q.k / (|q| |k|)."""
@@ -659,7 +691,7 @@ def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid
     own = carried + torch.arange(length, device=queries.device).unsqueeze(1)
     source = torch.arange(carried + length, device=queries.device).unsqueeze(0)
     eligible = ((source < own) & (source >= own - window)).unsqueeze(0) & all_valid.unsqueeze(1)
-    value, raw, any_slot = _two_part_read(carried_keys, carried_values, keys, values, queries, eligible)
+    value, raw, any_slot = _two_part_read(carried_keys, carried_values, keys, values, queries, eligible, low_queries)
     key_norm = torch.cat((carried_keys.norm(dim=-1), keys.norm(dim=-1)), dim=1).clamp_min(1e-12)
     query_norm = queries.norm(dim=-1).clamp_min(1e-12)
     similarity = (raw / (query_norm.unsqueeze(-1) * key_norm.unsqueeze(1))).masked_fill(~eligible, float("-inf"))
@@ -667,7 +699,7 @@ def _local_read(carried_keys, carried_values, carried_valid, keys, values, valid
     return value, novelty.clamp(0.0, 1.0)
 
 
-def _salient_read(carried_keys, carried_values, carried_valid, keys, values, admission, queries):
+def _salient_read(carried_keys, carried_values, carried_valid, keys, values, admission, queries, low_queries=None):
     """Read over every valid carried slot plus earlier admitted window entries
     (memory.py:405-429)."""
     batch, length, width = queries.shape
@@ -675,7 +707,7 @@ def _salient_read(carried_keys, carried_values, carried_valid, keys, values, adm
     earlier = position.unsqueeze(1) > position.unsqueeze(0)
     eligible = torch.cat((carried_valid.unsqueeze(1).expand(batch, length, carried_keys.shape[1]),
                           admission.unsqueeze(1) & earlier.unsqueeze(0)), dim=-1)
-    return _two_part_read(carried_keys, carried_values, keys, values, queries, eligible)[0]
+    return _two_part_read(carried_keys, carried_values, keys, values, queries, eligible, low_queries)[0]
 
 
 def _ring_tail(carried, window, keep: int):

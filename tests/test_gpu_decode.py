@@ -298,3 +298,26 @@ def test_window_associative_kernel_matches_oracle(batch, length, d, m, cuda):
     torch.testing.assert_close(read.cpu().double(), expected[0], rtol=1e-4, atol=1e-6)
     torch.testing.assert_close(new_basis.cpu().double(), expected[1], rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(new_norm.cpu().double(), expected[2], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("carried,length", [(128, 128), (0, 128), (37, 100)])
+def test_window_ring_reads_on_tensor_cores_match_fp32(carried, length, cuda):
+    """The bf16 models' window ring reads (tcgen05 products with bf16
+    operands, fp32 results) against the fp32 reads of the same stored values:
+    within bf16 rounding of queries, keys, values and weights."""
+    from koemi_5hom_b200.model.network import _local_read, _salient_read
+    g = torch.Generator(device=cuda).manual_seed(carried + length)
+    batch, d = 5, 256
+    t = lambda *shape: torch.randn(*shape, generator=g, device=cuda)  # noqa: E731
+    ck, cv, k, v, q = t(batch, carried, d), t(batch, carried, d), t(batch, length, d), t(batch, length, d), t(batch, length, d)
+    cvalid = torch.rand(batch, carried, generator=g, device=cuda) > 0.3
+    valid = torch.rand(batch, length, generator=g, device=cuda) > 0.2
+    admission = torch.rand(batch, length, generator=g, device=cuda) > 0.5
+    low = q.bfloat16()
+    for low_q in (None, low):
+        value, novelty = _local_read(ck, cv, cvalid, k, v, valid, q, 64, low_q)
+        salient = _salient_read(ck, cv, cvalid, k, v, admission, q, low_q)
+        if low_q is None:
+            reference = (value, novelty, salient)
+    for got, want in zip((value, novelty, salient), reference):
+        assert (got - want).abs().max() <= 2e-2 * max(1.0, want.abs().max().item())

@@ -306,3 +306,18 @@ def test_combine_with_next_norm_equals_two_ops(with_next, out_dtype, cuda):
     assert torch.equal(got, expected)
 
 
+
+
+@pytest.mark.parametrize("groups,rows,n,k", [(4, 128, 256, 2048), (3, 100, 136, 64), (256, 128, 256, 2048),
+                                             (2, 130, 2048, 256), (5, 7, 24, 8)])
+def test_grouped_projection_matches_fp64(groups, rows, n, k, cuda):
+    """Per-group products on tensor cores (the prefill's ring reads: queries x
+    keys, weights x transposed values) against fp64 on the same bf16 operands;
+    groups whose rows share a 128-row tile with the next group (rows < 128 or
+    not a multiple of 128) keep their rows apart."""
+    g = torch.Generator(device=cuda).manual_seed(groups * 1000 + rows + n)
+    a = torch.randn(groups * rows, k, generator=g, device=cuda).bfloat16()
+    b = (torch.randn(groups * n, k, generator=g, device=cuda) * k ** -0.5).bfloat16()
+    out = _ops.grouped_projection(a, b, groups)
+    expected = torch.bmm(a.double().view(groups, rows, k), b.double().view(groups, n, k).transpose(1, 2))
+    torch.testing.assert_close(out.view(groups, rows, n).double(), expected, rtol=1e-4, atol=1e-4)
