@@ -197,6 +197,33 @@ KOEMI_API int koemi_dense_projection(const void *a, int64_t a_stride, const void
 KOEMI_API int koemi_grouped_projection(const void *a, const void *b, float *out, int64_t groups,
                                        int64_t rows_per_group, int64_t n, int64_t k, int dtype, void *stream);
 
+/* Row blocks converted to `dtype` (F32/BF16/F16) and packed side by side:
+ * out[r, o_p + j] = sources[p][r * strides[p] + j] for j < widths[p], where
+ * o_p = widths[0] + ... + widths[p-1], for rows r < rows and 1 to 8 parts
+ * (fp32 sources; widths, strides and out_stride multiples of 4; rows 16-byte
+ * aligned; `sources`, `strides`, `widths` are host arrays). The window path
+ * builds the fusion input [h | memory | local | salient] (network.py:723-732)
+ * and the prior [state ; h[:-1]] (network.py:320-325) with it in the GEMMs'
+ * operand type, one read of each fp32 element. */
+KOEMI_API int koemi_window_pack_rows(const float *const *sources, const int64_t *strides, const int64_t *widths,
+                                     int parts, int64_t rows, void *out, int64_t out_stride, int dtype, void *stream);
+
+/* The slot operands of a window ring read (LocalKeyValueMemory.read_window
+ * and the salient read, model/memory.py:332-361, 405-429): for every stream b
+ * the slots [carried ring (carried rows) ; window (length rows)] padded with
+ * zero slots to `padded` (a multiple of 8, >= carried + length), as stacked
+ * keys keys_out [batch, padded, width] and transposed values values_t_out
+ * [batch, width, padded] in `dtype` (F32/BF16/F16). Inputs are fp32 with
+ * contiguous rows of `width` (a multiple of 4): carried keys/values at batch
+ * stride carried_stride, window keys/values at batch stride window_stride.
+ * These are the B operands of koemi_grouped_projection for the scores and
+ * the weighted sum. */
+KOEMI_API int koemi_window_slot_operands(const float *carried_keys, const float *carried_values,
+                                         int64_t carried_stride, int64_t carried, const float *keys,
+                                         const float *values, int64_t window_stride, int64_t length, int64_t batch,
+                                         int64_t width, int64_t padded, void *keys_out, void *values_t_out, int dtype,
+                                         void *stream);
+
 /* ------------------------------------------------------------- core front */
 
 /* y = silu(x * rsqrt(mean(x^2) + eps) * w), inv_rms[row] = rsqrt(...).

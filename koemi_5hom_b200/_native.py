@@ -72,6 +72,8 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_dense_projection_workspace": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_dense_projection": (_int, (_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
     "koemi_grouped_projection": (_int, (_p, _p, _p, _i64, _i64, _i64, _i64, _int, _p)),
+    "koemi_window_pack_rows": (_int, (_p, _p, _p, _int, _i64, _p, _i64, _int, _p)),
+    "koemi_window_slot_operands": (_int, (_p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _int, _p)),
     "koemi_core_rmsnorm_silu_forward": (_int, (_p, _p, _p, _p, _i64, _i64, _f, _int, _p)),
     "koemi_core_rmsnorm_silu_backward_workspace": (_sz, (_i64, _i64)),
     "koemi_core_rmsnorm_silu_backward": (

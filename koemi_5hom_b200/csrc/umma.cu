@@ -248,6 +248,23 @@ __device__ __forceinline__ Tile tile_at(const UmmaArgs &a, int64_t t) {
         tile.split = 0;
         return tile;
     }
+    if (kProblem == kDense && a.band > 0 && a.splits == 1) {
+        // many row tiles (prefill): bands of `band` row tiles, N walked inside
+        // a band, so the CTAs running together reuse the band's activation
+        // tiles and each weight tile from L2 (row-tile-fastest order streams
+        // the activations from HBM once per wave of weight tiles)
+        const int64_t m_tiles = (a.rows + kTileRows - 1) / kTileRows;
+        const int64_t per_band = a.band * a.n_tiles;
+        const int64_t band = t / per_band;
+        const int64_t in_band = t - band * per_band;
+        const int64_t band_rows = min(a.band, m_tiles - band * a.band);
+        tile.n = in_band / band_rows;
+        tile.m_tile = band * a.band + (in_band - tile.n * band_rows);
+        tile.split = 0;
+        tile.row0 = tile.m_tile * kTileRows;
+        tile.row_end = a.rows;
+        return tile;
+    }
     if (kProblem == kDense) {
         // m fastest, so CTAs running together share one weight tile from L2
         const int64_t m_tiles = (a.rows + kTileRows - 1) / kTileRows;
@@ -553,11 +570,14 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                     const int64_t col0 = tile.n * kTileN + c * 32;
                     if (row_ok && col0 < args.n_out) {
                         float o[32];
+                        if (direct && bias != nullptr) {
+                            load_bias32(bias, col0, args.n_out, o);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int64_t col = col0 + j;
-                            o[j] = __uint_as_float(y[j]) + (direct && bias != nullptr && col < args.n_out ? to_acc(bias[col]) : 0.0f);
+                            for (int j = 0; j < 32; ++j) o[j] = 0.0f;
                         }
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(y[j]);
                         float *dst = dst_row + col0;
                         if (col0 + 32 <= args.n_out && aligned16(dst)) {
 #pragma unroll
@@ -1205,8 +1225,17 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     args.partials = nullptr;
     args.status = device_status_word();
     args.idesc = make_idesc(dtype);
-    const int64_t tiles = ((rows + kBM - 1) / kBM) * args.n_tiles * plan.splits;
+    const int64_t m_tiles = (rows + kBM - 1) / kBM;
+    const int64_t tiles = m_tiles * args.n_tiles * plan.splits;
     if (plan.splits > 1) return launch_clustered<kDenseCluster>(args, dtype, tiles, static_cast<int>(plan.splits), s);
+    if (m_tiles >= 32) {
+        // prefill-sized row counts: paired 256-row tiles (two M = 128 MMAs
+        // share every weight stage, halving the weight bytes each MMA needs
+        // from L2) in bands of 8 paired row tiles, N walked inside a band so
+        // the CTAs running together reuse the band's activations from L2
+        args.band = 8;
+        return launch<kDense, true>(args, dtype, ((rows + 2 * kBM - 1) / (2 * kBM)) * args.n_tiles, s);
+    }
     return launch<kDense>(args, dtype, tiles, s);
 }
 

@@ -133,6 +133,66 @@ def _(a, b, groups):
     return a.new_empty(a.shape[0], b.shape[0] // groups, dtype=torch.float32)
 
 
+def _rows_view(t: Tensor) -> tuple[Tensor, int]:
+    """A 2-D fp32 row block whose rows are contiguous, and its row stride."""
+    if t.dim() != 2 or t.stride(1) != 1 or t.stride(0) % 4 or t.data_ptr() % 16:
+        t = t.contiguous()
+    return t, t.stride(0)
+
+
+@torch.library.custom_op("koemi_b200::pack_rows", mutates_args=("out",))
+def pack_rows(out: Tensor, sources: list[Tensor]) -> None:
+    """out[:, o_p : o_p + w_p] = sources[p] converted to out's dtype, the fp32
+    row blocks [rows, w_p] side by side (o_p = w_0 + ... + w_{p-1}); out is a
+    2-D block [rows, >= sum w_p] with contiguous rows."""
+    import ctypes
+    stream = _prepare(out)
+    views = [_rows_view(t) for t in sources]
+    count = len(views)
+    source_ptrs = (ctypes.c_void_p * count)(*[v.data_ptr() for v, _ in views])
+    strides = (ctypes.c_int64 * count)(*[stride for _, stride in views])
+    widths = (ctypes.c_int64 * count)(*[v.shape[1] for v, _ in views])
+    call("koemi_window_pack_rows", ctypes.cast(source_ptrs, ctypes.c_void_p), ctypes.cast(strides, ctypes.c_void_p),
+         ctypes.cast(widths, ctypes.c_void_p), count, out.shape[0], ptr(out), out.stride(0), dtype_code(out.dtype),
+         stream)
+
+
+@pack_rows.register_fake
+def _(out, sources):
+    return None
+
+
+@torch.library.custom_op("koemi_b200::window_slot_operands", mutates_args=())
+def window_slot_operands(carried_keys: Tensor, carried_values: Tensor, keys: Tensor, values: Tensor, padded: int,
+                         dtype: torch.dtype) -> tuple[Tensor, Tensor]:
+    """Stacked keys [B, padded, d] and transposed values [B, d, padded] in
+    ``dtype`` of the slots [carried ; window] (fp32 [B, C, d] and [B, T, d]),
+    zero past C + T: the B operands of a window ring read's two products."""
+    def rows_of(t):
+        return t if t.stride(2) == 1 and t.stride(1) == t.shape[2] and t.stride(0) % 4 == 0 else t.contiguous()
+    carried_keys, carried_values = rows_of(carried_keys), rows_of(carried_values)
+    keys, values = rows_of(keys), rows_of(values)
+    if carried_keys.stride() != carried_values.stride():
+        carried_keys, carried_values = carried_keys.contiguous(), carried_values.contiguous()
+    if keys.stride() != values.stride():
+        keys, values = keys.contiguous(), values.contiguous()
+    stream = _prepare(keys)
+    batch, length, width = keys.shape
+    carried = carried_keys.shape[1]
+    stacked = torch.empty(batch, padded, width, dtype=dtype, device=keys.device)
+    transposed = torch.empty(batch, width, padded, dtype=dtype, device=keys.device)
+    call("koemi_window_slot_operands", ptr(carried_keys), ptr(carried_values), carried_keys.stride(0), carried,
+         ptr(keys), ptr(values), keys.stride(0), length, batch, width, padded, ptr(stacked), ptr(transposed),
+         dtype_code(dtype), stream)
+    return stacked, transposed
+
+
+@window_slot_operands.register_fake
+def _(carried_keys, carried_values, keys, values, padded, dtype):
+    batch, _, width = keys.shape
+    return (keys.new_empty(batch, padded, width, dtype=dtype), keys.new_empty(batch, width, padded, dtype=dtype))
+
+
 # ----------------------------------------------------------------- core front
 
 @torch.library.custom_op("koemi_b200::rmsnorm_silu_forward", mutates_args=())

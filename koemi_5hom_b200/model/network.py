@@ -518,10 +518,10 @@ class KoemiModel(nn.Module):
             surprise = torch.zeros(batch, length, device=h.device)
         else:
             # the prior (state before each position) built straight in the
-            # compute dtype: one converting copy per part, no fp32 concatenation
+            # compute dtype in one native pass (koemi_window_pack_rows)
             prior = torch.empty(batch, length, d, dtype=self.compute_dtype, device=h.device)
-            prior[:, 0].copy_(state.working_state)
-            prior[:, 1:].copy_(h[:, :-1])
+            _ops.pack_rows(prior.view(batch, length * d),
+                           [state.working_state, h.reshape(batch, length * d)[:, :(length - 1) * d]])
             targets = torch.where(ids > PAD_TOKEN_ID, ids - 1, ids) if s.vocabulary_size != PAD_TOKEN_ID + 1 else ids
             surprise = _ops.causal_surprise_forward(prior, self._cache["content_w"],
                                                     self._cache["content_b"], targets, valid, torch.float32)
@@ -574,11 +574,11 @@ class KoemiModel(nn.Module):
             refine_basis, refine_normalizer = state.refine_basis, state.refine_normalizer
 
         # fusion (cuBLAS + core rms_norm): network.py:723-732
-        # fusion input [h | memory | local | salient] written part by part in
+        # fusion input [h | memory | local | salient] packed in one native pass in
         # the compute dtype (the GEMM's operand type), no fp32 concatenation
         fusion_in = torch.empty(batch, length, 4 * d, dtype=self.compute_dtype, device=h.device)
-        for part, piece in enumerate((h, memory_value, local_value, salient_value)):
-            fusion_in[..., part * d:(part + 1) * d].copy_(piece)
+        _ops.pack_rows(fusion_in.view(rows, 4 * d),
+                       [piece.reshape(rows, d) for piece in (h, memory_value, local_value, salient_value)])
         fused = self._linear(fusion_in, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused.reshape(rows, d), None, cache["fusion_norm"], None, NORM_EPSILON, torch.float32)
 
@@ -645,28 +645,22 @@ def _two_part_read(carried_keys, carried_values, keys, values, queries, eligible
     sum split the same way. 16-bit (``low_queries``: the queries in the
     model's compute dtype, on CUDA): per stream, one tcgen05 product of the
     queries with the stacked keys and one of the softmax weights with the
-    stacked, transposed values, bf16 operands and fp32 results; the slot
-    count is padded to a multiple of 8 with ineligible zero slots."""
+    stacked, transposed values, bf16 operands (built in one native pass,
+    koemi_window_slot_operands) and fp32 results; the slot count is padded to
+    a multiple of 8 with ineligible zero slots."""
     carried = carried_keys.shape[1]
     batch, length, width = queries.shape
     if low_queries is not None:
         dtype = low_queries.dtype
         slots = carried + length
         padded = (slots + 7) // 8 * 8
-        stacked = torch.empty(batch, padded, width, dtype=dtype, device=queries.device)
-        stacked[:, :carried].copy_(carried_keys)
-        stacked[:, carried:slots].copy_(keys)
-        stacked[:, slots:].zero_()
+        stacked, transposed = _ops.window_slot_operands(carried_keys, carried_values, keys, values, padded, dtype)
         raw = _ops.grouped_projection(low_queries.reshape(batch * length, width), stacked.view(batch * padded, width),
                                       batch).view(batch, length, padded)[..., :slots]
         scores = (raw / math.sqrt(width)).masked_fill(~eligible, float("-inf"))
         any_slot = eligible.any(dim=-1, keepdim=True)
         weights = torch.zeros(batch, length, padded, dtype=dtype, device=queries.device)
         weights[..., :slots].copy_(torch.where(any_slot, torch.softmax(scores, dim=-1), 0.0))
-        transposed = torch.empty(batch, width, padded, dtype=dtype, device=queries.device)
-        transposed[:, :, :carried].copy_(carried_values.transpose(1, 2))
-        transposed[:, :, carried:slots].copy_(values.transpose(1, 2))
-        transposed[:, :, slots:].zero_()
         read = _ops.grouped_projection(weights.view(batch * length, padded), transposed.view(batch * width, padded),
                                        batch).view(batch, length, width)
         return read, raw, any_slot

@@ -259,9 +259,11 @@ def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
                                                   (3000, 1000, 512, 512, False), (256, 16, 2048, 8192, True),
                                                   (7, 300, 64, 64, True), (32, 10242, 2048, 2048, True),
                                                   (200, 1030, 4096, 4096, True), (129, 2048, 8192, 8192, False),
-                                                  (256, 6146, 2048, 2048, True)])
+                                                  (256, 6146, 2048, 2048, True), (8192, 4096, 2048, 2048, True),
+                                                  (5000, 1000, 512, 512, True), (4100, 300, 64, 72, False)])
 def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
-    """tcgen05 projection (split-K or direct) against fp64 on the same bf16 operands."""
+    """tcgen05 projection (split-K, direct, or banded tile order from 4096 rows
+    on, ragged last band included) against fp64 on the same bf16 operands."""
     g = torch.Generator(device=cuda).manual_seed(rows + n)
     wide = torch.randn(rows, stride, generator=g, device=cuda).bfloat16()
     a = wide[:, :k]

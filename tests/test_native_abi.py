@@ -117,3 +117,13 @@ def test_device_init_path_loads_library_without_deadlock(monkeypatch):
     worker.join(timeout=30)
     assert not worker.is_alive(), "ensure_device deadlocked"
     assert calls
+
+
+def test_window_operand_builders_reject_bad_arguments_on_the_host():
+    lib = _native.library()
+    assert lib.koemi_window_pack_rows(None, None, None, 0, 4, None, 8, _native.BF16, None) == _native.KOEMI_ERR_INVALID
+    assert "1 to 8 parts" in _native.last_error()
+    status = lib.koemi_window_slot_operands(None, None, 0, 3, None, None, 0, 4, 2, 64, 12, None, None, _native.BF16,
+                                            None)
+    assert status == _native.KOEMI_ERR_INVALID
+    assert "multiple of 8" in _native.last_error()
