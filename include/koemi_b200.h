@@ -200,8 +200,9 @@ KOEMI_API int koemi_grouped_projection(const void *a, const void *b, float *out,
 /* Row blocks converted to `dtype` (F32/BF16/F16) and packed side by side:
  * out[r, o_p + j] = sources[p][r * strides[p] + j] for j < widths[p], where
  * o_p = widths[0] + ... + widths[p-1], for rows r < rows and 1 to 8 parts
- * (fp32 sources; widths, strides and out_stride multiples of 4; rows 16-byte
- * aligned; `sources`, `strides`, `widths` are host arrays). The window path
+ * (fp32 sources; widths and out_stride multiples of 4, strides even; source
+ * rows 16-byte aligned, 8 where the stride is not a multiple of 4; `sources`,
+ * `strides`, `widths` are host arrays). The window path
  * builds the fusion input [h | memory | local | salient] (network.py:723-732)
  * and the prior [state ; h[:-1]] (network.py:320-325) with it in the GEMMs'
  * operand type, one read of each fp32 element. */

@@ -9,52 +9,112 @@
 // which is what the reference's chunk-pairwise closed form computes (every
 // write strictly before t, decayed by the product of the later decays). The
 // state (basis rows [d, m], normaliser [m]) is read once and written once per
-// window; value and read rows stream through once, so the kernel is
-// HBM-bound where the closed form materialises [T, T] pair weights.
+// window and value and read rows stream through once, where the closed form
+// materialises [T, T] pair weights.
 //
-// Grid (stream, row block): m/4 threads own one basis row as float4 packets
-// in registers; per chunk of 64 positions the CTA stages the features,
-// query features, gates and its rows' values in shared memory (coalesced),
-// warp 0 walks the normaliser recurrence to produce each position's
-// confidence and regulariser, then every row steps through the chunk.
+// Grid (stream, row block), 128 threads: every thread owns R = 64 / m
+// consecutive basis rows (2 for 32 features) in registers, so the staged
+// per-position operands (query features, features, gates) are read from
+// shared memory once per R rows and the dot products need no shuffles; the
+// kernel is FMA-bound (2 m FMAs per row and position). Per chunk of 64
+// positions the CTA stages the features, query features and gates, warp 0
+// walks the normaliser recurrence (one FMA per step and feature, the state
+// before each position kept), every position's confidence and regulariser
+// follow in parallel, then every thread steps its rows through the chunk,
+// its value rows loaded from global two positions ahead and its read rows
+// stored straight back (R consecutive floats per thread: coalesced).
 #include "common.cuh"
 
 namespace koemi {
 namespace {
 
-constexpr int kWindowThreads = 256;
+constexpr int kWindowThreads = 128;
+constexpr int kWindowChunk = 64;
 constexpr float kReadEpsilon = 1.0f / 256.0f;
 
-// Positions staged per chunk: 64, or 32 for 4 features (256 rows per CTA
-// then, and the staged values must stay within the static shared memory).
 template <int kM>
-constexpr int window_chunk() {
-    return kM >= 8 ? 64 : 32;
+constexpr int rows_per_thread() {
+    return kM >= 32 ? 2 : 64 / kM;
 }
 
-template <int kM>
+// R consecutive floats of a row block starting at `p` (rows past `live`
+// read as zero). kVec: p is 8-byte (R = 2) or 16-byte aligned and live is a
+// multiple of the vector width.
+template <int kR, bool kVec>
+__device__ __forceinline__ void load_rows(const float *p, int live, float (&out)[kR]) {
+    if constexpr (kVec && kR % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < kR; i += 4) {
+            const float4 v = i < live ? __ldg(reinterpret_cast<const float4 *>(p + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            out[i] = v.x;
+            out[i + 1] = v.y;
+            out[i + 2] = v.z;
+            out[i + 3] = v.w;
+        }
+    } else if constexpr (kVec && kR == 2) {
+        const float2 v = live > 0 ? __ldg(reinterpret_cast<const float2 *>(p)) : make_float2(0.f, 0.f);
+        out[0] = v.x;
+        out[1] = v.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < kR; ++i) out[i] = i < live ? __ldg(p + i) : 0.0f;
+    }
+}
+
+template <int kR, bool kVec>
+__device__ __forceinline__ void store_rows(float *p, int live, const float (&in)[kR]) {
+    if constexpr (kVec && kR % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < kR; i += 4) {
+            if (i < live) *reinterpret_cast<float4 *>(p + i) = make_float4(in[i], in[i + 1], in[i + 2], in[i + 3]);
+        }
+    } else if constexpr (kVec && kR == 2) {
+        if (live > 0) *reinterpret_cast<float2 *>(p) = make_float2(in[0], in[1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < kR; ++i) {
+            if (i < live) p[i] = in[i];
+        }
+    }
+}
+
+template <int kM, bool kVec>
 __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
     const float *__restrict__ decay, const float *__restrict__ write, const float *__restrict__ value,
     const float *__restrict__ features, const float *__restrict__ query_features, float *__restrict__ basis,
     float *__restrict__ normalizer, float *__restrict__ read_out, int64_t length, int64_t d) {
-    static_assert(kM % 4 == 0 && kM <= 32 && 32 % (kM / 4) == 0, "4, 8, 16 or 32 features");
-    constexpr int kWindowChunk = window_chunk<kM>();
-    constexpr int kParts = kM / 4;
-    constexpr int kRows = kWindowThreads / kParts;
+    static_assert(kM % 4 == 0 && kM <= 32, "4, 8, 16 or 32 features");
+    constexpr int kR = rows_per_thread<kM>();
+    constexpr int kQ = kM / 4;
     __shared__ __align__(16) float sf[kWindowChunk][kM];
     __shared__ __align__(16) float sq[kWindowChunk][kM];
-    __shared__ float sval[kWindowChunk][kRows];
+    __shared__ __align__(16) float sn[kWindowChunk][kM];
     __shared__ float sdecay[kWindowChunk], swrite[kWindowChunk], sconf[kWindowChunk], sreg[kWindowChunk];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t b = blockIdx.x;
-    const int64_t row0 = static_cast<int64_t>(blockIdx.y) * kRows;
-    const int local_row = threadIdx.x / kParts;
-    const int part = threadIdx.x % kParts;
-    const int64_t row = row0 + local_row;
-    const bool live = row < d;
-    float *brow = basis + (b * d + row) * kM;
-    float4 x = live ? reinterpret_cast<const float4 *>(brow)[part] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int64_t row = static_cast<int64_t>(blockIdx.y) * (kWindowThreads * kR) + threadIdx.x * kR;
+    const int live = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(kR), d - row)));
+
+    float x[kR][kM];
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+        const float *brow = basis + (b * d + row + r) * kM;
+#pragma unroll
+        for (int q = 0; q < kQ; ++q) {
+            const float4 v = r < live ? reinterpret_cast<const float4 *>(brow)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+            x[r][4 * q] = v.x;
+            x[r][4 * q + 1] = v.y;
+            x[r][4 * q + 2] = v.z;
+            x[r][4 * q + 3] = v.w;
+        }
+    }
     float nrm = warp == 0 && lane < kM ? normalizer[b * kM + lane] : 0.0f;
+
+    // value rows two positions ahead
+    const float *vbase = value + b * length * d + row;
+    float v0[kR], v1[kR] = {};
+    load_rows<kR, kVec>(vbase, live, v0);
+    if (length > 1) load_rows<kR, kVec>(vbase + d, live, v1);
 
     for (int64_t t0 = 0; t0 < length; t0 += kWindowChunk) {
         const int n = static_cast<int>(length - t0 < kWindowChunk ? length - t0 : kWindowChunk);
@@ -68,40 +128,73 @@ __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
             sdecay[i] = decay[b * length + t0 + i];
             swrite[i] = write[b * length + t0 + i];
         }
-        for (int i = threadIdx.x; i < n * kRows; i += kWindowThreads) {
-            const int t = i / kRows, r = i % kRows;
-            sval[t][r] = row0 + r < d ? value[(b * length + t0 + t) * d + row0 + r] : 0.0f;
-        }
         __syncthreads();
-        if (warp == 0) {  // normaliser recurrence: each position's confidence and regulariser
+        if (warp == 0 && lane < kM) {  // normaliser before each position
             for (int t = 0; t < n; ++t) {
-                float den = lane < kM ? nrm * sq[t][lane] : 0.0f;
-                den = warp_sum(den);
-                if (lane == 0) {
-                    const float reg = den + kReadEpsilon;
-                    sconf[t] = den / reg;
-                    sreg[t] = reg;
-                }
-                if (lane < kM) nrm = sdecay[t] * nrm + swrite[t] * sf[t][lane];
+                sn[t][lane] = nrm;
+                nrm = sdecay[t] * nrm + swrite[t] * sf[t][lane];
             }
         }
         __syncthreads();
-        for (int t = 0; t < n; ++t) {
-            const float4 qv = reinterpret_cast<const float4 *>(sq[t])[part];
-            float num = x.x * qv.x + x.y * qv.y + x.z * qv.z + x.w * qv.w;
+        for (int t = threadIdx.x; t < n; t += kWindowThreads) {  // confidence and regulariser
+            float den = 0.0f;
 #pragma unroll
-            for (int o = 1; o < kParts; o <<= 1) num += __shfl_xor_sync(0xffffffffu, num, o);
-            if (live && part == 0) read_out[(b * length + t0 + t) * d + row] = sconf[t] * num / sreg[t];
-            const float4 fv = reinterpret_cast<const float4 *>(sf[t])[part];
-            const float dk = sdecay[t];
-            const float v = swrite[t] * sval[t][local_row];
-            x.x = dk * x.x + v * fv.x;
-            x.y = dk * x.y + v * fv.y;
-            x.z = dk * x.z + v * fv.z;
-            x.w = dk * x.w + v * fv.w;
+            for (int m = 0; m < kM; ++m) den += sn[t][m] * sq[t][m];
+            const float reg = den + kReadEpsilon;
+            sconf[t] = den / reg;
+            sreg[t] = reg;
+        }
+        __syncthreads();
+        for (int t = 0; t < n; ++t) {
+            const int64_t tt = t0 + t;
+            float v2[kR] = {};
+            if (tt + 2 < length) load_rows<kR, kVec>(vbase + (tt + 2) * d, live, v2);
+            float num[kR];
+#pragma unroll
+            for (int r = 0; r < kR; ++r) num[r] = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) {
+                const float4 qv = reinterpret_cast<const float4 *>(sq[t])[q];
+#pragma unroll
+                for (int r = 0; r < kR; ++r) {
+                    num[r] += x[r][4 * q] * qv.x + x[r][4 * q + 1] * qv.y + x[r][4 * q + 2] * qv.z + x[r][4 * q + 3] * qv.w;
+                }
+            }
+            const float conf = sconf[t], reg = sreg[t];
+            float out[kR];
+#pragma unroll
+            for (int r = 0; r < kR; ++r) out[r] = conf * num[r] / reg;
+            store_rows<kR, kVec>(read_out + (b * length + tt) * d + row, live, out);
+            const float dk = sdecay[t], wr = swrite[t];
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) {
+                const float4 fv = reinterpret_cast<const float4 *>(sf[t])[q];
+#pragma unroll
+                for (int r = 0; r < kR; ++r) {
+                    const float v = wr * v0[r];
+                    x[r][4 * q] = dk * x[r][4 * q] + v * fv.x;
+                    x[r][4 * q + 1] = dk * x[r][4 * q + 1] + v * fv.y;
+                    x[r][4 * q + 2] = dk * x[r][4 * q + 2] + v * fv.z;
+                    x[r][4 * q + 3] = dk * x[r][4 * q + 3] + v * fv.w;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kR; ++r) {
+                v0[r] = v1[r];
+                v1[r] = v2[r];
+            }
         }
     }
-    if (live) reinterpret_cast<float4 *>(brow)[part] = x;
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+        if (r < live) {
+            float *brow = basis + (b * d + row + r) * kM;
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) {
+                reinterpret_cast<float4 *>(brow)[q] = make_float4(x[r][4 * q], x[r][4 * q + 1], x[r][4 * q + 2], x[r][4 * q + 3]);
+            }
+        }
+    }
     if (blockIdx.y == 0 && warp == 0 && lane < kM) normalizer[b * kM + lane] = nrm;
 }
 
@@ -124,6 +217,7 @@ extern "C" int koemi_assoc_window_scan_read(const float *decay, const float *wri
     }
     if (!aligned(basis, 16)) return fail(KOEMI_ERR_INVALID, "basis must be 16-byte aligned");
     if (batch > 2147483647) return fail(KOEMI_ERR_INVALID, "too many streams");
+    const bool vec = width % 4 == 0 && aligned(value, 16) && aligned(read_out, 16);
     auto run = [&](auto kernel, int rows_per_cta) -> int {
         const int64_t blocks_y = ceil_div(width, rows_per_cta);
         if (blocks_y > 65535) return fail(KOEMI_ERR_INVALID, "width too large");
@@ -133,10 +227,15 @@ extern "C" int koemi_assoc_window_scan_read(const float *decay, const float *wri
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };
+    auto pick = [&](auto features_tag) -> int {
+        constexpr int kM = decltype(features_tag)::value;
+        constexpr int rows = kWindowThreads * rows_per_thread<kM>();
+        return vec ? run(assoc_window_kernel<kM, true>, rows) : run(assoc_window_kernel<kM, false>, rows);
+    };
     switch (feature_count) {
-        case 4: return run(assoc_window_kernel<4>, kWindowThreads / 1);
-        case 8: return run(assoc_window_kernel<8>, kWindowThreads / 2);
-        case 16: return run(assoc_window_kernel<16>, kWindowThreads / 4);
-        default: return run(assoc_window_kernel<32>, kWindowThreads / 8);
+        case 4: return pick(std::integral_constant<int, 4>());
+        case 8: return pick(std::integral_constant<int, 8>());
+        case 16: return pick(std::integral_constant<int, 16>());
+        default: return pick(std::integral_constant<int, 32>());
     }
 }

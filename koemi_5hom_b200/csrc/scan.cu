@@ -792,6 +792,30 @@ __global__ void bounded_gates_kernel(const float *__restrict__ projections,
     retention[index] = a;
     increment[index] = (1.0f - a) * tanhf(pre_c);
 }
+// Four features per thread (16-byte loads and stores), grid (feature
+// chunks, row blocks): the window path's [rows, 2 F] projections stream
+// through once.
+__global__ __launch_bounds__(256) void bounded_gates_vec_kernel(const float *__restrict__ projections,
+                                                                const uint8_t *__restrict__ valid,
+                                                                float *__restrict__ retention,
+                                                                float *__restrict__ increment, int64_t rows,
+                                                                int64_t features, float lo, float hi) {
+    const int64_t f = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (f >= features) return;
+    for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+        float4 a = make_float4(1.0f, 1.0f, 1.0f, 1.0f), inc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (valid == nullptr || valid[row] != 0) {
+            const float4 pa = __ldg(reinterpret_cast<const float4 *>(projections + row * 2 * features + f));
+            const float4 pc = __ldg(reinterpret_cast<const float4 *>(projections + row * 2 * features + features + f));
+            a = make_float4(lo + (hi - lo) * sigmoidf_(pa.x), lo + (hi - lo) * sigmoidf_(pa.y),
+                            lo + (hi - lo) * sigmoidf_(pa.z), lo + (hi - lo) * sigmoidf_(pa.w));
+            inc = make_float4((1.0f - a.x) * tanhf(pc.x), (1.0f - a.y) * tanhf(pc.y), (1.0f - a.z) * tanhf(pc.z),
+                              (1.0f - a.w) * tanhf(pc.w));
+        }
+        *reinterpret_cast<float4 *>(retention + row * features + f) = a;
+        *reinterpret_cast<float4 *>(increment + row * features + f) = inc;
+    }
+}
 }  // namespace
 }  // namespace koemi
 
@@ -802,6 +826,14 @@ extern "C" int koemi_dense_bounded_gates(const float *projections, const uint8_t
     clear_error();
     if (rows < 0 || features < 0) return fail(KOEMI_ERR_INVALID, "negative gate sizes");
     if (rows == 0 || features == 0) return KOEMI_OK;
+    if (features % 4 == 0 && aligned(projections, 16) && aligned(retention, 16) && aligned(increment, 16)) {
+        const unsigned chunks = static_cast<unsigned>(ceil_div(features / 4, 256));
+        const unsigned row_blocks = static_cast<unsigned>(rows < 65535 ? rows : 65535);
+        bounded_gates_vec_kernel<<<dim3(chunks, row_blocks), 256, 0, as_stream(stream)>>>(
+            projections, valid, retention, increment, rows, features, minimum_retention, maximum_retention);
+        KOEMI_LAUNCH_CHECK();
+        return KOEMI_OK;
+    }
     const int64_t total = rows * features;
     bounded_gates_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, as_stream(stream)>>>(
         projections, valid, retention, increment, rows, features, minimum_retention,

@@ -162,6 +162,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 }
 
 __device__ __forceinline__ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+__device__ __forceinline__ bool aligned8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
 // Cluster barrier over every thread of every CTA of the cluster, with
 // release/acquire ordering of shared-memory writes at cluster scope.
@@ -584,6 +585,11 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                             for (int q = 0; q < 8; ++q) {
                                 reinterpret_cast<float4 *>(dst)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
                             }
+                        } else if (col0 + 32 <= args.n_out && aligned8(dst)) {
+                            // rows of an even but not 4-aligned stride (the
+                            // associative projection's 3 d + 2 columns)
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) reinterpret_cast<float2 *>(dst)[q] = make_float2(o[2 * q], o[2 * q + 1]);
                         } else {
                             for (int j = 0; j < 32 && col0 + j < args.n_out; ++j) dst[j] = o[j];
                         }
@@ -782,6 +788,9 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         float *dst = out + (half_row0 + r) * args.out_stride + col;
                         if (col + 4 <= args.n_out && aligned16(dst)) {
                             *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                        } else if (col + 4 <= args.n_out && aligned8(dst)) {
+                            reinterpret_cast<float2 *>(dst)[0] = make_float2(o[0], o[1]);
+                            reinterpret_cast<float2 *>(dst)[1] = make_float2(o[2], o[3]);
                         } else {
                             for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
                         }

@@ -68,7 +68,14 @@ __global__ __launch_bounds__(kPackThreads) void pack_rows_kernel(const __grid_co
             if (col[j] >= 0) {
                 int p = 0;
                 while (p + 1 < a.parts && col[j] >= a.offset[p + 1]) ++p;
-                v[j] = __ldg(reinterpret_cast<const float4 *>(a.source[p] + r * a.stride[p] + (col[j] - a.offset[p])));
+                const float *src = a.source[p] + r * a.stride[p] + (col[j] - a.offset[p]);
+                if (a.stride[p] % 4 == 0) {
+                    v[j] = __ldg(reinterpret_cast<const float4 *>(src));
+                } else {  // rows of an even stride: two 8-byte loads
+                    const float2 lo = __ldg(reinterpret_cast<const float2 *>(src));
+                    const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + 2));
+                    v[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                }
             }
         }
 #pragma unroll
@@ -166,9 +173,12 @@ extern "C" int koemi_window_pack_rows(const float *const *sources, const int64_t
     PackArgs args{};
     int64_t total = 0;
     for (int p = 0; p < parts; ++p) {
-        if (widths[p] < 0 || widths[p] % 4 != 0 || strides[p] % 4 != 0 || (widths[p] > 0 && !aligned(sources[p], 16))) {
+        const bool wide = strides[p] % 4 == 0;
+        if (widths[p] < 0 || widths[p] % 4 != 0 || strides[p] % 2 != 0 ||
+            (widths[p] > 0 && !aligned(sources[p], wide ? 16 : 8))) {
             return fail(KOEMI_ERR_INVALID,
-                        "pack_rows part %d: widths and row strides must be multiples of 4 and the rows 16-byte aligned", p);
+                        "pack_rows part %d: widths must be multiples of 4, row strides even and the rows aligned "
+                        "(16 bytes, 8 for strides that are not multiples of 4)", p);
         }
         args.source[p] = sources[p];
         args.stride[p] = strides[p];

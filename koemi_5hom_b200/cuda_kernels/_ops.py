@@ -135,7 +135,7 @@ def _(a, b, groups):
 
 def _rows_view(t: Tensor) -> tuple[Tensor, int]:
     """A 2-D fp32 row block whose rows are contiguous, and its row stride."""
-    if t.dim() != 2 or t.stride(1) != 1 or t.stride(0) % 4 or t.data_ptr() % 16:
+    if t.dim() != 2 or t.stride(1) != 1 or t.stride(0) % 2 or t.data_ptr() % (16 if t.stride(0) % 4 == 0 else 8):
         t = t.contiguous()
     return t, t.stride(0)
 

@@ -496,8 +496,13 @@ class KoemiModel(nn.Module):
         rows = batch * length
         valid_flat = valid.reshape(-1)
 
+        # 16-bit models on CUDA: every GEMM operand is produced once in the
+        # compute dtype (the norm writes it, h is converted once)
+        low = self.compute_dtype != torch.float32 and x.is_cuda and d % 8 == 0
+        operand_dtype = self.compute_dtype if low else torch.float32
+
         # input norm (core), gates (dense), scan (dense): network.py:305-310
-        u = _ops.rms_norm(x.reshape(rows, d), None, cache["input_norm"], None, NORM_EPSILON, torch.float32)
+        u = _ops.rms_norm(x.reshape(rows, d), None, cache["input_norm"], None, NORM_EPSILON, operand_dtype)
         pre = self._linear(u, block.gates_weight, block.gates_bias)
         retention, increment = _ops.bounded_gates(pre, valid_flat, MIN_RETENTION, MAX_RETENTION)
         h = _ops.affine_scan_forward(retention.reshape(batch, length, d), increment.reshape(batch, length, d),
@@ -526,24 +531,31 @@ class KoemiModel(nn.Module):
             surprise = _ops.causal_surprise_forward(prior, self._cache["content_w"],
                                                     self._cache["content_b"], targets, valid, torch.float32)
 
-        # local ring entries + sliding-window read: memory.py:297-361
-        local = self._linear(h, block.local_weight, block.local_bias)
+        # local ring entries + sliding-window read: memory.py:297-361; 16-bit
+        # models read the rings on tensor cores (bf16 operands, fp32 results)
+        low_queries = h.to(self.compute_dtype) if low else None
+        projection_in = low_queries if low else h
+        local = self._linear(projection_in, block.local_weight, block.local_bias)
         keep = valid.unsqueeze(-1)
         keys = torch.where(keep, local[..., :d], 0.0)
         values = torch.where(keep, local[..., d:], 0.0)
-        # 16-bit models read the rings on tensor cores (bf16 operands, fp32 results)
-        low_queries = (h.to(self.compute_dtype) if self.compute_dtype != torch.float32 and h.is_cuda
-                       and d % 8 == 0 else None)
         local_value, novelty = _local_read(state.local_keys, state.local_values, state.local_valid, keys, values, valid,
                                            h, s.local_memory_size, low_queries)
 
         # associative memory: memory.py:82-144,244-255
-        assoc = self._linear(h, block.assoc_weight, block.assoc_bias)
+        assoc = self._linear(projection_in, block.assoc_weight, block.assoc_bias)
         key, query = assoc[..., :d], assoc[..., d:2 * d]
         mem_value = torch.tanh(assoc[..., 2 * d:3 * d])
         decay = MIN_DECAY + (MAX_DECAY - MIN_DECAY) * torch.sigmoid(assoc[..., 3 * d])
         write = torch.sigmoid(assoc[..., 3 * d + 1])
-        both = self._linear(torch.stack((key, query)), block.feature_weight, block.feature_bias).softmax(dim=-1)
+        if low:  # key and query rows converted straight into one operand block
+            stacked = torch.empty(2 * rows, d, dtype=self.compute_dtype, device=h.device)
+            _ops.pack_rows(stacked[:rows], [key.reshape(rows, d)])
+            _ops.pack_rows(stacked[rows:], [query.reshape(rows, d)])
+            both = self._linear(stacked, block.feature_weight, block.feature_bias).view(2, batch, length, -1)
+        else:
+            both = self._linear(torch.stack((key, query)), block.feature_weight, block.feature_bias)
+        both = both.softmax(dim=-1)
         features, query_features = both[0], both[1]
         fast_decay = torch.where(valid, decay, 1.0)
         fast_write = torch.where(valid, write * (0.25 + 0.75 * surprise.clamp(0.0, 1.0)), 0.0)
