@@ -73,7 +73,7 @@ def parse_args(argv=None):
                    help="after the measurement, write per-kernel device times of 3 profiled decode steps "
                         "(torch profiler, CUDA activity) to this JSON file")
     p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "permute", "expert_decode", "surprise_decode",
-                                    "surprise_prefill", "dense_decode"),
+                                    "surprise_prefill", "dense_decode", "window"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
     p.add_argument("--op-rows", type=int, default=None,
                    help="activation rows of --op dense_decode (default 256; 32 is one rank's share at 8 GPUs)")
@@ -723,6 +723,58 @@ def run_op(args) -> None:
         shape = f"config 5 decode block: {rows} rows; gates 4096x2048, local 4096x2048, assoc 6146x2048, " \
                 "fusion 2048x8192 bf16 -> fp32"
         extra = {"per_projection": per}
+    elif args.op == "window":  # the prefill window's bandwidth kernels, config-5 window shape
+        batch, length, d, m, carried = 256, 128, 2048, 16, 128
+        rows, padded = batch * length, carried + length
+        t = lambda *shape: torch.randn(*shape, device=device, generator=g)  # noqa: E731
+        ring_k, ring_v, keys, values = t(batch, carried, d), t(batch, carried, d), t(batch, length, d), t(batch, length, d)
+        basis, norm = t(batch, d, m) * 0.1, torch.rand(batch, m, device=device, generator=g)
+        decay = torch.sigmoid(t(batch, length)) * 0.5 + 0.5
+        write = torch.sigmoid(t(batch, length))
+        feats = torch.softmax(t(batch, length, m), -1)
+        query = torch.softmax(t(batch, length, m), -1)
+        pre = t(rows, 2 * d)
+        valid = torch.ones(rows, dtype=torch.bool, device=device)
+        parts = [t(rows, d) for _ in range(4)]
+        fusion_in = torch.empty(rows, 4 * d, dtype=torch.bfloat16, device=device)
+        queries = t(rows, d).bfloat16()
+        weights = torch.softmax(t(rows, padded), -1).bfloat16()
+        stacked, transposed = _ops.window_slot_operands(ring_k, ring_v, keys, values, padded, torch.bfloat16)
+        read_out = torch.empty_like(values)
+        f32, b16 = 4, 2
+        kernels = {
+            # name: (call, algorithmic bytes per launch)
+            # through the C ABI in place (the op clones the state first)
+            "assoc_window_scan_read": (
+                lambda: _native.call("koemi_assoc_window_scan_read", decay.data_ptr(), write.data_ptr(),
+                                     values.data_ptr(), feats.data_ptr(), query.data_ptr(), basis.data_ptr(),
+                                     norm.data_ptr(), read_out.data_ptr(), batch, length, d, m,
+                                     _native.stream_of(values)),
+                2 * rows * d * f32 + 2 * batch * d * m * f32 + 2 * rows * m * f32 + 2 * rows * f32),
+            "window_slot_operands": (
+                lambda: _ops.window_slot_operands(ring_k, ring_v, keys, values, padded, torch.bfloat16),
+                2 * batch * padded * d * f32 + 2 * batch * padded * d * b16),
+            "pack_rows_fusion_input": (lambda: _ops.pack_rows(fusion_in, parts), 4 * rows * d * (f32 + b16)),
+            "bounded_gates": (lambda: _ops.bounded_gates(pre, valid, 0.05, 0.995),
+                              rows * 2 * d * f32 + 2 * rows * d * f32 + rows),
+            "ring_scores_grouped_projection": (
+                lambda: _ops.grouped_projection(queries, stacked.view(batch * padded, d), batch),
+                rows * d * b16 + batch * padded * d * b16 + rows * padded * f32),
+            "ring_read_grouped_projection": (
+                lambda: _ops.grouped_projection(weights, transposed.view(batch * d, padded), batch),
+                rows * padded * b16 + batch * d * padded * b16 + rows * d * f32),
+        }
+        per = {}
+        for name, (fn, nbytes) in kernels.items():
+            t_op = _time_op(fn, args.steps, args.warmup, graph=True)
+            per[name] = {"us": t_op * 1e6, "gbs": nbytes / t_op / 1e9, "frac": nbytes / t_op / 1e9 / hbm,
+                         "bytes": nbytes}
+        seconds = sum(v["us"] for v in per.values()) / 1e6
+        moved = sum(v["bytes"] for v in per.values())
+        work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = (f"config-5 prefill window: {batch} streams x {length} positions, d={d}, {m} memory features, "
+                 f"{carried} carried ring slots (every input > L2)")
+        extra = {"per_kernel": per}
     else:  # surprise head: decode (256 rows) or one prefill window (32768 rows) of config 5
         rows = 256 if args.op == "surprise_decode" else 32768
         prior = torch.randn(rows, 2048, device=device, generator=g).bfloat16()

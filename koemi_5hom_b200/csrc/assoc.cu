@@ -19,8 +19,8 @@
 // kernel is FMA-bound (2 m FMAs per row and position). Per chunk of 64
 // positions the CTA stages the features, query features and gates, warp 0
 // walks the normaliser recurrence (one FMA per step and feature, the state
-// before each position kept), every position's confidence and regulariser
-// follow in parallel, then every thread steps its rows through the chunk,
+// before each position kept), every position's read scale (den / reg) / reg
+// follows in parallel, then every thread steps its rows through the chunk,
 // its value rows loaded from global two positions ahead and its read rows
 // stored straight back (R consecutive floats per thread: coalesced).
 #include "common.cuh"
@@ -89,7 +89,7 @@ __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
     __shared__ __align__(16) float sf[kWindowChunk][kM];
     __shared__ __align__(16) float sq[kWindowChunk][kM];
     __shared__ __align__(16) float sn[kWindowChunk][kM];
-    __shared__ float sdecay[kWindowChunk], swrite[kWindowChunk], sconf[kWindowChunk], sreg[kWindowChunk];
+    __shared__ float sdecay[kWindowChunk], swrite[kWindowChunk], sscale[kWindowChunk];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t b = blockIdx.x;
     const int64_t row = static_cast<int64_t>(blockIdx.y) * (kWindowThreads * kR) + threadIdx.x * kR;
@@ -141,8 +141,7 @@ __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
 #pragma unroll
             for (int m = 0; m < kM; ++m) den += sn[t][m] * sq[t][m];
             const float reg = den + kReadEpsilon;
-            sconf[t] = den / reg;
-            sreg[t] = reg;
+            sscale[t] = den / reg / reg;  // read = (den / reg) (B . q) / reg
         }
         __syncthreads();
         for (int t = 0; t < n; ++t) {
@@ -160,10 +159,10 @@ __global__ __launch_bounds__(kWindowThreads) void assoc_window_kernel(
                     num[r] += x[r][4 * q] * qv.x + x[r][4 * q + 1] * qv.y + x[r][4 * q + 2] * qv.z + x[r][4 * q + 3] * qv.w;
                 }
             }
-            const float conf = sconf[t], reg = sreg[t];
+            const float scale = sscale[t];
             float out[kR];
 #pragma unroll
-            for (int r = 0; r < kR; ++r) out[r] = conf * num[r] / reg;
+            for (int r = 0; r < kR; ++r) out[r] = scale * num[r];
             store_rows<kR, kVec>(read_out + (b * length + tt) * d + row, live, out);
             const float dk = sdecay[t], wr = swrite[t];
 #pragma unroll

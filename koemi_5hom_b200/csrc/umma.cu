@@ -48,10 +48,13 @@ constexpr int kThreads = 192;  // problems with four epilogue warps
 
 // The gated problem's SwiGLU epilogue (two TMEM reads, bias adds and a SiLU
 // per output) takes longer than the MMAs of a tile with four warps, so it
-// runs eight: two per TMEM lane quarter, each on half of the columns.
+// runs eight: two per TMEM lane quarter, each on half of the columns. The
+// direct dense problem runs eight as well: its paired tiles use both TMEM
+// accumulators, so its epilogue (256 rows x 256 fp32 columns) does not
+// overlap the next tile's MMAs and its length is lost time.
 template <int kProblem>
 constexpr int epilogue_warps() {
-    return kProblem == 0 ? 8 : 4;
+    return kProblem == 0 || kProblem == 3 ? 8 : 4;
 }
 template <int kProblem>
 constexpr int threads_for() {
@@ -563,8 +566,10 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                 const bool direct = args.splits == 1;
                 float *dst_row = direct ? static_cast<float *>(args.out) + row * args.out_stride
                                         : args.partials + (tile.split * args.rows + row) * args.n_out;
+                constexpr int kChunks = kTileN / 32 / kParts;
 #pragma unroll 1
-                for (int c = 0; c < kTileN / 32; ++c) {
+                for (int cc = 0; cc < kChunks; ++cc) {
+                    const int c = part * kChunks + cc;
                     uint32_t y[32];
                     KOEMI_TMEM_LD32(taddr + c * 32, y);
                     tmem_wait_ld();
