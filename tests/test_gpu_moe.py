@@ -261,10 +261,13 @@ def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
                                                   (200, 1030, 4096, 4096, True), (129, 2048, 8192, 8192, False),
                                                   (256, 6146, 2048, 2048, True), (8192, 4096, 2048, 2048, True),
                                                   (5000, 1000, 512, 512, True), (4100, 300, 64, 72, False),
-                                                  (4608, 6146, 512, 512, True)])
+                                                  (4608, 6146, 512, 512, True), (40, 4096, 2048, 2048, True),
+                                                  (1, 8192, 1024, 1024, False), (64, 5000, 8192, 8200, True),
+                                                  (17, 3600, 256, 264, True)])
 def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
-    """tcgen05 projection (split-K, direct, or banded tile order from 4096 rows
-    on, ragged last band included) against fp64 on the same bf16 operands."""
+    """tcgen05 projection (cluster split-K, direct, or paired tiles in banded
+    order from 4096 rows on, ragged last band included) against fp64 on the
+    same bf16 operands."""
     g = torch.Generator(device=cuda).manual_seed(rows + n)
     wide = torch.randn(rows, stride, generator=g, device=cuda).bfloat16()
     a = wide[:, :k]
