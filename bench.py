@@ -73,7 +73,7 @@ def parse_args(argv=None):
                    help="after the measurement, write per-kernel device times of 3 profiled decode steps "
                         "(torch profiler, CUDA activity) to this JSON file")
     p.add_argument("--op", choices=("scan", "rmsnorm", "moe", "moe_ep", "permute", "expert_decode", "surprise_decode",
-                                    "surprise_prefill", "dense_decode", "window"),
+                                    "surprise_prefill", "dense_decode", "window", "ring_decode"),
                    default=None, help="time one operator at its BASELINE shape instead of the decode step")
     p.add_argument("--op-rows", type=int, default=None,
                    help="activation rows of --op dense_decode (default 256; 32 is one rank's share at 8 GPUs)")
@@ -723,6 +723,28 @@ def run_op(args) -> None:
         shape = f"config 5 decode block: {rows} rows; gates 4096x2048, local 4096x2048, assoc 6146x2048, " \
                 "fusion 2048x8192 bf16 -> fp32"
         extra = {"per_projection": per}
+    elif args.op == "ring_decode":  # both exact-memory rings of one config-5 decode block, full, bf16
+        batch, d, slots = 256, 2048, 128
+        rings = [(torch.randn(batch, slots, d, device=device, generator=g) * 0.1).bfloat16() for _ in range(4)]
+        valid_slots = [torch.ones(batch, slots, dtype=torch.uint8, device=device) for _ in range(2)]
+        head = torch.zeros(1, dtype=torch.int64, device=device)
+        s_head = torch.zeros(batch, dtype=torch.int32, device=device)
+        s_count = torch.full((batch,), slots, dtype=torch.int32, device=device)
+        queries = torch.randn(batch, d, device=device, generator=g)
+        entries = torch.randn(batch, 2 * d, device=device, generator=g) * 0.1
+        valid = torch.ones(batch, dtype=torch.uint8, device=device)
+        surprise = torch.zeros(batch, device=device)  # nothing admitted: the salient ring stays full
+        out = torch.empty(batch, 2 * d, dtype=torch.bfloat16, device=device)
+        novelty = torch.empty(batch, device=device)
+        seconds = _time_op(lambda: _native.call(
+            "koemi_think_ring_decode_step", queries.data_ptr(), d, entries.data_ptr(), 2 * d, valid.data_ptr(),
+            surprise.data_ptr(), 0.64, rings[0].data_ptr(), rings[1].data_ptr(), valid_slots[0].data_ptr(),
+            head.data_ptr(), rings[2].data_ptr(), rings[3].data_ptr(), valid_slots[1].data_ptr(), s_head.data_ptr(),
+            s_count.data_ptr(), out.data_ptr(), out[:, d:].data_ptr(), 2 * d, novelty.data_ptr(), None, batch, d,
+            slots, slots, _native.BF16, _native.BF16, _native.stream_of(queries)), args.steps, args.warmup, graph=True)
+        moved = 4 * batch * slots * d * 2 + batch * d * 4 + batch * 2 * d * 2
+        work, unit, peak, bound = moved / seconds / 1e9, "GB/s", hbm, "hbm"
+        shape = f"config-5 decode block: {batch} streams, local + salient rings of {slots} bf16 slots, d={d}, all valid"
     elif args.op == "window":  # the prefill window's bandwidth kernels, config-5 window shape
         batch, length, d, m, carried = 256, 128, 2048, 16, 128
         rows, padded = batch * length, carried + length
