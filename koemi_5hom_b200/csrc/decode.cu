@@ -634,10 +634,18 @@ __device__ void assoc_feature_logits_staged(const float *__restrict__ proj, cons
                 } else {
                     unpack(raw[i][0], wv, TW{});
                 }
+                // the staged rows read as 16-byte packets (c is a multiple of
+                // 8 and d of 8): two loads per row instead of eight
+                // bank-conflicted scalar ones; the FMAs keep their order
+                float xk[8], xq[8];
+                *reinterpret_cast<float4 *>(xk) = reinterpret_cast<const float4 *>(xs + c)[0];
+                *reinterpret_cast<float4 *>(xk + 4) = reinterpret_cast<const float4 *>(xs + c)[1];
+                *reinterpret_cast<float4 *>(xq) = reinterpret_cast<const float4 *>(xs + d + c)[0];
+                *reinterpret_cast<float4 *>(xq + 4) = reinterpret_cast<const float4 *>(xs + d + c)[1];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    acc0 = fmaf(xs[c + e], wv[e], acc0);
-                    acc1 = fmaf(xs[d + c + e], wv[e], acc1);
+                    acc0 = fmaf(xk[e], wv[e], acc0);
+                    acc1 = fmaf(xq[e], wv[e], acc1);
                 }
             }
         }
@@ -875,10 +883,18 @@ __global__ __launch_bounds__(kAssocThreads, 2) void assoc_decode_prefetch_kernel
                 } else {
                     unpack(wraw[i][0], wv, TW{});
                 }
+                // the staged rows read as 16-byte packets (c is a multiple of
+                // 8 and d of 8): two loads per row instead of eight
+                // bank-conflicted scalar ones; the FMAs keep their order
+                float xk[8], xq[8];
+                *reinterpret_cast<float4 *>(xk) = reinterpret_cast<const float4 *>(xs + c)[0];
+                *reinterpret_cast<float4 *>(xk + 4) = reinterpret_cast<const float4 *>(xs + c)[1];
+                *reinterpret_cast<float4 *>(xq) = reinterpret_cast<const float4 *>(xs + d + c)[0];
+                *reinterpret_cast<float4 *>(xq + 4) = reinterpret_cast<const float4 *>(xs + d + c)[1];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    acc0 = fmaf(xs[c + e], wv[e], acc0);
-                    acc1 = fmaf(xs[d + c + e], wv[e], acc1);
+                    acc0 = fmaf(xk[e], wv[e], acc0);
+                    acc1 = fmaf(xq[e], wv[e], acc1);
                 }
             }
         }
