@@ -186,11 +186,15 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_kernel(RingArgs a) {
         float dot = 0.0f, kk = 0.0f;
 #pragma unroll 8
         for (int64_t c = lane; c < packets; c += 32) {
-            float k[W];
+            float k[W], qv[W];
             P::load(row + c * W, k);
 #pragma unroll
+            for (int e = 0; e < W; e += 4) {  // the query packet as 16-byte shared loads (q is 16-byte aligned)
+                *reinterpret_cast<float4 *>(qv + e) = *reinterpret_cast<const float4 *>(q + c * W + e);
+            }
+#pragma unroll
             for (int e = 0; e < W; ++e) {
-                dot = fmaf(k[e], q[c * W + e], dot);
+                dot = fmaf(k[e], qv[e], dot);
                 kk = fmaf(k[e], k[e], kk);
             }
         }
@@ -397,11 +401,15 @@ __global__ __launch_bounds__(kRingThreads) void ring_decode_split_kernel(RingArg
         float dot = 0.0f, kk = 0.0f;
 #pragma unroll 8
         for (int64_t c = lane; c < packets; c += 32) {
-            float k[W];
+            float k[W], qv[W];
             P::load(row + c * W, k);
 #pragma unroll
+            for (int e = 0; e < W; e += 4) {  // the query packet as 16-byte shared loads (q is 16-byte aligned)
+                *reinterpret_cast<float4 *>(qv + e) = *reinterpret_cast<const float4 *>(q + c * W + e);
+            }
+#pragma unroll
             for (int e = 0; e < W; ++e) {
-                dot = fmaf(k[e], q[c * W + e], dot);
+                dot = fmaf(k[e], qv[e], dot);
                 kk = fmaf(k[e], k[e], kk);
             }
         }
