@@ -186,6 +186,15 @@ KOEMI_API size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int64
 KOEMI_API int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
                            float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
                            void *workspace, size_t workspace_bytes, void *stream);
+/* The same projection for weights that no work still in flight on `stream`
+ * writes (model parameters): the kernel is launched with programmatic stream
+ * serialization and loads its first weight tiles while the previous kernel of
+ * the stream finishes, reading `a` (and the bias) only after that kernel has
+ * completed. Same arguments, results and limits as koemi_dense_projection;
+ * the decode step's block projections use it (same reference lines). */
+KOEMI_API int koemi_dense_projection_resident(const void *a, int64_t a_stride, const void *weight, const void *bias,
+                           float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
+                           void *workspace, size_t workspace_bytes, void *stream);
 
 /* A batch of small products on tcgen05 tensor cores, fp32 output:
  * out[g * M + i, j] = sum_k A[g * M + i, k] B[g * N + j, k] for every group

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
                                        _p)),
     "koemi_dense_projection_workspace": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_dense_projection": (_int, (_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
+    "koemi_dense_projection_resident": (_int, (_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p, _sz, _p)),
     "koemi_grouped_projection": (_int, (_p, _p, _p, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_window_pack_rows": (_int, (_p, _p, _p, _int, _i64, _p, _i64, _int, _p)),
     "koemi_window_slot_operands": (_int, (_p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _int, _p)),

@@ -65,9 +65,13 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // cost ~5% at 32 streams, so it is off; the waits are then no-ops. `cluster`
 // with more than one CTA also sets thread-block cluster dims.
 constexpr bool kProgrammaticLaunch = false;
+// The same with the programmatic attribute chosen per launch: the weight-
+// streaming GEMMs whose weights no earlier kernel writes set it, start loading
+// those weights while the previous kernel finishes, and wait (pdl_wait) before
+// they read anything that kernel wrote.
 template <typename... KernelArgs, typename... Args>
-inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
-                              cudaStream_t stream, dim3 cluster, Args &&...args) {
+inline cudaError_t launch_programmatic(bool programmatic, void (*kernel)(KernelArgs...), dim3 grid, dim3 block,
+                                       size_t smem, cudaStream_t stream, dim3 cluster, Args &&...args) {
     cudaLaunchConfig_t config{};
     config.gridDim = grid;
     config.blockDim = block;
@@ -75,7 +79,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 blo
     config.stream = stream;
     cudaLaunchAttribute attributes[2];
     attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attributes[0].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch ? 1 : 0;
+    attributes[0].val.programmaticStreamSerializationAllowed = programmatic ? 1 : 0;
     unsigned count = 1;
     if (cluster.x * cluster.y * cluster.z > 1) {
         attributes[1].id = cudaLaunchAttributeClusterDimension;
@@ -87,6 +91,13 @@ inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 blo
     config.attrs = attributes;
     config.numAttrs = count;
     return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KernelArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, dim3 cluster, Args &&...args) {
+    return launch_programmatic(kProgrammaticLaunch, kernel, grid, block, smem, stream, cluster,
+                               std::forward<Args>(args)...);
 }
 
 #define KOEMI_CUDA_TRY(expr)                                                                      \

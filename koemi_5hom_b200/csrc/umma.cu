@@ -107,6 +107,7 @@ struct UmmaArgs {
     const float *row_lse;     // surprise gradient: per-row log-sum-exp (NULL: forward modes)
     const float *row_scale;   // surprise gradient: per-row dL/dNLL (0 on invalid rows)
     float *grad_out;          // surprise gradient: fp32 dlogits [rows, n_out]
+    int64_t weights_ready;    // dense: no earlier kernel of the stream writes B (its first stages load before pdl_wait)
     int *status;
     uint32_t idesc;
 };
@@ -332,6 +333,53 @@ __device__ __forceinline__ void load_bias32(const T *bias, int64_t col0, int64_t
     }
 }
 
+// Rows of one column quad summed over the S parked split accumulators of a
+// cluster (distributed shared memory) in split order, plus the bias, stored
+// as fp32. The loads of 32 / S rows (32 float4 per thread) are all requested
+// before the first sum, so the remote latency is paid once per batch of rows.
+// `dst` is the quad's column in row 0; `n_left` the valid columns from there.
+template <int S>
+__device__ __forceinline__ void reduce_parked_rows(uint32_t parked_base, int my_row, int row_step, int valid_rows,
+                                                   int q, const float (&bias4)[4], float *dst, int64_t out_stride,
+                                                   int64_t n_left) {
+    constexpr int R = 32 / S;
+    for (int r0 = my_row; r0 < valid_rows; r0 += R * row_step) {
+        float4 v[R][S];
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+            const int r = r0 + u * row_step;
+            if (r < valid_rows) {
+                const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
+#pragma unroll
+                for (int sp = 0; sp < S; ++sp) v[u][sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+            const int r = r0 + u * row_step;
+            if (r >= valid_rows) continue;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int sp = 0; sp < S; ++sp) {
+                acc.x += v[u][sp].x;
+                acc.y += v[u][sp].y;
+                acc.z += v[u][sp].z;
+                acc.w += v[u][sp].w;
+            }
+            const float o[4] = {acc.x + bias4[0], acc.y + bias4[1], acc.z + bias4[2], acc.w + bias4[3]};
+            float *p = dst + static_cast<int64_t>(r) * out_stride;
+            if (n_left >= 4 && aligned16(p)) {
+                *reinterpret_cast<float4 *>(p) = make_float4(o[0], o[1], o[2], o[3]);
+            } else if (n_left >= 4 && aligned8(p)) {
+                reinterpret_cast<float2 *>(p)[0] = make_float2(o[0], o[1]);
+                reinterpret_cast<float2 *>(p)[1] = make_float2(o[2], o[3]);
+            } else {
+                for (int e = 0; e < 4 && e < n_left; ++e) p[e] = o[e];
+            }
+        }
+    }
+}
+
 // kTileN < 256 (output and direct dense problems): N = 128 or 64 tiles, for
 // decode-sized problems whose 256-wide tiles would leave SMs idle or need a
 // split-K reduction; the smaller stages run a deeper ring.
@@ -390,8 +438,26 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // the prologue above touched no global memory; everything below may read
-    // what the previous kernel of the stream wrote
+    // Dense problems whose weights no earlier kernel writes (launched with the
+    // programmatic attribute): the weight tiles of this CTA's first stages are
+    // requested before waiting for the previous kernel of the stream, so
+    // their DRAM latency overlaps its tail. Everything else below pdl_wait may
+    // read what the previous kernel wrote.
+    int64_t early = 0;
+    if constexpr (kProblem == kDense || kProblem == kDenseCluster) {
+        if (args.weights_ready && warp == 0 && lane == 0 &&
+            static_cast<int64_t>(blockIdx.x) < total_tiles<kProblem, kTileRows>(args)) {
+            prefetch_tensor_map(&args.map_b0);
+            const Tile tile = tile_at<kProblem, kTileRows>(args, blockIdx.x);
+            early = min(static_cast<int64_t>(kPipe), tile.k_end - tile.k_begin);
+            for (int s = 0; s < early; ++s) {
+                mbar_arrive_expect_tx(&full[s], kStage);
+                tma_load_2d(stages + s * kStage + kAStage, &args.map_b0, &full[s],
+                            static_cast<int32_t>((tile.k_begin + s) * kBK),
+                            static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kTileN));
+            }
+        }
+    }
     pdl_wait();
     const int64_t tiles = total_tiles<kProblem, kTileRows>(args);
 
@@ -408,7 +474,10 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                     if (!wait_or_abort(&empty[stage], phase ^ 1, abort, args.status)) break;
                     uint8_t *a_dst = stages + stage * kStage;
                     uint8_t *b_dst = a_dst + kAStage;
-                    mbar_arrive_expect_tx(&full[stage], kStage);
+                    // a stage whose weight tile went out before pdl_wait
+                    // already expects the whole stage's bytes
+                    const bool b_issued = t == static_cast<int64_t>(blockIdx.x) && kb - tile.k_begin < early;
+                    if (!b_issued) mbar_arrive_expect_tx(&full[stage], kStage);
                     const int32_t kc = static_cast<int32_t>(kb * kBK);
                     tma_load_2d(a_dst, &args.map_a, &full[stage], kc, static_cast<int32_t>(tile.row0));
                     if (kPair) {  // rows past the end read as zeros (full box bytes still arrive)
@@ -419,7 +488,7 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * 128);
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
                         tma_load_2d(b_dst + kBBytes / 2, &args.map_b1, &full[stage], kc, r);
-                    } else {
+                    } else if (!b_issued) {
                         const int32_t r = static_cast<int32_t>(tile.group * args.b_rows_per_group + tile.n * kTileN);
                         tma_load_2d(b_dst, &args.map_b0, &full[stage], kc, r);
                     }
@@ -748,9 +817,8 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                                                                     min(static_cast<int64_t>(kBM), args.rows - half_row0)))
                                              : 0;
             // Thread t owns column quad q_begin + t % q_count (its bias read
-            // once) and rows t / q_count + j * row_step. Four rows' loads from
-            // every split are requested before any is summed, so the remote
-            // latency is paid once per four rows; sums run in split order.
+            // once) and rows t / q_count + j * row_step; the loads of 32 / S
+            // rows from every split are requested before any is summed.
             const int row_step = kThreads / q_count;
             const int my_row = threadIdx.x / q_count;
             const int q = q_begin + threadIdx.x % q_count;
@@ -761,45 +829,15 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
 #pragma unroll
                     for (int e = 0; e < 4; ++e) bias4[e] = col + e < args.n_out ? to_acc(bias[col + e]) : 0.0f;
                 }
-                constexpr int kRowsInFlight = 4;
-                for (int r0 = my_row; r0 < valid_rows; r0 += kRowsInFlight * row_step) {
-                    float4 v[kRowsInFlight][kMaxClusterSplits];
-#pragma unroll
-                    for (int u = 0; u < kRowsInFlight; ++u) {
-                        const int r = r0 + u * row_step;
-                        if (r < valid_rows) {
-                            const uint32_t offset = parked_base + static_cast<uint32_t>((r * kAccStride + q * 4) * 4);
-#pragma unroll
-                            for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                                if (sp < splits) v[u][sp] = ld_dsmem_f4(offset, static_cast<uint32_t>(sp));
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < kRowsInFlight; ++u) {
-                        const int r = r0 + u * row_step;
-                        if (r >= valid_rows) continue;
-                        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                        for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
-                            if (sp < splits) {
-                                acc.x += v[u][sp].x;
-                                acc.y += v[u][sp].y;
-                                acc.z += v[u][sp].z;
-                                acc.w += v[u][sp].w;
-                            }
-                        }
-                        const float o[4] = {acc.x + bias4[0], acc.y + bias4[1], acc.z + bias4[2], acc.w + bias4[3]};
-                        float *dst = out + (half_row0 + r) * args.out_stride + col;
-                        if (col + 4 <= args.n_out && aligned16(dst)) {
-                            *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-                        } else if (col + 4 <= args.n_out && aligned8(dst)) {
-                            reinterpret_cast<float2 *>(dst)[0] = make_float2(o[0], o[1]);
-                            reinterpret_cast<float2 *>(dst)[1] = make_float2(o[2], o[3]);
-                        } else {
-                            for (int e = 0; e < 4 && col + e < args.n_out; ++e) dst[e] = o[e];
-                        }
-                    }
+                float *dst_col = out + half_row0 * args.out_stride + col;
+                switch (splits) {
+                    case 2: reduce_parked_rows<2>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    case 3: reduce_parked_rows<3>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    case 4: reduce_parked_rows<4>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    case 5: reduce_parked_rows<5>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    case 6: reduce_parked_rows<6>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    case 7: reduce_parked_rows<7>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
+                    default: reduce_parked_rows<8>(parked_base, my_row, row_step, valid_rows, q, bias4, dst_col, args.out_stride, args.n_out - col); break;
                 }
             }
             cluster_sync_all();
@@ -840,8 +878,8 @@ int launch(const UmmaArgs &args, int dtype, int64_t max_tiles, cudaStream_t stre
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
     int64_t grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads_for<kProblem>()), kSmemBytes, stream,
-                              dim3(1, 1, 1), args));
+    KOEMI_CUDA_TRY(launch_programmatic(args.weights_ready != 0, kernel, dim3(static_cast<unsigned>(grid)),
+                                       dim3(threads_for<kProblem>()), kSmemBytes, stream, dim3(1, 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -852,8 +890,9 @@ int launch_clustered(const UmmaArgs &args, int dtype, int64_t ctas, int cluster,
     auto kernel = dtype == KOEMI_BF16 ? umma_gemm_kernel<kProblem, __nv_bfloat16, kPair>
                                       : umma_gemm_kernel<kProblem, __half, kPair>;
     KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
-    KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(threads_for<kProblem>()), kSmemBytes, stream,
-                              dim3(static_cast<unsigned>(cluster), 1, 1), args));
+    KOEMI_CUDA_TRY(launch_programmatic(args.weights_ready != 0, kernel, dim3(static_cast<unsigned>(ctas)),
+                                       dim3(threads_for<kProblem>()), kSmemBytes, stream,
+                                       dim3(static_cast<unsigned>(cluster), 1, 1), args));
     KOEMI_LAUNCH_CHECK();
     return KOEMI_OK;
 }
@@ -1200,10 +1239,10 @@ extern "C" size_t koemi_dense_projection_workspace(int64_t rows, int64_t n, int6
     return 256;
 }
 
-extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
-                                      float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
-                                      void *workspace, size_t workspace_bytes, void *stream) {
-    clear_error();
+namespace {
+int dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias, float *out,
+                     int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype, void *stream,
+                     bool weights_ready) {
     if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "dense projection takes bf16 or f16 operands");
     if (rows < 0 || n < 1 || k < 1) return fail(KOEMI_ERR_INVALID, "need rows >= 0 and positive n, k");
     if (rows == 0) return KOEMI_OK;
@@ -1211,8 +1250,6 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
         rows >= (int64_t(1) << 31) || n >= (int64_t(1) << 31)) {
         return fail(KOEMI_ERR_UNSUPPORTED, "dense projection needs K and the A row stride to be multiples of 8 and 16-byte aligned operands");
     }
-    (void)workspace;
-    (void)workspace_bytes;
     const DensePlan plan = dense_plan(rows, n, k);
     cudaStream_t s = as_stream(stream);
     UmmaArgs args{};
@@ -1239,6 +1276,7 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     args.partials = nullptr;
     args.status = device_status_word();
     args.idesc = make_idesc(dtype);
+    args.weights_ready = weights_ready ? 1 : 0;
     const int64_t m_tiles = (rows + kBM - 1) / kBM;
     const int64_t tiles = m_tiles * args.n_tiles * plan.splits;
     if (plan.splits > 1) return launch_clustered<kDenseCluster>(args, dtype, tiles, static_cast<int>(plan.splits), s);
@@ -1252,4 +1290,22 @@ extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const voi
     }
     return launch<kDense>(args, dtype, tiles, s);
 }
+}  // namespace
 
+extern "C" int koemi_dense_projection(const void *a, int64_t a_stride, const void *weight, const void *bias,
+                                      float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k, int dtype,
+                                      void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    (void)workspace;
+    (void)workspace_bytes;
+    return dense_projection(a, a_stride, weight, bias, out, out_stride, rows, n, k, dtype, stream, false);
+}
+
+extern "C" int koemi_dense_projection_resident(const void *a, int64_t a_stride, const void *weight, const void *bias,
+                                               float *out, int64_t out_stride, int64_t rows, int64_t n, int64_t k,
+                                               int dtype, void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    (void)workspace;
+    (void)workspace_bytes;
+    return dense_projection(a, a_stride, weight, bias, out, out_stride, rows, n, k, dtype, stream, true);
+}

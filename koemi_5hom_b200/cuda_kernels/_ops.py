@@ -91,9 +91,12 @@ def _(projections, valid, minimum, maximum):
 
 
 @torch.library.custom_op("koemi_b200::dense_projection", mutates_args=())
-def dense_projection(a: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+def dense_projection(a: Tensor, weight: Tensor, bias: Tensor | None, weights_ready: bool = False) -> Tensor:
     """fp32 [rows, n] = a [rows, k] @ weight[n, k]^T + bias on tensor cores
-    (bf16/f16 operands); `a` may be a view with strided rows."""
+    (bf16/f16 operands); `a` may be a view with strided rows. With
+    ``weights_ready`` (model parameters: nothing in flight on the stream
+    writes weight or bias) the kernel starts loading weights while the
+    previous kernel of the stream finishes."""
     weight, bias = _dense(weight, bias)
     if a.stride(-1) != 1:
         a = a.contiguous()
@@ -104,13 +107,14 @@ def dense_projection(a: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
     code = dtype_code(weight.dtype)
     size = _native.library().koemi_dense_projection_workspace(rows, n, k, code)
     scratch = _native.workspace(size, a.device)
-    call("koemi_dense_projection", ptr(a), a.stride(0), ptr(weight), ptr(bias), ptr(out), n, rows, n, k, code,
+    entry = "koemi_dense_projection_resident" if weights_ready else "koemi_dense_projection"
+    call(entry, ptr(a), a.stride(0), ptr(weight), ptr(bias), ptr(out), n, rows, n, k, code,
          ptr(scratch), scratch.numel(), stream)
     return out
 
 
 @dense_projection.register_fake
-def _(a, weight, bias):
+def _(a, weight, bias, weights_ready=False):
     return a.new_empty(a.shape[0], weight.shape[0], dtype=torch.float32)
 
 

@@ -47,6 +47,16 @@ MIN_RETENTION, MAX_RETENTION = 2.0 ** -8, 1.0 - 2.0 ** -8
 NORM_EPSILON = 1e-6
 
 
+def _assoc_step(call, ptr, block, st, assoc, surprise, valid, concat, batch, d, features, out_code, stream):
+    """Associative read/update of one block (feature projection of key and
+    query fused into the kernel), writing the memory columns of the fusion
+    input in place."""
+    call("koemi_assoc_decode_step", ptr(assoc), assoc.stride(0), None, ptr(block.feature_weight),
+         ptr(block.feature_bias), _native.dtype_code(block.feature_weight.dtype), ptr(surprise), ptr(valid),
+         ptr(st.memory_basis), ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d, features, out_code,
+         stream)
+
+
 @dataclass
 class DecodeBlockState:
     working: Tensor
@@ -286,10 +296,11 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
              ptr(dstate.local_head), ptr(st.salient_keys), ptr(st.salient_values), ptr(st.salient_valid),
              ptr(st.salient_head), ptr(st.salient_count), ptr(concat[:, 2 * d:]), ptr(concat[:, 3 * d:]), 4 * d,
              None, None, batch, d, st.local_keys.shape[1], st.salient_keys.shape[1], ring_code, out_code, stream)
-        # the feature projection of key and query runs inside the kernel
-        call("koemi_assoc_decode_step", ptr(assoc), assoc.stride(0), None, ptr(block.feature_weight),
-             ptr(block.feature_bias), _native.dtype_code(block.feature_weight.dtype), ptr(surprise), ptr(valid), ptr(st.memory_basis),
-             ptr(st.memory_normalizer), ptr(concat[:, d:]), 4 * d, batch, d, s.memory_features, out_code, stream)
+        # (run beside the ring kernel on a side stream, a parallel graph
+        # branch, it measured slower: at 32 streams the two cluster kernels
+        # contend for SMs, ring 23.7 -> 36.7 us, step 4.24 -> 4.34 ms)
+        _assoc_step(call, ptr, block, st, assoc, surprise, valid, concat, batch, d, s.memory_features,
+                    out_code, stream)
         fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
         context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
         u = None

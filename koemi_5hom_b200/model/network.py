@@ -481,7 +481,7 @@ class KoemiModel(nn.Module):
         k = flat.shape[1]
         if (k % 8 == 0 and flat.stride(1) == 1 and flat.stride(0) % 8 == 0 and flat.data_ptr() % 16 == 0
                 and flat.shape[0] > 0):
-            y = _ops.dense_projection(flat, weight, bias)
+            y = _ops.dense_projection(flat, weight, bias, True)  # parameters: nothing in flight writes them
         else:
             y = torch.mm(flat, weight.T, out_dtype=torch.float32)
             if bias is not None:
