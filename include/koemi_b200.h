@@ -606,20 +606,76 @@ KOEMI_API int koemi_ep_dispatch_gather(const void *context, int context_dtype, c
                                        int64_t ranks, int64_t local_experts, int64_t capacity, int dtype,
                                        void *stream);
 
+/* koemi_ep_dispatch_gather fused with the RMSNorm that makes the rows: token
+ * row t of `fused` (fp32 [tokens, width]) is normalised, x * rsqrt(mean(x^2)
+ * + eps) * norm_weight, into `context` (fp32, the combine's residual; the
+ * same arithmetic as koemi_core_rmsnorm_forward with fp32 in and out), and
+ * each of its top_k pairs with a sorted index below the valid count (from
+ * pair_positions, segment_offsets global [ranks * local_experts + 1]) is
+ * stored, in the exchange dtype, into its owner's buffer; ids and epoch flags
+ * as in koemi_ep_dispatch. 16-bit exchange rows, width a multiple of 4 up to
+ * 2048. Replaces the block's fusion norm (src/koemi/model/network.py:723-732 in the
+ * reference) plus the dispatch. */
+KOEMI_API int koemi_ep_norm_dispatch(const float *fused, const float *norm_weight, float eps, float *context,
+                                     const int64_t *pair_positions, const int64_t *sorted_experts,
+                                     const int64_t *segment_offsets, int64_t tokens, int64_t top_k,
+                                     const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
+                                     int64_t local_experts, int64_t capacity, int dtype, void *stream);
+
 /* Owner side of an exchange in one launch: the bounded wait for every
  * sender's flag, then the stable sort of the received slots ([sender][j]) by
  * local expert and the gather of the live rows into expert-major order:
  * sorted_rows [ranks * capacity, width] (rows past the live count are left
  * as they were), segment_offsets [local_experts + 1], sorted_experts
  * [ranks * capacity] (local_experts for empty slots) and positions
- * [ranks * capacity] (sorted index of every slot). A wait that gives up
- * records KOEMI_ERR_TIMEOUT and yields empty segments. At most 4096 slots and
- * 255 local experts. Replaces koemi_ep_wait_dispatch plus a general
- * permutation of the received rows. */
+ * [ranks * capacity] (sorted index of every slot). Optional (NULL: not
+ * written): slots [ranks * capacity], the slot at every sorted index (the
+ * inverse of positions), and tile_prefix [local_experts + 1] int32, the
+ * number of 128-row tiles before each local expert (the tile map of
+ * koemi_ep_expert_mlp_return). A wait that gives up records KOEMI_ERR_TIMEOUT
+ * and yields empty segments. At most 4096 slots and 255 local experts.
+ * Replaces koemi_ep_wait_dispatch plus a general permutation of the received
+ * rows. */
 KOEMI_API int koemi_ep_owner_sort(const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
                                   int64_t local_experts, int64_t capacity, int dtype, void *sorted_rows,
                                   int64_t *segment_offsets, int64_t *sorted_experts, int64_t *positions,
-                                  void *stream);
+                                  int64_t *slots, int32_t *tile_prefix, void *stream);
+
+/* The owner's grouped gated expert MLP (koemi_moe_grouped_expert_mlp on
+ * tcgen05 tensor cores, bf16/f16 only) over the rows of koemi_ep_owner_sort
+ * (`rows` = ranks * capacity sorted rows, their segment_offsets, tile_prefix
+ * and slots), whose output GEMM stores every live row's result straight into
+ * its sender's exchange buffer (this owner's block of ret_rows, at the row's
+ * slot) and then raises the return flag in every sender's buffer: it replaces
+ * the grouped MLP, its output tensor and koemi_ep_return. Weights are this
+ * rank's local experts in the grouped-MLP layout. workspace: at least
+ * rows * hidden_width * 2 bytes (the gated hidden rows), 16-byte aligned. The
+ * senders read the returned rows with koemi_ep_combine_residual_rmsnorm_next
+ * (or koemi_ep_collect). Same reference lines as the grouped MLP. */
+KOEMI_API int koemi_ep_expert_mlp_return(const void *sorted_rows, const int64_t *segment_offsets,
+                                         const int32_t *tile_prefix, const int64_t *slots, const void *gate_weights,
+                                         const void *gate_biases, const void *value_weights,
+                                         const void *value_biases, const void *output_weights,
+                                         const void *output_biases, int64_t rows, int64_t input_width,
+                                         int64_t hidden_width, int64_t local_experts, int dtype, void *workspace,
+                                         size_t workspace_bytes, const uint64_t *peers, void *own, int64_t rank,
+                                         int64_t ranks, int64_t capacity, void *stream);
+
+/* koemi_moe_combine_residual_rmsnorm_next for a sender of an exchange whose
+ * owners returned their outputs with koemi_ep_expert_mlp_return: each CTA
+ * waits (bounded) for every owner's return flag in `own`, then pair p's
+ * expert row is read in place from the ret_rows block of the owner whose
+ * segments hold p (segment_offsets are the global ones, expert_count = ranks
+ * * local_experts). Replaces koemi_ep_collect, its sorted output tensor and
+ * the combine's read of it. dtype: the exchange row type. */
+KOEMI_API int koemi_ep_combine_residual_rmsnorm_next(const float *context, const int64_t *pair_positions,
+                                                     const int64_t *segment_offsets, const float *weights,
+                                                     const uint8_t *valid, const float *norm_weight,
+                                                     const float *next_norm_weight, void *out, int out_dtype,
+                                                     int64_t tokens, int64_t width, int64_t top_k,
+                                                     int64_t expert_count, float eps, int dtype, const void *own,
+                                                     int64_t ranks, int64_t local_experts, int64_t capacity,
+                                                     void *stream);
 KOEMI_API int koemi_ep_wait_dispatch(const void *own, int64_t ranks, void *stream);
 KOEMI_API int koemi_ep_return(const void *local_out, const int64_t *local_positions, const uint64_t *peers,
                     void *own, int64_t width, int64_t rank, int64_t ranks, int64_t local_experts,

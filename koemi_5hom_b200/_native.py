@@ -113,7 +113,13 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_ep_dispatch": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_ep_dispatch_gather": (
         _int, (_p, _int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),
-    "koemi_ep_owner_sort": (_int, (_p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _p, _p, _p, _p)),
+    "koemi_ep_norm_dispatch": (_int, (_p, _p, _f, _p, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                      _int, _p)),
+    "koemi_ep_owner_sort": (_int, (_p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _p, _p, _p, _p, _p, _p)),
+    "koemi_ep_expert_mlp_return": (_int, (_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p,
+                                          _sz, _p, _p, _i64, _i64, _i64, _p)),
+    "koemi_ep_combine_residual_rmsnorm_next": (_int, (_p, _p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64,
+                                                      _f, _int, _p, _i64, _i64, _i64, _p)),
     "koemi_ep_wait_dispatch": (_int, (_p, _i64, _p)),
     "koemi_ep_return": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_ep_collect": (_int, (_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p)),

@@ -13,6 +13,7 @@
 // sort, histogram, scan, gathers) and model/experts.py:171-216,261-289.
 #include <type_traits>
 
+#include "peer.cuh"
 #include "vec.cuh"
 
 namespace koemi {
@@ -683,12 +684,25 @@ __device__ __forceinline__ void store_quad(TO *dst, float4 v) {
     }
 }
 
+// Expert outputs still in the exchange buffer (expert-parallel decode): pair
+// p's row was returned by the owner g whose segments hold p, at slot
+// p - segment_offsets[g * local_experts] of g's block of ret_rows. own ==
+// nullptr: the rows are y[p] as usual.
+struct ReturnedRows {
+    const uint8_t *own;
+    size_t ret;
+    int64_t capacity, local_experts, ranks;
+    int *status;
+};
+
 // The vector combine with the row held in registers (NQ quads per lane):
 // every load of a row is issued before its values are used, and the output
 // is written once. With `next_norm`, the stored row is instead the next
 // block's normalised input RMSNorm(x) * next_norm of the combined row x.
+// With returned rows, the CTA first waits (bounded) for every owner's return
+// flag and reads the rows where the owners stored them.
 template <typename T, int NQ, typename TO>
-__global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__ context, const T *__restrict__ y,
+__global__ void combine_residual_rmsnorm_cached_kernel(const ReturnedRows returned, const float *__restrict__ context, const T *__restrict__ y,
                                                        const int64_t *__restrict__ positions,
                                                        const int64_t *__restrict__ segment_offsets,
                                                        const float *__restrict__ weights,
@@ -699,6 +713,8 @@ __global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__
                                                        float eps) {
     pdl_trigger();
     pdl_wait();
+    // a wait that gives up (status word set) combines no expert rows
+    const bool arrived = returned.own == nullptr || peer::wait_flags(returned.own, 1, returned.ranks, returned.status);
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= tokens) return;
@@ -716,8 +732,14 @@ __global__ void combine_residual_rmsnorm_cached_kernel(const float *__restrict__
         const int64_t valid_pairs = segment_offsets[experts];
         for (int64_t s = 0; s < top_k; ++s) {
             const int64_t pos = positions[row * top_k + s];
-            if (pos < 0 || pos >= valid_pairs) continue;
+            if (pos < 0 || pos >= valid_pairs || !arrived) continue;
             const T *src = y + pos * width;
+            if (returned.own != nullptr) {
+                int64_t g = returned.ranks - 1;
+                while (g > 0 && segment_offsets[g * returned.local_experts] > pos) --g;
+                src = reinterpret_cast<const T *>(returned.own + returned.ret) +
+                      (g * returned.capacity + pos - segment_offsets[g * returned.local_experts]) * width;
+            }
             const float scale = weights != nullptr ? weights[row * top_k + s] : 1.0f / static_cast<float>(top_k);
             float4 e[NQ];
 #pragma unroll
@@ -1017,8 +1039,9 @@ extern "C" int koemi_moe_combine_residual_rmsnorm(const float *context, const vo
                         aligned(norm_weight, 16) && aligned(expert_out, 8);
     const int64_t quads_per_lane = ceil_div(width / 4, 32);
     if (vector && quads_per_lane <= 16) {
+        const ReturnedRows returned{};
         auto run = [&](auto kernel, const auto *typed) -> int {
-            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), context, typed, pair_positions, segment_offsets, weights, valid,
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), returned, context, typed, pair_positions, segment_offsets, weights, valid,
                                               norm_weight, nullptr, out, tokens, width, top_k, expert_count, eps));
             KOEMI_LAUNCH_CHECK();
             return KOEMI_OK;
@@ -1221,14 +1244,12 @@ extern "C" int koemi_moe_ep_unpack(const void *slab, const int64_t *sorted_exper
 // ---------------------------------------------------------------------------
 // Combine fused with the next block's input norm (decode chains of blocks).
 
-extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, const void *expert_out,
-                                                       const int64_t *pair_positions,
-                                                       const int64_t *segment_offsets, const float *weights,
-                                                       const uint8_t *valid, const float *norm_weight,
-                                                       const float *next_norm_weight, void *out, int out_dtype,
-                                                       int64_t tokens, int64_t width, int64_t top_k,
-                                                       int64_t expert_count, float eps, int dtype, void *stream) {
-    clear_error();
+namespace {
+int combine_next(const ReturnedRows &returned, const float *context, const void *expert_out,
+                 const int64_t *pair_positions, const int64_t *segment_offsets, const float *weights,
+                 const uint8_t *valid, const float *norm_weight, const float *next_norm_weight, void *out,
+                 int out_dtype, int64_t tokens, int64_t width, int64_t top_k, int64_t expert_count, float eps,
+                 int dtype, void *stream) {
     if (tokens < 0 || width < 0 || top_k < 1) return fail(KOEMI_ERR_INVALID, "bad combine sizes");
     if (tokens == 0 || width == 0) return KOEMI_OK;
     const int64_t quads_per_lane = ceil_div(width / 4, 32);
@@ -1244,7 +1265,7 @@ extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, con
         using T = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
         using TO = std::remove_pointer_t<decltype(out_typed)>;
         auto launch = [&](auto kernel) -> int {
-            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), context, typed, pair_positions, segment_offsets, weights, valid,
+            KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(threads), 0, s, dim3(1, 1, 1), returned, context, typed, pair_positions, segment_offsets, weights, valid,
                                               norm_weight, next_norm_weight, out_typed, tokens, width, top_k,
                                               expert_count, eps));
             KOEMI_LAUNCH_CHECK();
@@ -1268,6 +1289,46 @@ extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, con
         case KOEMI_BF16: return by_out(static_cast<const __nv_bfloat16 *>(expert_out));
         default: return fail(KOEMI_ERR_INVALID, "expert outputs must be f32, f16 or bf16");
     }
+}
+}  // namespace
+
+extern "C" int koemi_moe_combine_residual_rmsnorm_next(const float *context, const void *expert_out,
+                                                       const int64_t *pair_positions,
+                                                       const int64_t *segment_offsets, const float *weights,
+                                                       const uint8_t *valid, const float *norm_weight,
+                                                       const float *next_norm_weight, void *out, int out_dtype,
+                                                       int64_t tokens, int64_t width, int64_t top_k,
+                                                       int64_t expert_count, float eps, int dtype, void *stream) {
+    clear_error();
+    return combine_next(ReturnedRows{}, context, expert_out, pair_positions, segment_offsets, weights, valid,
+                        norm_weight, next_norm_weight, out, out_dtype, tokens, width, top_k, expert_count, eps, dtype,
+                        stream);
+}
+
+extern "C" int koemi_ep_combine_residual_rmsnorm_next(const float *context, const int64_t *pair_positions,
+                                                      const int64_t *segment_offsets, const float *weights,
+                                                      const uint8_t *valid, const float *norm_weight,
+                                                      const float *next_norm_weight, void *out, int out_dtype,
+                                                      int64_t tokens, int64_t width, int64_t top_k,
+                                                      int64_t expert_count, float eps, int dtype, const void *own,
+                                                      int64_t ranks, int64_t local_experts, int64_t capacity,
+                                                      void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16 && dtype != KOEMI_F32) {
+        return fail(KOEMI_ERR_INVALID, "returned rows must be f32, f16 or bf16");
+    }
+    if (own == nullptr || !aligned(own, 256) || ranks < 1 || ranks > peer::kMaxRanks || local_experts < 1 ||
+        capacity < 1 || expert_count != ranks * local_experts) {
+        return fail(KOEMI_ERR_INVALID, "bad exchange arguments for the returned-row combine");
+    }
+    const peer::Layout l = peer::layout(ranks, capacity, width, dtype_size(dtype));
+    const ReturnedRows returned{static_cast<const uint8_t *>(own), l.ret, capacity, local_experts, ranks,
+                                device_status_word()};
+    // the returned rows are the exchange buffer's: expert_out only fixes the
+    // row type and its alignment check
+    return combine_next(returned, context, static_cast<const uint8_t *>(own) + l.ret, pair_positions,
+                        segment_offsets, weights, valid, norm_weight, next_norm_weight, out, out_dtype, tokens, width,
+                        top_k, expert_count, eps, dtype, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -9,90 +9,22 @@
 // limit runs out they record KOEMI_ERR_TIMEOUT in the device status word and
 // return, so a missing peer never hangs the GPU.
 //
-// Buffer layout (every rank the same):
-//   [0, 256)                     header: flags[2][ranks] (uint64, written by peers),
-//                                epoch (uint64), ticket (uint32) at the end
-//   recv_ids   [ranks][capacity] int32    rows' owner-local expert ids (-1 padding)
-//   recv_rows  [ranks][capacity][width]   rows dispatched to this rank, block = sender
-//   ret_rows   [ranks][capacity][width]   outputs returned to this rank, block = owner
+// The buffer layout and the flag protocol are in peer.cuh.
 #include <algorithm>
 #include <cstring>
 
+#include "peer.cuh"
 #include "vec.cuh"
 
 namespace koemi {
 namespace {
 
-constexpr int64_t kMaxPeerRanks = 8;
-constexpr size_t kHeaderBytes = 256;
-constexpr int64_t kEpochSlot = 2 * kMaxPeerRanks;      // uint64 index of the local epoch
-constexpr int64_t kTicketSlot = 2 * kMaxPeerRanks + 1;  // uint64 index of the CTA ticket
-constexpr uint64_t kPeerSpinLimit = uint64_t(1) << 22;  // about a second of polling
-
-struct Layout {
-    size_t ids, rows, ret, total;
-};
-
-Layout layout(int64_t ranks, int64_t capacity, int64_t width, size_t es) {
-    auto align = [](size_t v) { return (v + 255) & ~size_t(255); };
-    Layout l{};
-    l.ids = kHeaderBytes;
-    l.rows = align(l.ids + static_cast<size_t>(ranks * capacity) * 4);
-    l.ret = align(l.rows + static_cast<size_t>(ranks * capacity * width) * es);
-    l.total = align(l.ret + static_cast<size_t>(ranks * capacity * width) * es);
-    return l;
-}
-
-__device__ __forceinline__ void store_release_sys(uint64_t *p, uint64_t v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ uint64_t load_acquire_sys(const uint64_t *p) {
-    uint64_t v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Thread 0 of every CTA waits until flags[which][r] >= epoch for every rank r
-// (bounded); the CTA then proceeds. Returns false after a timeout.
-__device__ bool wait_flags(const uint8_t *own, int which, int64_t ranks, int *status) {
-    __shared__ int ok;
-    if (threadIdx.x == 0) {
-        const uint64_t *flags = reinterpret_cast<const uint64_t *>(own);
-        const uint64_t epoch = reinterpret_cast<const volatile uint64_t *>(own)[kEpochSlot];
-        ok = 1;
-        for (int64_t r = 0; r < ranks && ok; ++r) {
-            uint64_t spin = 0;
-            while (load_acquire_sys(flags + which * kMaxPeerRanks + r) < epoch) {
-                if (++spin == kPeerSpinLimit) {
-                    ok = 0;
-                    if (status != nullptr) atomicExch(status, KOEMI_ERR_TIMEOUT);
-                    break;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    return ok != 0;
-}
-
-// After every CTA's stores: the last CTA to arrive publishes `epoch` in
-// flags[which][rank] of every peer (release, system scope).
-__device__ void signal_peers(uint8_t *own, const uint64_t *peers, int which, int64_t rank, int64_t ranks,
-                             uint64_t epoch, bool advance_epoch) {
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x != 0) return;
-    unsigned int *ticket = reinterpret_cast<unsigned int *>(reinterpret_cast<uint64_t *>(own) + kTicketSlot);
-    if (atomicAdd(ticket, 1u) != gridDim.x - 1) return;
-    __threadfence_system();
-    *ticket = 0;
-    if (advance_epoch) reinterpret_cast<volatile uint64_t *>(own)[kEpochSlot] = epoch;
-    for (int64_t g = 0; g < ranks; ++g) {
-        uint64_t *flags = reinterpret_cast<uint64_t *>(peers[g]);
-        store_release_sys(flags + which * kMaxPeerRanks + rank, epoch);
-    }
-}
+constexpr int64_t kMaxPeerRanks = peer::kMaxRanks;
+constexpr int64_t kEpochSlot = peer::kEpochSlot;
+using peer::Layout;
+using peer::layout;
+using peer::signal_peers;
+using peer::wait_flags;
 
 template <typename T>
 __device__ __forceinline__ void copy_row(T *dst, const T *src, int64_t width, bool vector, int lane) {
@@ -188,6 +120,109 @@ __global__ void ep_dispatch_gather_kernel(ExchangeArgs a, const TI *__restrict__
     signal_peers(a.own, a.peers, 0, a.rank, a.ranks, epoch, true);
 }
 
+// Sender, fused with the fusion RMSNorm of a decode block: token row t of
+// `fused` (fp32 [tokens, width]) is normalised exactly as rms_rows_cached
+// does it (x * rsqrt(mean(x^2) + eps) * weight, the same loads and sum
+// order) into `context` (fp32, the combine's residual), and for each of its
+// top_k pairs that routes to an expert the normalised row, converted to the
+// exchange dtype T, goes straight into the owner's recv block `rank` at the
+// pair's slot (its sorted index minus the owner's first pair). The ids of
+// every slot of this sender's block in every owner (the owner-local expert,
+// -1 past the owner's pairs) and the epoch flags follow, as in the gathering
+// dispatch. One warp per row; width a multiple of 4 and at most 2048.
+template <typename T>
+__global__ void ep_norm_dispatch_kernel(ExchangeArgs a, const float *__restrict__ fused,
+                                        const float *__restrict__ norm_weight, float *__restrict__ context,
+                                        const int64_t *__restrict__ positions,
+                                        const int64_t *__restrict__ sorted_experts,
+                                        const int64_t *__restrict__ offsets, int64_t tokens, int64_t top_k,
+                                        float eps) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int NV = 16;  // 16-byte fp32 packets per lane: width <= 2048
+    const int lane = threadIdx.x & 31;
+    const uint64_t epoch = peer::current_epoch(a.own) + 1;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    const int64_t packets = a.width / 4;
+    const int64_t valid_pairs = offsets[a.ranks * a.local_experts];
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); t < tokens;
+         t += warps) {
+        const float *xr = fused + t * a.width;
+        float4 v[NV], w[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t p = lane + 32 * i;
+            if (p < packets) {
+                const uint4 raw = load_stream(xr + p * 4);
+                v[i] = *reinterpret_cast<const float4 *>(&raw);
+                const uint4 wraw = load_cached(norm_weight + p * 4);
+                w[i] = *reinterpret_cast<const float4 *>(&wraw);
+            }
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            if (lane + 32 * i < packets) {
+                sum = fmaf(v[i].x, v[i].x, sum);
+                sum = fmaf(v[i].y, v[i].y, sum);
+                sum = fmaf(v[i].z, v[i].z, sum);
+                sum = fmaf(v[i].w, v[i].w, sum);
+            }
+        }
+        sum = warp_sum(sum);
+        const float inv = rsqrtf(sum / static_cast<float>(a.width) + eps);
+        float *cr = context + t * a.width;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t p = lane + 32 * i;
+            if (p < packets) {
+                v[i] = make_float4(v[i].x * inv * w[i].x, v[i].y * inv * w[i].y, v[i].z * inv * w[i].z,
+                                   v[i].w * inv * w[i].w);
+                *reinterpret_cast<float4 *>(cr + p * 4) = v[i];
+            }
+        }
+        for (int64_t s = 0; s < top_k; ++s) {
+            const int64_t pos = positions[t * top_k + s];
+            if (pos < 0 || pos >= valid_pairs) continue;
+            int64_t g = a.ranks - 1;
+            while (g > 0 && offsets[g * a.local_experts] > pos) --g;
+            const int64_t slot = a.rank * a.capacity + pos - offsets[g * a.local_experts];
+            uint8_t *peer_buffer = reinterpret_cast<uint8_t *>(a.peers[g]);
+            if (lane == 0) {
+                reinterpret_cast<int32_t *>(peer_buffer + a.ids)[slot] =
+                    static_cast<int32_t>(sorted_experts[pos] - g * a.local_experts);
+            }
+            T *dst = reinterpret_cast<T *>(peer_buffer + a.rows) + slot * a.width;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int64_t p = lane + 32 * i;
+                if (p < packets) {
+                    union {
+                        T h[4];
+                        uint2 u;
+                    } out;
+                    out.h[0] = from_acc<T>(v[i].x);
+                    out.h[1] = from_acc<T>(v[i].y);
+                    out.h[2] = from_acc<T>(v[i].z);
+                    out.h[3] = from_acc<T>(v[i].w);
+                    *reinterpret_cast<uint2 *>(dst + p * 4) = out.u;
+                }
+            }
+        }
+    }
+    // this sender's dead slots in every owner's block
+    const int64_t threads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < a.ranks * a.capacity;
+         q += threads) {
+        const int64_t g = q / a.capacity;
+        const int64_t j = q - g * a.capacity;
+        if (j >= offsets[(g + 1) * a.local_experts] - offsets[g * a.local_experts]) {
+            reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(a.peers[g]) + a.ids)[a.rank * a.capacity + j] = -1;
+        }
+    }
+    signal_peers(a.own, a.peers, 0, a.rank, a.ranks, epoch, true);
+}
+
 // Owner, fused: wait for every sender's rows, then (every CTA redundantly, in
 // shared memory) the stable counting sort of the received slots by local
 // expert -- slot order [sender][j], dead slots (id -1) last -- and each CTA
@@ -199,12 +234,15 @@ constexpr int kOwnerThreads = 512;
 constexpr int kOwnerWarps = kOwnerThreads / 32;
 constexpr int64_t kOwnerMaxSlots = 4096;
 constexpr int64_t kOwnerMaxExperts = 255;
+constexpr int32_t kExpertTileRows = 128;  // row tile of the tcgen05 grouped GEMM (umma.cu kBM)
 
 template <typename T>
 __global__ __launch_bounds__(kOwnerThreads) void ep_owner_sort_kernel(ExchangeArgs a, T *__restrict__ sorted_rows,
                                                                       int64_t *__restrict__ offsets_out,
                                                                       int64_t *__restrict__ experts_out,
                                                                       int64_t *__restrict__ positions_out,
+                                                                      int64_t *__restrict__ slots_out,
+                                                                      int32_t *__restrict__ tile_prefix_out,
                                                                       bool vector) {
     pdl_trigger();
     pdl_wait();
@@ -232,13 +270,21 @@ __global__ __launch_bounds__(kOwnerThreads) void ep_owner_sort_kernel(ExchangeAr
     }
     __syncthreads();
     if (threadIdx.x == 0) {  // exclusive scan (at most 256 buckets)
-        int32_t carry = 0;
+        int32_t carry = 0, tiles = 0;
         for (int b = 0; b < buckets; ++b) {
             const int32_t v = running[b];
             running[b] = carry;
-            if (blockIdx.x == 0) offsets_out[b] = carry;
+            if (blockIdx.x == 0) {
+                offsets_out[b] = carry;
+                // the grouped GEMM's tile map: 128-row tiles before each local expert
+                if (tile_prefix_out != nullptr && b < a.local_experts) {
+                    tile_prefix_out[b] = tiles;
+                    tiles += (v + kExpertTileRows - 1) / kExpertTileRows;
+                }
+            }
             carry += v;
         }
+        if (blockIdx.x == 0 && tile_prefix_out != nullptr) tile_prefix_out[a.local_experts] = tiles;
     }
     __syncthreads();
     const unsigned lower = (1u << lane) - 1u;
@@ -275,6 +321,7 @@ __global__ __launch_bounds__(kOwnerThreads) void ep_owner_sort_kernel(ExchangeAr
             const int32_t q = order[i];
             experts_out[i] = keys[q];
             positions_out[q] = i;
+            if (slots_out != nullptr) slots_out[i] = q;
         }
     }
     // rows of sorted positions [0, live_rows): one warp per row, CTAs strided
@@ -519,10 +566,45 @@ extern "C" int koemi_ep_dispatch_gather(const void *context, int context_dtype, 
     return KOEMI_OK;
 }
 
+extern "C" int koemi_ep_norm_dispatch(const float *fused, const float *norm_weight, float eps, float *context,
+                                      const int64_t *pair_positions, const int64_t *sorted_experts,
+                                      const int64_t *segment_offsets, int64_t tokens, int64_t top_k,
+                                      const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
+                                      int64_t local_experts, int64_t capacity, int dtype, void *stream) {
+    clear_error();
+    ExchangeArgs a;
+    int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
+    if (rc != KOEMI_OK) return rc;
+    if (tokens < 0 || top_k < 1) return fail(KOEMI_ERR_INVALID, "bad token count or top_k");
+    if (capacity < tokens * top_k) {
+        return fail(KOEMI_ERR_INVALID, "capacity %lld is below the %lld pairs one owner may receive",
+                    (long long)capacity, (long long)(tokens * top_k));
+    }
+    if ((dtype != KOEMI_BF16 && dtype != KOEMI_F16) || width % 4 != 0 || width > 2048 || !aligned(fused, 16) ||
+        !aligned(norm_weight, 16) || !aligned(context, 16) || pair_positions == nullptr || sorted_experts == nullptr ||
+        segment_offsets == nullptr) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the normalising dispatch takes 16-bit exchange rows, width a multiple of 4 "
+                                           "up to 2048 and 16-byte aligned rows");
+    }
+    const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, ceil_div(tokens, 8)));
+    cudaStream_t s = as_stream(stream);
+    if (dtype == KOEMI_BF16) {
+        KOEMI_CUDA_TRY(launch_pdl(ep_norm_dispatch_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a,
+                                  fused, norm_weight, context, pair_positions, sorted_experts, segment_offsets, tokens,
+                                  top_k, eps));
+    } else {
+        KOEMI_CUDA_TRY(launch_pdl(ep_norm_dispatch_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), a,
+                                  fused, norm_weight, context, pair_positions, sorted_experts, segment_offsets, tokens,
+                                  top_k, eps));
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
 extern "C" int koemi_ep_owner_sort(const uint64_t *peers, void *own, int64_t width, int64_t rank, int64_t ranks,
                                    int64_t local_experts, int64_t capacity, int dtype, void *sorted_rows,
                                    int64_t *segment_offsets, int64_t *sorted_experts, int64_t *positions,
-                                   void *stream) {
+                                   int64_t *slots, int32_t *tile_prefix, void *stream) {
     clear_error();
     ExchangeArgs a;
     int rc = exchange_args(&a, peers, own, rank, ranks, local_experts, capacity, width, dtype);
@@ -545,7 +627,7 @@ extern "C" int koemi_ep_owner_sort(const uint64_t *peers, void *own, int64_t wid
             KOEMI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         }
         KOEMI_CUDA_TRY(launch_pdl(kernel, dim3(blocks), dim3(kOwnerThreads), smem, s, dim3(1, 1, 1), a, typed,
-                                  segment_offsets, sorted_experts, positions, vector));
+                                  segment_offsets, sorted_experts, positions, slots, tile_prefix, vector));
         KOEMI_LAUNCH_CHECK();
         return KOEMI_OK;
     };

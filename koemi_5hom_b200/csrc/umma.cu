@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "peer.cuh"
 #include "vec.cuh"
 
 namespace koemi {
@@ -77,7 +78,6 @@ enum Problem : int { kGated = 0, kOutput = 1, kSurprise = 2, kDense = 3, kDenseC
 // adds the bias and stores. Row stride of the parked accumulator, in floats
 // (padded so the per-row float4 stores of a warp hit distinct banks):
 constexpr int kAccStride = kBN + 4;
-constexpr int kMaxClusterSplits = 8;  // portable cluster size
 static_assert(kBM * kAccStride * 4 <= kStages * kStageBytes, "parked accumulator must fit in the stage ring");
 
 struct UmmaArgs {
@@ -108,6 +108,13 @@ struct UmmaArgs {
     const float *row_scale;   // surprise gradient: per-row dL/dNLL (0 on invalid rows)
     float *grad_out;          // surprise gradient: fp32 dlogits [rows, n_out]
     int64_t weights_ready;    // dense: no earlier kernel of the stream writes B (its first stages load before pdl_wait)
+    // expert-parallel return (output problem): row r's output goes to slot
+    // ret_slots[r] = sender * ret_capacity + j of this owner's block in the
+    // sender's exchange buffer, then the senders' return flags are raised
+    const uint64_t *ret_peers;  // [ret_ranks] exchange buffer of every rank (NULL: store to out)
+    uint8_t *ret_own;
+    const int64_t *ret_slots;
+    int64_t ret_offset, ret_capacity, ret_rank, ret_ranks;
     int *status;
     uint32_t idesc;
 };
@@ -600,7 +607,15 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                 }
             } else if (kProblem == kOutput) {
                 const T *bo = static_cast<const T *>(args.bias0) + tile.group * args.b_rows_per_group;
-                T *out = static_cast<T *>(args.out);
+                T *out_row = static_cast<T *>(args.out) + row * args.out_stride;
+                if (args.ret_peers != nullptr && row_ok) {
+                    // the received slot of this row: straight back to its sender
+                    const int64_t slot = args.ret_slots[row];
+                    const int64_t sender = slot / args.ret_capacity;
+                    const int64_t j = slot - sender * args.ret_capacity;
+                    out_row = reinterpret_cast<T *>(reinterpret_cast<uint8_t *>(args.ret_peers[sender]) + args.ret_offset) +
+                              (args.ret_rank * args.ret_capacity + j) * args.out_stride;
+                }
 #pragma unroll 1
                 for (int c = 0; c < kTileN / 32; ++c) {
                     uint32_t y[32];
@@ -612,7 +627,7 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
                         load_bias32(bo, col0, args.n_out, o);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(y[j]);
-                        T *dst = out + row * args.out_stride + col0;
+                        T *dst = out_row + col0;
                         if (col0 + 32 <= args.n_out) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
@@ -772,6 +787,14 @@ __global__ __launch_bounds__(threads_for<kProblem>(), 1) void umma_gemm_kernel(c
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (kProblem == kOutput) {
+        // every CTA's returned rows are stored: the last CTA raises this
+        // owner's return flag in every sender's buffer
+        if (args.ret_peers != nullptr) {
+            peer::signal_peers(args.ret_own, args.ret_peers, 1, args.ret_rank, args.ret_ranks,
+                               peer::current_epoch(args.ret_own), false);
+        }
+    }
     if constexpr (kProblem == kDenseCluster) {
         // Per 128-row half: the epilogue warps park the accumulator rows in
         // this CTA's shared memory (the stage ring is idle: every load was
@@ -1020,6 +1043,74 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     KOEMI_LAUNCH_CHECK();
     *handled = true;
     return KOEMI_OK;
+}
+
+// The owner's grouped expert MLP of an expert-parallel exchange: the same two
+// GEMMs as grouped_mlp_umma over the received rows in local expert order
+// (tile map from the owner sort), with the output GEMM storing each row's
+// result straight into its sender's exchange buffer and raising the return
+// flags; no output tensor, no pad-row zeroing.
+int expert_mlp_return_umma(const void *sorted_rows, const int64_t *segment_offsets, const int32_t *tile_prefix,
+                           const int64_t *slots, const void *gate_w, const void *gate_b, const void *value_w,
+                           const void *value_b, const void *out_w, const void *out_b, int64_t rows, int64_t d,
+                           int64_t h, int64_t local_experts, int dtype, void *hidden, const uint64_t *peers,
+                           uint8_t *own, size_t ret_offset, int64_t rank, int64_t ranks, int64_t capacity,
+                           cudaStream_t stream) {
+    const int64_t max_m_tiles = (rows + kBM - 1) / kBM + local_experts;
+    UmmaArgs g1{};
+    int rc = encode_kmajor(&g1.map_a, dtype, sorted_rows, rows, d, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g1.map_b0, dtype, gate_w, local_experts * h, d, 128);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g1.map_b1, dtype, value_w, local_experts * h, d, 128);
+    if (rc != KOEMI_OK) return rc;
+    g1.k = d;
+    g1.rows = rows;
+    g1.n_tiles = (h + 127) / 128;
+    g1.b_rows_per_group = h;
+    g1.n_out = h;
+    g1.out_stride = h;
+    g1.experts = local_experts;
+    g1.offsets = segment_offsets;
+    g1.tile_prefix = tile_prefix;
+    g1.bias0 = gate_b;
+    g1.bias1 = value_b;
+    g1.out = hidden;
+    g1.status = device_status_word();
+    g1.idesc = make_idesc(dtype);
+    rc = launch<kGated>(g1, dtype, max_m_tiles * g1.n_tiles, stream);
+    if (rc != KOEMI_OK) return rc;
+    // narrow output tiles when the 256-wide ones cannot fill the SMs (as in
+    // grouped_mlp_umma, with the received slots as the pair count)
+    const int64_t est_m_tiles = std::min(max_m_tiles, std::max((rows + kBM - 1) / kBM, std::min(rows, local_experts)));
+    const bool narrow = est_m_tiles * ((d + kBN - 1) / kBN) < sm_count();
+    const int64_t tile_n = narrow ? kBN / 2 : kBN;
+    UmmaArgs g2{};
+    rc = encode_kmajor(&g2.map_a, dtype, hidden, rows, h, kBM);
+    if (rc == KOEMI_OK) rc = encode_kmajor(&g2.map_b0, dtype, out_w, local_experts * d, h, static_cast<uint32_t>(tile_n));
+    if (rc != KOEMI_OK) return rc;
+    g2.k = h;
+    g2.rows = rows;
+    g2.n_tiles = (d + tile_n - 1) / tile_n;
+    g2.b_rows_per_group = d;
+    g2.n_out = d;
+    g2.out_stride = d;
+    g2.experts = local_experts;
+    g2.offsets = segment_offsets;
+    g2.tile_prefix = tile_prefix;
+    g2.bias0 = out_b;
+    g2.out = nullptr;
+    g2.ret_peers = peers;
+    g2.ret_own = own;
+    g2.ret_slots = slots;
+    g2.ret_offset = static_cast<int64_t>(ret_offset);
+    g2.ret_capacity = capacity;
+    g2.ret_rank = rank;
+    g2.ret_ranks = ranks;
+    g2.status = g1.status;
+    g2.idesc = make_idesc(dtype, static_cast<int>(tile_n));
+    // the return flags need every CTA of the launch to reach the end, so the
+    // grid is at least one CTA even when no tile exists
+    return narrow ? launch<kOutput, false, kBN / 2>(g2, dtype, max_m_tiles * g2.n_tiles, stream)
+                  : launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
 }
 
 // K splits of a dense projection: the largest S <= 8 whose tiles x S CTAs
@@ -1308,4 +1399,39 @@ extern "C" int koemi_dense_projection_resident(const void *a, int64_t a_stride, 
     (void)workspace;
     (void)workspace_bytes;
     return dense_projection(a, a_stride, weight, bias, out, out_stride, rows, n, k, dtype, stream, true);
+}
+
+extern "C" int koemi_ep_expert_mlp_return(const void *sorted_rows, const int64_t *segment_offsets,
+                                          const int32_t *tile_prefix, const int64_t *slots, const void *gate_weights,
+                                          const void *gate_biases, const void *value_weights,
+                                          const void *value_biases, const void *output_weights,
+                                          const void *output_biases, int64_t rows, int64_t input_width,
+                                          int64_t hidden_width, int64_t local_experts, int dtype, void *workspace,
+                                          size_t workspace_bytes, const uint64_t *peers, void *own, int64_t rank,
+                                          int64_t ranks, int64_t capacity, void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "the returning expert MLP takes bf16 or f16 rows");
+    if (rows < 1 || input_width < 1 || hidden_width < 1 || local_experts < 1 || capacity < 1 || ranks < 1 ||
+        ranks > peer::kMaxRanks || rank < 0 || rank >= ranks || rows > ranks * capacity) {
+        return fail(KOEMI_ERR_INVALID, "bad returning expert MLP sizes");
+    }
+    if (sorted_rows == nullptr || segment_offsets == nullptr || tile_prefix == nullptr || slots == nullptr ||
+        peers == nullptr || own == nullptr || !aligned(own, 256)) {
+        return fail(KOEMI_ERR_INVALID, "returning expert MLP pointers must be non-NULL (own 256-byte aligned)");
+    }
+    if (!umma_shape_ok(sorted_rows, input_width) || !umma_shape_ok(gate_weights, input_width) ||
+        !umma_shape_ok(value_weights, input_width) || !umma_shape_ok(output_weights, hidden_width) ||
+        rows >= (int64_t(1) << 31) || local_experts * hidden_width >= (int64_t(1) << 31) ||
+        local_experts * input_width >= (int64_t(1) << 31)) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the returning expert MLP needs widths that are multiples of 8 and 16-byte aligned operands");
+    }
+    const size_t hidden_bytes = static_cast<size_t>(rows) * static_cast<size_t>(hidden_width) * 2;
+    if (workspace == nullptr || workspace_bytes < hidden_bytes || !aligned(workspace, 16)) {
+        return fail(KOEMI_ERR_WORKSPACE, "the returning expert MLP needs %zu workspace bytes (16-byte aligned)", hidden_bytes);
+    }
+    const peer::Layout l = peer::layout(ranks, capacity, input_width, 2);
+    return expert_mlp_return_umma(sorted_rows, segment_offsets, tile_prefix, slots, gate_weights, gate_biases,
+                                  value_weights, value_biases, output_weights, output_biases, rows, input_width,
+                                  hidden_width, local_experts, dtype, workspace, peers, static_cast<uint8_t *>(own),
+                                  l.ret, rank, ranks, capacity, as_stream(stream));
 }

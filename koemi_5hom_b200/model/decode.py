@@ -268,6 +268,8 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             valid.repeat(count), torch.float32).view(count, batch)
     # the combine of block i also writes block i + 1's normalised input
     fused_combine = s.expert_count > 0 and d % 4 == 0 and d <= 2048 and s.expert_top_k <= 8
+    exchange = (model.fused_return_exchange(batch * s.expert_top_k, d)
+                if shared_route and fused_combine and model.expert_shard is not None else None)
     u = None
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
@@ -302,12 +304,21 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         _assoc_step(call, ptr, block, st, assoc, surprise, valid, concat, batch, d, s.memory_features,
                     out_code, stream)
         fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
-        context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
+        if exchange is not None:
+            # expert parallel: the fusion norm dispatches each pair's row to its
+            # owner; the owners' outputs come back into this rank's exchange
+            # buffer, where the fused combine reads them
+            context = exchange.dispatch_normed(fused, bc["fusion_norm"], NORM_EPSILON, positions, sorted_experts,
+                                               offsets, s.expert_top_k)
+        else:
+            context = _ops.rms_norm(fused, None, bc["fusion_norm"], None, NORM_EPSILON, torch.float32)
         u = None
         if s.expert_count == 0:
             x = context
             continue
-        if shared_route:
+        if exchange is not None:
+            exchange.serve_and_return(block.expert_weights())
+        elif shared_route:
             expert_out = model.expert_mlp_of_tokens(block, context, sorted_tokens, sorted_experts, offsets)
         else:
             gate_logits = model._linear(torch.where(valid.unsqueeze(-1), context, 0.0), block.router_weight, None)
@@ -318,9 +329,17 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         if fused_combine:
             last = index + 1 == len(model.blocks)
             next_norm = None if last else cache["blocks"][index + 1]["input_norm"]
-            y = _ops.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, weights, valid,
-                                                   bc["expert_norm"], next_norm, s.expert_top_k, NORM_EPSILON,
-                                                   model.compute_dtype)
+            if exchange is not None:
+                y = torch.empty(batch, d, dtype=model.compute_dtype, device=device)
+                call("koemi_ep_combine_residual_rmsnorm_next", ptr(context), ptr(positions), ptr(offsets),
+                     ptr(weights), ptr(valid), ptr(bc["expert_norm"]), ptr(next_norm), ptr(y),
+                     _native.dtype_code(model.compute_dtype), batch, d, s.expert_top_k, s.expert_count,
+                     NORM_EPSILON, _native.dtype_code(exchange.dtype), exchange.own, exchange.shard.world,
+                     exchange.shard.local_count, exchange.capacity, stream)
+            else:
+                y = _ops.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, weights, valid,
+                                                       bc["expert_norm"], next_norm, s.expert_top_k, NORM_EPSILON,
+                                                       model.compute_dtype)
             if last:
                 x = y
             else:

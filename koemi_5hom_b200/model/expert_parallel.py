@@ -260,7 +260,7 @@ class PeerExchange:
             local_positions = torch.empty(slots, dtype=torch.int64, device=self.device)
             call("koemi_ep_owner_sort", ptr(self.peers), self.own, width, shard.rank, shard.world, shard.local_count,
                  self.capacity, code, ptr(local_sorted), ptr(local_offsets), ptr(local_experts), ptr(local_positions),
-                 stream)
+                 None, None, stream)
         else:
             call("koemi_ep_wait_dispatch", self.own, shard.world, stream)
             local_sorted, _, local_experts, local_offsets, local_positions = _ops.permute_topk(
@@ -272,3 +272,79 @@ class PeerExchange:
         call("koemi_ep_collect", ptr(sorted_experts), ptr(offsets), ptr(out), ptr(self.peers), self.own, pairs, width,
              shard.rank, shard.world, shard.local_count, self.capacity, code, stream)
         return out
+
+    def supports_return_to_combine(self) -> bool:
+        """The fused return (the owner's output GEMM stores into the senders'
+        buffers, the sender's combine reads them in place) needs 16-bit rows
+        and the one-launch owner sort."""
+        return (self.dtype in (torch.bfloat16, torch.float16) and self.width % 8 == 0
+                and self.shard.world * self.capacity <= OWNER_SORT_MAX_SLOTS
+                and self.shard.local_count <= OWNER_SORT_MAX_EXPERTS)
+
+    def dispatch_normed(self, fused: Tensor, norm_weight: Tensor, eps: float, pair_positions: Tensor,
+                        sorted_experts: Tensor, offsets: Tensor, top_k: int) -> Tensor:
+        """The sender's half with the block's fusion RMSNorm fused in: returns
+        the fp32 normalised rows (the combine's residual) after storing every
+        routed pair's row, in the exchange dtype, into its owner's buffer."""
+        from koemi_5hom_b200 import _native
+        shard = self.shard
+        tokens, width = fused.shape
+        if tokens * top_k > self.capacity or width != self.width or not self.supports_return_to_combine():
+            raise ValueError("rows do not fit this exchange")
+        fused = fused.contiguous()
+        context = torch.empty_like(fused)
+        _native.call("koemi_ep_norm_dispatch", _native.ptr(fused), _native.ptr(norm_weight.contiguous()), eps,
+                     _native.ptr(context), _native.ptr(pair_positions.contiguous()),
+                     _native.ptr(sorted_experts.contiguous()), _native.ptr(offsets.contiguous()), tokens, top_k,
+                     _native.ptr(self.peers), self.own, width, shard.rank, shard.world, shard.local_count,
+                     self.capacity, _native.dtype_code(self.dtype), torch.cuda.current_stream(self.device).cuda_stream)
+        return context
+
+    def run_to_combine(self, context: Tensor, sorted_tokens: Tensor, sorted_experts: Tensor, offsets: Tensor,
+                       weights: tuple[Tensor, ...]) -> None:
+        """One exchange whose expert outputs stay in the senders' buffers:
+        the gathering dispatch, then ``serve_and_return``. The caller then
+        combines with ``koemi_ep_combine_residual_rmsnorm_next`` on this
+        exchange's buffer."""
+        from koemi_5hom_b200 import _native
+        shard = self.shard
+        pairs = sorted_experts.shape[0]
+        width = self.width
+        if pairs > self.capacity or context.shape[1] != width or not self.supports_return_to_combine():
+            raise ValueError("rows do not fit this exchange")
+        ptr = _native.ptr
+        _native.call("koemi_ep_dispatch_gather", ptr(context.contiguous()), _native.dtype_code(context.dtype),
+                     ptr(sorted_tokens.contiguous()), ptr(sorted_experts.contiguous()), ptr(offsets.contiguous()),
+                     ptr(self.peers), self.own, pairs, width, shard.rank, shard.world, shard.local_count, self.capacity,
+                     _native.dtype_code(self.dtype), torch.cuda.current_stream(self.device).cuda_stream)
+        self.serve_and_return(weights)
+
+    def serve_and_return(self, weights: tuple[Tensor, ...]) -> None:
+        """The owner's half: the owner sort (which also emits the slot of
+        every sorted row and the grouped GEMM's tile map) and the expert MLP
+        of the local experts, whose output GEMM stores each row back into its
+        sender's buffer and raises the return flags. Three launches fewer
+        than ``run`` (the tile map, the return and the collect) and no sorted
+        output tensor."""
+        from koemi_5hom_b200 import _native
+        shard = self.shard
+        width = self.width
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        code = _native.dtype_code(self.dtype)
+        ptr, call = _native.ptr, _native.call
+        slots = shard.world * self.capacity
+        local_sorted = torch.empty(slots, width, dtype=self.dtype, device=self.device)
+        local_offsets = torch.empty(shard.local_count + 1, dtype=torch.int64, device=self.device)
+        local_experts = torch.empty(slots, dtype=torch.int64, device=self.device)
+        local_positions = torch.empty(slots, dtype=torch.int64, device=self.device)
+        local_slots = torch.empty(slots, dtype=torch.int64, device=self.device)
+        tile_prefix = torch.empty(shard.local_count + 1, dtype=torch.int32, device=self.device)
+        call("koemi_ep_owner_sort", ptr(self.peers), self.own, width, shard.rank, shard.world, shard.local_count,
+             self.capacity, code, ptr(local_sorted), ptr(local_offsets), ptr(local_experts), ptr(local_positions),
+             ptr(local_slots), ptr(tile_prefix), stream)
+        weights = tuple(w.contiguous() for w in weights)
+        hidden_width = weights[0].shape[1]
+        hidden = torch.empty(slots * hidden_width * 2, dtype=torch.uint8, device=self.device)
+        call("koemi_ep_expert_mlp_return", ptr(local_sorted), ptr(local_offsets), ptr(tile_prefix), ptr(local_slots),
+             *(ptr(w) for w in weights), slots, width, hidden_width, shard.local_count, code, ptr(hidden),
+             hidden.numel(), ptr(self.peers), self.own, shard.rank, shard.world, self.capacity, stream)

@@ -310,6 +310,17 @@ class KoemiModel(nn.Module):
         rows = _ops.gather_rows(context, sorted_tokens, offsets, self.compute_dtype)
         return self.expert_mlp(block, rows, sorted_experts, offsets, mode="padded")
 
+    def fused_return_exchange(self, pairs: int, width: int) -> PeerExchange | None:
+        """The peer exchange for ``pairs`` sorted pairs of ``width`` when its
+        fused return applies (expert parallel, peer exchange, 16-bit rows):
+        the owners store the expert outputs straight into this rank's buffer
+        and the combine reads them in place. Otherwise None."""
+        if not (self.expert_shard is not None and self.exchange == "peer" and width % 8 == 0
+                and self.compute_dtype != torch.float32):
+            return None
+        exchange = self.peer_exchange(pairs, width, self.compute_dtype)
+        return exchange if exchange.supports_return_to_combine() else None
+
     def peer_exchange(self, capacity: int, width: int, dtype: torch.dtype) -> PeerExchange:
         """The peer-memory exchange for decode-sized pair counts (created by
         all ranks together on first use, then reused by every block)."""

@@ -74,7 +74,59 @@ def test_peer_exchange_with_itself_equals_grouped_mlp(tokens, experts, steps, ga
         exchange.close()
 
 
-@pytest.mark.parametrize("stage", ["dispatch", "collect"])
+@pytest.mark.parametrize("tokens,experts,steps", [(64, 8, 3), (256, 64, 2), (5, 4, 1), (1000, 16, 2)])
+@pytest.mark.parametrize("normed", [False, True])
+def test_fused_return_with_itself_equals_local_combine(tokens, experts, steps, normed, cuda):
+    """The fused return on one GPU, one rank exchanging with its own buffer:
+    the dispatch (gathering context rows, or normalising the fusion output and
+    dispatching in one launch), owner sort (with slots and tile map), the
+    expert MLP whose output GEMM stores the rows into the sender's return
+    block, and the combine that waits for the return flag and reads them in
+    place. It must equal the local norm + grouped MLP + combine bit for bit,
+    over several exchanges (epochs)."""
+    from koemi_5hom_b200 import _native
+    from koemi_5hom_b200.model.expert_parallel import ExpertShard, PeerExchange
+    g = torch.Generator().manual_seed(tokens + 7)
+    width, hidden, top_k = 128, 256, 2
+    weights = tuple((torch.randn(*shape, generator=g) * 0.05).bfloat16().to(cuda) for shape in
+                    ((experts, hidden, width), (experts, hidden), (experts, hidden, width), (experts, hidden),
+                     (experts, width, hidden), (experts, width)))
+    norm = (1.0 + 0.1 * torch.randn(width, generator=g)).to(cuda)
+    next_norm = (1.0 + 0.1 * torch.randn(width, generator=g)).to(cuda)
+    exchange = PeerExchange(ExpertShard(1, 0, experts), tokens * top_k, width, torch.bfloat16, cuda)
+    assert exchange.supports_return_to_combine()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    try:
+        fusion_norm = (1.0 + 0.1 * torch.randn(width, generator=g)).to(cuda)
+        for step in range(steps):
+            fused = torch.randn(tokens, width, generator=g).to(cuda) * 3.0
+            context = _ops.rms_norm(fused, None, fusion_norm, None, 1e-6, torch.float32) if normed else fused
+            assignments = torch.randint(-1, experts, (tokens, top_k), generator=g).to(cuda)
+            valid = (torch.rand(tokens, generator=g) > 0.1).to(cuda)
+            sorted_rows, sorted_tokens, sorted_experts, offsets, positions = _ops.permute_topk(
+                context.bfloat16(), assignments, valid, experts, True)
+            expert_out = _ops.grouped_expert_mlp(sorted_rows, sorted_experts, offsets, *weights)
+            expected = _ops.combine_residual_rmsnorm_next(context, expert_out, positions, offsets, None, valid, norm,
+                                                          next_norm, top_k, 1e-6, torch.bfloat16)
+            if normed:
+                mine = exchange.dispatch_normed(fused, fusion_norm, 1e-6, positions, sorted_experts, offsets, top_k)
+                assert torch.equal(mine, context), step
+                exchange.serve_and_return(weights)
+            else:
+                exchange.run_to_combine(context, sorted_tokens, sorted_experts, offsets, weights)
+            got = torch.empty(tokens, width, dtype=torch.bfloat16, device=cuda)
+            _native.call("koemi_ep_combine_residual_rmsnorm_next", context.data_ptr(), positions.data_ptr(),
+                         offsets.data_ptr(), None, valid.data_ptr(), norm.data_ptr(), next_norm.data_ptr(),
+                         got.data_ptr(), _native.BF16, tokens, width, top_k, experts, 1e-6, _native.BF16,
+                         exchange.own, 1, experts, exchange.capacity, stream)
+            torch.cuda.synchronize()
+            assert _native.device_status(cuda) == 0
+            assert torch.equal(got, expected), step
+    finally:
+        exchange.close()
+
+
+@pytest.mark.parametrize("stage", ["dispatch", "collect", "combine"])
 def test_peer_waits_give_up_when_no_flag_arrives(stage, cuda):
     """The bounded waits of the exchange, made to run out on one GPU: the
     buffer's epoch says an exchange is due but no rank ever raises its flag
@@ -93,6 +145,18 @@ def test_peer_waits_give_up_when_no_flag_arrives(stage, cuda):
         stream = torch.cuda.current_stream(cuda).cuda_stream
         if stage == "dispatch":
             _native.call("koemi_ep_wait_dispatch", exchange.own, ranks, stream)
+        elif stage == "combine":  # the fused return's combine waits for every owner's return flag
+            tokens = 3
+            context = torch.randn(tokens, width, device=cuda)
+            positions = torch.tensor([0, 1, 2, 3, 4, 5], dtype=torch.int64, device=cuda)
+            offsets = torch.tensor([0, 6, 6, 6, 6], dtype=torch.int64, device=cuda)
+            valid = torch.ones(tokens, dtype=torch.bool, device=cuda)
+            norm = torch.ones(width, device=cuda)
+            out = torch.empty(tokens, width, dtype=torch.bfloat16, device=cuda)
+            _native.call("koemi_ep_combine_residual_rmsnorm_next", context.data_ptr(), positions.data_ptr(),
+                         offsets.data_ptr(), None, valid.data_ptr(), norm.data_ptr(), None, out.data_ptr(),
+                         _native.BF16, tokens, width, 2, experts, 1e-6, _native.BF16, exchange.own, ranks,
+                         experts // ranks, capacity, stream)
         else:
             pairs = 6
             sorted_experts = torch.zeros(pairs, dtype=torch.int64, device=cuda)
