@@ -285,12 +285,10 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
              next_prior, batch, d, MIN_RETENTION, MAX_RETENTION, prior_dtype, stream)
         h = concat[:, :d]
         surprise = None if all_surprise is None else all_surprise[index]
-        if batch <= 128:  # one row tile: a single wider GEMM fills the GPU better than two
-            local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
-            local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
-        else:
-            local = model._linear(h, block.local_weight, block.local_bias)
-            assoc = model._linear(h, block.assoc_weight, block.assoc_bias)
+        # local | assoc as one GEMM over h: fills the GPU better than two at
+        # every decode batch (256 rows: 24.7 us against 13.2 + 16.1 us)
+        local_assoc = model._linear(h, bc["local_assoc_weight"], bc["local_assoc_bias"])
+        local, assoc = local_assoc[:, :2 * d], local_assoc[:, 2 * d:]
         scored = surprise if surprise is not None else torch.zeros(batch, device=device)
         # ring queries read the fp32 working state (the new h) directly
         call("koemi_think_ring_decode_step", ptr(st.working), d, ptr(local), local.stride(0), ptr(valid), ptr(scored),
