@@ -265,7 +265,8 @@ def test_grouped_mlp_tensor_core_baseline_shapes(tokens, d, h, e, k, cuda):
                                                   (1, 8192, 1024, 1024, False), (64, 5000, 8192, 8200, True),
                                                   (17, 3600, 256, 264, True)])
 def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
-    """tcgen05 projection (cluster split-K, direct, or paired tiles in banded
+    """tcgen05 projection (at most 64 rows: full-K column tiles with several
+    TMEM accumulators; then cluster split-K, direct, or paired tiles in banded
     order from 4096 rows on, ragged last band included) against fp64 on the
     same bf16 operands."""
     g = torch.Generator(device=cuda).manual_seed(rows + n)
@@ -278,6 +279,9 @@ def test_dense_projection_matches_fp64(rows, n, k, stride, bias, cuda):
     torch.testing.assert_close(out.double(), expected, rtol=1e-4, atol=1e-4)
     again = _ops.dense_projection(a, w, b)
     assert torch.equal(out, again)  # fixed-order split-K reduction
+    # launched as for model parameters (weights requested before the wait on
+    # the previous kernel): the same result
+    assert torch.equal(_ops.dense_projection(a, w, b, True), out)
 
 
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
