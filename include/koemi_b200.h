@@ -508,6 +508,38 @@ KOEMI_API int koemi_moe_combine_residual_rmsnorm(const float *context, const voi
                                        int64_t top_k, int64_t expert_count, float eps,
                                        int dtype, void *stream);
 
+/* The decode step's expert path with one permutation per step (the hash route
+ * of every block is the same): koemi_moe_tile_prefix writes the grouped GEMMs'
+ * tile map of segment_offsets (int32 [expert_count + 1], the 128-row tiles
+ * before each expert) once, and koemi_moe_grouped_expert_mlp_mapped runs
+ * koemi_moe_grouped_expert_mlp (tcgen05, bf16/f16 only) with that map, leaving
+ * output rows past the valid pairs unwritten instead of zeroing them (the
+ * combine never reads them). Workspace: koemi_moe_grouped_mlp_workspace.
+ * Same reference lines as the grouped MLP (moe/__init__.py:179-312). */
+KOEMI_API int koemi_moe_tile_prefix(const int64_t *segment_offsets, int64_t expert_count, int32_t *tile_prefix,
+                                    void *stream);
+KOEMI_API int koemi_moe_grouped_expert_mlp_mapped(const void *sorted_context, const int32_t *tile_prefix,
+                                                  const int64_t *segment_offsets, const void *gate_weights,
+                                                  const void *gate_biases, const void *value_weights,
+                                                  const void *value_biases, const void *output_weights,
+                                                  const void *output_biases, void *output, int64_t pairs,
+                                                  int64_t input_width, int64_t hidden_width, int64_t expert_count,
+                                                  int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The decode block's fusion RMSNorm (src/koemi/model/network.py:723-732)
+ * fused with the row gather of its expert pairs: token row t of `fused` (fp32
+ * [tokens, width]) is normalised, x * rsqrt(mean(x^2) + eps) * norm_weight,
+ * into `context` (fp32; the arithmetic of koemi_core_rmsnorm_forward with fp32
+ * in and out), and the normalised row is stored in rows_dtype (bf16/f16) at
+ * rows_out[pair_positions[t * top_k + j]] for every pair below the valid count
+ * (segment_offsets[expert_count]); other rows of rows_out are left as they were.
+ * Width a multiple of 4 up to 2048. Replaces the norm plus a gather of the
+ * sorted rows. */
+KOEMI_API int koemi_moe_norm_gather(const float *fused, const float *norm_weight, float eps, float *context,
+                                    const int64_t *pair_positions, const int64_t *segment_offsets,
+                                    int64_t expert_count, void *rows_out, int rows_dtype, int64_t tokens,
+                                    int64_t width, int64_t top_k, void *stream);
+
 /* koemi_moe_combine_residual_rmsnorm for a chain of blocks: the combined,
  * normalised row x is stored as out_dtype, or, when next_norm_weight (fp32
  * [width]) is given, the next block's input RMSNorm(x) * next_norm_weight

@@ -103,6 +103,10 @@ SIGNATURES: dict[str, tuple[object, tuple[object, ...]]] = {
     "koemi_moe_ep_unpack": (_int, (_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p)),
     "koemi_moe_combine_residual_rmsnorm_next": (
         _int, (_p, _p, _p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _f, _int, _p)),
+    "koemi_moe_tile_prefix": (_int, (_p, _i64, _p, _p)),
+    "koemi_moe_grouped_expert_mlp_mapped": (_int, (_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int,
+                                                   _p, _sz, _p)),
+    "koemi_moe_norm_gather": (_int, (_p, _p, _f, _p, _p, _p, _i64, _p, _int, _i64, _i64, _i64, _p)),
     "koemi_moe_gather_rows": (_int, (_p, _int, _p, _p, _i64, _p, _int, _i64, _i64, _p)),
     "koemi_peer_exchange_bytes": (_sz, (_i64, _i64, _i64, _int)),
     "koemi_peer_exchange_offsets": (_int, (_i64, _i64, _i64, _int, _p, _p)),

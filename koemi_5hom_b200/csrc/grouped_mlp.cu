@@ -21,7 +21,8 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
                      const void *gate_b, const void *value_w, const void *value_b, const void *out_w,
                      const void *out_b, void *output, int64_t pairs, int64_t input_width,
                      int64_t hidden_width, int64_t expert_count, int dtype, void *workspace,
-                     size_t workspace_bytes, cudaStream_t stream, bool *handled);
+                     size_t workspace_bytes, cudaStream_t stream, bool *handled, const int32_t *tile_prefix_in,
+                     bool zero_tail);
 size_t grouped_mlp_umma_workspace(int64_t pairs, int64_t input_width, int64_t hidden_width,
                                   int64_t expert_count, int dtype);
 
@@ -221,7 +222,8 @@ extern "C" int koemi_moe_grouped_expert_mlp(const void *sorted_context, const in
         bool handled = false;
         int rc = grouped_mlp_umma(sorted_context, segment_offsets, gate_weights, gate_biases, value_weights,
                                   value_biases, output_weights, output_biases, output, pairs, input_width,
-                                  hidden_width, expert_count, dtype, workspace, workspace_bytes, s, &handled);
+                                  hidden_width, expert_count, dtype, workspace, workspace_bytes, s, &handled, nullptr,
+                                  true);
         if (rc != KOEMI_OK || handled) return rc;
     }
     char *ws = static_cast<char *>(workspace);
@@ -232,3 +234,43 @@ extern "C" int koemi_moe_grouped_expert_mlp(const void *sorted_context, const in
         default: return fail(KOEMI_ERR_INVALID, "grouped MLP supports f32, f16 and bf16");
     }
 }
+
+extern "C" int koemi_moe_tile_prefix(const int64_t *segment_offsets, int64_t expert_count, int32_t *tile_prefix,
+                                     void *stream) {
+    clear_error();
+    if (segment_offsets == nullptr || tile_prefix == nullptr || expert_count < 1) {
+        return fail(KOEMI_ERR_INVALID, "tile prefix needs offsets, an output and expert_count >= 1");
+    }
+    KOEMI_CUDA_TRY(launch_pdl(tile_prefix_kernel, dim3(1), dim3(32), 0, as_stream(stream), dim3(1, 1, 1),
+                              segment_offsets, expert_count, static_cast<int64_t>(128), tile_prefix));
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}
+
+extern "C" int koemi_moe_grouped_expert_mlp_mapped(const void *sorted_context, const int32_t *tile_prefix,
+                                                   const int64_t *segment_offsets, const void *gate_weights,
+                                                   const void *gate_biases, const void *value_weights,
+                                                   const void *value_biases, const void *output_weights,
+                                                   const void *output_biases, void *output, int64_t pairs,
+                                                   int64_t input_width, int64_t hidden_width, int64_t expert_count,
+                                                   int dtype, void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (dtype != KOEMI_BF16 && dtype != KOEMI_F16) return fail(KOEMI_ERR_INVALID, "the mapped expert MLP takes bf16 or f16 rows");
+    if (pairs < 0 || input_width < 1 || hidden_width < 1 || expert_count < 1 || tile_prefix == nullptr) {
+        return fail(KOEMI_ERR_INVALID, "need pairs >= 0, positive widths and expert_count, and a tile prefix");
+    }
+    if (pairs == 0) return KOEMI_OK;
+    const size_t need = grouped_mlp_umma_workspace(pairs, input_width, hidden_width, expert_count, dtype);
+    if (workspace_bytes < need) return fail(KOEMI_ERR_WORKSPACE, "mapped expert MLP needs %zu workspace bytes", need);
+    bool handled = false;
+    const int rc = grouped_mlp_umma(sorted_context, segment_offsets, gate_weights, gate_biases, value_weights,
+                                    value_biases, output_weights, output_biases, output, pairs, input_width,
+                                    hidden_width, expert_count, dtype, workspace, workspace_bytes, as_stream(stream),
+                                    &handled, tile_prefix, false);
+    if (rc != KOEMI_OK) return rc;
+    if (!handled) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "the mapped expert MLP needs widths that are multiples of 8 and 16-byte aligned operands");
+    }
+    return KOEMI_OK;
+}
+

@@ -1395,3 +1395,117 @@ extern "C" int koemi_moe_gather_rows(const void *rows, int rows_dtype, const int
         default: return fail(KOEMI_ERR_INVALID, "rows must be f32, f16 or bf16");
     }
 }
+
+// ---------------------------------------------------------------------------
+// The decode block's fusion RMSNorm fused with the row gather of its expert
+// pairs: token row t of `fused` (fp32) is normalised with exactly the
+// arithmetic of the cached RMSNorm row kernel (the same loads and sum order)
+// into `context` (fp32, the combine's residual), and the normalised row is
+// also stored, in the rows' dtype, at the sorted position of each of its
+// top_k pairs below the valid count. Rows of `rows_out` past the valid pairs
+// are left as they were (the expert GEMMs never store their results).
+
+namespace koemi {
+namespace {
+
+template <typename T>
+__global__ void norm_gather_kernel(const float *__restrict__ fused, const float *__restrict__ norm_weight,
+                                   float eps, float *__restrict__ context, const int64_t *__restrict__ positions,
+                                   const int64_t *__restrict__ offsets, int64_t experts, T *__restrict__ rows_out,
+                                   int64_t tokens, int64_t width, int64_t top_k) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int NV = 16;  // 16-byte fp32 packets per lane: width <= 2048
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= tokens) return;
+    const int64_t packets = width / 4;
+    const float *xr = fused + t * width;
+    float4 v[NV], w[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int64_t p = lane + 32 * i;
+        if (p < packets) {
+            const uint4 raw = load_stream(xr + p * 4);
+            v[i] = *reinterpret_cast<const float4 *>(&raw);
+            const uint4 wraw = load_cached(norm_weight + p * 4);
+            w[i] = *reinterpret_cast<const float4 *>(&wraw);
+        }
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < packets) {
+            sum = fmaf(v[i].x, v[i].x, sum);
+            sum = fmaf(v[i].y, v[i].y, sum);
+            sum = fmaf(v[i].z, v[i].z, sum);
+            sum = fmaf(v[i].w, v[i].w, sum);
+        }
+    }
+    sum = warp_sum(sum);
+    const float inv = rsqrtf(sum / static_cast<float>(width) + eps);
+    float *cr = context + t * width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int64_t p = lane + 32 * i;
+        if (p < packets) {
+            v[i] = make_float4(v[i].x * inv * w[i].x, v[i].y * inv * w[i].y, v[i].z * inv * w[i].z,
+                               v[i].w * inv * w[i].w);
+            *reinterpret_cast<float4 *>(cr + p * 4) = v[i];
+        }
+    }
+    const int64_t valid_pairs = offsets[experts];
+    for (int64_t s = 0; s < top_k; ++s) {
+        const int64_t pos = positions[t * top_k + s];
+        if (pos < 0 || pos >= valid_pairs) continue;
+        T *dst = rows_out + pos * width;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t p = lane + 32 * i;
+            if (p < packets) {
+                union {
+                    T h[4];
+                    uint2 u;
+                } out;
+                out.h[0] = from_acc<T>(v[i].x);
+                out.h[1] = from_acc<T>(v[i].y);
+                out.h[2] = from_acc<T>(v[i].z);
+                out.h[3] = from_acc<T>(v[i].w);
+                *reinterpret_cast<uint2 *>(dst + p * 4) = out.u;
+            }
+        }
+    }
+}
+
+}  // namespace
+}  // namespace koemi
+
+extern "C" int koemi_moe_norm_gather(const float *fused, const float *norm_weight, float eps, float *context,
+                                     const int64_t *pair_positions, const int64_t *segment_offsets,
+                                     int64_t expert_count, void *rows_out, int rows_dtype, int64_t tokens,
+                                     int64_t width, int64_t top_k, void *stream) {
+    clear_error();
+    if (tokens < 0 || width < 1 || top_k < 1 || expert_count < 1) return fail(KOEMI_ERR_INVALID, "bad norm-gather sizes");
+    if (tokens == 0) return KOEMI_OK;
+    if (width % 4 != 0 || width > 2048 || !aligned(fused, 16) || !aligned(norm_weight, 16) || !aligned(context, 16) ||
+        !aligned(rows_out, 8) || pair_positions == nullptr || segment_offsets == nullptr) {
+        return fail(KOEMI_ERR_UNSUPPORTED, "norm-gather needs width a multiple of 4 up to 2048 and aligned rows");
+    }
+    const unsigned blocks = static_cast<unsigned>(ceil_div(tokens, 8));
+    cudaStream_t s = as_stream(stream);
+    switch (rows_dtype) {
+        case KOEMI_BF16:
+            KOEMI_CUDA_TRY(launch_pdl(norm_gather_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1),
+                                      fused, norm_weight, eps, context, pair_positions, segment_offsets, expert_count,
+                                      static_cast<__nv_bfloat16 *>(rows_out), tokens, width, top_k));
+            break;
+        case KOEMI_F16:
+            KOEMI_CUDA_TRY(launch_pdl(norm_gather_kernel<__half>, dim3(blocks), dim3(256), 0, s, dim3(1, 1, 1), fused,
+                                      norm_weight, eps, context, pair_positions, segment_offsets, expert_count,
+                                      static_cast<__half *>(rows_out), tokens, width, top_k));
+            break;
+        default: return fail(KOEMI_ERR_INVALID, "gathered rows must be bf16 or f16");
+    }
+    KOEMI_LAUNCH_CHECK();
+    return KOEMI_OK;
+}

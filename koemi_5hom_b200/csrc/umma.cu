@@ -973,7 +973,8 @@ size_t grouped_mlp_umma_workspace(int64_t pairs, int64_t input_width, int64_t hi
 int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets, const void *gate_w, const void *gate_b,
                      const void *value_w, const void *value_b, const void *out_w, const void *out_b, void *output,
                      int64_t pairs, int64_t input_width, int64_t hidden_width, int64_t expert_count, int dtype,
-                     void *workspace, size_t workspace_bytes, cudaStream_t stream, bool *handled) {
+                     void *workspace, size_t workspace_bytes, cudaStream_t stream, bool *handled,
+                     const int32_t *tile_prefix_in, bool zero_tail) {
     *handled = false;
     const int64_t d = input_width, h = hidden_width;
     if (!umma_shape_ok(sorted_context, d) || !umma_shape_ok(gate_w, d) || !umma_shape_ok(value_w, d) ||
@@ -985,10 +986,14 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
         return fail(KOEMI_ERR_WORKSPACE, "grouped MLP tensor-core path needs more workspace");
     }
     char *ws = static_cast<char *>(workspace);
-    int32_t *prefix = reinterpret_cast<int32_t *>(ws);
+    const int32_t *prefix = tile_prefix_in;
     void *hidden = ws + align256((expert_count + 1) * sizeof(int32_t));
-    KOEMI_CUDA_TRY(launch_pdl(tile_prefix_kernel, dim3(1), dim3(32), 0, stream, dim3(1, 1, 1), segment_offsets, expert_count, kBM, prefix));
-    KOEMI_LAUNCH_CHECK();
+    if (prefix == nullptr) {  // the tile map of these segments (a caller may pass one it already has)
+        int32_t *own_prefix = reinterpret_cast<int32_t *>(ws);
+        KOEMI_CUDA_TRY(launch_pdl(tile_prefix_kernel, dim3(1), dim3(32), 0, stream, dim3(1, 1, 1), segment_offsets, expert_count, kBM, own_prefix));
+        KOEMI_LAUNCH_CHECK();
+        prefix = own_prefix;
+    }
     const int64_t max_m_tiles = (pairs + kBM - 1) / kBM + expert_count;
 
     UmmaArgs g1{};
@@ -1039,8 +1044,10 @@ int grouped_mlp_umma(const void *sorted_context, const int64_t *segment_offsets,
     rc = narrow ? launch<kOutput, false, kBN / 2>(g2, dtype, max_m_tiles * g2.n_tiles, stream)
                 : launch<kOutput>(g2, dtype, max_m_tiles * g2.n_tiles, stream);
     if (rc != KOEMI_OK) return rc;
-    KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, segment_offsets, expert_count, pairs, d * 2));
-    KOEMI_LAUNCH_CHECK();
+    if (zero_tail) {
+        KOEMI_CUDA_TRY(launch_pdl(zero_tail_rows_kernel, dim3(256), dim3(256), 0, stream, dim3(1, 1, 1), output, segment_offsets, expert_count, pairs, d * 2));
+        KOEMI_LAUNCH_CHECK();
+    }
     *handled = true;
     return KOEMI_OK;
 }

@@ -270,6 +270,17 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
     fused_combine = s.expert_count > 0 and d % 4 == 0 and d <= 2048 and s.expert_top_k <= 8
     exchange = (model.fused_return_exchange(batch * s.expert_top_k, d)
                 if shared_route and fused_combine and model.expert_shard is not None else None)
+    # one GPU with a shared route and 16-bit experts: the grouped GEMMs' tile
+    # map is computed once per step (every block has the same segments) and
+    # each block's fusion norm gathers its expert rows itself
+    mapped = None
+    if (shared_route and fused_combine and model.expert_shard is None and d % 8 == 0
+            and model.compute_dtype in (torch.bfloat16, torch.float16)):
+        pairs = sorted_tokens.shape[0]
+        mapped = {"tile_prefix": torch.empty(s.expert_count + 1, dtype=torch.int32, device=device),
+                  "workspace_bytes": _native.library().koemi_moe_grouped_mlp_workspace(
+                      pairs, d, model.blocks[0].expert_gate_weight.shape[1], s.expert_count, prior_dtype)}
+        call("koemi_moe_tile_prefix", ptr(offsets), s.expert_count, ptr(mapped["tile_prefix"]), stream)
     u = None
     for index, block in enumerate(model.blocks):
         bc = cache["blocks"][index]
@@ -302,7 +313,15 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
         _assoc_step(call, ptr, block, st, assoc, surprise, valid, concat, batch, d, s.memory_features,
                     out_code, stream)
         fused = model._linear(concat, block.fusion_weight, block.fusion_bias)
-        if exchange is not None:
+        if mapped is not None:
+            # one GPU, one permutation per step: the fusion norm also writes each
+            # pair's row at its sorted position
+            context = torch.empty(batch, d, dtype=torch.float32, device=device)
+            rows = torch.empty(pairs, d, dtype=model.compute_dtype, device=device)
+            call("koemi_moe_norm_gather", ptr(fused), ptr(bc["fusion_norm"]), NORM_EPSILON, ptr(context),
+                 ptr(positions), ptr(offsets), s.expert_count, ptr(rows), prior_dtype, batch, d, s.expert_top_k,
+                 stream)
+        elif exchange is not None:
             # expert parallel: the fusion norm dispatches each pair's row to its
             # owner; the owners' outputs come back into this rank's exchange
             # buffer, where the fused combine reads them
@@ -316,6 +335,13 @@ def decode_step(model, token_ids: Tensor, dstate: DecodeState) -> Tensor:
             continue
         if exchange is not None:
             exchange.serve_and_return(block.expert_weights())
+        elif mapped is not None:
+            expert_weights = block.expert_weights()
+            expert_out = torch.empty(pairs, d, dtype=model.compute_dtype, device=device)
+            workspace = _native.workspace(mapped["workspace_bytes"], device)
+            call("koemi_moe_grouped_expert_mlp_mapped", ptr(rows), ptr(mapped["tile_prefix"]), ptr(offsets),
+                 *(ptr(w) for w in expert_weights), ptr(expert_out), pairs, d, expert_weights[0].shape[1],
+                 s.expert_count, prior_dtype, ptr(workspace), workspace.numel(), stream)
         elif shared_route:
             expert_out = model.expert_mlp_of_tokens(block, context, sorted_tokens, sorted_experts, offsets)
         else:

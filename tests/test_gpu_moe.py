@@ -331,3 +331,47 @@ def test_grouped_projection_matches_fp64(groups, rows, n, k, cuda):
     out = _ops.grouped_projection(a, b, groups)
     expected = torch.bmm(a.double().view(groups, rows, k), b.double().view(groups, n, k).transpose(1, 2))
     torch.testing.assert_close(out.view(groups, rows, n).double(), expected, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("tokens,experts,top_k,width,hidden", [(256, 64, 2, 256, 512), (32, 8, 2, 128, 256),
+                                                                 (77, 5, 3, 64, 128)])
+def test_decode_norm_gather_and_mapped_mlp_equal_the_general_path(tokens, experts, top_k, width, hidden, cuda):
+    """The decode step's expert path with one permutation per step: the
+    fusion norm that also gathers each pair's row (koemi_moe_norm_gather) and
+    the grouped MLP on a tile map computed once (koemi_moe_tile_prefix +
+    koemi_moe_grouped_expert_mlp_mapped) equal the norm, the row gather and
+    the grouped MLP bit for bit on every valid pair."""
+    from koemi_5hom_b200 import _native
+    g = torch.Generator().manual_seed(tokens + experts)
+    fused = (torch.randn(tokens, width, generator=g) * 2.0).to(cuda)
+    norm = (1.0 + 0.1 * torch.randn(width, generator=g)).to(cuda)
+    assignments = torch.randint(-1, experts, (tokens, top_k), generator=g).to(cuda)
+    valid = (torch.rand(tokens, generator=g) > 0.1).to(cuda)
+    weights = tuple((torch.randn(*shape, generator=g) * 0.05).bfloat16().to(cuda) for shape in
+                    ((experts, hidden, width), (experts, hidden), (experts, hidden, width), (experts, hidden),
+                     (experts, width, hidden), (experts, width)))
+    context = _ops.rms_norm(fused, None, norm, None, 1e-6, torch.float32)
+    _, sorted_tokens, sorted_experts, offsets, positions = _ops.permute_topk(context, assignments, valid, experts,
+                                                                              False)
+    rows = _ops.gather_rows(context, sorted_tokens, offsets, torch.bfloat16)
+    expected = _ops.grouped_expert_mlp(rows, sorted_experts, offsets, *weights)
+    pairs = tokens * top_k
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    mine_context = torch.empty_like(context)
+    mine_rows = torch.zeros(pairs, width, dtype=torch.bfloat16, device=cuda)
+    _native.call("koemi_moe_norm_gather", fused.data_ptr(), norm.data_ptr(), 1e-6, mine_context.data_ptr(),
+                 positions.data_ptr(), offsets.data_ptr(), experts, mine_rows.data_ptr(), _native.BF16, tokens, width,
+                 top_k, stream)
+    prefix = torch.empty(experts + 1, dtype=torch.int32, device=cuda)
+    _native.call("koemi_moe_tile_prefix", offsets.data_ptr(), experts, prefix.data_ptr(), stream)
+    out = torch.empty(pairs, width, dtype=torch.bfloat16, device=cuda)
+    size = _native.library().koemi_moe_grouped_mlp_workspace(pairs, width, hidden, experts, _native.BF16)
+    workspace = _native.workspace(size, cuda)
+    _native.call("koemi_moe_grouped_expert_mlp_mapped", mine_rows.data_ptr(), prefix.data_ptr(), offsets.data_ptr(),
+                 *(w.data_ptr() for w in weights), out.data_ptr(), pairs, width, hidden, experts, _native.BF16,
+                 workspace.data_ptr(), workspace.numel(), stream)
+    torch.cuda.synchronize()
+    live = int(offsets[-1])
+    assert torch.equal(mine_context, context)
+    assert torch.equal(mine_rows[:live], rows[:live])
+    assert torch.equal(out[:live], expected[:live])
