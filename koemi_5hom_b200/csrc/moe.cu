@@ -163,26 +163,42 @@ __global__ __launch_bounds__(kSortThreads) void digit_count_kernel(const int32_t
 
 // Exclusive scan of the bucket-major counts array in place (one CTA, 16
 // consecutive counts per thread per round: two rounds for the config-4
-// permutation's 32768 counts). With `offsets` it also writes offsets[e] =
-// data[e * stride] for e < offsets_count: after a single-pass sort's scan that
-// is the number of keys below bucket e, i.e. the segment offsets.
+// permutation's 32768 counts). Each round's 16384 counts move between global
+// and shared memory with coalesced accesses (element i of the round at
+// i + i / 16 in shared memory, so each thread's 16 consecutive counts sit in
+// distinct banks across a warp); the scan itself reads and writes shared
+// memory. With `offsets` it also writes offsets[e] = data[e * stride] for
+// e < offsets_count: after a single-pass sort's scan that is the number of
+// keys below bucket e, i.e. the segment offsets.
 constexpr int kScanPerThread = 16;
-__global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restrict__ data, int64_t n,
-                                                              int64_t *__restrict__ offsets, int64_t stride,
-                                                              int64_t offsets_count) {
+constexpr int kScanThreads = 1024;
+constexpr int kScanRound = kScanThreads * kScanPerThread;
+constexpr size_t kScanSmemBytes = static_cast<size_t>(kScanRound + kScanRound / kScanPerThread) * sizeof(int32_t);
+__device__ __forceinline__ int scan_slot(int i) { return i + i / kScanPerThread; }
+
+__global__ __launch_bounds__(kScanThreads) void exclusive_scan_kernel(int32_t *__restrict__ data, int64_t n,
+                                                                      int64_t *__restrict__ offsets, int64_t stride,
+                                                                      int64_t offsets_count) {
+    extern __shared__ int32_t staged[];  // [kScanRound + kScanRound / 16]
     __shared__ int32_t warp_totals[32];
     __shared__ int32_t carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    for (int64_t base = 0; base < n; base += 1024 * kScanPerThread) {
-        const int64_t start = base + static_cast<int64_t>(threadIdx.x) * kScanPerThread;
+    for (int64_t base = 0; base < n; base += kScanRound) {
+#pragma unroll
+        for (int j = 0; j < kScanPerThread; ++j) {
+            const int i = j * kScanThreads + static_cast<int>(threadIdx.x);
+            staged[scan_slot(i)] = base + i < n ? data[base + i] : 0;
+        }
+        __syncthreads();
+        const int first = static_cast<int>(threadIdx.x) * kScanPerThread;
         int32_t v[kScanPerThread];
         int32_t sum = 0;
 #pragma unroll
         for (int j = 0; j < kScanPerThread; ++j) {
-            v[j] = start + j < n ? data[start + j] : 0;
+            v[j] = staged[scan_slot(first + j)];
             sum += v[j];
         }
         int32_t inclusive = sum;
@@ -206,24 +222,34 @@ __global__ __launch_bounds__(1024) void exclusive_scan_kernel(int32_t *__restric
         int32_t running = carry + (warp == 0 ? 0 : warp_totals[warp - 1]) + inclusive - sum;
 #pragma unroll
         for (int j = 0; j < kScanPerThread; ++j) {
-            if (start + j < n) data[start + j] = running;
+            staged[scan_slot(first + j)] = running;
             running += v[j];
         }
         __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kScanPerThread; ++j) {
+            const int i = j * kScanThreads + static_cast<int>(threadIdx.x);
+            if (base + i < n) data[base + i] = staged[scan_slot(i)];
+        }
         if (threadIdx.x == 0) carry += warp_totals[31];
         __syncthreads();
     }
     if (offsets != nullptr) {
-        for (int64_t e = threadIdx.x; e < offsets_count; e += 1024) offsets[e] = data[e * stride];
+        for (int64_t e = threadIdx.x; e < offsets_count; e += kScanThreads) offsets[e] = data[e * stride];
     }
 }
 
 // Scatter with the block's stable ranks. Round r handles pairs
 // base + r*256 + tid, so (round, warp, lane) order equals pair order.
+// With `final_positions` (the last pass, when nothing later needs the sorted
+// key and value arrays) the pass writes the finishing outputs instead:
+// sorted_rows[position] = pair / top_k, sorted_experts[position] = key and
+// final_positions[pair] = position (either of the first two may be NULL).
 __global__ __launch_bounds__(kSortThreads) void digit_scatter_kernel(
     const int32_t *__restrict__ keys_in, const int32_t *__restrict__ values_in, int64_t pairs, int shift,
     int buckets, const int32_t *__restrict__ offsets, int32_t *__restrict__ keys_out,
-    int32_t *__restrict__ values_out) {
+    int32_t *__restrict__ values_out, int64_t top_k, int64_t *__restrict__ sorted_rows,
+    int64_t *__restrict__ sorted_experts, int64_t *__restrict__ final_positions) {
     extern __shared__ int32_t shared[];
     int32_t *running = shared;                   // [buckets]
     int32_t *warp_counts = shared + buckets;     // [kSortWarps][buckets]
@@ -250,8 +276,15 @@ __global__ __launch_bounds__(kSortThreads) void digit_scatter_kernel(
         if (live) {
             for (int w = 0; w < warp; ++w) before += warp_counts[w * buckets + digit];
             const int32_t position = running[digit] + before + rank;
-            keys_out[position] = key;
-            values_out[position] = values_in[p];
+            if (final_positions != nullptr) {
+                const int32_t pair = values_in[p];
+                if (sorted_rows != nullptr) sorted_rows[position] = pair / top_k;
+                if (sorted_experts != nullptr) sorted_experts[position] = key;
+                final_positions[pair] = position;
+            } else {
+                keys_out[position] = key;
+                values_out[position] = values_in[p];
+            }
         }
         __syncthreads();
         for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
@@ -931,17 +964,24 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
         if (scatter_smem > 48 * 1024) {
             KOEMI_CUDA_TRY(cudaFuncSetAttribute(digit_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(scatter_smem)));
         }
+        KOEMI_CUDA_TRY(cudaFuncSetAttribute(exclusive_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(kScanSmemBytes)));
         for (int pass = 0; pass < l.passes; ++pass) {
             const int shift = pass * kDigitBits;
             digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
             KOEMI_LAUNCH_CHECK();
             // a single pass's scan also yields the segment offsets (every key in its own bucket)
             const bool last_single = l.passes == 1;
-            exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, l.blocks * l.buckets, last_single ? segment_offsets : nullptr,
-                                                     l.blocks, expert_count + 1);
+            exclusive_scan_kernel<<<1, kScanThreads, kScanSmemBytes, s>>>(
+                counts, l.blocks * l.buckets, last_single ? segment_offsets : nullptr, l.blocks, expert_count + 1);
             KOEMI_LAUNCH_CHECK();
+            // a single pass that also produces the pair positions writes the
+            // finishing outputs itself (the rows then move token-major)
+            const bool fused_finish = last_single && pair_positions != nullptr;
             digit_scatter_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, scatter_smem, s>>>(
-                keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b);
+                keys_a, values_a, pairs, shift, l.buckets, counts, keys_b, values_b, top_k,
+                fused_finish ? sorted_rows : nullptr, fused_finish ? sorted_experts : nullptr,
+                fused_finish ? pair_positions : nullptr);
             KOEMI_LAUNCH_CHECK();
             int32_t *t = keys_a; keys_a = keys_b; keys_b = t;
             t = values_a; values_a = values_b; values_b = t;
@@ -950,8 +990,10 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
             segment_offsets_kernel<<<static_cast<unsigned>(ceil_div(expert_count + 1, 256)), 256, 0, s>>>(keys_a, pairs, expert_count, segment_offsets);
             KOEMI_LAUNCH_CHECK();
         }
-        finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
-        KOEMI_LAUNCH_CHECK();
+        if (!(l.passes == 1 && pair_positions != nullptr)) {
+            finish_permutation_kernel<<<pair_blocks, 256, 0, s>>>(keys_a, values_a, pairs, top_k, sorted_rows, sorted_experts, pair_positions);
+            KOEMI_LAUNCH_CHECK();
+        }
     }
     if (sorted_context != nullptr && width > 0 && pair_positions != nullptr) {
         const size_t es = dtype_size(context_dtype);
