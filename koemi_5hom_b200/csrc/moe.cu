@@ -133,16 +133,6 @@ __device__ __forceinline__ int32_t pair_key(const Index *assignments, const uint
     return ok ? static_cast<int32_t>(e) : static_cast<int32_t>(experts);
 }
 
-template <typename Index>
-__global__ void build_keys_kernel(const Index *__restrict__ assignments, const uint8_t *__restrict__ valid,
-                                  int32_t *__restrict__ keys, int32_t *__restrict__ values, int64_t pairs,
-                                  int64_t top_k, int64_t experts) {
-    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (p >= pairs) return;
-    keys[p] = pair_key(assignments, valid, p, top_k, experts);
-    values[p] = static_cast<int32_t>(p);
-}
-
 // counts[bucket * blocks + block] = number of keys of `block` in `bucket`.
 __global__ __launch_bounds__(kSortThreads) void digit_count_kernel(const int32_t *__restrict__ keys, int64_t pairs,
                                                                    int shift, int buckets,
@@ -154,6 +144,35 @@ __global__ __launch_bounds__(kSortThreads) void digit_count_kernel(const int32_t
     for (int r = 0; r < kPairsPerThread; ++r) {
         const int64_t p = base + r * kSortThreads + threadIdx.x;
         if (p < pairs) atomicAdd(&hist[(keys[p] >> shift) & (buckets - 1)], 1);
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
+        counts[static_cast<int64_t>(b) * gridDim.x + blockIdx.x] = hist[b];
+    }
+}
+
+// The first pass's count fused with building the keys: each thread makes the
+// keys of the pairs it counts (the same pair-to-thread mapping as
+// digit_count_kernel) and stores them with their pair index for the scatter.
+template <typename Index>
+__global__ __launch_bounds__(kSortThreads) void keys_count_kernel(const Index *__restrict__ assignments,
+                                                                  const uint8_t *__restrict__ valid,
+                                                                  int32_t *__restrict__ keys,
+                                                                  int32_t *__restrict__ values, int64_t pairs,
+                                                                  int64_t top_k, int64_t experts, int buckets,
+                                                                  int32_t *__restrict__ counts) {
+    extern __shared__ int32_t hist[];
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) hist[b] = 0;
+    __syncthreads();
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kPairsPerBlock;
+    for (int r = 0; r < kPairsPerThread; ++r) {
+        const int64_t p = base + r * kSortThreads + threadIdx.x;
+        if (p < pairs) {
+            const int32_t key = pair_key(assignments, valid, p, top_k, experts);
+            keys[p] = key;
+            values[p] = static_cast<int32_t>(p);
+            atomicAdd(&hist[key & (buckets - 1)], 1);
+        }
     }
     __syncthreads();
     for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
@@ -953,12 +972,6 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
         if (rc != KOEMI_OK) return rc;
     } else {
         const unsigned pair_blocks = static_cast<unsigned>(ceil_div(pairs, 256));
-        if (wide_index) {
-            build_keys_kernel<int64_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int64_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
-        } else {
-            build_keys_kernel<int32_t><<<pair_blocks, 256, 0, s>>>(static_cast<const int32_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count);
-        }
-        KOEMI_LAUNCH_CHECK();
         const size_t count_smem = static_cast<size_t>(l.buckets) * sizeof(int32_t);
         const size_t scatter_smem = static_cast<size_t>(l.buckets) * (kSortWarps + 1) * sizeof(int32_t);
         if (scatter_smem > 48 * 1024) {
@@ -968,7 +981,17 @@ extern "C" int koemi_moe_permute_topk(const void *context, const void *assignmen
                                             static_cast<int>(kScanSmemBytes)));
         for (int pass = 0; pass < l.passes; ++pass) {
             const int shift = pass * kDigitBits;
-            digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
+            if (pass > 0) {
+                digit_count_kernel<<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(keys_a, pairs, shift, l.buckets, counts);
+            } else if (wide_index) {  // the keys are built by the first count
+                keys_count_kernel<int64_t><<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(
+                    static_cast<const int64_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count,
+                    l.buckets, counts);
+            } else {
+                keys_count_kernel<int32_t><<<static_cast<unsigned>(l.blocks), kSortThreads, count_smem, s>>>(
+                    static_cast<const int32_t *>(assignments), valid, keys_a, values_a, pairs, top_k, expert_count,
+                    l.buckets, counts);
+            }
             KOEMI_LAUNCH_CHECK();
             // a single pass's scan also yields the segment offsets (every key in its own bucket)
             const bool last_single = l.passes == 1;
