@@ -145,10 +145,17 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.process = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                             "--format=csv,noheader,nounits", "-lms", "100"],
+                                             "--format=csv,noheader,nounits", "-lms", "50"],
                                             stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.process = None
+        # nvidia-smi needs a few hundred ms before its first row: wait for it, so
+        # that a short timed region (20 steps at 8 GPUs is ~0.1 s) is sampled,
+        # and count only the rows written after this point
+        deadline = time.perf_counter() + 3.0
+        while self.process is not None and time.perf_counter() < deadline and os.path.getsize(self.file.name) == 0:
+            time.sleep(0.01)
+        self.start_offset = os.path.getsize(self.file.name)
         return self
 
     def __exit__(self, *exc):
@@ -161,20 +168,29 @@ class ClockSampler:
         self.file.flush()
 
     def summary(self) -> dict:
-        rows = []
+        rows, before = [], []
         with open(self.file.name) as handle:
-            for line in handle:
+            text = handle.read()
+        for chunk, into in ((text[getattr(self, "start_offset", 0):], rows), (text[:getattr(self, "start_offset", 0)], before)):
+            for line in chunk.splitlines():
                 parts = [p.strip() for p in line.split(",")]
                 if len(parts) >= 9:
-                    rows.append(parts)
+                    into.append(parts)
         os.unlink(self.file.name)
+        adjacent = not rows and bool(before)
+        if adjacent:  # no row inside the region: the last one taken just before it starts
+            rows = before[-1:]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+        summary = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                   "reasons": reasons, "samples": 0 if adjacent else len(rows),
+                   "power_w_max": max(float(r[3]) for r in rows)}
+        if adjacent:
+            summary["sampled"] = "the last row before the timed region (none fell inside it)"
+        return summary
 
 
 # ----------------------------------------------------------------- CPU side

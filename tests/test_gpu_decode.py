@@ -167,6 +167,38 @@ def test_assoc_decode_step_matches_oracle(feature_source, batch, d, cuda):
     torch.testing.assert_close(n_dev.cpu().double(), new_norm, rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("weight_dtype", [torch.float32, torch.bfloat16])
+def test_assoc_decode_stream_does_not_depend_on_its_batch(weight_dtype, cuda):
+    """A stream's read, basis and normalizer are bit-identical whether it is
+    stepped in a batch of 256 streams, 100 or 5: the batch size sets how many
+    CTAs share a stream's rows (on 148 SMs one at 256 streams, 2 at 100, 8 at
+    5), and every CTA computes the stream's feature logits in full and only
+    its own rows, so the split leaves the arithmetic unchanged."""
+    g = torch.Generator().manual_seed(11)
+    batch, d, m = 256, 2048, 16
+    proj = torch.randn(batch, 3 * d + 2, generator=g).to(cuda)
+    weight = (torch.randn(m, d, generator=g) * 0.1).to(weight_dtype).to(cuda)
+    bias = (torch.randn(m, generator=g) * 0.1).to(weight_dtype).to(cuda)
+    surprise = torch.rand(batch, generator=g).to(cuda)
+    valid = (torch.rand(batch, generator=g) > 0.2).to(cuda)
+    basis = (torch.randn(batch, d, m, generator=g) * 0.1).to(cuda)
+    normalizer = torch.rand(batch, m, generator=g).to(cuda)
+    results = {}
+    for rows in (256, 100, 5):
+        b_dev, n_dev = basis[:rows].clone(), normalizer[:rows].clone()
+        out = torch.zeros(rows, d, device=cuda)
+        p = _native.ptr
+        _native.call("koemi_assoc_decode_step", p(proj), 3 * d + 2, None, p(weight), p(bias),
+                     _native.dtype_code(weight_dtype), p(surprise), p(valid), p(b_dev), p(n_dev), p(out), d, rows,
+                     d, m, _native.F32, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        results[rows] = (out, b_dev, n_dev)
+    for rows in (100, 5):
+        for got, full in zip(results[rows], results[256]):
+            assert torch.equal(got, full[:rows]), rows
+    _native.raise_for_device_status(cuda)
+
+
 def _oracle_scan_read(basis, normalizer, decay, value, features, write, qf):
     from oracle.herm import HermOracle
     reads, b, n = HermOracle._scan_read(None, basis, normalizer, decay.unsqueeze(1), value.unsqueeze(1),
