@@ -585,8 +585,9 @@ def run_b200(args) -> None:
                      "unit": "GB/s", "frac": achieved / hbm_peak,
                      # dram__bytes_read.sum + dram__bytes_write.sum of both expert GEMMs for one call at this
                      # workload's pair distribution (512 pairs, 64 experts), from one ncu capture of
-                     # `bench.py --op expert_decode` (profiles/expert_mlp_decode_config5.md); none was taken
-                     # of an expert-parallel owner's share
+                     # `bench.py --op expert_decode` (2,163,557,888 B for the gated GEMM, 1,082,892,544 B for
+                     # the output GEMM, first launches under ncu); none was taken of an expert-parallel
+                     # owner's share
                      "traffic": 3246450432 if not expert_parallel(args, world) else None,
                      "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mlp["bytes"], "launch_us": mlp["seconds"] * 1e6,
