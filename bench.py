@@ -155,8 +155,13 @@ class ClockSampler:
         deadline = time.perf_counter() + 3.0
         while self.process is not None and time.perf_counter() < deadline and os.path.getsize(self.file.name) == 0:
             time.sleep(0.01)
-        self.start_offset = os.path.getsize(self.file.name)
+        self.mark()
         return self
+
+    def mark(self) -> None:
+        """The timed region starts here: rows written so far are not counted
+        as inside it (call it after any barrier that follows ``__enter__``)."""
+        self.start_offset = os.path.getsize(self.file.name)
 
     def __exit__(self, *exc):
         if self.process is not None:
@@ -492,11 +497,14 @@ def run_b200(args) -> None:
 
     stream = torch.cuda.current_stream(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    progress(rank, "graph captured and warmed up; timing")
+    # the sampler starts (and waits for its first row) before the barrier, so
+    # the ranks leave the barrier together and enter the timed region at once
     with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        progress(rank, "graph captured and warmed up; timing")
+        clocks.mark()
         torch.cuda.nvtx.range_push("decode_timed")
         start.record(stream)
         for _ in range(args.steps):

@@ -64,3 +64,17 @@ def test_missing_tool_is_unsampled(monkeypatch, tmp_path):
     with bench.ClockSampler(0) as sampler:
         pass
     assert sampler.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+
+def test_mark_excludes_rows_before_the_region(fake_path):
+    """Rows written between ``__enter__`` and ``mark()`` (a barrier between
+    the ranks, in the bench) are not counted as inside the timed region."""
+    fake_path(delay_s=0.0, period_s=0.02, mhz=1700)
+    with bench.ClockSampler(0) as sampler:
+        time.sleep(0.2)  # rows here belong to the barrier, not the region
+        sampler.mark()
+        marked = sampler.start_offset
+        time.sleep(0.1)
+    summary = sampler.summary()
+    assert marked > 0
+    assert 1 <= summary["samples"] <= 10  # ~5 rows at 20 ms in 0.1 s, none of the ~10 before mark()
